@@ -1,0 +1,483 @@
+"""Benchmark of the hachiue attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0).  The default workload is configuration 2 of the
+benchmark set: Qwen3-8B-shape batched GQA decode attention, 64 sequences,
+32 query / 8 KV heads, head_dim 128, per-sequence contexts U[512, 8192]
+(seed 1), f16 KV cache, f32 q / out.  A step is one decode-attention pass over
+the whole batch.  Other configurations (--config 1, 4) are available for
+profiling; their parity is covered by the tests.
+
+Timing: CUDA events on the launching stream, W untimed warm-up steps, K timed
+steps bracketed by barrier + synchronize, max over ranks.  The config-2 working
+set (1.1 GB of K/V) is larger than L2 (126 MB), so no flush is needed; the
+smaller configurations rotate through enough input copies to exceed L2.
+
+``value`` is aggregate algorithmic HBM GB/s of the attention kernel over all
+ranks (inputs resident in HBM); ``e2e`` is the same metric through the public
+``CudaBackend`` API with the step's inputs (q and the step's new K/V rows)
+copied from pinned host memory, the K/V append, the attention and the output
+read back every step.  Multi-GPU (torchrun) is weak scaling: each rank owns its
+own 64-sequence batch, and the per-head outputs of all ranks are all-gathered
+over NCCL every step.
+
+``--impl reference`` times the reference algorithm on the host cores instead:
+the reference is TypeScript and cannot run here, so this arm runs the C
+restatement in oracle/ (its JS-semantics port), multi-threaded over sequences,
+on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return PEAKS_FALLBACK, "fallback"
+
+
+def load_traffic(key: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/dram_traffic.txt: '<key> <bytes>' lines), or None."""
+    p = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+    try:
+        for line in open(p):
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == key:
+                return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------
+# workloads (device side)
+# ---------------------------------------------------------------------------
+def setup_cfg2(torch, be, dev):
+    from hachiue_b200 import KV_F16, workloads
+    from hachiue_b200.backend import KVCache
+    w = workloads.decode_cfg2()
+    k = torch.from_numpy(w["k"].view(np.int16)).to(dev).view(torch.float16)
+    v = torch.from_numpy(w["v"].view(np.int16)).to(dev).view(torch.float16)
+    cache = KVCache(KV_F16, k, v)
+    q = torch.from_numpy(w["q"]).to(dev)
+    out = torch.zeros_like(q)
+    pos = torch.from_numpy(w["pos_base"]).to(dev)
+    off = torch.from_numpy(w["row_offset"]).to(dev)
+    maxc = int(w["lens"].max())
+    nbytes = workloads.cfg2_bytes(w["lens"])
+
+    def step(i):
+        be.attention(q, cache, out, pos, 0, kv_row_offset=off, max_context=maxc)
+
+    # e2e: the user-facing decode step through the public API with host buffers.
+    B, KV, Dh = 64, 8, 128
+    q_host = torch.from_numpy(w["q"]).pin_memory()
+    kv_new_host = torch.from_numpy(
+        np.random.default_rng(99).standard_normal((2, B, KV, Dh), dtype=np.float32)).pin_memory()
+    out_host = torch.empty_like(q_host).pin_memory()
+    q_dev = torch.empty_like(q)
+    kv_new_dev = torch.empty((2, B, KV, Dh), device=dev)
+    # the step appends one row per sequence at its last position (rows already
+    # counted in lens), then runs attention over the full context
+    last_rows = torch.from_numpy(w["row_offset"] + w["lens"] - 1).to(dev)
+
+    def e2e_step(i):
+        q_dev.copy_(q_host, non_blocking=True)
+        kv_new_dev.copy_(kv_new_host, non_blocking=True)
+        be.kv_append_rows(kv_new_dev[0], cache, "k", last_rows)
+        be.kv_append_rows(kv_new_dev[1], cache, "v", last_rows)
+        be.attention(q_dev, cache, out, pos, 0, kv_row_offset=off, max_context=maxc)
+        out_host.copy_(out, non_blocking=True)
+
+    h2d = q_host.numel() * 4 + kv_new_host.numel() * 4
+    d2h = out_host.numel() * 4
+    info = dict(workload="cfg2 Qwen3-8B batched GQA decode attention", sequences=64, q_heads=32, kv_heads=8,
+                head_dim=128, kv_dtype="f16", context="U[512,8192] seed 1", sum_context=int(w["lens"].sum()),
+                l2="inputs (1.1 GB K/V) larger than L2")
+    cpu = dict(w=w, kind="cfg2")
+    return dict(step=step, e2e_step=e2e_step, bytes=nbytes, tokens=64, info=info, h2d=h2d, d2h=d2h,
+                kernels_per_step=1, e2e_kernels_per_step=3, cpu=cpu, out=out, traffic_key="cfg2")
+
+
+def setup_cfg1(torch, be, dev):
+    from hachiue_b200 import KV_F32, workloads
+    from hachiue_b200.backend import KVCache
+    w = workloads.decode_cfg1()
+    copies = 32  # 32 x 8.4 MB > L2: each step reads a cold copy
+    caches = [KVCache(KV_F32, torch.from_numpy(w["k"]).to(dev), torch.from_numpy(w["v"]).to(dev))
+              for _ in range(copies)]
+    q = torch.from_numpy(w["q"]).to(dev)
+    out = torch.zeros_like(q)
+
+    def step(i):
+        be.attention(q, caches[i % copies], out, w["pos_base"])
+
+    q_host = torch.from_numpy(w["q"]).pin_memory()
+    out_host = torch.empty_like(q_host).pin_memory()
+    q_dev = torch.empty_like(q)
+
+    def e2e_step(i):
+        q_dev.copy_(q_host, non_blocking=True)
+        be.attention(q_dev, caches[i % copies], out, w["pos_base"])
+        out_host.copy_(out, non_blocking=True)
+
+    info = dict(workload="cfg1 Qwen3-1.7B GQA decode attention", q_heads=16, kv_heads=8, head_dim=128, context=1024,
+                kv_dtype="f32", l2=f"rotates {copies} cache copies (> L2)")
+    return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg1_bytes(), tokens=1, info=info,
+                h2d=q_host.numel() * 4, d2h=out_host.numel() * 4, kernels_per_step=1, e2e_kernels_per_step=1,
+                cpu=dict(w=w, kind="cfg1"), out=out, traffic_key="cfg1")
+
+
+def setup_cfg4(torch, be, dev):
+    from hachiue_b200 import workloads
+    w = workloads.gdn_decode_cfg4()
+    NK, NV = w["NK"], w["NV"]
+    copies = 2  # 2 x 268 MB of state > L2
+    states = [torch.from_numpy(w["state"]).to(dev) for _ in range(copies)]
+    qkv = torch.from_numpy(w["qkv"]).to(dev)
+    a = torch.from_numpy(w["a"]).to(dev)
+    b = torch.from_numpy(w["b"]).to(dev)
+    an = torch.from_numpy(w["a_neg"]).to(dev)
+    dtb = torch.from_numpy(w["dt_bias"]).to(dev)
+    core = torch.zeros((64, 1, NV, 128), device=dev)
+
+    def step(i):
+        st = states[i % copies]
+        be.deltanet_decode(qkv, a, b, an, dtb, st, core, st, NK, NV)
+
+    qkv_h = torch.from_numpy(w["qkv"]).pin_memory()
+    a_h = torch.from_numpy(w["a"]).pin_memory()
+    b_h = torch.from_numpy(w["b"]).pin_memory()
+    core_h = torch.empty(core.shape).pin_memory()
+    qkv_d, a_d, b_d = torch.empty_like(qkv), torch.empty_like(a), torch.empty_like(b)
+
+    def e2e_step(i):
+        qkv_d.copy_(qkv_h, non_blocking=True)
+        a_d.copy_(a_h, non_blocking=True)
+        b_d.copy_(b_h, non_blocking=True)
+        st = states[i % copies]
+        be.deltanet_decode(qkv_d, a_d, b_d, an, dtb, st, core, st, NK, NV)
+        core_h.copy_(core, non_blocking=True)
+
+    info = dict(workload="cfg4 Qwen3.5 Gated DeltaNet decode step", sequences=64, qk_heads=16, v_heads=32, d=128,
+                state="f32 [64,32,128,128]", l2="rotates 2 state copies (> L2)")
+    return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg4_bytes(), tokens=64, info=info,
+                h2d=(qkv_h.numel() + a_h.numel() + b_h.numel()) * 4, d2h=core_h.numel() * 4, kernels_per_step=1,
+                e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg4"), out=core, traffic_key="cfg4")
+
+
+SETUPS = {1: setup_cfg1, 2: setup_cfg2, 4: setup_cfg4}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (the reference's algorithm on the host cores)
+# ---------------------------------------------------------------------------
+def cpu_sample(kind: str, w: dict, threads: int, budget_s: float = 12.0):
+    """Times the oracle (JS-semantics C restatement) on a bounded sample of the
+    workload; returns (GB/s, tokens/s, description)."""
+    import oracle
+    from hachiue_b200 import workloads
+    if kind == "cfg2":
+        lens = w["lens"]
+        t0 = time.perf_counter()
+        done_b, done_bytes, reps = 0, 0, 0
+        k16, v16 = w["k"].view(np.uint16), w["v"].view(np.uint16)
+        while time.perf_counter() - t0 < budget_s and reps < 4:
+            oracle.attention_batch(w["q"], k16, v16, w["pos_base"], w["row_offset"], 0, oracle.KV_F16,
+                                   threads=threads)
+            done_b += 64
+            done_bytes += workloads.cfg2_bytes(lens)
+            reps += 1
+        dt = time.perf_counter() - t0
+        return done_bytes / dt / 1e9, done_b / dt, f"{reps} full passes of cfg2 (64 sequences, f16 KV) on {threads} threads"
+    if kind == "cfg1":
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < min(budget_s, 5.0):
+            oracle.attention(w["q"][0], w["k"], w["v"], w["pos_base"])
+            n += 1
+        dt = time.perf_counter() - t0
+        return n * workloads.cfg1_bytes() / dt / 1e9, n / dt, f"{n} cfg1 calls, 1 thread"
+    if kind == "cfg4":
+        B = 16
+        gb = np.stack([oracle.deltanet_gbeta(w["a"][b], w["b"][b], w["a_neg"], w["dt_bias"]) for b in range(B)])
+        t0 = time.perf_counter()
+        oracle.deltanet_recur_batch(w["qkv"][:B], gb, w["state"][:B], w["NK"], w["NV"], True, threads=threads)
+        dt = time.perf_counter() - t0
+        return workloads.cfg4_bytes(B=B) / dt / 1e9, B / dt, f"{B} of 64 sequences of cfg4 on {threads} threads"
+    raise ValueError(kind)
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's algorithm (oracle port) on the host."""
+    if rank != 0:
+        return 0
+    import oracle
+    from hachiue_b200 import workloads
+    threads = os.cpu_count() or 1
+    if args.config == 2:
+        w = workloads.decode_cfg2()
+    elif args.config == 1:
+        w = workloads.decode_cfg1()
+    else:
+        w = workloads.gdn_decode_cfg4()
+    kind = f"cfg{args.config}"
+    for _ in range(args.warmup):
+        cpu_sample(kind, w, threads, budget_s=0.5)
+    vals = []
+    t_all = time.perf_counter()
+    desc = ""
+    for _ in range(args.steps):
+        gbs, tps, desc = cpu_sample(kind, w, threads, budget_s=2.0)
+        vals.append(gbs)
+    elapsed = time.perf_counter() - t_all
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": metric_name(args.config), "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * elapsed / max(args.steps, 1), 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(args.config), "data": "synthetic",
+        "config": {"workload": f"cfg{args.config} (see --impl ours)", "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": desc + "; the reference is TypeScript with no runtime on this box, so its "
+                                          "JS-semantics C restatement (oracle/) is timed"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def metric_name(cfg: int) -> str:
+    return {1: "decode attn HBM GB/s", 2: "decode attn HBM GB/s", 4: "GDN decode HBM GB/s"}[cfg]
+
+
+def dtype_name(cfg: int) -> str:
+    return {1: "f32", 2: "f16", 4: "f32"}[cfg]
+
+
+# ---------------------------------------------------------------------------
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(SETUPS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from hachiue_b200 import CudaBackend
+    be = CudaBackend(local)
+    W = SETUPS[args.config](torch, be, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    gather_out = None
+    if world > 1:
+        gather_out = torch.empty((world,) + tuple(W["out"].shape), device=dev, dtype=W["out"].dtype)
+
+    def full_step(i):
+        W["step"](i)
+        if world > 1:
+            dist.all_gather_into_tensor(gather_out, W["out"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # ---- device-resident timing ----
+    for i in range(args.warmup):
+        full_step(i)
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        kev[i][0].record(stream)
+        W["step"](i)
+        kev[i][1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gather_out, W["out"])
+    t_end.record(stream)
+    barrier()
+    clk = clocks.stop()
+    total_ms = t_start.elapsed_time(t_end)
+    kernel_ms = [a.elapsed_time(b) for a, b in kev]
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    status = be.device_status()
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
+
+    ms_per_step = total_ms / args.steps
+    value = world * W["bytes"] / (ms_per_step / 1e3) / 1e9
+    kavg = statistics.mean(kernel_ms)
+    achieved = W["bytes"] / (kavg / 1e3) / 1e9
+
+    # ---- end to end through the public API (host buffers) ----
+    for i in range(args.warmup):
+        W["e2e_step"](i)
+        if world > 1:
+            dist.all_gather_into_tensor(gather_out, W["out"])
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        W["e2e_step"](i)
+        if world > 1:
+            dist.all_gather_into_tensor(gather_out, W["out"])
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * W["bytes"] / (e2e_ms / args.steps / 1e3) / 1e9
+
+    peaks, peak_src = load_peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        gbs, _, desc = cpu_sample(W["cpu"]["kind"], W["cpu"]["w"], threads)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": desc + " (the reference is TypeScript with no runtime here; its JS-semantics C "
+                                "restatement in oracle/ is timed)"}
+
+    if rank == 0:
+        traffic = load_traffic(W["traffic_key"])
+        line = {
+            "metric": metric_name(args.config), "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(args.config),
+            "data": "synthetic (seeded numpy PCG64, benchmark-config shapes)",
+            "config": dict(W["info"], parallelism=f"dp{world} (sequences per rank) + NCCL all-gather of outputs"
+                           if world > 1 else "single GPU"),
+            "tokens_per_s": round(world * W["tokens"] / (ms_per_step / 1e3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peak_src,
+                         "algorithmic_bytes_per_launch": W["bytes"], "kernel_ms": round(kavg, 5),
+                         "traffic": traffic},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": W["h2d"],
+                    "d2h_bytes_per_step": W["d2h"], "ms_per_step": round(e2e_ms / args.steps, 5)},
+            "gpu_launches": args.steps * W["kernels_per_step"],
+            "e2e_gpu_launches": args.steps * W["e2e_kernels_per_step"],
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    be.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

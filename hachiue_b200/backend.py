@@ -1,0 +1,212 @@
+"""The ``cuda`` backend: hachiue's attention-dispatch seam over libhachiue_cuda.
+
+``CudaBackend.dispatch(shader_name, words, buffers)`` mirrors
+``HachiueEngine.dispatch(pass, shaderName, uniformBuf, storageBufs, gx)``
+(src/engine.ts:1056-1075) with the uniform words of ``mkUniform``
+(src/engine.ts:1040-1054): the same op names, the same words, the same buffer
+order, and ``HachiueError('hachiue: missing pipeline <name>')`` for an unknown
+name.  The typed methods are the same ops with named arguments plus the
+batched forms the B200 build adds.
+
+Buffers are CUDA ``torch.Tensor`` objects (torch is only the device-memory and
+stream plumbing); every call enqueues on the current torch stream of the
+backend's device, like a WebGPU dispatch, and never allocates.
+"""
+from __future__ import annotations
+
+import ctypes
+import struct
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import (KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueError, check, hcu_attention_params,
+                   hcu_deltanet_params, hcu_kv_cache)
+
+# The reference's op names on this path (src/kernels.ts SHADERS keys).
+SHADERS = ("kv_append_q8", "attention_q8", "deltanet_gbeta", "deltanet_recur")
+
+_DTYPE_OF_FORMAT = {KV_F32: torch.float32, KV_F16: torch.float16, KV_BF16: torch.bfloat16, KV_Q8_0: torch.int8}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise HachiueError(_lib.HCU_EINVAL, "hachiue: buffers must be CUDA tensors (no CPU fallback)")
+    return t.data_ptr()
+
+
+def f32_word(x: float) -> int:
+    """A float uniform word, as mkUniform's setFloat32 (src/engine.ts:1043)."""
+    return struct.unpack("<I", struct.pack("<f", x))[0]
+
+
+@dataclass
+class KVCache:
+    """One layer's KV cache: K and V [rows, KV, Dh] (+ f32 scales [rows, KV,
+    Dh/32] for Q8_0), the engine's kCacheQ/kCacheS/vCacheQ/vCacheS
+    (src/engine.ts:339-343, :483-492)."""
+    fmt: int
+    k: torch.Tensor
+    v: torch.Tensor
+    k_scale: torch.Tensor | None = None
+    v_scale: torch.Tensor | None = None
+
+    @staticmethod
+    def allocate(rows: int, kv_heads: int, head_dim: int, fmt: int = KV_Q8_0, device="cuda") -> "KVCache":
+        dt = _DTYPE_OF_FORMAT[fmt]
+        k = torch.zeros((rows, kv_heads, head_dim), dtype=dt, device=device)
+        v = torch.zeros_like(k)
+        ks = vs = None
+        if fmt == KV_Q8_0:
+            ks = torch.zeros((rows, kv_heads, head_dim // 32), dtype=torch.float32, device=device)
+            vs = torch.zeros_like(ks)
+        return KVCache(fmt, k, v, ks, vs)
+
+    @property
+    def rows(self) -> int:
+        return self.k.shape[0]
+
+    def c_struct(self) -> hcu_kv_cache:
+        return hcu_kv_cache(self.fmt, self.rows, _ptr(self.k), _ptr(self.v), _ptr(self.k_scale), _ptr(self.v_scale))
+
+
+class CudaBackend:
+    """A libhachiue_cuda handle bound to one CUDA device."""
+
+    def __init__(self, device: int | torch.device | None = None, workspace_bytes: int = 0):
+        self.lib = _lib.load()
+        if device is None:
+            device = torch.cuda.current_device()
+        self.device = torch.device("cuda", device if isinstance(device, int) else device.index or 0)
+        h = ctypes.c_void_p()
+        check(self.lib.hcu_create(self.device.index, workspace_bytes, ctypes.byref(h)))
+        self._h = h
+
+    # -- lifecycle -----------------------------------------------------------
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self.lib.hcu_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _bind_stream(self) -> None:
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        check(self.lib.hcu_set_stream(self._h, ctypes.c_void_p(s)))
+
+    def sync(self) -> None:
+        self._bind_stream()
+        check(self.lib.hcu_stream_sync(self._h))
+
+    def device_status(self, clear: bool = True) -> int:
+        self._bind_stream()
+        st = ctypes.c_uint32()
+        check(self.lib.hcu_device_status(self._h, ctypes.byref(st), int(clear)))
+        return st.value
+
+    def inject_failure(self, status: int, n: int = 1) -> None:
+        """Make the next ``n`` op calls fail on the host with ``status``."""
+        check(self.lib.hcu_inject_failure(self._h, status, n))
+
+    # -- the reference's seam --------------------------------------------------
+    def dispatch(self, shader_name: str, words, buffers) -> None:
+        """engine.dispatch(): ``words`` are up to eight u32 uniform words (use
+        :func:`f32_word` for float words), ``buffers`` the storage buffers in
+        binding order."""
+        self._bind_stream()
+        w = (ctypes.c_uint32 * 8)(*([int(x) & 0xFFFFFFFF for x in words] + [0] * (8 - len(words))))
+        bufs = (ctypes.c_void_p * max(1, len(buffers)))(*[_ptr(b) for b in buffers])
+        check(self.lib.hcu_dispatch(self._h, shader_name.encode(), w, bufs, len(buffers)))
+
+    # -- typed ops -----------------------------------------------------------
+    def kv_append(self, src: torch.Tensor, cache: KVCache, which: str, pos_base: int) -> None:
+        """Append src f32 [S, KV, Dh] to K (``which='k'``) or V at row pos_base."""
+        self._bind_stream()
+        S, KV, Dh = src.shape
+        data, scale = (cache.k, cache.k_scale) if which == "k" else (cache.v, cache.v_scale)
+        if pos_base + S > cache.rows:
+            raise HachiueError(_lib.HCU_EINVAL, f"hachiue: context length {pos_base + S} exceeds cache rows {cache.rows}")
+        check(self.lib.hcu_kv_append(self._h, S, KV, Dh, pos_base, cache.fmt, _ptr(src.contiguous()), _ptr(data),
+                                     _ptr(scale)))
+
+    def kv_append_rows(self, src: torch.Tensor, cache: KVCache, which: str, dst_rows: torch.Tensor) -> None:
+        """Append src f32 [n, KV, Dh]: row i goes to cache row dst_rows[i]
+        (int64 CUDA tensor), e.g. one new token per sequence of a batch."""
+        self._bind_stream()
+        n, KV, Dh = src.shape
+        data, scale = (cache.k, cache.k_scale) if which == "k" else (cache.v, cache.v_scale)
+        check(self.lib.hcu_kv_append_rows(self._h, n, KV, Dh, cache.fmt, _ptr(src.contiguous()), _ptr(dst_rows),
+                                          _ptr(data), _ptr(scale)))
+
+    def attention(self, q: torch.Tensor, cache: KVCache, out: torch.Tensor, pos_base, window_size: int = 0,
+                  kv_heads: int | None = None, kv_row_offset: torch.Tensor | None = None,
+                  max_context: int = 0, seq_row_stride: int = 0) -> None:
+        """GQA attention of q [S, H, Dh] (or [B, S, H, Dh]) over ``cache``.
+
+        ``pos_base`` is an int (single sequence) or an int32 CUDA tensor [B];
+        batched sequences read cache rows ``kv_row_offset[b] + j``."""
+        self._bind_stream()
+        batched = q.dim() == 4
+        B = q.shape[0] if batched else 1
+        S, H, Dh = q.shape[-3:]
+        KV = kv_heads or cache.k.shape[1]
+        p = hcu_attention_params()
+        p.S, p.H, p.KV, p.Dh = S, H, KV, Dh
+        p.windowSize = window_size
+        p.batch = B
+        if isinstance(pos_base, torch.Tensor):
+            p.posBase = 0
+            p.pos_base = _ptr(pos_base)
+            if not max_context:  # convenience only: costs a device sync; pass it on hot paths
+                max_context = int(pos_base.max().item()) + S
+        else:
+            p.posBase = int(pos_base)
+            p.pos_base = None
+        p.max_context = max_context
+        p.kv_row_offset = _ptr(kv_row_offset)
+        p.seq_row_stride = seq_row_stride
+        kv = cache.c_struct()
+        check(self.lib.hcu_attention(self._h, ctypes.byref(p), _ptr(q), ctypes.byref(kv), _ptr(out)))
+
+    def deltanet_gbeta(self, a: torch.Tensor, b: torch.Tensor, a_neg: torch.Tensor, dt_bias: torch.Tensor,
+                       out: torch.Tensor) -> None:
+        """g / beta of a, b [S, NV] into out [2, S, NV]."""
+        self._bind_stream()
+        S, NV = a.shape
+        check(self.lib.hcu_deltanet_gbeta(self._h, S, NV, _ptr(a), _ptr(b), _ptr(a_neg), _ptr(dt_bias), _ptr(out)))
+
+    @staticmethod
+    def _dn_params(qkv_conv: torch.Tensor, NK: int, NV: int, D: int, load_state: bool) -> hcu_deltanet_params:
+        p = hcu_deltanet_params()
+        batched = qkv_conv.dim() == 3
+        p.batch = qkv_conv.shape[0] if batched else 1
+        p.S = qkv_conv.shape[-2]
+        p.H, p.DK, p.DV, p.HK = NV, D, D, NK
+        p.loadState = int(bool(load_state))
+        return p
+
+    def deltanet_recur(self, qkv_conv: torch.Tensor, gbeta: torch.Tensor, state_in: torch.Tensor,
+                       core: torch.Tensor, state_out: torch.Tensor, NK: int, NV: int, load_state: bool = True,
+                       D: int = 128) -> None:
+        """deltanet_recur: qkv_conv [(B,) S, convDim], gbeta [(B,) 2, S, NV],
+        states [(B,) NV, D, D], core [(B,) S, NV, D]."""
+        self._bind_stream()
+        p = self._dn_params(qkv_conv, NK, NV, D, load_state)
+        check(self.lib.hcu_deltanet_recur(self._h, ctypes.byref(p), _ptr(qkv_conv), _ptr(gbeta), _ptr(state_in),
+                                          _ptr(core), _ptr(state_out)))
+
+    def deltanet_decode(self, qkv_conv: torch.Tensor, a: torch.Tensor, b: torch.Tensor, a_neg: torch.Tensor,
+                        dt_bias: torch.Tensor, state_in: torch.Tensor, core: torch.Tensor, state_out: torch.Tensor,
+                        NK: int, NV: int, load_state: bool = True, D: int = 128) -> None:
+        """deltanet_gbeta fused into deltanet_recur (a, b [(B,) S, NV])."""
+        self._bind_stream()
+        p = self._dn_params(qkv_conv, NK, NV, D, load_state)
+        check(self.lib.hcu_deltanet_decode(self._h, ctypes.byref(p), _ptr(qkv_conv), _ptr(a), _ptr(b), _ptr(a_neg),
+                                           _ptr(dt_bias), _ptr(state_in), _ptr(core), _ptr(state_out)))

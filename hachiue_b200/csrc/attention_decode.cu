@@ -1,0 +1,598 @@
+// attention_decode.cu - split-K flash-decoding GQA attention over the KV cache.
+//
+// Replaces attention_q8 (src/kernels.ts:1341-1426) and runAttentionQ8
+// (src/wasm-backend.ts:826-895).  Semantics kept from the reference: grouped
+// head map kvh = h / (H / KV), key range [jStart, pos] with
+// jStart = pos + 1 - windowSize when windowSize > 0 and pos + 1 > windowSize,
+// score scale 1/sqrt(Dh), online softmax, output acc / l.
+//
+// B200 design (the reference runs one 32-thread workgroup per (query, head),
+// serial over keys, and re-reads each KV head once per query head):
+//  * One CTA per (sequence, KV head, query block, key split).  All G = H/KV
+//    query heads of the KV head (and up to 16/G queries) are the CTA's R
+//    "rows", so every K/V byte crosses HBM once per call.
+//  * A producer warp streams [TT tokens x Dh] K and V tiles (16 KB each) with
+//    3-D TMA (cp.async.bulk.tensor, no multicast) into a 3-stage mbarrier
+//    ring; four consumer warps each own a quarter of every tile.
+//  * q.k: each lane owns Dh/32 dimensions; partial dots for 32 (token, row)
+//    pairs are summed across the warp with a transpose-reduce (31 shuffles
+//    for 32 values instead of 5 per value).
+//  * Online softmax per row in the log2 domain (q pre-scaled by log2(e)/sqrt(Dh)).
+//  * Splits write (m, l, acc) partials to the handle's workspace; the last CTA
+//    of a unit (atomic ticket, no spinning) merges them and writes out.
+#include <stdlib.h>
+
+#include "common.cuh"
+#include "context.h"
+
+namespace {
+
+using namespace hcu;
+
+constexpr int NW = 4;                   // consumer warps
+constexpr int NTHREADS = (NW + 1) * 32; // + 1 TMA producer warp
+constexpr int NST = 3;                  // pipeline stages
+constexpr float LOG2E = 1.4426950408889634f;
+
+template <int FMT, int DH>
+struct Cfg {
+  static constexpr int ES = FMT == HCU_KV_F32 ? 4 : (FMT == HCU_KV_Q8_0 ? 1 : 2);
+  static constexpr int TT = 16384 / (DH * ES);  // tokens per tile
+  static constexpr int TPW = TT / NW;           // tokens per warp per tile
+  static constexpr int DPL = DH / 32;           // dims per lane
+  static constexpr int TILE_BYTES = TT * DH * ES;
+  static constexpr int SC_BYTES = FMT == HCU_KV_Q8_0 ? TT * (DH / 32) * 4 : 0;
+  static constexpr int STAGE_BYTES = 2 * (TILE_BYTES + SC_BYTES);
+};
+
+struct AttnArgs {
+  const float* q;
+  float* out;
+  const int32_t* pos_base;
+  const int64_t* row_off;
+  unsigned long long seq_row_stride;
+  int S, H, KV, G, QB, nqb, window, pos_base_default;
+  int chunk;       // keys per split (multiple of TT)
+  int max_splits;  // gridDim.x
+  float qscale;    // log2(e) / sqrt(Dh)
+  float* part;     // [units, max_splits, R, DH + 2]
+  int* counters;   // [units]
+  uint32_t* status;
+};
+
+// Loads the lane's DPL elements of tile row `row` as f32 (Q8_0: times the
+// block scale, like `kQ * kS` in wasm-backend.ts:861-866).
+template <int FMT, int DH>
+__device__ __forceinline__ void load_row(const uint8_t* tile, const float* scales, int row, int lane,
+                                         float (&v)[DH / 32]) {
+  constexpr int DPL = DH / 32;
+  if constexpr (FMT == HCU_KV_F32) {
+    const float4* p = reinterpret_cast<const float4*>(tile + (size_t)row * DH * 4) + lane * (DPL / 4);
+#pragma unroll
+    for (int i = 0; i < DPL / 4; i++) {
+      float4 x = p[i];
+      v[4 * i] = x.x;
+      v[4 * i + 1] = x.y;
+      v[4 * i + 2] = x.z;
+      v[4 * i + 3] = x.w;
+    }
+  } else if constexpr (FMT == HCU_KV_F16 || FMT == HCU_KV_BF16) {
+    const uint32_t* p = reinterpret_cast<const uint32_t*>(tile + (size_t)row * DH * 2) + lane * (DPL / 2);
+    uint32_t w[DPL / 2];
+    if constexpr (DPL == 4) {
+      uint2 x = *reinterpret_cast<const uint2*>(p);
+      w[0] = x.x;
+      w[1] = x.y;
+    } else {
+      uint4 x = *reinterpret_cast<const uint4*>(p);
+      w[0] = x.x;
+      w[1] = x.y;
+      w[2] = x.z;
+      w[3] = x.w;
+    }
+#pragma unroll
+    for (int i = 0; i < DPL / 2; i++) {
+      if constexpr (FMT == HCU_KV_F16) {
+        float2 f = f16x2_to_f2(w[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      } else {
+        v[2 * i] = bf16_lo(w[i]);
+        v[2 * i + 1] = bf16_hi(w[i]);
+      }
+    }
+  } else {  // Q8_0
+    const int8_t* p = reinterpret_cast<const int8_t*>(tile + (size_t)row * DH) + lane * DPL;
+    const float s = scales[row * (DH / 32) + (lane * DPL) / 32];
+    if constexpr (DPL == 4) {
+      char4 x = *reinterpret_cast<const char4*>(p);
+      v[0] = (float)x.x * s;
+      v[1] = (float)x.y * s;
+      v[2] = (float)x.z * s;
+      v[3] = (float)x.w * s;
+    } else {
+      int2 xx = *reinterpret_cast<const int2*>(p);
+      const int8_t* b = reinterpret_cast<const int8_t*>(&xx);
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] = (float)b[i] * s;
+    }
+  }
+}
+
+// Transpose-reduce: sums N per-lane values across the warp.  Afterwards lane L
+// holds the totals of entries (L*N)/32 + i, i < max(N/32, 1).
+template <int N>
+__device__ __forceinline__ void treduce(float (&v)[N], int lane) {
+  int n = N;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (n >= 2) {
+      const int half = n / 2;
+      const bool up = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < N / 2; i++) {
+        if (i < half) {
+          float send = up ? v[i] : v[i + half];
+          float keep = up ? v[i + half] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      n = half;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+  }
+}
+
+template <int FMT, int DH, int R>
+__global__ void __launch_bounds__(NTHREADS, 2)
+    attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                       const __grid_constant__ CUtensorMap tmKs, const __grid_constant__ CUtensorMap tmVs,
+                       const AttnArgs a) {
+  using C = Cfg<FMT, DH>;
+  constexpr int TT = C::TT, TPW = C::TPW, DPL = C::DPL;
+  constexpr int TG = (32 / R) < TPW ? (32 / R > 0 ? 32 / R : 1) : TPW;  // tokens per reduce group
+  constexpr int NV = TG * R;                                            // values per reduce
+  constexpr int NPL = NV >= 32 ? NV / 32 : 1;                           // results per lane
+  constexpr int TPL = (TPW + 31) / 32;                                  // softmax entries per lane
+
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * C::STAGE_BYTES);
+  uint64_t* empty = full + NST;
+  float* sc_all = reinterpret_cast<float*>(empty + NST);
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.x, g = blockIdx.y;
+  const int b = blockIdx.z / a.nqb, qb = blockIdx.z % a.nqb;
+
+  const int pb = a.pos_base ? a.pos_base[b] : a.pos_base_default;
+  const long long roff = a.row_off ? a.row_off[b] : (long long)b * (long long)a.seq_row_stride;
+  const int q0 = qb * a.QB;
+  const int qn = min(a.QB, a.S - q0);
+  const int pos_first = pb + q0, pos_last = pb + q0 + qn - 1;
+  const int kstart = (a.window > 0 && pos_first + 1 > a.window) ? pos_first + 1 - a.window : 0;
+  const int kend = pos_last + 1;
+  const int nsplit = (kend - kstart + a.chunk - 1) / a.chunk;
+  if (nsplit > (int)gridDim.x) {  // max_context under-stated by the caller: refuse, never half-merge
+    if (split == 0 && threadIdx.x == 0) atomicOr(a.status, HCU_DEVERR_BADARG);
+    return;
+  }
+  if (split >= nsplit) return;  // uniform for the CTA, before any barrier
+  const int k_lo = kstart + split * a.chunk;
+  const int k_hi = min(kend, k_lo + a.chunk);
+  const int ntiles = (k_hi - k_lo + TT - 1) / TT;
+  const int unit = (b * a.KV + g) * a.nqb + qb;
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == NW) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&tmK);
+      prefetch_tensormap(&tmV);
+      for (int it = 0; it < ntiles; ++it) {
+        const int s = it % NST, rnd = it / NST;
+        if (rnd > 0 && !mbar_wait(&empty[s], (rnd - 1) & 1, a.status)) break;
+        uint8_t* st = stages + s * C::STAGE_BYTES;
+        const int row = (int)(roff + k_lo + it * TT);
+        mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+        tma_load_3d(st, &tmK, &full[s], 0, g, row);
+        tma_load_3d(st + C::TILE_BYTES, &tmV, &full[s], 0, g, row);
+        if constexpr (FMT == HCU_KV_Q8_0) {
+          tma_load_3d(st + 2 * C::TILE_BYTES, &tmKs, &full[s], 0, g, row);
+          tma_load_3d(st + 2 * C::TILE_BYTES + C::SC_BYTES, &tmVs, &full[s], 0, g, row);
+        }
+      }
+    }
+    return;  // the producer takes no part in the epilogue (named barriers below)
+  }
+
+  // ---------------- consumers ----------------
+  float qv[R][DPL];
+  int jlo[R], jhi[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    const int qi = q0 + r / a.G;
+    const bool valid = (r < a.QB * a.G) && (r / a.G < qn);
+    const int h = g * a.G + (r % a.G);
+    const int pos = pb + qi;
+    jlo[r] = valid ? ((a.window > 0 && pos + 1 > a.window) ? pos + 1 - a.window : 0) : 1;
+    jhi[r] = valid ? pos : 0;
+    if (valid) {
+      const float4* qp = reinterpret_cast<const float4*>(a.q + (((long long)b * a.S + qi) * a.H + h) * DH) +
+                         lane * (DPL / 4);
+#pragma unroll
+      for (int i = 0; i < DPL / 4; i++) {
+        float4 x = __ldg(qp + i);
+        qv[r][4 * i] = x.x * a.qscale;
+        qv[r][4 * i + 1] = x.y * a.qscale;
+        qv[r][4 * i + 2] = x.z * a.qscale;
+        qv[r][4 * i + 3] = x.w * a.qscale;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < DPL; i++) qv[r][i] = 0.f;
+    }
+  }
+
+  float m[R], l[R], acc[R][DPL];
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    m[r] = -1e30f;
+    l[r] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DPL; i++) acc[r][i] = 0.f;
+  }
+  float* sc = sc_all + warp * TPW * R;
+  bool aborted = false;
+
+  for (int it = 0; it < ntiles; ++it) {
+    const int s = it % NST, rnd = it / NST;
+    if (!mbar_wait(&full[s], rnd & 1, a.status)) {
+      aborted = true;
+      break;
+    }
+    const uint8_t* st = stages + s * C::STAGE_BYTES;
+    const uint8_t* ktile = st;
+    const uint8_t* vtile = st + C::TILE_BYTES;
+    const float* kscale = reinterpret_cast<const float*>(st + 2 * C::TILE_BYTES);
+    const float* vscale = reinterpret_cast<const float*>(st + 2 * C::TILE_BYTES + C::SC_BYTES);
+    const int wk0 = k_lo + it * TT + warp * TPW;  // key index of this warp's first row
+    const int wrow0 = warp * TPW;
+
+    // ---- scores: sc[t * R + r] = q_r . k_t (log2 domain) ----
+#pragma unroll
+    for (int t0 = 0; t0 < TPW; t0 += TG) {
+      float part[NV];
+#pragma unroll
+      for (int tt = 0; tt < TG; tt++) {
+        float kvec[DPL];
+        load_row<FMT, DH>(ktile, kscale, wrow0 + t0 + tt, lane, kvec);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          float d = 0.f;
+#pragma unroll
+          for (int i = 0; i < DPL; i++) d = fmaf(qv[r][i], kvec[i], d);
+          part[tt * R + r] = d;
+        }
+      }
+      treduce<NV>(part, lane);
+      const int idx = (lane * NV) >> 5;
+      if (NV >= 32 || (lane & ((32 / NV) - 1)) == 0) {
+#pragma unroll
+        for (int i = 0; i < NPL; i++) sc[t0 * R + idx + i] = part[i];
+      }
+    }
+    __syncwarp();
+
+    // ---- online softmax per row over this warp's TPW keys ----
+    float corr[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      float sv[TPL];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < TPL; i++) {
+        const int t = lane + 32 * i;
+        sv[i] = -INFINITY;
+        if (t < TPW) {
+          const int key = wk0 + t;
+          if (key >= jlo[r] && key <= jhi[r] && key < k_hi) sv[i] = sc[t * R + r];
+          mx = fmaxf(mx, sv[i]);
+        }
+      }
+      mx = warp_max(mx);
+      const float mnew = fmaxf(m[r], mx);
+      corr[r] = exp2f(m[r] - mnew);
+      float ps = 0.f;
+#pragma unroll
+      for (int i = 0; i < TPL; i++) {
+        const int t = lane + 32 * i;
+        if (t < TPW) {
+          const float p = exp2f(sv[i] - mnew);
+          sc[t * R + r] = p;
+          ps += p;
+        }
+      }
+      ps = warp_sum(ps);
+      l[r] = l[r] * corr[r] + ps;
+      m[r] = mnew;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+      for (int i = 0; i < DPL; i++) acc[r][i] *= corr[r];
+
+    // ---- acc += p . V over the warp's valid rows ----
+    const int tcount = min(TPW, k_hi - wk0);
+    for (int t = 0; t < tcount; t++) {
+      float vvec[DPL];
+      load_row<FMT, DH>(vtile, vscale, wrow0 + t, lane, vvec);
+      float p[R];
+      if constexpr (R % 4 == 0) {
+#pragma unroll
+        for (int r = 0; r < R; r += 4) {
+          float4 x = *reinterpret_cast<const float4*>(sc + t * R + r);
+          p[r] = x.x;
+          p[r + 1] = x.y;
+          p[r + 2] = x.z;
+          p[r + 3] = x.w;
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; r++) p[r] = sc[t * R + r];
+      }
+#pragma unroll
+      for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int i = 0; i < DPL; i++) acc[r][i] = fmaf(p[r], vvec[i], acc[r][i]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---------------- merge the four warps ----------------
+  named_bar(1, NW * 32);  // every consumer is done with the stage buffers
+  float* cb = reinterpret_cast<float*>(stages);  // [NW][R][DH]
+  float* cm = cb + NW * R * DH;                  // [NW][R]
+  float* cl = cm + NW * R;                       // [NW][R]
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+#pragma unroll
+    for (int i = 0; i < DPL; i++) cb[(warp * R + r) * DH + lane * DPL + i] = acc[r][i];
+    if (lane == 0) {
+      cm[warp * R + r] = m[r];
+      cl[warp * R + r] = l[r];
+    }
+  }
+  named_bar(1, NW * 32);
+  if (aborted) return;
+
+  const int rows_valid = min(a.QB * a.G, qn * a.G);
+  float* part = a.part + ((size_t)unit * a.max_splits + split) * R * (DH + 2);
+  for (int e = tid; e < R * DH; e += NW * 32) {
+    const int r = e / DH, d = e % DH;
+    float M = -1e30f;
+#pragma unroll
+    for (int w = 0; w < NW; w++) M = fmaxf(M, cm[w * R + r]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; w++) {
+      const float f = exp2f(cm[w * R + r] - M);
+      L += cl[w * R + r] * f;
+      A += cb[(w * R + r) * DH + d] * f;
+    }
+    if (nsplit == 1) {
+      if (r < rows_valid) {
+        const int qi = q0 + r / a.G, h = g * a.G + r % a.G;
+        a.out[(((long long)b * a.S + qi) * a.H + h) * DH + d] = A / L;
+      }
+    } else {
+      part[r * (DH + 2) + d] = A;
+      if (d == 0) {
+        part[r * (DH + 2) + DH] = M;
+        part[r * (DH + 2) + DH + 1] = L;
+      }
+    }
+  }
+  if (nsplit == 1) return;
+
+  // ---------------- split merge by the last CTA of the unit ----------------
+  __threadfence();
+  named_bar(1, NW * 32);
+  if (tid == 0) s_last = (atomicAdd(&a.counters[unit], 1) == nsplit - 1);
+  named_bar(1, NW * 32);
+  if (!s_last) return;
+  __threadfence();
+  const float* up = a.part + (size_t)unit * a.max_splits * R * (DH + 2);
+  for (int e = tid; e < rows_valid * DH; e += NW * 32) {
+    const int r = e / DH, d = e % DH;
+    float M = -1e30f;
+    for (int sp = 0; sp < nsplit; sp++) M = fmaxf(M, __ldcg(up + ((size_t)sp * R + r) * (DH + 2) + DH));
+    float L = 0.f, A = 0.f;
+    for (int sp = 0; sp < nsplit; sp++) {
+      const float* pp = up + ((size_t)sp * R + r) * (DH + 2);
+      const float f = exp2f(__ldcg(pp + DH) - M);
+      L += __ldcg(pp + DH + 1) * f;
+      A += __ldcg(pp + d) * f;
+    }
+    const int qi = q0 + r / a.G, h = g * a.G + r % a.G;
+    a.out[(((long long)b * a.S + qi) * a.H + h) * DH + d] = A / L;
+  }
+  if (tid == 0) a.counters[unit] = 0;  // re-arm for the next call
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+template <int FMT, int DH, int R>
+int launch_t(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap& tk, const CUtensorMap& tv,
+             const CUtensorMap& tks, const CUtensorMap& tvs) {
+  using C = Cfg<FMT, DH>;
+  auto kern = attn_decode_kernel<FMT, DH, R>;
+  const size_t smem = NST * C::STAGE_BYTES + 2 * NST * sizeof(uint64_t) + NW * C::TPW * R * sizeof(float);
+  static bool attr_done = false;  // per instantiation
+  if (!attr_done) {
+    HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                       "hcu_attention: smem attribute"));
+    attr_done = true;
+  }
+  kern<<<grid, NTHREADS, smem, h->stream>>>(tk, tv, tks, tvs, args);
+  return after_launch("hcu_attention: launch");
+}
+
+template <int FMT, int DH>
+int launch_r(hcu_context* h, int R, const AttnArgs& args, dim3 grid, const CUtensorMap& tk, const CUtensorMap& tv,
+             const CUtensorMap& tks, const CUtensorMap& tvs) {
+  switch (R) {
+    case 1: return launch_t<FMT, DH, 1>(h, args, grid, tk, tv, tks, tvs);
+    case 2: return launch_t<FMT, DH, 2>(h, args, grid, tk, tv, tks, tvs);
+    case 4: return launch_t<FMT, DH, 4>(h, args, grid, tk, tv, tks, tvs);
+    case 8: return launch_t<FMT, DH, 8>(h, args, grid, tk, tv, tks, tvs);
+    case 16:
+      if constexpr (DH == 128) return launch_t<FMT, DH, 16>(h, args, grid, tk, tv, tks, tvs);
+      break;
+  }
+  return fail(HCU_EUNSUPPORTED, "hcu_attention: %d rows per CTA not built for Dh=%d", R, DH);
+}
+
+template <int FMT>
+int launch_d(hcu_context* h, int DH, int R, const AttnArgs& args, dim3 grid, const CUtensorMap& tk,
+             const CUtensorMap& tv, const CUtensorMap& tks, const CUtensorMap& tvs) {
+  if (DH == 128) return launch_r<FMT, 128>(h, R, args, grid, tk, tv, tks, tvs);
+  return launch_r<FMT, 256>(h, R, args, grid, tk, tv, tks, tvs);
+}
+
+int tile_tokens(int fmt, int dh) {
+  const int es = fmt == HCU_KV_F32 ? 4 : (fmt == HCU_KV_Q8_0 ? 1 : 2);
+  return 16384 / (dh * es);
+}
+
+}  // namespace
+
+extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const float* q, const hcu_kv_cache* kv,
+                             float* out) {
+  HCU_TRY(hcu::begin_op(h, "hcu_attention"));
+  if (!p || !q || !kv || !out || !kv->k || !kv->v) return fail(HCU_EINVAL, "hcu_attention: null argument");
+  const int S = (int)p->S, H = (int)p->H, KV = (int)p->KV, Dh = (int)p->Dh;
+  const int batch = p->batch ? (int)p->batch : 1;
+  const int fmt = (int)kv->format;
+  if (S < 1 || H < 1 || KV < 1) return fail(HCU_EINVAL, "hcu_attention: S, H and KV must be positive");
+  if (H % KV) return fail(HCU_EINVAL, "hcu_attention: H (%d) is not a multiple of KV (%d)", H, KV);
+  if (Dh != 128 && Dh != 256) return fail(HCU_EUNSUPPORTED, "hcu_attention: Dh=%d (built: 128, 256)", Dh);
+  if (fmt < HCU_KV_F32 || fmt > HCU_KV_Q8_0) return fail(HCU_EINVAL, "hcu_attention: unknown KV format %d", fmt);
+  if (fmt == HCU_KV_Q8_0 && (!kv->k_scale || !kv->v_scale))
+    return fail(HCU_EINVAL, "hcu_attention: Q8_0 cache needs k_scale and v_scale");
+  if (batch > 1 && !p->pos_base && p->max_context == 0)
+    ;  // every sequence uses posBase: max_context defaults below
+  if (reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(HCU_EINVAL, "hcu_attention: q and out must be 16-byte aligned");
+  const int G = H / KV;
+  const int rmax = Dh == 128 ? 16 : 8;
+  if (G > rmax) return fail(HCU_EUNSUPPORTED, "hcu_attention: group size %d > %d", G, rmax);
+  const int QB = S < rmax / G ? S : rmax / G;
+  int R = 1;
+  while (R < QB * G) R <<= 1;
+  const int nqb = (S + QB - 1) / QB;
+  if ((long long)batch * nqb > 65535) return fail(HCU_EINVAL, "hcu_attention: batch x query blocks > 65535");
+  if (KV > 65535) return fail(HCU_EINVAL, "hcu_attention: KV > 65535");
+  const long long max_ctx = p->max_context ? (long long)p->max_context : (long long)p->posBase + S;
+  if (max_ctx < S) return fail(HCU_EINVAL, "hcu_attention: max_context < S");
+  const int W = (int)p->windowSize;
+  long long max_range = max_ctx;
+  if (W > 0 && (long long)W + QB - 1 < max_range) max_range = (long long)W + QB - 1;
+  if (batch == 1 && !p->pos_base && (long long)p->posBase + S > (long long)kv->rows)
+    return fail(HCU_EINVAL, "hcu_attention: cache holds %u rows, need posBase+S = %lld", kv->rows,
+                (long long)p->posBase + S);
+  if (kv->rows == 0 || kv->rows > 0x7fffffffu) return fail(HCU_EINVAL, "hcu_attention: bad cache row count");
+
+  const int TT = tile_tokens(fmt, Dh);
+  const long long units = (long long)batch * KV * nqb;
+  long long target = 8LL * h->sm_count;
+  long long want_splits = (target + units - 1) / units;
+  if (want_splits < 1) want_splits = 1;
+  long long chunk = (max_range + want_splits - 1) / want_splits;
+  if (const char* env = getenv("HCU_ATTN_CHUNK")) {
+    long long c = atoll(env);
+    if (c > 0) chunk = c;
+  }
+  chunk = ((chunk + TT - 1) / TT) * TT;
+  if (chunk < TT) chunk = TT;
+  const size_t cnt_bytes = ((size_t)units * sizeof(int) + 255) & ~(size_t)255;
+  auto need = [&](long long c) {
+    long long ms = (max_range + c - 1) / c;
+    return cnt_bytes + (size_t)units * ms * R * (Dh + 2) * sizeof(float);
+  };
+  while (need(chunk) > h->workspace_bytes && chunk < max_range) chunk *= 2;
+  if (need(chunk) > h->workspace_bytes)
+    return fail(HCU_ENOMEM, "hcu_attention: workspace of %zu bytes too small (need %zu)", h->workspace_bytes,
+                need(chunk));
+  const long long max_splits = (max_range + chunk - 1) / chunk;
+  if (max_splits > 0x7fffffff) return fail(HCU_EINVAL, "hcu_attention: too many splits");
+
+  // TMA descriptors over the whole cache: dims (Dh, KV, rows).
+  const int es = fmt == HCU_KV_F32 ? 4 : (fmt == HCU_KV_Q8_0 ? 1 : 2);
+  const CUtensorMapDataType dt = fmt == HCU_KV_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : fmt == HCU_KV_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                 : fmt == HCU_KV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUtensorMap tk, tv, tks, tvs;
+  {
+    uint64_t dims[3] = {(uint64_t)Dh, (uint64_t)KV, (uint64_t)kv->rows};
+    uint64_t strides[2] = {(uint64_t)Dh * es, (uint64_t)KV * Dh * es};
+    uint32_t box[3] = {(uint32_t)Dh, 1u, (uint32_t)TT};
+    HCU_TRY(hcu::make_tensor_map(&tk, dt, 3, kv->k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE));
+    HCU_TRY(hcu::make_tensor_map(&tv, dt, 3, kv->v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE));
+  }
+  if (fmt == HCU_KV_Q8_0) {
+    uint64_t dims[3] = {(uint64_t)Dh / 32, (uint64_t)KV, (uint64_t)kv->rows};
+    uint64_t strides[2] = {(uint64_t)Dh / 32 * 4, (uint64_t)KV * Dh / 32 * 4};
+    uint32_t box[3] = {(uint32_t)Dh / 32, 1u, (uint32_t)TT};
+    HCU_TRY(hcu::make_tensor_map(&tks, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, kv->k_scale, dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE));
+    HCU_TRY(hcu::make_tensor_map(&tvs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, kv->v_scale, dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE));
+  } else {
+    tks = tk;
+    tvs = tv;
+  }
+
+  AttnArgs args{};
+  args.q = q;
+  args.out = out;
+  args.pos_base = p->pos_base;
+  args.row_off = p->kv_row_offset;
+  args.seq_row_stride = p->seq_row_stride;
+  args.S = S;
+  args.H = H;
+  args.KV = KV;
+  args.G = G;
+  args.QB = QB;
+  args.nqb = nqb;
+  args.window = W;
+  args.pos_base_default = (int)p->posBase;
+  args.chunk = (int)chunk;
+  args.max_splits = (int)max_splits;
+  args.qscale = LOG2E / sqrtf((float)Dh);
+  args.counters = static_cast<int*>(h->workspace);
+  args.part = reinterpret_cast<float*>(static_cast<char*>(h->workspace) + cnt_bytes);
+  args.status = h->dev_status;
+  dim3 grid((unsigned)max_splits, (unsigned)KV, (unsigned)(batch * nqb));
+  switch (fmt) {
+    case HCU_KV_F32: return launch_d<HCU_KV_F32>(h, Dh, R, args, grid, tk, tv, tks, tvs);
+    case HCU_KV_F16: return launch_d<HCU_KV_F16>(h, Dh, R, args, grid, tk, tv, tks, tvs);
+    case HCU_KV_BF16: return launch_d<HCU_KV_BF16>(h, Dh, R, args, grid, tk, tv, tks, tvs);
+    default: return launch_d<HCU_KV_Q8_0>(h, Dh, R, args, grid, tk, tv, tks, tvs);
+  }
+}

@@ -1,0 +1,47 @@
+// context.h - host-side handle state and error plumbing of libhachiue_cuda.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "hachiue_cuda.h"
+
+struct hcu_context {
+  int device = 0;
+  int sm_count = 148;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  void* workspace = nullptr;  // split-K partials + counters (zeroed at create)
+  size_t workspace_bytes = 0;
+  uint32_t* dev_status = nullptr;  // device status word (HCU_DEVERR_*)
+  int inject_status = 0;
+  int inject_count = 0;
+};
+
+namespace hcu {
+
+// Records `msg` as this thread's last error and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Maps a CUDA error to HCU_ECUDA with context; HCU_OK for cudaSuccess.
+int check_cuda(cudaError_t e, const char* what);
+// Validates the handle and consumes one injected failure, if armed.
+int begin_op(hcu_context* h, const char* op);
+// Launch-status check after a kernel launch.
+int after_launch(const char* what);
+
+// Encodes a tiled TMA descriptor (row-major tensor, dims innermost first).
+int make_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
+                    const uint64_t* dims, const uint64_t* strides_bytes /* rank-1 */,
+                    const uint32_t* box, CUtensorMapSwizzle swizzle);
+
+}  // namespace hcu
+
+#define HCU_TRY(expr)            \
+  do {                           \
+    int _st = (expr);            \
+    if (_st != HCU_OK) return _st; \
+  } while (0)

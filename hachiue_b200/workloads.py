@@ -1,0 +1,124 @@
+"""Seeded synthetic inputs with the shapes of the benchmark configurations.
+
+The reference publishes no dataset for this path; every configuration is
+synthetic.  Inputs come from ``numpy.random.default_rng(seed)`` (PCG64) drawn in
+the order listed, so the oracle, the parity tests and the benchmark see the
+same values.  "N(0, 0.02)" is read as standard deviation 0.02.
+
+  cfg1  Qwen3-1.7B GQA decode: 1 seq, H=16, KV=8, Dh=128, T=1024, f32 KV
+  cfg2  Qwen3-8B batched GQA decode: 64 seqs, H=32, KV=8, T_b ~ U[512, 8192], f16 KV
+  cfg3  PLaMo-3 SWA prefill: 8 x 4096, H=16, KV=4, Dh=128, W=1024, bf16
+  cfg4  Qwen3.5 GDN decode step: 64 seqs, NK=16, NV=32, D=128, f32 state
+  cfg5  Qwen3.5 GDN chunked prefill: 8 x 8192, NK=16, NV=32, D=128, bf16 in
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def _normal(rng, shape, std=1.0, dtype=np.float32):
+    x = rng.standard_normal(shape, dtype=np.float32)
+    if std != 1.0:
+        x *= np.float32(std)
+    return x.astype(dtype, copy=False)
+
+
+def _l2n(x: np.ndarray) -> np.ndarray:
+    n = np.sqrt((x.astype(np.float64) ** 2).sum(-1, keepdims=True))
+    return (x / n).astype(np.float32)
+
+
+def decode_cfg1(seed: int = 0, T: int = 1024):
+    """q [1, 16, 128] (S=1), K / V caches [T, 8, 128] f32, pos_base T-1."""
+    rng = np.random.default_rng(seed)
+    q = _normal(rng, (16, 128))
+    k = _normal(rng, (8, T, 128))
+    v = _normal(rng, (8, T, 128))
+    return dict(q=q[None], k=np.ascontiguousarray(k.transpose(1, 0, 2)), v=np.ascontiguousarray(v.transpose(1, 0, 2)),
+                pos_base=T - 1, H=16, KV=8, Dh=128)
+
+
+def decode_cfg2(seed: int = 1, batch: int = 64, lo: int = 512, hi: int = 8193, H: int = 32, KV: int = 8, Dh: int = 128):
+    """Packed f16 caches: sequence b's rows are [off[b], off[b] + T_b) of
+    K / V [sum(T), KV, Dh]; q [B, 1, H, Dh] f32; pos_base[b] = T_b - 1."""
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(lo, hi, batch).astype(np.int64)
+    q = _normal(rng, (batch, H, Dh))
+    total = int(lens.sum())
+    k = _normal(rng, (total, KV, Dh), dtype=np.float16)
+    v = _normal(rng, (total, KV, Dh), dtype=np.float16)
+    off = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+    return dict(q=q[:, None], k=k, v=v, lens=lens, row_offset=off, pos_base=(lens - 1).astype(np.int32),
+                H=H, KV=KV, Dh=Dh)
+
+
+def swa_cfg3(seed: int = 2, B: int = 8, T: int = 4096, H: int = 16, KV: int = 4, D: int = 128, window: int = 1024):
+    """bf16 Q [B, T, H, D], K / V [B, T, KV, D] (as uint16 bit patterns)."""
+    import torch  # bf16 rounding
+
+    rng = np.random.default_rng(seed)
+    out = {}
+    for name, heads in (("q", H), ("k", KV), ("v", KV)):
+        x = torch.from_numpy(_normal(rng, (B, T, heads, D))).to(torch.bfloat16)
+        out[name] = x.view(torch.int16).numpy().view(np.uint16)
+    out.update(window=window, H=H, KV=KV, D=D)
+    return out
+
+
+def gdn_decode_cfg4(seed: int = 3, batch: int = 64, NK: int = 16, NV: int = 32, D: int = 128):
+    """state [B, NV, D, D] f32 (reference [dk][dv] order), qkv_conv
+    [B, 1, 2*NK*D + NV*D] f32 (q, k L2-normalised), a / b [B, 1, NV]
+    (alpha = exp(-softplus(a)) via aNeg = -1, dtBias = 0; beta = sigmoid(b))."""
+    rng = np.random.default_rng(seed)
+    state = _normal(rng, (batch, NV, D, D), std=0.02)
+    q = _l2n(_normal(rng, (batch, NK, D)))
+    k = _l2n(_normal(rng, (batch, NK, D)))
+    v = _normal(rng, (batch, NV, D))
+    a = _normal(rng, (batch, NV))
+    b = _normal(rng, (batch, NV))
+    qkv = np.concatenate([q.reshape(batch, -1), k.reshape(batch, -1), v.reshape(batch, -1)], 1)[:, None]
+    return dict(state=state, qkv=np.ascontiguousarray(qkv), a=a[:, None].copy(), b=b[:, None].copy(),
+                a_neg=-np.ones(NV, np.float32), dt_bias=np.zeros(NV, np.float32), NK=NK, NV=NV, D=D)
+
+
+def gdn_prefill_cfg5(seed: int = 4, B: int = 8, T: int = 8192, NK: int = 16, NV: int = 32, D: int = 128):
+    """q, k [B, T, NK, D] (L2-normalised), v [B, T, NV, D] as bf16 bit
+    patterns; g = -softplus(a), beta = sigmoid(b) f32 [B, T, NV]."""
+    import torch
+
+    rng = np.random.default_rng(seed)
+    q = _l2n(_normal(rng, (B, T, NK, D)))
+    k = _l2n(_normal(rng, (B, T, NK, D)))
+    v = _normal(rng, (B, T, NV, D))
+    a = _normal(rng, (B, T, NV)).astype(np.float64)
+    b = _normal(rng, (B, T, NV)).astype(np.float64)
+    g = (-(np.maximum(a, 0) + np.log1p(np.exp(-np.abs(a))))).astype(np.float32)
+    beta = (1.0 / (1.0 + np.exp(-b))).astype(np.float32)
+
+    def bf(x):
+        return torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+    return dict(q=bf(q), k=bf(k), v=bf(v), g=g, beta=beta, NK=NK, NV=NV, D=D)
+
+
+def bf16_bits_to_f32(x: np.ndarray) -> np.ndarray:
+    return (x.astype(np.uint32) << 16).view(np.float32)
+
+
+def f16_bits(x: np.ndarray) -> np.ndarray:
+    return x.astype(np.float16).view(np.uint16)
+
+
+# Algorithmic bytes / flops per call (the roofline numerators).
+def cfg2_bytes(lens: np.ndarray, H=32, KV=8, Dh=128) -> int:
+    """K and V f16 read once + q read + out written (f32)."""
+    return int(lens.sum()) * KV * Dh * 2 * 2 + 2 * len(lens) * H * Dh * 4
+
+
+def cfg1_bytes(T=1024, H=16, KV=8, Dh=128) -> int:
+    return 2 * KV * T * Dh * 4 + 2 * H * Dh * 4
+
+
+def cfg4_bytes(B=64, NK=16, NV=32, D=128) -> int:
+    """state read + write, q, k, v, out (f32), a, b (f32)."""
+    return 2 * B * NV * D * D * 4 + B * (2 * NK * D + NV * D) * 4 + B * NV * D * 4 + 2 * B * NV * 4

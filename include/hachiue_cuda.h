@@ -1,0 +1,223 @@
+/*
+ * hachiue_cuda.h - C ABI of libhachiue_cuda.so, the sm_100a (B200) backend for
+ * hachiue's attention hot path: GQA decode attention over the KV cache
+ * (qwen3 / qwen35 full-attention layers), causal sliding-window attention
+ * (plamo3) and the gated delta-rule recurrence of qwen35's Gated DeltaNet
+ * layers.
+ *
+ * The reference drives these ops through one seam,
+ *     HachiueEngine.dispatch(pass, shaderName, uniformBuf, storageBufs, gx)
+ * (src/engine.ts:1056-1075), with at most eight u32/f32 uniform words packed by
+ * mkUniform (src/engine.ts:1040-1054) and storage buffers bound in order at
+ * bindings 1..n.  hcu_dispatch() below is that seam; the typed entry points
+ * after it are the same ops with named arguments and the batched / tensor-core
+ * extensions the B200 build adds.
+ *
+ * Conventions
+ *  - Every function returns HCU_OK (0) or a negative-free status code; the
+ *    message of the last failure on the calling thread is hcu_last_error().
+ *    No C++ exception crosses this ABI.
+ *  - Pointers named "device" are CUDA device pointers on the handle's device.
+ *  - Op calls only enqueue work on the handle's stream (asynchronous, like a
+ *    WebGPU dispatch); hcu_stream_sync() is the flushDeviceQueue analogue
+ *    (src/engine.ts:927-933).  Calls on one handle are not thread-safe, as in
+ *    the reference.
+ *  - Op calls never allocate device memory.  Split-K partials and counters use
+ *    the workspace reserved at hcu_create() time (the reference likewise
+ *    pre-allocates every scratch buffer, src/engine.ts:445-474).
+ */
+#ifndef HACHIUE_CUDA_H
+#define HACHIUE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HCU_ABI_VERSION 1
+
+/* Status codes. */
+#define HCU_OK 0
+#define HCU_EINVAL 1        /* bad argument (size, shape, null pointer, alignment) */
+#define HCU_ECUDA 2         /* CUDA runtime / driver error */
+#define HCU_ENCCL 3         /* collective error (multi-GPU helpers) */
+#define HCU_ETIMEDOUT 4     /* a bounded device-side wait gave up (see hcu_device_status) */
+#define HCU_ENOMEM 5        /* allocation or workspace too small */
+#define HCU_EUNSUPPORTED 6  /* shape / format combination not built */
+
+/* KV-cache element formats.  The reference always stores Q8_0
+ * (src/engine.ts:483-492, src/wasm-backend.ts:358-374): int8 values plus one
+ * f32 scale per 32 elements.  F32 / F16 / BF16 are the formats
+ * EngineOptions.kvCache (src/types.ts:177) declares. */
+#define HCU_KV_F32 0
+#define HCU_KV_F16 1
+#define HCU_KV_BF16 2
+#define HCU_KV_Q8_0 3
+
+/* Element types of the tensor-core prefill inputs and outputs. */
+#define HCU_DT_F32 0
+#define HCU_DT_BF16 2
+
+typedef struct hcu_context *hcu_handle;
+
+/* ------------------------------------------------------------------------ */
+/* Housekeeping                                                              */
+/* ------------------------------------------------------------------------ */
+
+/* ABI version (HCU_ABI_VERSION). */
+int hcu_version(void);
+
+/* Message of the last failed call on this thread ("" if none).  Messages start
+ * with "hachiue: " like the reference's thrown Errors (src/engine.ts:1066). */
+const char *hcu_last_error(void);
+
+/* Create a handle on CUDA device `device` with its own non-blocking stream and
+ * `workspace_bytes` of device workspace (0 = default, 64 MiB).  The workspace
+ * bounds how many split-K partials one attention call may use. */
+int hcu_create(int device, size_t workspace_bytes, hcu_handle *out);
+int hcu_destroy(hcu_handle h);
+
+/* Use an existing cudaStream_t (e.g. torch.cuda.current_stream().cuda_stream)
+ * instead of the handle's own stream.  NULL restores the handle's stream. */
+int hcu_set_stream(hcu_handle h, void *cuda_stream);
+void *hcu_get_stream(hcu_handle h);
+int hcu_stream_sync(hcu_handle h);
+
+int hcu_alloc(hcu_handle h, size_t bytes, void **device_ptr);
+int hcu_free(hcu_handle h, void *device_ptr);
+int hcu_memset(hcu_handle h, void *device_ptr, int value, size_t bytes);
+int hcu_copy_to_device(hcu_handle h, void *device_dst, const void *host_src, size_t bytes);
+int hcu_copy_to_host(hcu_handle h, void *host_dst, const void *device_src, size_t bytes);
+
+/* Device-side status word of the handle: 0, or a bit set by a kernel whose
+ * bounded wait gave up (1 = pipeline barrier timeout) or that found its
+ * arguments inconsistent and skipped its work (2, e.g. a sequence longer than
+ * hcu_attention_params.max_context).  Reading it
+ * synchronises the stream.  `clear` resets it. */
+int hcu_device_status(hcu_handle h, uint32_t *status, int clear);
+
+/* Test hook for failure detection: the next `n` op calls on this handle fail
+ * with `status` on the host before launching anything (0 disables). */
+int hcu_inject_failure(hcu_handle h, int status, int n);
+
+/* ------------------------------------------------------------------------ */
+/* The reference's dispatch seam                                              */
+/* ------------------------------------------------------------------------ */
+
+/* Run the op the reference names `shader` with its uniform words and storage
+ * buffers in binding order (src/engine.ts:1056-1075).  Supported names and the
+ * buffer lists (all device pointers) are exactly the reference's:
+ *
+ *   "kv_append_q8"   words [S, KV, Dh, posBase]                 (kernels.ts:1287)
+ *                    buffers [src f32, cacheQ int8, cacheS f32]
+ *   "attention_q8"   words [S, H, KV, Dh, posBase, windowSize]  (kernels.ts:1341)
+ *                    buffers [q f32, Kq int8, Ks f32, Vq int8, Vs f32, out f32]
+ *                    The Q8 cache must hold at least posBase+S rows.
+ *   "deltanet_gbeta" words [S, H]                               (kernels.ts:1471)
+ *                    buffers [a f32, b f32, aNeg f32, dtBias f32, out f32]
+ *   "deltanet_recur" words [S, H, DK, DV, HK, loadState]        (kernels.ts:1496)
+ *                    buffers [qkvConv f32, gbeta f32, stateIn f32, core f32,
+ *                             stateOut f32]   (stateIn == stateOut allowed)
+ *
+ * Q8 scales are stored as in the JS backend (amax/127, wasm-backend.ts:815),
+ * not the WGSL's amax (kernels.ts:1333); a cache written by this library is
+ * read consistently by it.  Unknown names fail with
+ * "hachiue: missing pipeline <name>" (src/engine.ts:1066). */
+int hcu_dispatch(hcu_handle h, const char *shader, const uint32_t words[8],
+                 void *const *buffers, int n_buffers);
+
+/* ------------------------------------------------------------------------ */
+/* Typed ops                                                                 */
+/* ------------------------------------------------------------------------ */
+
+/* KV cache of one attention layer: K and V as [rows, KV, Dh] elements of
+ * `format` (int8 for Q8_0), row-major; Q8_0 adds f32 scales [rows, KV, Dh/32].
+ * Mirrors kCacheQ/kCacheS/vCacheQ/vCacheS (src/engine.ts:339-343). */
+typedef struct {
+  uint32_t format;     /* HCU_KV_* */
+  uint32_t rows;       /* capacity in token rows (all sequences of a packed batch) */
+  void *k;             /* device */
+  void *v;             /* device */
+  float *k_scale;      /* device, Q8_0 only */
+  float *v_scale;      /* device, Q8_0 only */
+} hcu_kv_cache;
+
+/* Uniform words of attention_q8 (src/kernels.ts:1342) plus a batch extension.
+ * Sequence b (0 <= b < batch) has queries q[b, 0..S) at positions
+ * pos_base[b] + qi, and its keys / values at cache rows
+ * kv_row_offset[b] + j, j in [jStart, pos], jStart = pos+1-windowSize when
+ * windowSize > 0 and pos+1 > windowSize, else 0 (kernels.ts:1373-1377,
+ * wasm-backend.ts:847).  batch <= 1 with NULL arrays is exactly the
+ * reference's single-sequence call. */
+typedef struct {
+  uint32_t S, H, KV, Dh, posBase, windowSize;
+  uint32_t batch;               /* 0 or 1: single sequence */
+  uint32_t max_context;         /* >= max_b(pos_base[b] + S); 0 = posBase + S */
+  const int32_t *pos_base;      /* device [batch] or NULL: posBase for every sequence */
+  const int64_t *kv_row_offset; /* device [batch] or NULL: b * seq_row_stride */
+  uint64_t seq_row_stride;      /* rows per sequence when kv_row_offset is NULL */
+} hcu_attention_params;
+
+/* out[b, qi, h, :] = softmax_j(q . k_j / sqrt(Dh)) . v_j with the grouped head
+ * map kvh = h / (H / KV) (kernels.ts:1361, wasm-backend.ts:851).
+ * q and out are f32 [batch, S, H, Dh].  Replaces runAttentionQ8
+ * (src/wasm-backend.ts:826-895) and attention_q8 (src/kernels.ts:1341-1426).
+ * Split-K flash-decoding over the key range; Dh in {128, 256}. */
+int hcu_attention(hcu_handle h, const hcu_attention_params *p, const float *q,
+                  const hcu_kv_cache *kv, float *out);
+
+/* Append S rows of K or V (f32 [S, KV, Dh]) at cache row posBase in `format`.
+ * For Q8_0 this is appendKvQ8 (src/wasm-backend.ts:793-824) bit for bit:
+ * scale = amax/127 stored as f32, q = clamp(Math.round(x*127/amax), +-127).
+ * `data` is K or V of an hcu_kv_cache, `scale` its scale array (Q8_0 only). */
+int hcu_kv_append(hcu_handle h, uint32_t S, uint32_t KV, uint32_t Dh, uint32_t posBase,
+                  uint32_t format, const float *src, void *data, float *scale);
+
+/* Batched decode form of hcu_kv_append: source row i (f32 [n, KV, Dh]) goes to
+ * cache row dst_rows[i] (device int64 array), e.g. one new token per sequence
+ * of a packed batch.  Same per-row arithmetic as hcu_kv_append. */
+int hcu_kv_append_rows(hcu_handle h, uint32_t n, uint32_t KV, uint32_t Dh, uint32_t format,
+                       const float *src, const int64_t *dst_rows, void *data, float *scale);
+
+/* g = aNeg[h]*softplus(a + dtBias[h]), beta = sigmoid(b); a, b f32 [S, H];
+ * out f32 [2, S, H] (g block, then beta block).  deltanet_gbeta
+ * (src/kernels.ts:1471-1491, src/wasm-backend.ts:1036-1045). */
+int hcu_deltanet_gbeta(hcu_handle h, uint32_t S, uint32_t H, const float *a, const float *b,
+                       const float *a_neg, const float *dt_bias, float *out);
+
+/* Uniform words of deltanet_recur (src/kernels.ts:1497) plus a batch
+ * extension: sequence b's tensors start at the given per-sequence strides
+ * (elements).  H = number of V heads (NV), HK = number of QK heads (NK); V head
+ * h reads QK head h % HK (tiled map, kernels.ts:1511). */
+typedef struct {
+  uint32_t S, H, DK, DV, HK, loadState;
+  uint32_t batch;                 /* 0 or 1: single sequence */
+  uint64_t qkv_seq_stride;        /* default S * (2*HK*DK + H*DV) */
+  uint64_t gbeta_seq_stride;      /* default 2 * S * H */
+  uint64_t state_seq_stride;      /* default H * DK * DV */
+  uint64_t core_seq_stride;       /* default S * H * DV */
+} hcu_deltanet_params;
+
+/* Gated delta-rule scan over S tokens (deltanet_recur, src/kernels.ts:1496-1573;
+ * JS src/wasm-backend.ts:1047-1102).  qkvConv f32 [batch, S, 2*HK*DK + H*DV];
+ * gbeta f32 [batch, 2, S, H]; state f32 [batch, H, DK, DV] ([dk][dv] order);
+ * core f32 [batch, S, H, DV].  loadState = 0 starts from a zero state.
+ * state_in == state_out updates in place.  DK = DV = 128. */
+int hcu_deltanet_recur(hcu_handle h, const hcu_deltanet_params *p, const float *qkv_conv,
+                       const float *gbeta, const float *state_in, float *core, float *state_out);
+
+/* deltanet_gbeta fused into deltanet_recur: one kernel reads a, b
+ * ([batch, S, H] f32), aNeg[H], dtBias[H] instead of a precomputed gbeta
+ * buffer.  Same results as the two calls in sequence. */
+int hcu_deltanet_decode(hcu_handle h, const hcu_deltanet_params *p, const float *qkv_conv,
+                        const float *a, const float *b, const float *a_neg,
+                        const float *dt_bias, const float *state_in, float *core,
+                        float *state_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HACHIUE_CUDA_H */

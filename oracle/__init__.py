@@ -1,0 +1,236 @@
+"""CPU oracle for hachiue's attention hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline legs of
+``bench.py`` may import this package, and only as the checker.  The product path
+(``hachiue_b200``) never imports it.
+
+Parity status: **unpinned** by the reference.  hachiue is TypeScript and no JS
+runtime exists where this build runs, its WGSL twin needs a WebGPU browser, and
+its tests hold no golden vectors for this path.  ``hachiue_oracle.c`` restates
+the JS functions line by line (src/wasm-backend.ts:793-895, :1036-1102) with
+their number semantics; ``closed_form`` below restates the same maths in dense
+numpy f64 as an independent self-check.
+
+All arrays are numpy; the C library is built by ``oracle/Makefile``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_SO = os.path.join(_HERE, "_build", "liboracle.so")
+_lock = threading.Lock()
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compile the C oracle (gcc, no GPU needed).  Returns the .so path."""
+    src = os.path.join(_HERE, "hachiue_oracle.c")
+    if force or not os.path.exists(_SO) or os.path.getmtime(_SO) < os.path.getmtime(src):
+        env = dict(os.environ)
+        env.setdefault("CC", "gcc")
+        subprocess.run(["make", "-s", "-C", _HERE], check=True, env=env)
+    return _SO
+
+
+def lib():
+    global _lib
+    with _lock:
+        if _lib is None:
+            build()
+            L = ctypes.CDLL(_SO)
+            vp, i32, i64, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_long, ctypes.c_float
+            L.oracle_append_kv_q8.argtypes = [vp, vp, vp, i32, i32, i32, i32]
+            L.oracle_attention.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i64]
+            L.oracle_attention_batch.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp,
+                                                 i32, i32, i32]
+            L.oracle_attention_q8_wgsl.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32]
+            L.oracle_deltanet_gbeta.argtypes = [vp, vp, vp, vp, vp, i32, i32]
+            L.oracle_deltanet_recur.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32]
+            L.oracle_deltanet_recur_wgsl.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32]
+            L.oracle_deltanet_recur_batch.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i64, i64,
+                                                      i64, i64, i32]
+            L.oracle_f16_to_f64.argtypes = [ctypes.c_uint16]
+            L.oracle_f16_to_f64.restype = ctypes.c_double
+            _ = f
+            _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+KV_F32, KV_F16, KV_BF16, KV_Q8_0 = 0, 1, 2, 3
+
+
+def append_kv_q8(src: np.ndarray, cache_q: np.ndarray, cache_s: np.ndarray, pos_base: int) -> None:
+    """appendKvQ8 (src/wasm-backend.ts:793-824): src f32 [S, KV, Dh] into the
+    int8 cache [rows, KV, Dh] and f32 scales [rows, KV, Dh/32] at row pos_base."""
+    S, KV, Dh = src.shape
+    assert src.dtype == np.float32 and cache_q.dtype == np.int8 and cache_s.dtype == np.float32
+    assert cache_q.shape[0] >= pos_base + S
+    lib().oracle_append_kv_q8(_p(src), _p(cache_q), _p(cache_s), S, KV, Dh, pos_base)
+
+
+def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, pos_base: int, window: int = 0,
+              kv_format: int = KV_F32, k_scale: np.ndarray | None = None,
+              v_scale: np.ndarray | None = None, row_offset: int = 0) -> np.ndarray:
+    """runAttentionQ8 (src/wasm-backend.ts:826-895) for one sequence.
+
+    q f32 [S, H, Dh]; k / v [rows, KV, Dh] as f32, f16 (uint16 bits or float16),
+    bf16 (uint16 bits) or int8 (Q8_0, with f32 scales [rows, KV, Dh/32])."""
+    S, H, Dh = q.shape
+    KV = k.shape[1]
+    if kv_format == KV_Q8_0:
+        assert k_scale is not None and v_scale is not None
+        ks, vs = _p(k_scale), _p(v_scale)
+    else:
+        ks = vs = None
+    k = np.ascontiguousarray(k)
+    v = np.ascontiguousarray(v)
+    out = np.zeros_like(q)
+    lib().oracle_attention(_p(q), _p(k), ks, _p(v), vs, _p(out), S, H, KV, Dh, pos_base, window, kv_format,
+                           row_offset)
+    return out
+
+
+def attention_batch(q: np.ndarray, k: np.ndarray, v: np.ndarray, pos_base: np.ndarray,
+                    row_offset: np.ndarray, window: int = 0, kv_format: int = KV_F32,
+                    k_scale=None, v_scale=None, threads: int = 0) -> np.ndarray:
+    """Batched runAttentionQ8: q f32 [B, S, H, Dh]; sequence b reads cache rows
+    row_offset[b] + j; runs sequences on `threads` host threads (0 = all)."""
+    B, S, H, Dh = q.shape
+    KV = k.shape[1]
+    pos_base = np.ascontiguousarray(pos_base, dtype=np.int32)
+    row_offset = np.ascontiguousarray(row_offset, dtype=np.int64)
+    if threads <= 0:
+        threads = os.cpu_count() or 1
+    out = np.zeros_like(q)
+    ks = _p(k_scale) if kv_format == KV_Q8_0 else None
+    vs = _p(v_scale) if kv_format == KV_Q8_0 else None
+    lib().oracle_attention_batch(_p(q), _p(np.ascontiguousarray(k)), ks, _p(np.ascontiguousarray(v)), vs,
+                                 _p(out), B, S, H, KV, Dh, _p(pos_base), _p(row_offset), window, kv_format,
+                                 threads)
+    return out
+
+
+def attention_q8_wgsl(q, kq, k_amax, vq, v_amax, pos_base: int, window: int = 0) -> np.ndarray:
+    """attention_q8 WGSL semantics (src/kernels.ts:1341-1426), f32 arithmetic;
+    the scale arrays hold amax (= the JS scale x 127)."""
+    S, H, Dh = q.shape
+    KV = kq.shape[1]
+    out = np.zeros_like(q)
+    lib().oracle_attention_q8_wgsl(_p(q), _p(kq), _p(k_amax), _p(vq), _p(v_amax), _p(out), S, H, KV, Dh,
+                                   pos_base, window)
+    return out
+
+
+def deltanet_gbeta(a: np.ndarray, b: np.ndarray, a_neg: np.ndarray, dt_bias: np.ndarray) -> np.ndarray:
+    """g / beta (src/wasm-backend.ts:1036-1045): a, b f32 [S, NV] -> [2, S, NV]."""
+    S, NV = a.shape
+    out = np.zeros((2, S, NV), np.float32)
+    lib().oracle_deltanet_gbeta(_p(a), _p(b), _p(a_neg), _p(dt_bias), _p(out), S, NV)
+    return out
+
+
+def deltanet_recur(qkv_conv: np.ndarray, gbeta: np.ndarray, state: np.ndarray, NK: int, NV: int,
+                   load_state: bool = True, threads: int = 1):
+    """Recurrence (src/wasm-backend.ts:1047-1102).  qkv_conv f32 [S, convDim];
+    gbeta f32 [2, S, NV]; state f32 [NV, D, D] ([dk][dv]).  Returns
+    (core [S, NV, D], new_state); the input state is not modified."""
+    S = qkv_conv.shape[0]
+    D = state.shape[-1]
+    st = np.array(state, dtype=np.float32, copy=True, order="C")
+    core = np.zeros((S, NV, D), np.float32)
+    lib().oracle_deltanet_recur(_p(np.ascontiguousarray(qkv_conv)), _p(np.ascontiguousarray(gbeta)), _p(st),
+                                _p(core), S, NK, NV, D, int(load_state), threads)
+    return core, st
+
+
+def deltanet_recur_wgsl(qkv_conv, gbeta, state, NK: int, NV: int, load_state: bool = True):
+    """deltanet_recur WGSL semantics (src/kernels.ts:1496-1573), f32 arithmetic."""
+    S = qkv_conv.shape[0]
+    D = state.shape[-1]
+    core = np.zeros((S, NV, D), np.float32)
+    out = np.zeros_like(state)
+    lib().oracle_deltanet_recur_wgsl(_p(qkv_conv), _p(gbeta), _p(np.ascontiguousarray(state)), _p(core),
+                                     _p(out), S, NV, D, D, NK, int(load_state))
+    return core, out
+
+
+def deltanet_recur_batch(qkv_conv: np.ndarray, gbeta: np.ndarray, state: np.ndarray, NK: int, NV: int,
+                         load_state: bool = True, threads: int = 0):
+    """Batched recurrence: qkv_conv [B, S, convDim], gbeta [B, 2, S, NV],
+    state [B, NV, D, D]; sequences on `threads` host threads (0 = all)."""
+    B, S, _ = qkv_conv.shape
+    D = state.shape[-1]
+    st = np.array(state, dtype=np.float32, copy=True, order="C")
+    core = np.zeros((B, S, NV, D), np.float32)
+    if threads <= 0:
+        threads = os.cpu_count() or 1
+    qkv_conv = np.ascontiguousarray(qkv_conv)
+    gbeta = np.ascontiguousarray(gbeta)
+    lib().oracle_deltanet_recur_batch(_p(qkv_conv), _p(gbeta), _p(st), _p(core), B, S, NK, NV, D,
+                                      int(load_state), qkv_conv[0].size, gbeta[0].size, st[0].size,
+                                      core[0].size, threads)
+    return core, st
+
+
+# --------------------------------------------------------------------------
+# Independent dense restatements (numpy f64) used to self-check the C oracle.
+# --------------------------------------------------------------------------
+class closed_form:
+    @staticmethod
+    def attention(q, k, v, pos_base: int, window: int = 0):
+        """softmax(q k^T / sqrt(Dh)) v with the causal sliding-window mask, f64.
+        q [S, H, Dh]; k, v [rows, KV, Dh] as float arrays."""
+        q = q.astype(np.float64)
+        k = k.astype(np.float64)
+        v = v.astype(np.float64)
+        S, H, Dh = q.shape
+        KV = k.shape[1]
+        G = H // KV
+        out = np.zeros((S, H, Dh))
+        for qi in range(S):
+            pos = pos_base + qi
+            j0 = pos + 1 - window if (window > 0 and pos + 1 > window) else 0
+            for h in range(H):
+                kk = k[j0:pos + 1, h // G]
+                vv = v[j0:pos + 1, h // G]
+                s = kk @ q[qi, h] / np.sqrt(Dh)
+                p = np.exp(s - s.max())
+                out[qi, h] = p @ vv / p.sum()
+        return out
+
+    @staticmethod
+    def deltanet(q, k, v, g, beta, state0):
+        """Gated delta rule in the matrix form S <- a S (I - b k k^T) + b v k^T,
+        o = S q / sqrt(D), with q, k L2-normalised (eps 1e-6).  Here S is the
+        [dv, dk] matrix (the transpose of the reference's [dk][dv] storage).
+        q, k [T, NV, D] (already mapped to V heads), v [T, NV, D], g, beta
+        [T, NV]; state0 [NV, D(dk), D(dv)] in the reference order."""
+        T, NV, D = v.shape
+        S = np.transpose(state0.astype(np.float64), (0, 2, 1)).copy()
+        o = np.zeros((T, NV, D))
+        for t in range(T):
+            for h in range(NV):
+                kk = k[t, h].astype(np.float64)
+                qq = q[t, h].astype(np.float64)
+                kk = kk / np.sqrt(kk @ kk + 1e-6)
+                qq = qq / np.sqrt(qq @ qq + 1e-6) / np.sqrt(D)
+                a = np.exp(g[t, h])
+                b = beta[t, h]
+                S[h] = a * S[h] @ (np.eye(D) - b * np.outer(kk, kk)) + b * np.outer(v[t, h], kk)
+                o[t, h] = S[h] @ qq
+        return o, np.transpose(S, (0, 2, 1))
+
+
+def threads_available() -> int:
+    return os.cpu_count() or 1

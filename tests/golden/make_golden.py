@@ -1,0 +1,93 @@
+"""Generates the golden fixtures in this folder from the CPU oracle.
+
+    python tests/golden/make_golden.py
+
+The reference (TypeScript) cannot run where this build runs and its own tests
+hold no vectors for this path, so these fixtures are produced by the C
+restatement in oracle/ (which is itself checked against independent numpy
+closed forms and the WGSL-semantics variant in tests/test_oracle.py).  They pin
+the oracle against regressions and give the GPU tests fixed inputs.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+import oracle  # noqa: E402
+
+
+def attention_q8_case(rng, S, H, KV, Dh, pos_base, window):
+    """The engine's exact sequence for one layer and segment (src/engine.ts
+    :1305-1317): append K and V [S, KV, Dh] into Q8_0 caches at pos_base,
+    then attention_q8 over rows [.., pos_base + S)."""
+    rows = pos_base + S
+    k_hist = rng.standard_normal((rows, KV, Dh), dtype=np.float32)
+    v_hist = rng.standard_normal((rows, KV, Dh), dtype=np.float32)
+    q = rng.standard_normal((S, H, Dh), dtype=np.float32)
+    kq = np.zeros((rows, KV, Dh), np.int8)
+    ks = np.zeros((rows, KV, Dh // 32), np.float32)
+    vq, vs = kq.copy(), ks.copy()
+    oracle.append_kv_q8(k_hist, kq, ks, 0)
+    oracle.append_kv_q8(v_hist, vq, vs, 0)
+    out = oracle.attention(q, kq, vq, pos_base, window, oracle.KV_Q8_0, ks, vs)
+    return dict(k=k_hist, v=v_hist, q=q, kq=kq, ks=ks, vq=vq, vs=vs, out=out,
+                meta=np.array([S, H, KV, Dh, pos_base, window], np.int64))
+
+
+def attention_dense_case(rng, fmt, B, H, KV, Dh, lens, S=1, window=0):
+    lens = np.asarray(lens, np.int64)
+    off = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+    total = int(lens.sum())
+    q = rng.standard_normal((B, S, H, Dh), dtype=np.float32)
+    k = rng.standard_normal((total, KV, Dh), dtype=np.float32)
+    v = rng.standard_normal((total, KV, Dh), dtype=np.float32)
+    if fmt == oracle.KV_F16:
+        k, v = k.astype(np.float16).view(np.uint16), v.astype(np.float16).view(np.uint16)
+    elif fmt == oracle.KV_BF16:
+        k = (k.view(np.uint32) >> 16).astype(np.uint16)  # truncation is fine for inputs
+        v = (v.view(np.uint32) >> 16).astype(np.uint16)
+    pos = (lens - S).astype(np.int32)
+    out = oracle.attention_batch(q, k, v, pos, off, window, fmt)
+    return dict(q=q, k=k, v=v, lens=lens, off=off, pos=pos, out=out,
+                meta=np.array([fmt, B, S, H, KV, Dh, window], np.int64))
+
+
+def gdn_case(rng, S, NK, NV, D, load_state):
+    conv_dim = 2 * NK * D + NV * D
+    qkv = rng.standard_normal((S, conv_dim), dtype=np.float32)
+    a = rng.standard_normal((S, NV), dtype=np.float32)
+    b = rng.standard_normal((S, NV), dtype=np.float32)
+    a_neg = -np.exp(rng.standard_normal(NV, dtype=np.float32) * np.float32(0.5))
+    dt_bias = (rng.standard_normal(NV, dtype=np.float32) * np.float32(0.5)).astype(np.float32)
+    state = (rng.standard_normal((NV, D, D), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    gbeta = oracle.deltanet_gbeta(a, b, a_neg.astype(np.float32), dt_bias)
+    core, new_state = oracle.deltanet_recur(qkv, gbeta, state, NK, NV, load_state)
+    return dict(qkv=qkv, a=a, b=b, a_neg=a_neg.astype(np.float32), dt_bias=dt_bias, state=state, gbeta=gbeta,
+                core=core, new_state=new_state, meta=np.array([S, NK, NV, D, int(load_state)], np.int64))
+
+
+def main():
+    rng = np.random.default_rng(20240601)
+    cases = {
+        "attn_q8_decode": attention_q8_case(rng, 1, 4, 2, 128, 77, 0),
+        "attn_q8_segment": attention_q8_case(rng, 8, 8, 4, 128, 24, 0),
+        "attn_q8_swa": attention_q8_case(rng, 3, 4, 1, 128, 50, 16),
+        "attn_q8_dh256": attention_q8_case(rng, 1, 8, 2, 256, 20, 0),
+        "attn_f32_batch": attention_dense_case(rng, oracle.KV_F32, 3, 4, 2, 128, [5, 40, 70]),
+        "attn_f16_batch": attention_dense_case(rng, oracle.KV_F16, 3, 8, 2, 128, [1, 64, 90]),
+        "attn_bf16_batch": attention_dense_case(rng, oracle.KV_BF16, 2, 4, 4, 128, [33, 45]),
+        "gdn_decode": gdn_case(rng, 1, 1, 2, 128, True),
+        "gdn_segment_fresh": gdn_case(rng, 8, 1, 2, 128, False),
+    }
+    for name, arrays in cases.items():
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)
+        print(name, sum(a.nbytes for a in arrays.values()), "bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,182 @@
+"""GPU parity of the attention path against the oracle (through the C ABI).
+
+Tolerance (fp32 decode paths): relative L2 <= 1e-4.  Q8_0 appends are
+bit-exact (int8 values and f32 scales)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from hachiue_b200 import KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueError, workloads
+from hachiue_b200.backend import KVCache
+from tests.conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+TOL = 1e-4
+dev = "cuda"
+
+
+def g(name):
+    return dict(np.load(os.path.join(GOLDEN, name + ".npz")))
+
+
+def T(x, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    return t if dtype is None else t.view(dtype)
+
+
+@pytest.mark.parametrize("name", ["attn_q8_decode", "attn_q8_segment", "attn_q8_swa", "attn_q8_dh256"])
+def test_q8_engine_sequence_via_dispatch(backend, name):
+    """kv_append_q8 x2 then attention_q8, as forwardSegment dispatches them
+    (src/engine.ts:1305-1317), over several segments of the golden case."""
+    d = g(name)
+    S, H, KV, Dh, pos, W = (int(x) for x in d["meta"])
+    rows = pos + S
+    cache = KVCache.allocate(rows, KV, Dh, KV_Q8_0)
+    # history rows first (one segment), then the case's own S rows
+    kf, vf = T(d["k"]), T(d["v"])
+    for lo, hi in ((0, pos), (pos, rows)):
+        if hi > lo:
+            for src, q8, sc in ((kf, cache.k, cache.k_scale), (vf, cache.v, cache.v_scale)):
+                backend.dispatch("kv_append_q8", [hi - lo, KV, Dh, lo], [src[lo:hi].contiguous(), q8, sc])
+    out = torch.zeros((S, H, Dh), device=dev)
+    backend.dispatch("attention_q8", [S, H, KV, Dh, pos, W, 0, 0],
+                     [T(d["q"]), cache.k, cache.k_scale, cache.v, cache.v_scale, out])
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(cache.k.cpu().numpy(), d["kq"])
+    np.testing.assert_array_equal(cache.k_scale.cpu().numpy(), d["ks"])
+    np.testing.assert_array_equal(cache.v.cpu().numpy(), d["vq"])
+    np.testing.assert_array_equal(cache.v_scale.cpu().numpy(), d["vs"])
+    assert rel_l2(out.cpu().numpy(), d["out"]) < TOL
+    assert backend.device_status() == 0
+
+
+@pytest.mark.parametrize("name,fmt,tdt", [("attn_f32_batch", KV_F32, None), ("attn_f16_batch", KV_F16, torch.float16),
+                                          ("attn_bf16_batch", KV_BF16, torch.bfloat16)])
+def test_dense_batches_golden(backend, name, fmt, tdt):
+    d = g(name)
+    _, B, S, H, KV, Dh, W = (int(x) for x in d["meta"])
+    k = T(d["k"].view(np.int16) if tdt is not None else d["k"], tdt)
+    v = T(d["v"].view(np.int16) if tdt is not None else d["v"], tdt)
+    cache = KVCache(fmt, k, v)
+    out = torch.zeros((B, S, H, Dh), device=dev)
+    backend.attention(T(d["q"]), cache, out, T(d["pos"]), W, kv_row_offset=T(d["off"]),
+                      max_context=int(d["lens"].max()))
+    torch.cuda.synchronize()
+    assert rel_l2(out.cpu().numpy(), d["out"]) < TOL
+
+
+def test_cfg1_qwen3_1p7b_decode(backend):
+    w = workloads.decode_cfg1()
+    cache = KVCache(KV_F32, T(w["k"]), T(w["v"]))
+    out = torch.zeros((1, 16, 128), device=dev)
+    backend.attention(T(w["q"]), cache, out, w["pos_base"])
+    ref = oracle.attention(w["q"], w["k"], w["v"], w["pos_base"])
+    assert rel_l2(out.cpu().numpy(), ref) < TOL
+
+
+@pytest.fixture(scope="module")
+def cfg2():
+    return workloads.decode_cfg2()
+
+
+def test_cfg2_qwen3_8b_batched_decode(backend, cfg2):
+    w = cfg2
+    k = T(w["k"].view(np.int16), torch.float16)
+    v = T(w["v"].view(np.int16), torch.float16)
+    cache = KVCache(KV_F16, k, v)
+    out = torch.zeros((64, 1, 32, 128), device=dev)
+    run = lambda: backend.attention(T(w["q"]), cache, out, T(w["pos_base"]), 0,  # noqa: E731
+                                    kv_row_offset=T(w["row_offset"]), max_context=int(w["lens"].max()))
+    run()
+    first = out.cpu().numpy()
+    out.zero_()
+    run()  # second call: the split-merge tickets must have re-armed
+    second = out.cpu().numpy()
+    np.testing.assert_array_equal(first, second)
+    assert np.isfinite(first).all()
+    # oracle on the shortest, longest and a spread of sequences
+    lens = w["lens"]
+    pick = sorted(set([int(np.argmin(lens)), int(np.argmax(lens))] + list(range(0, 64, 9))))
+    for b in pick:
+        o, n = int(w["row_offset"][b]), int(lens[b])
+        ref = oracle.attention(w["q"][b], w["k"][o:o + n].view(np.uint16), w["v"][o:o + n].view(np.uint16),
+                               n - 1, 0, oracle.KV_F16)
+        assert rel_l2(first[b], ref) < TOL, b
+
+
+@pytest.mark.parametrize("H,KV,Dh", [(4, 4, 128), (32, 2, 128), (16, 2, 256), (8, 1, 256)])
+@pytest.mark.parametrize("fmt", [KV_F32, KV_F16, KV_BF16, KV_Q8_0])
+def test_head_layouts_and_formats(backend, H, KV, Dh, fmt):
+    rng = np.random.default_rng(H * 100 + KV + Dh + fmt)
+    rows = 300
+    q = rng.standard_normal((1, H, Dh), dtype=np.float32)
+    kf = rng.standard_normal((rows, KV, Dh), dtype=np.float32)
+    vf = rng.standard_normal((rows, KV, Dh), dtype=np.float32)
+    cache = KVCache.allocate(rows, KV, Dh, fmt)
+    backend.kv_append(T(kf), cache, "k", 0)
+    backend.kv_append(T(vf), cache, "v", 0)
+    out = torch.zeros((1, H, Dh), device=dev)
+    pos = rows - 1
+    backend.attention(T(q), cache, out, pos)
+    torch.cuda.synchronize()
+    if fmt == KV_Q8_0:
+        kk, vv = cache.k.cpu().numpy(), cache.v.cpu().numpy()
+        ref = oracle.attention(q, kk, vv, pos, 0, KV_Q8_0, cache.k_scale.cpu().numpy(), cache.v_scale.cpu().numpy())
+    else:
+        kk = cache.k.view(torch.int16).cpu().numpy().view(np.uint16) if fmt != KV_F32 else cache.k.cpu().numpy()
+        vv = cache.v.view(torch.int16).cpu().numpy().view(np.uint16) if fmt != KV_F32 else cache.v.cpu().numpy()
+        if fmt == KV_F16:
+            np.testing.assert_array_equal(kk, kf.astype(np.float16).view(np.uint16))
+        ref = oracle.attention(q, kk, vv, pos, 0, fmt)
+    assert rel_l2(out.cpu().numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("S,pos,W", [(1, 0, 0), (5, 0, 0), (16, 100, 0), (12, 700, 64), (40, 250, 33), (3, 2, 1)])
+def test_segments_and_windows(backend, S, pos, W):
+    """Prefill segments (S > 1), the first token (posBase 0), sliding windows
+    smaller than a segment, and window 1."""
+    rng = np.random.default_rng(S * 1000 + pos + W)
+    H, KV, Dh = 16, 4, 128
+    rows = pos + S
+    q = rng.standard_normal((S, H, Dh), dtype=np.float32)
+    k = rng.standard_normal((rows, KV, Dh), dtype=np.float32)
+    v = rng.standard_normal((rows, KV, Dh), dtype=np.float32)
+    cache = KVCache(KV_F32, T(k), T(v))
+    out = torch.zeros((S, H, Dh), device=dev)
+    backend.attention(T(q), cache, out, pos, W)
+    ref = oracle.attention(q, k, v, pos, W)
+    assert rel_l2(out.cpu().numpy(), ref) < TOL
+
+
+def test_long_context_many_splits(backend):
+    rng = np.random.default_rng(5)
+    rows, H, KV, Dh = 20000, 8, 2, 128
+    q = rng.standard_normal((1, H, Dh), dtype=np.float32)
+    k = rng.standard_normal((rows, KV, Dh), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((rows, KV, Dh), dtype=np.float32).astype(np.float16)
+    cache = KVCache(KV_F16, T(k.view(np.int16), torch.float16), T(v.view(np.int16), torch.float16))
+    out = torch.zeros((1, H, Dh), device=dev)
+    backend.attention(T(q), cache, out, rows - 1)
+    ref = oracle.attention(q, k.view(np.uint16), v.view(np.uint16), rows - 1, 0, KV_F16)
+    assert rel_l2(out.cpu().numpy(), ref) < TOL
+
+
+def test_errors_are_reported(backend):
+    cache = KVCache.allocate(8, 2, 128, KV_F32)
+    out = torch.zeros((1, 4, 128), device=dev)
+    with pytest.raises(HachiueError, match="cache holds 8 rows"):
+        backend.attention(torch.zeros((1, 4, 128), device=dev), cache, out, 8)
+    with pytest.raises(HachiueError, match="Dh=64"):
+        backend.attention(torch.zeros((1, 4, 64), device=dev), KVCache.allocate(8, 2, 64, KV_F32),
+                          torch.zeros((1, 4, 64), device=dev), 3)
+    with pytest.raises(HachiueError, match="missing pipeline"):
+        backend.dispatch("rope", [1, 2, 3], [out])
+    backend.inject_failure(5, 1)
+    with pytest.raises(HachiueError, match="injected"):
+        backend.attention(torch.zeros((1, 4, 128), device=dev), cache, out, 3)
+    backend.attention(torch.zeros((1, 4, 128), device=dev), cache, out, 3)  # recovers
+    torch.cuda.synchronize()

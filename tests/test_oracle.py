@@ -1,0 +1,185 @@
+"""CPU checks of the oracle (the checker the GPU parity tests trust).
+
+Parity is unpinned by the reference (TypeScript, no runtime here, no golden
+vectors for this path), so the oracle is pinned three other ways: against the
+committed fixtures, against independent dense numpy f64 closed forms, against
+the WGSL-semantics variant of each reference kernel, and against known answers
+worked out by hand.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from tests.conftest import rel_l2
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def load(name):
+    return dict(np.load(os.path.join(GOLDEN, name + ".npz")))
+
+
+@pytest.mark.parametrize("name", sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))))
+def test_golden_reproduces(name):
+    d = load(name)
+    if name.startswith("attn_q8"):
+        S, H, KV, Dh, pos, W = (int(x) for x in d["meta"])
+        kq = np.zeros_like(d["kq"])
+        ks = np.zeros_like(d["ks"])
+        oracle.append_kv_q8(d["k"], kq, ks, 0)
+        np.testing.assert_array_equal(kq, d["kq"])
+        np.testing.assert_array_equal(ks, d["ks"])
+        out = oracle.attention(d["q"], d["kq"], d["vq"], pos, W, oracle.KV_Q8_0, d["ks"], d["vs"])
+        np.testing.assert_array_equal(out, d["out"])
+    elif name.startswith("attn_"):
+        fmt, B, S, H, KV, Dh, W = (int(x) for x in d["meta"])
+        out = oracle.attention_batch(d["q"], d["k"], d["v"], d["pos"], d["off"], W, fmt)
+        np.testing.assert_array_equal(out, d["out"])
+    else:
+        S, NK, NV, D, ls = (int(x) for x in d["meta"])
+        gb = oracle.deltanet_gbeta(d["a"], d["b"], d["a_neg"], d["dt_bias"])
+        np.testing.assert_array_equal(gb, d["gbeta"])
+        core, st = oracle.deltanet_recur(d["qkv"], d["gbeta"], d["state"], NK, NV, bool(ls))
+        np.testing.assert_array_equal(core, d["core"])
+        np.testing.assert_array_equal(st, d["new_state"])
+
+
+@pytest.mark.parametrize("window", [0, 5, 64])
+@pytest.mark.parametrize("S", [1, 4])
+def test_attention_matches_closed_form(S, window):
+    rng = np.random.default_rng(7)
+    H, KV, Dh, pos = 8, 2, 128, 60
+    q = rng.standard_normal((S, H, Dh), dtype=np.float32)
+    k = rng.standard_normal((pos + S, KV, Dh), dtype=np.float32)
+    v = rng.standard_normal((pos + S, KV, Dh), dtype=np.float32)
+    ref = oracle.closed_form.attention(q, k, v, pos, window)
+    assert rel_l2(oracle.attention(q, k, v, pos, window), ref) < 1e-6
+
+
+def test_attention_f16_bf16_decode_like_f32():
+    rng = np.random.default_rng(8)
+    H, KV, Dh, pos = 4, 2, 128, 30
+    q = rng.standard_normal((1, H, Dh), dtype=np.float32)
+    k = rng.standard_normal((pos + 1, KV, Dh), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((pos + 1, KV, Dh), dtype=np.float32).astype(np.float16)
+    a16 = oracle.attention(q, k.view(np.uint16), v.view(np.uint16), pos, 0, oracle.KV_F16)
+    a32 = oracle.attention(q, k.astype(np.float32), v.astype(np.float32), pos, 0, oracle.KV_F32)
+    np.testing.assert_array_equal(a16, a32)
+    kb = (k.astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    vb = (v.astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    abf = oracle.attention(q, kb, vb, pos, 0, oracle.KV_BF16)
+    kf = (kb.astype(np.uint32) << 16).view(np.float32)
+    vf = (vb.astype(np.uint32) << 16).view(np.float32)
+    np.testing.assert_array_equal(abf, oracle.attention(q, kf, vf, pos, 0, oracle.KV_F32))
+
+
+def test_f16_decode_matches_numpy():
+    L = oracle.lib()
+    for bits in [0, 1, 0x3ff, 0x400, 0x3c00, 0x7bff, 0x8001, 0xfbff, 0x7c00]:
+        assert L.oracle_f16_to_f64(bits) == float(np.array([bits], np.uint16).view(np.float16)[0])
+
+
+def test_q8_attention_js_and_wgsl_agree():
+    rng = np.random.default_rng(9)
+    S, H, KV, Dh, pos = 3, 4, 2, 128, 40
+    k = rng.standard_normal((pos + S, KV, Dh), dtype=np.float32)
+    v = rng.standard_normal((pos + S, KV, Dh), dtype=np.float32)
+    q = rng.standard_normal((S, H, Dh), dtype=np.float32)
+    kq = np.zeros((pos + S, KV, Dh), np.int8)
+    ks = np.zeros((pos + S, KV, Dh // 32), np.float32)
+    vq, vs = kq.copy(), ks.copy()
+    oracle.append_kv_q8(k, kq, ks, 0)
+    oracle.append_kv_q8(v, vq, vs, 0)
+    for W in (0, 9):
+        js = oracle.attention(q, kq, vq, pos, W, oracle.KV_Q8_0, ks, vs)
+        wg = oracle.attention_q8_wgsl(q, kq, (ks * np.float32(127)).astype(np.float32), vq,
+                                      (vs * np.float32(127)).astype(np.float32), pos, W)
+        assert rel_l2(wg, js) < 1e-6
+        kd = (kq.reshape(-1, 32) * ks.reshape(-1, 1).astype(np.float64)).reshape(k.shape)
+        vd = (vq.reshape(-1, 32) * vs.reshape(-1, 1).astype(np.float64)).reshape(v.shape)
+        assert rel_l2(js, oracle.closed_form.attention(q, kd, vd, pos, W)) < 1e-6
+
+
+def test_append_q8_known_answers():
+    # Math.round ties go toward +infinity: with amax = 127, x = +-2.5 maps to 3 / -2.
+    src = np.zeros((1, 1, 32), np.float32)
+    src[0, 0, :6] = [127.0, 2.5, -2.5, 0.5, -0.5, -127.0]
+    cq = np.zeros((1, 1, 32), np.int8)
+    cs = np.zeros((1, 1, 1), np.float32)
+    oracle.append_kv_q8(src, cq, cs, 0)
+    assert list(cq[0, 0, :6]) == [127, 3, -2, 1, 0, -127]
+    assert cs[0, 0, 0] == np.float32(1.0)
+    # An all-zero block stores scale 0 and zeros.
+    oracle.append_kv_q8(np.zeros((1, 1, 32), np.float32), cq, cs, 0)
+    assert cs[0, 0, 0] == 0 and not cq.any()
+
+
+def test_attention_known_answers():
+    Dh = 128
+    q = np.zeros((1, 1, Dh), np.float32)
+    v = np.arange(3 * Dh, dtype=np.float32).reshape(3, 1, Dh)
+    k = np.zeros((3, 1, Dh), np.float32)
+    # Equal scores: the mean of the values.
+    out = oracle.attention(q, k, v, 2, 0)
+    np.testing.assert_allclose(out[0, 0], v[:, 0].mean(0), rtol=1e-6)
+    # Window 1: only the query's own key.
+    out = oracle.attention(q, k, v, 2, 1)
+    np.testing.assert_allclose(out[0, 0], v[2, 0], rtol=1e-6)
+
+
+def test_deltanet_matches_closed_form_and_wgsl():
+    rng = np.random.default_rng(10)
+    T, NK, NV, D = 6, 2, 4, 128
+    q = rng.standard_normal((T, NK, D), dtype=np.float32)
+    k = rng.standard_normal((T, NK, D), dtype=np.float32)
+    v = rng.standard_normal((T, NV, D), dtype=np.float32)
+    qkv = np.concatenate([q.reshape(T, -1), k.reshape(T, -1), v.reshape(T, -1)], 1).astype(np.float32)
+    a = rng.standard_normal((T, NV), dtype=np.float32)
+    b = rng.standard_normal((T, NV), dtype=np.float32)
+    gb = oracle.deltanet_gbeta(a, b, -np.ones(NV, np.float32), np.zeros(NV, np.float32))
+    # alpha = exp(g) = exp(-softplus(a)), beta = sigmoid(b)
+    np.testing.assert_allclose(np.exp(gb[0]), np.exp(-np.logaddexp(0, a.astype(np.float64))), rtol=1e-6)
+    np.testing.assert_allclose(gb[1], 1 / (1 + np.exp(-b.astype(np.float64))), rtol=1e-6)
+    st0 = (0.02 * rng.standard_normal((NV, D, D))).astype(np.float32)
+    core, st = oracle.deltanet_recur(qkv, gb, st0, NK, NV, True)
+    hmap = np.arange(NV) % NK  # tiled QK-head map (kernels.ts:1511)
+    o, stc = oracle.closed_form.deltanet(q[:, hmap], k[:, hmap], v, gb[0], gb[1], st0)
+    assert rel_l2(core, o) < 1e-6 and rel_l2(st, stc) < 1e-6
+    cw, sw = oracle.deltanet_recur_wgsl(qkv, gb, st0, NK, NV, True)
+    assert rel_l2(cw, core) < 1e-5 and rel_l2(sw, st) < 1e-5
+    # loadState = 0 ignores the incoming state.
+    c0, s0 = oracle.deltanet_recur(qkv, gb, st0, NK, NV, False)
+    c1, s1 = oracle.deltanet_recur(qkv, gb, np.zeros_like(st0), NK, NV, True)
+    np.testing.assert_array_equal(c0, c1)
+    np.testing.assert_array_equal(s0, s1)
+
+
+def test_deltanet_known_answer_single_step():
+    # Zero state, alpha = 1, beta = 1, unit k = q = e0: S = e0 v^T, o = v / sqrt(D).
+    D = 128
+    qkv = np.zeros((1, 3 * D), np.float32)
+    qkv[0, 0] = 1.0
+    qkv[0, D] = 1.0
+    qkv[0, 2 * D:] = np.arange(D, dtype=np.float32)
+    gb = np.zeros((2, 1, 1), np.float32)
+    gb[1] = 1.0
+    core, st = oracle.deltanet_recur(qkv, gb, np.zeros((1, D, D), np.float32), 1, 1, True)
+    kn = 1 / np.sqrt(1 + 1e-6)
+    np.testing.assert_allclose(st[0, 0], np.arange(D) * kn, rtol=1e-6)
+    np.testing.assert_allclose(core[0, 0], np.arange(D) * kn * kn / np.sqrt(D), rtol=1e-6)
+
+
+def test_batch_drivers_match_single_calls():
+    rng = np.random.default_rng(11)
+    lens = np.array([3, 17, 9])
+    off = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    k = rng.standard_normal((lens.sum(), 2, 128), dtype=np.float32)
+    v = rng.standard_normal((lens.sum(), 2, 128), dtype=np.float32)
+    q = rng.standard_normal((3, 1, 4, 128), dtype=np.float32)
+    out = oracle.attention_batch(q, k, v, lens - 1, off, 0, oracle.KV_F32, threads=3)
+    for b in range(3):
+        ref = oracle.attention(q[b], k[off[b]:off[b] + lens[b]], v[off[b]:off[b] + lens[b]], lens[b] - 1)
+        np.testing.assert_array_equal(out[b], ref)
