@@ -474,6 +474,8 @@ int launch_d(hcu_context* h, int DH, int R, const AttnArgs& args, dim3 grid, con
   return launch_r<FMT, 256>(h, R, args, grid, tk, tv, tks, tvs);
 }
 
+constexpr int kMaxUnits = 1 << 16;  // ticket slots at the head of the workspace
+
 int tile_tokens(int fmt, int dh) {
   const int es = fmt == HCU_KV_F32 ? 4 : (fmt == HCU_KV_Q8_0 ? 1 : 2);
   return 16384 / (dh * es);
@@ -529,7 +531,12 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   }
   chunk = ((chunk + TT - 1) / TT) * TT;
   if (chunk < TT) chunk = TT;
-  const size_t cnt_bytes = ((size_t)units * sizeof(int) + 255) & ~(size_t)255;
+  // Split-merge tickets live in a fixed region at the start of the workspace so
+  // that no call's partials ever overlap another call's tickets (each ticket is
+  // re-armed to 0 by the CTA that consumes it).
+  const size_t cnt_bytes = (size_t)kMaxUnits * sizeof(int);
+  if (units > kMaxUnits)
+    return fail(HCU_EINVAL, "hcu_attention: batch x KV x query blocks = %lld > %d", units, kMaxUnits);
   auto need = [&](long long c) {
     long long ms = (max_range + c - 1) / c;
     return cnt_bytes + (size_t)units * ms * R * (Dh + 2) * sizeof(float);

@@ -136,7 +136,9 @@ int hcu_destroy(hcu_handle h) {
 
 int hcu_set_stream(hcu_handle h, void* stream) {
   if (!h) return fail(HCU_EINVAL, "hcu_set_stream: null handle");
-  h->stream = stream ? reinterpret_cast<cudaStream_t>(stream) : h->own_stream;
+  // NULL is the CUDA legacy default stream (what torch's default stream is),
+  // not "the handle's own stream": ops must stay ordered with the caller's work.
+  h->stream = reinterpret_cast<cudaStream_t>(stream);
   return HCU_OK;
 }
 

@@ -79,8 +79,10 @@ const char *hcu_last_error(void);
 int hcu_create(int device, size_t workspace_bytes, hcu_handle *out);
 int hcu_destroy(hcu_handle h);
 
-/* Use an existing cudaStream_t (e.g. torch.cuda.current_stream().cuda_stream)
- * instead of the handle's own stream.  NULL restores the handle's stream. */
+/* Enqueue subsequent ops on `cuda_stream` (e.g. torch.cuda.current_stream()
+ * .cuda_stream) instead of the handle's own stream.  NULL is the CUDA legacy
+ * default stream.  hcu_get_stream() returns the stream in use (save it to
+ * switch back to the handle's own stream). */
 int hcu_set_stream(hcu_handle h, void *cuda_stream);
 void *hcu_get_stream(hcu_handle h);
 int hcu_stream_sync(hcu_handle h);
