@@ -21,9 +21,9 @@
 //  * Splits write (m, l, acc) partials to the handle's workspace; the last CTA
 //    of a unit (atomic ticket, no spinning) merges them and writes out.
 #include <stdlib.h>
+#include <string.h>
 
-#include "common.cuh"
-#include "context.h"
+#include "attention.cuh"
 
 namespace {
 
@@ -32,7 +32,6 @@ using namespace hcu;
 constexpr int NW = 4;                   // consumer warps
 constexpr int NTHREADS = (NW + 1) * 32; // + 1 TMA producer warp
 constexpr int NST = 3;                  // pipeline stages
-constexpr float LOG2E = 1.4426950408889634f;
 
 template <int FMT, int DH>
 struct Cfg {
@@ -45,20 +44,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = 2 * (TILE_BYTES + SC_BYTES);
 };
 
-struct AttnArgs {
-  const float* q;
-  float* out;
-  const int32_t* pos_base;
-  const int64_t* row_off;
-  unsigned long long seq_row_stride;
-  int S, H, KV, G, QB, nqb, window, pos_base_default;
-  int chunk;       // keys per split (multiple of TT)
-  int max_splits;  // gridDim.x
-  float qscale;    // log2(e) / sqrt(Dh)
-  float* part;     // [units, max_splits, R, DH + 2]
-  int* counters;   // [units]
-  uint32_t* status;
-};
+
 
 // Loads the lane's DPL elements of tile row `row` as f32 (Q8_0: times the
 // block scale, like `kQ * kS` in wasm-backend.ts:861-866).
@@ -165,26 +151,17 @@ __global__ void __launch_bounds__(NTHREADS, 2)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int split = blockIdx.x, g = blockIdx.y;
-  const int b = blockIdx.z / a.nqb, qb = blockIdx.z % a.nqb;
-
-  const int pb = a.pos_base ? a.pos_base[b] : a.pos_base_default;
-  const long long roff = a.row_off ? a.row_off[b] : (long long)b * (long long)a.seq_row_stride;
-  const int q0 = qb * a.QB;
-  const int qn = min(a.QB, a.S - q0);
-  const int pos_first = pb + q0, pos_last = pb + q0 + qn - 1;
-  const int kstart = (a.window > 0 && pos_first + 1 > a.window) ? pos_first + 1 - a.window : 0;
-  const int kend = pos_last + 1;
-  const int nsplit = (kend - kstart + a.chunk - 1) / a.chunk;
-  if (nsplit > (int)gridDim.x) {  // max_context under-stated by the caller: refuse, never half-merge
+  const int split = blockIdx.x;
+  const AttnUnit u = attn_unit(a, split);
+  if (u.nsplit > (int)gridDim.x) {  // max_context under-stated by the caller: refuse, never half-merge
     if (split == 0 && threadIdx.x == 0) atomicOr(a.status, HCU_DEVERR_BADARG);
     return;
   }
-  if (split >= nsplit) return;  // uniform for the CTA, before any barrier
-  const int k_lo = kstart + split * a.chunk;
-  const int k_hi = min(kend, k_lo + a.chunk);
+  if (split >= u.nsplit) return;  // uniform for the CTA, before any barrier
+  const int g = u.g, b = u.b, pb = u.pb, q0 = u.q0, qn = u.qn;
+  const int k_lo = u.k_lo, k_hi = u.k_hi;
+  const long long roff = u.roff;
   const int ntiles = (k_hi - k_lo + TT - 1) / TT;
-  const int unit = (b * a.KV + g) * a.nqb + qb;
 
   if (tid == 0) {
     for (int s = 0; s < NST; s++) {
@@ -379,8 +356,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   named_bar(1, NW * 32);
   if (aborted) return;
 
-  const int rows_valid = min(a.QB * a.G, qn * a.G);
-  float* part = a.part + ((size_t)unit * a.max_splits + split) * R * (DH + 2);
+  const int rows_valid = u.rows_valid;
+  float* part = a.part + ((size_t)u.unit * a.max_splits + split) * R * (DH + 2);
   for (int e = tid; e < R * DH; e += NW * 32) {
     const int r = e / DH, d = e % DH;
     float M = -1e30f;
@@ -393,11 +370,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       L += cl[w * R + r] * f;
       A += cb[(w * R + r) * DH + d] * f;
     }
-    if (nsplit == 1) {
-      if (r < rows_valid) {
-        const int qi = q0 + r / a.G, h = g * a.G + r % a.G;
-        a.out[(((long long)b * a.S + qi) * a.H + h) * DH + d] = A / L;
-      }
+    if (u.nsplit == 1) {
+      if (r < rows_valid) a.out[out_index(a, u, r, d, DH)] = A / L;
     } else {
       part[r * (DH + 2) + d] = A;
       if (d == 0) {
@@ -406,31 +380,11 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       }
     }
   }
-  if (nsplit == 1) return;
-
-  // ---------------- split merge by the last CTA of the unit ----------------
-  __threadfence();
-  named_bar(1, NW * 32);
-  if (tid == 0) s_last = (atomicAdd(&a.counters[unit], 1) == nsplit - 1);
-  named_bar(1, NW * 32);
-  if (!s_last) return;
-  __threadfence();
-  const float* up = a.part + (size_t)unit * a.max_splits * R * (DH + 2);
-  for (int e = tid; e < rows_valid * DH; e += NW * 32) {
-    const int r = e / DH, d = e % DH;
-    float M = -1e30f;
-    for (int sp = 0; sp < nsplit; sp++) M = fmaxf(M, __ldcg(up + ((size_t)sp * R + r) * (DH + 2) + DH));
-    float L = 0.f, A = 0.f;
-    for (int sp = 0; sp < nsplit; sp++) {
-      const float* pp = up + ((size_t)sp * R + r) * (DH + 2);
-      const float f = exp2f(__ldcg(pp + DH) - M);
-      L += __ldcg(pp + DH + 1) * f;
-      A += __ldcg(pp + d) * f;
-    }
-    const int qi = q0 + r / a.G, h = g * a.G + r % a.G;
-    a.out[(((long long)b * a.S + qi) * a.H + h) * DH + d] = A / L;
-  }
-  if (tid == 0) a.counters[unit] = 0;  // re-arm for the next call
+  if (u.nsplit == 1) return;
+  named_bar(1, NW * 32);  // cb / cm / cl are read above; the merge reuses the stage memory
+  ticket_merge<R, DH>(a, u, tid, NW * 32, 1, reinterpret_cast<float*>(stages), &s_last);
+  (void)b;
+  (void)pb;
 }
 
 // ---------------------------------------------------------------------------
@@ -474,8 +428,6 @@ int launch_d(hcu_context* h, int DH, int R, const AttnArgs& args, dim3 grid, con
   return launch_r<FMT, 256>(h, R, args, grid, tk, tv, tks, tvs);
 }
 
-constexpr int kMaxUnits = 1 << 16;  // ticket slots at the head of the workspace
-
 int tile_tokens(int fmt, int dh) {
   const int es = fmt == HCU_KV_F32 ? 4 : (fmt == HCU_KV_Q8_0 ? 1 : 2);
   return 16384 / (dh * es);
@@ -501,11 +453,19 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   if (reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
     return fail(HCU_EINVAL, "hcu_attention: q and out must be 16-byte aligned");
   const int G = H / KV;
-  const int rmax = Dh == 128 ? 16 : 8;
+  // The tcgen05 kernel serves f16 / bf16 caches with Dh = 128; every other
+  // combination (and HCU_ATTN_IMPL=cuda) uses the CUDA-core kernel.
+  const char* impl = getenv("HCU_ATTN_IMPL");
+  const bool force_cuda = impl && !strcmp(impl, "cuda");
+  const int rmax_cuda = Dh == 128 ? 16 : 8;
+  const int rmax_tc = fmt == HCU_KV_F16 ? 16 : 8;
+  bool use_tc = !force_cuda && hcu::attn_tc_supported(fmt, Dh, G);
+  const int rmax = use_tc ? rmax_tc : rmax_cuda;
   if (G > rmax) return fail(HCU_EUNSUPPORTED, "hcu_attention: group size %d > %d", G, rmax);
   const int QB = S < rmax / G ? S : rmax / G;
   int R = 1;
   while (R < QB * G) R <<= 1;
+  if (use_tc && !hcu::attn_tc_supported(fmt, Dh, R)) use_tc = false;
   const int nqb = (S + QB - 1) / QB;
   if ((long long)batch * nqb > 65535) return fail(HCU_EINVAL, "hcu_attention: batch x query blocks > 65535");
   if (KV > 65535) return fail(HCU_EINVAL, "hcu_attention: KV > 65535");
@@ -519,8 +479,12 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
                 (long long)p->posBase + S);
   if (kv->rows == 0 || kv->rows > 0x7fffffffu) return fail(HCU_EINVAL, "hcu_attention: bad cache row count");
 
-  const int TT = tile_tokens(fmt, Dh);
+  // Key splits: about 8 CTAs per SM over the whole call, at most kMaxSplits
+  // per unit, each a whole number of tiles.
+  const int TT = use_tc ? hcu::kTcTile : tile_tokens(fmt, Dh);
   const long long units = (long long)batch * KV * nqb;
+  if (units > kMaxUnits)
+    return fail(HCU_EINVAL, "hcu_attention: batch x KV x query blocks = %lld > %d", units, kMaxUnits);
   long long target = 8LL * h->sm_count;
   long long want_splits = (target + units - 1) / units;
   if (want_splits < 1) want_splits = 1;
@@ -529,14 +493,14 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
     long long c = atoll(env);
     if (c > 0) chunk = c;
   }
+  const long long min_chunk = (max_range + kMaxSplits - 1) / kMaxSplits;
+  if (chunk < min_chunk) chunk = min_chunk;
   chunk = ((chunk + TT - 1) / TT) * TT;
   if (chunk < TT) chunk = TT;
   // Split-merge tickets live in a fixed region at the start of the workspace so
   // that no call's partials ever overlap another call's tickets (each ticket is
   // re-armed to 0 by the CTA that consumes it).
   const size_t cnt_bytes = (size_t)kMaxUnits * sizeof(int);
-  if (units > kMaxUnits)
-    return fail(HCU_EINVAL, "hcu_attention: batch x KV x query blocks = %lld > %d", units, kMaxUnits);
   auto need = [&](long long c) {
     long long ms = (max_range + c - 1) / c;
     return cnt_bytes + (size_t)units * ms * R * (Dh + 2) * sizeof(float);
@@ -546,9 +510,11 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
     return fail(HCU_ENOMEM, "hcu_attention: workspace of %zu bytes too small (need %zu)", h->workspace_bytes,
                 need(chunk));
   const long long max_splits = (max_range + chunk - 1) / chunk;
-  if (max_splits > 0x7fffffff) return fail(HCU_EINVAL, "hcu_attention: too many splits");
+  if (max_splits > kMaxSplits || chunk > 0x7fffffff) return fail(HCU_EINVAL, "hcu_attention: too many splits");
 
-  // TMA descriptors over the whole cache: dims (Dh, KV, rows).
+  // TMA descriptors over the whole cache: dims (Dh, KV, rows).  The tensor-core
+  // kernel loads 64-element (128-byte) boxes with the 128-byte swizzle its
+  // MMA operand descriptors expect.
   const int es = fmt == HCU_KV_F32 ? 4 : (fmt == HCU_KV_Q8_0 ? 1 : 2);
   const CUtensorMapDataType dt = fmt == HCU_KV_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : fmt == HCU_KV_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -558,9 +524,10 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   {
     uint64_t dims[3] = {(uint64_t)Dh, (uint64_t)KV, (uint64_t)kv->rows};
     uint64_t strides[2] = {(uint64_t)Dh * es, (uint64_t)KV * Dh * es};
-    uint32_t box[3] = {(uint32_t)Dh, 1u, (uint32_t)TT};
-    HCU_TRY(hcu::make_tensor_map(&tk, dt, 3, kv->k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE));
-    HCU_TRY(hcu::make_tensor_map(&tv, dt, 3, kv->v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE));
+    uint32_t box[3] = {use_tc ? 64u : (uint32_t)Dh, 1u, (uint32_t)TT};
+    const CUtensorMapSwizzle sw = use_tc ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    HCU_TRY(hcu::make_tensor_map(&tk, dt, 3, kv->k, dims, strides, box, sw));
+    HCU_TRY(hcu::make_tensor_map(&tv, dt, 3, kv->v, dims, strides, box, sw));
   }
   if (fmt == HCU_KV_Q8_0) {
     uint64_t dims[3] = {(uint64_t)Dh / 32, (uint64_t)KV, (uint64_t)kv->rows};
@@ -591,11 +558,12 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   args.pos_base_default = (int)p->posBase;
   args.chunk = (int)chunk;
   args.max_splits = (int)max_splits;
-  args.qscale = LOG2E / sqrtf((float)Dh);
+  args.qscale = kLog2e / sqrtf((float)Dh);
   args.counters = static_cast<int*>(h->workspace);
   args.part = reinterpret_cast<float*>(static_cast<char*>(h->workspace) + cnt_bytes);
   args.status = h->dev_status;
   dim3 grid((unsigned)max_splits, (unsigned)KV, (unsigned)(batch * nqb));
+  if (use_tc) return hcu::launch_attn_tc(h, fmt, R, args, grid, tk, tv);
   switch (fmt) {
     case HCU_KV_F32: return launch_d<HCU_KV_F32>(h, Dh, R, args, grid, tk, tv, tks, tvs);
     case HCU_KV_F16: return launch_d<HCU_KV_F16>(h, Dh, R, args, grid, tk, tv, tks, tvs);

@@ -1,0 +1,98 @@
+// tcgen05.cuh - 5th-generation tensor core (tcgen05 / TMEM) helpers, sm_100a.
+//
+// Shared-memory matrix descriptors, the kind::f16 instruction descriptor, TMEM
+// allocation, MMA issue / commit and TMEM loads, as inline PTX.  Field layouts
+// follow the PTX ISA's tcgen05 "matrix descriptor" and "instruction descriptor"
+// tables (the same layouts CUTLASS's cute/arch/mma_sm100_desc.hpp encodes).
+#pragma once
+
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace hcu {
+
+// Shared-memory matrix descriptor for a 128-byte-swizzled operand.
+//   K-major: rows of 128 B (64 x 16-bit elements along K), 8-row atoms of
+//            1024 B; sbo = byte distance between 8-row groups, lbo unused (16).
+//   MN-major: 128 B (64 elements) along M/N per row, rows along K; lbo = byte
+//            distance between 64-element M/N blocks, sbo = between 8-row K groups.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version (sm_100)
+  d |= (uint64_t)2u << 61;  // layout: SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: f32 accumulate, f16 or bf16 A/B, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                                   // D format: f32
+         | ((bf16 ? 1u : 0u) << 7)                   // A format
+         | ((bf16 ? 1u : 0u) << 10)                  // B format
+         | ((a_mn_major ? 1u : 0u) << 15)            // A major-ness
+         | ((b_mn_major ? 1u : 0u) << 16)            // B major-ness
+         | ((uint32_t)(N >> 3) << 17)                // N / 8
+         | ((uint32_t)(M >> 4) << 24);               // M / 16
+}
+
+// Byte offset of (row, byte_in_row) inside a 128B-swizzled region whose rows
+// are 128 B and whose base is 1024-B aligned (16-byte chunk index XOR row % 8).
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t byte_in_row) {
+  return row * 128u + ((((byte_in_row >> 4) ^ (row & 7u)) << 4) | (byte_in_row & 15u));
+}
+
+// ---- TMEM allocation (executed by one full warp) ----
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// ---- ordering of tcgen05 operations around thread synchronisation ----
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem], kind::f16, issued by one thread.
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation issued so far by this thread
+// has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane (32x32b shape: warp
+// w reads lanes 32*(w%4) .. +31).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+}  // namespace hcu

@@ -180,3 +180,36 @@ def test_errors_are_reported(backend):
         backend.attention(torch.zeros((1, 4, 128), device=dev), cache, out, 3)
     backend.attention(torch.zeros((1, 4, 128), device=dev), cache, out, 3)  # recovers
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("impl", ["tc", "cuda"])
+@pytest.mark.parametrize("fmt", [KV_F16, KV_BF16])
+@pytest.mark.parametrize("H,KV,S,pos,W", [(32, 8, 1, 4000, 0), (16, 4, 3, 700, 0), (8, 2, 5, 1000, 300),
+                                          (4, 4, 1, 129, 0), (16, 2, 1, 2049, 0), (12, 3, 2, 63, 17)])
+def test_tensor_core_and_cuda_core_paths(backend, monkeypatch, impl, fmt, H, KV, S, pos, W):
+    """The tcgen05 kernel (default for f16 / bf16, Dh=128) and the CUDA-core
+    kernel (HCU_ATTN_IMPL=cuda) against the oracle: GQA groups 1-8, S > 1,
+    windows, tile-edge context lengths."""
+    if impl == "cuda":
+        monkeypatch.setenv("HCU_ATTN_IMPL", "cuda")
+    else:
+        monkeypatch.delenv("HCU_ATTN_IMPL", raising=False)
+    rng = np.random.default_rng(H + KV + S + pos + W + fmt)
+    rows = pos + S
+    q = rng.standard_normal((S, H, 128), dtype=np.float32)
+    kf = rng.standard_normal((rows, KV, 128), dtype=np.float32)
+    vf = rng.standard_normal((rows, KV, 128), dtype=np.float32)
+    # capacity past the context holds NaN: masked rows must never reach the output
+    cache = KVCache.allocate(rows + 200, KV, 128, fmt)
+    cache.k.fill_(float("nan"))
+    cache.v.fill_(float("nan"))
+    backend.kv_append(T(kf), cache, "k", 0)
+    backend.kv_append(T(vf), cache, "v", 0)
+    out = torch.zeros((S, H, 128), device=dev)
+    backend.attention(T(q), cache, out, pos, W)
+    torch.cuda.synchronize()
+    kk = cache.k[:rows].view(torch.int16).cpu().numpy().view(np.uint16)
+    vv = cache.v[:rows].view(torch.int16).cpu().numpy().view(np.uint16)
+    ref = oracle.attention(q, kk, vv, pos, W, fmt)
+    assert rel_l2(out.cpu().numpy(), ref) < TOL
+    assert backend.device_status() == 0
