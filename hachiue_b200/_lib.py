@@ -24,7 +24,7 @@ STATUS_NAMES = {
 EXPORTS = (
     "hcu_version", "hcu_last_error", "hcu_create", "hcu_destroy", "hcu_set_stream", "hcu_get_stream",
     "hcu_stream_sync", "hcu_alloc", "hcu_free", "hcu_memset", "hcu_copy_to_device", "hcu_copy_to_host",
-    "hcu_device_status", "hcu_inject_failure", "hcu_dispatch", "hcu_attention", "hcu_kv_append", "hcu_kv_append_rows",
+    "hcu_device_status", "hcu_inject_failure", "hcu_dispatch", "hcu_attention", "hcu_attention_noalloc", "hcu_kv_append", "hcu_kv_append_rows",
     "hcu_deltanet_gbeta", "hcu_deltanet_recur", "hcu_deltanet_decode",
 )
 
@@ -90,6 +90,8 @@ def load(path: str | None = None):
             "hcu_inject_failure": ([vp, i32, i32], i32),
             "hcu_dispatch": ([vp, ctypes.c_char_p, ctypes.POINTER(u32), ctypes.POINTER(vp), i32], i32),
             "hcu_attention": ([vp, ctypes.POINTER(hcu_attention_params), vp, ctypes.POINTER(hcu_kv_cache), vp], i32),
+            "hcu_attention_noalloc": ([ctypes.POINTER(hcu_attention_params), vp, ctypes.POINTER(hcu_kv_cache), vp,
+                                       vp], i32),
             "hcu_kv_append": ([vp, u32, u32, u32, u32, u32, vp, vp, vp], i32),
             "hcu_kv_append_rows": ([vp, u32, u32, u32, u32, vp, vp, vp, vp], i32),
             "hcu_deltanet_gbeta": ([vp, u32, u32, vp, vp, vp, vp, vp], i32),

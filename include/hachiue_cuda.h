@@ -170,6 +170,36 @@ typedef struct {
 int hcu_attention(hcu_handle h, const hcu_attention_params *p, const float *q,
                   const hcu_kv_cache *kv, float *out);
 
+/* hcu_attention for callers that cannot allocate device memory.  This entry
+ * point has no counterpart in the reference.
+ *
+ * Who needs it: a process that reserves its whole HBM budget up front in its
+ * own pool (a library cudaMalloc would fail or fragment memory the pool owns),
+ * or a plugin reached through a stateless FFI call with nowhere to keep an
+ * hcu_handle (creating a handle allocates its workspace, status word and
+ * stream).
+ *
+ * How it works: same arguments and results as hcu_attention, on the caller's
+ * `cuda_stream` (NULL = default stream) of the current device, with no handle.
+ * The split-K scratch is a file-scope __device__ array of
+ * HCU_NOALLOC_SCRATCH_BYTES, which every GPU that loads this library holds
+ * until the process exits; the call makes no cudaMalloc / cudaFree or other
+ * allocating call.
+ *
+ * Limits and rules:
+ *  - A call whose partials do not fit fails with HCU_ENOMEM and a message
+ *    naming the limit (about batch x KV heads x query blocks <= 3800 at
+ *    Dh = 128 with 4 rows per KV head).
+ *  - The first call on a device looks up the array's device address and the
+ *    SM count; make it before any stream capture.
+ *  - All calls share the one array (its tickets are cleared at the start of
+ *    each call), so calls that overlap on the GPU race: issue them on one
+ *    stream or otherwise serialise them.
+ *  - Device-side wait timeouts are recorded in the array, not reported. */
+#define HCU_NOALLOC_SCRATCH_BYTES (8u << 20)
+int hcu_attention_noalloc(const hcu_attention_params *p, const float *q, const hcu_kv_cache *kv,
+                          float *out, void *cuda_stream);
+
 /* Append S rows of K or V (f32 [S, KV, Dh]) at cache row posBase in `format`.
  * For Q8_0 this is appendKvQ8 (src/wasm-backend.ts:793-824) bit for bit:
  * scale = amax/127 stored as f32, q = clamp(Math.round(x*127/amax), +-127).
