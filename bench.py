@@ -251,7 +251,46 @@ def setup_cfg4(torch, be, dev):
                 e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg4"), out=core, traffic_key="cfg4")
 
 
-SETUPS = {1: setup_cfg1, 2: setup_cfg2, 4: setup_cfg4}
+def swa_flops(T=4096, W=1024, B=8, H=16, D=128) -> int:
+    """Algorithmic FLOPs of causal sliding-window attention: 4*D per (query,
+    key) pair inside the window (QK^T and PV), pairs = sum_i min(i+1, W)."""
+    pairs = sum(min(i + 1, W) for i in range(T)) if W > 0 else T * (T + 1) // 2
+    return 4 * D * pairs * B * H
+
+
+def setup_cfg3(torch, be, dev):
+    from hachiue_b200 import workloads
+    w = workloads.swa_cfg3()
+
+    def bf(x):
+        return torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).to(dev).view(torch.bfloat16)
+
+    q, k, v = bf(w["q"]), bf(w["k"]), bf(w["v"])
+    out = torch.empty((8, 4096, 16, 128), device=dev, dtype=torch.bfloat16)
+
+    def step(i):
+        be.swa_prefill(q, k, v, out, w["window"])
+
+    qh, kh, vh = (torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).pin_memory() for x in (w["q"], w["k"], w["v"]))
+    out_h = torch.empty((8, 4096, 16, 128), dtype=torch.int16).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step(i):
+        qd.view(torch.int16).copy_(qh, non_blocking=True)
+        kd.view(torch.int16).copy_(kh, non_blocking=True)
+        vd.view(torch.int16).copy_(vh, non_blocking=True)
+        be.swa_prefill(qd, kd, vd, out, w["window"])
+        out_h.copy_(out.view(torch.int16), non_blocking=True)
+
+    info = dict(workload="cfg3 PLaMo-3 sliding-window causal attention prefill", sequences=8, tokens=4096,
+                q_heads=16, kv_heads=4, head_dim=128, window=1024, io_dtype="bf16 in, bf16 out",
+                l2="inputs 201 MB > L2")
+    return dict(step=step, e2e_step=e2e_step, flops=swa_flops(), tokens=8 * 4096, info=info,
+                h2d=(qh.numel() + kh.numel() + vh.numel()) * 2, d2h=out_h.numel() * 2, kernels_per_step=1,
+                e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg3"), out=out, traffic_key="cfg3")
+
+
+SETUPS = {1: setup_cfg1, 2: setup_cfg2, 3: setup_cfg3, 4: setup_cfg4}
 
 
 # ---------------------------------------------------------------------------
@@ -274,7 +313,7 @@ def cpu_sample(kind: str, w: dict, threads: int, budget_s: float = 12.0):
             done_bytes += workloads.cfg2_bytes(lens)
             reps += 1
         dt = time.perf_counter() - t0
-        return done_bytes / dt / 1e9, done_b / dt, f"{reps} full passes of cfg2 (64 sequences, f16 KV) on {threads} threads"
+        return done_bytes / dt / 1e9, done_b / dt, f"{reps} full passes of cfg2 (64 sequences, f16 KV) on {threads} threads", threads
     if kind == "cfg1":
         t0 = time.perf_counter()
         n = 0
@@ -282,14 +321,29 @@ def cpu_sample(kind: str, w: dict, threads: int, budget_s: float = 12.0):
             oracle.attention(w["q"][0], w["k"], w["v"], w["pos_base"])
             n += 1
         dt = time.perf_counter() - t0
-        return n * workloads.cfg1_bytes() / dt / 1e9, n / dt, f"{n} cfg1 calls, 1 thread"
+        return n * workloads.cfg1_bytes() / dt / 1e9, n / dt, f"{n} cfg1 calls, 1 thread", 1
     if kind == "cfg4":
         B = 16
         gb = np.stack([oracle.deltanet_gbeta(w["a"][b], w["b"][b], w["a_neg"], w["dt_bias"]) for b in range(B)])
         t0 = time.perf_counter()
         oracle.deltanet_recur_batch(w["qkv"][:B], gb, w["state"][:B], w["NK"], w["NV"], True, threads=threads)
         dt = time.perf_counter() - t0
-        return workloads.cfg4_bytes(B=B) / dt / 1e9, B / dt, f"{B} of 64 sequences of cfg4 on {threads} threads"
+        return workloads.cfg4_bytes(B=B) / dt / 1e9, B / dt, f"{B} of 64 sequences of cfg4 on {threads} threads", threads
+    if kind == "cfg3":
+        from hachiue_b200 import workloads as wl
+        qs, qe = 3000, 3064
+        q = np.ascontiguousarray(wl.bf16_bits_to_f32(w["q"][0, qs:qe]))
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            oracle.attention(q, np.ascontiguousarray(w["k"][0]), np.ascontiguousarray(w["v"][0]), qs, w["window"],
+                             oracle.KV_BF16)
+            n += 1
+            if time.perf_counter() - t0 > min(budget_s, 4.0):
+                break
+        dt = time.perf_counter() - t0
+        flops = n * 4 * 128 * (qe - qs) * 16 * w["window"]
+        return flops / dt / 1e12, n * (qe - qs) / dt, f"{n} x 64 queries x 16 heads of cfg3 sequence 0, 1 thread", 1
     raise ValueError(kind)
 
 
@@ -304,6 +358,8 @@ def run_reference(args, world, rank):
         w = workloads.decode_cfg2()
     elif args.config == 1:
         w = workloads.decode_cfg1()
+    elif args.config == 3:
+        w = workloads.swa_cfg3()
     else:
         w = workloads.gdn_decode_cfg4()
     kind = f"cfg{args.config}"
@@ -312,32 +368,40 @@ def run_reference(args, world, rank):
     vals = []
     t_all = time.perf_counter()
     desc = ""
+    cores = threads
     for _ in range(args.steps):
-        gbs, tps, desc = cpu_sample(kind, w, threads, budget_s=2.0)
+        gbs, tps, desc, cores = cpu_sample(kind, w, threads, budget_s=2.0)
         vals.append(gbs)
     elapsed = time.perf_counter() - t_all
     value = statistics.median(vals)
     line = {
-        "impl": "reference", "metric": metric_name(args.config), "value": round(value, 4), "unit": "GB/s",
+        "impl": "reference", "metric": metric_name(args.config), "value": round(value, 4),
+        "unit": metric_unit(args.config),
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1000 * elapsed / max(args.steps, 1), 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(args.config), "data": "synthetic",
         "config": {"workload": f"cfg{args.config} (see --impl ours)", "parallelism": "host threads"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+        "cpu_baseline": {"value": round(value, 4), "unit": metric_unit(args.config), "cores": cores, "kind": "port",
                          "sample": desc + "; the reference is TypeScript with no runtime on this box, so its "
                                           "JS-semantics C restatement (oracle/) is timed"},
-        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": round(value, 4), "unit": metric_unit(args.config), "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
 def metric_name(cfg: int) -> str:
-    return {1: "decode attn HBM GB/s", 2: "decode attn HBM GB/s", 4: "GDN decode HBM GB/s"}[cfg]
+    return {1: "decode attn HBM GB/s", 2: "decode attn HBM GB/s", 3: "SWA prefill TFLOP/s",
+            4: "GDN decode HBM GB/s"}[cfg]
+
+
+def metric_unit(cfg: int) -> str:
+    return "TFLOP/s" if cfg == 3 else "GB/s"
 
 
 def dtype_name(cfg: int) -> str:
-    return {1: "f32", 2: "f16", 4: "f32"}[cfg]
+    return {1: "f32", 2: "f16", 3: "bf16", 4: "f32"}[cfg]
 
 
 # ---------------------------------------------------------------------------
@@ -415,9 +479,12 @@ def main(argv=None):
         raise RuntimeError(f"device status {status} after the timed region")
 
     ms_per_step = total_ms / args.steps
-    value = world * W["bytes"] / (ms_per_step / 1e3) / 1e9
+    tensor = "flops" in W
+    work = W["flops"] if tensor else W["bytes"]
+    scale = 1e12 if tensor else 1e9  # TFLOP/s or GB/s
+    value = world * work / (ms_per_step / 1e3) / scale
     kavg = statistics.mean(kernel_ms)
-    achieved = W["bytes"] / (kavg / 1e3) / 1e9
+    achieved = work / (kavg / 1e3) / scale
 
     # ---- end to end through the public API (host buffers) ----
     for i in range(args.warmup):
@@ -439,32 +506,35 @@ def main(argv=None):
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = world * W["bytes"] / (e2e_ms / args.steps / 1e3) / 1e9
+    e2e_value = world * work / (e2e_ms / args.steps / 1e3) / scale
 
     peaks, peak_src = load_peaks()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        gbs, _, desc = cpu_sample(W["cpu"]["kind"], W["cpu"]["w"], threads)
-        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+        gbs, _, desc, cores = cpu_sample(W["cpu"]["kind"], W["cpu"]["w"], threads)
+        cpu = {"value": round(gbs, 4), "unit": metric_unit(args.config), "cores": cores, "kind": "port",
                "sample": desc + " (the reference is TypeScript with no runtime here; its JS-semantics C "
                                 "restatement in oracle/ is timed)"}
 
     if rank == 0:
         traffic = load_traffic(W["traffic_key"])
+        peak = peaks["bf16_tflops"] if tensor else peaks["hbm_gbs"]
         line = {
-            "metric": metric_name(args.config), "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "metric": metric_name(args.config), "value": round(value, 2), "unit": metric_unit(args.config),
+            "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(args.config),
             "data": "synthetic (seeded numpy PCG64, benchmark-config shapes)",
             "config": dict(W["info"], parallelism=f"dp{world} (sequences per rank) + NCCL all-gather of outputs"
                            if world > 1 else "single GPU"),
             "tokens_per_s": round(world * W["tokens"] / (ms_per_step / 1e3), 1),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peak_src,
-                         "algorithmic_bytes_per_launch": W["bytes"], "kernel_ms": round(kavg, 5),
-                         "traffic": traffic},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": W["h2d"],
+            "roofline": {"bound": "tensor" if tensor else "hbm", "achieved": round(achieved, 2), "peak": peak,
+                         "unit": metric_unit(args.config), "frac": round(achieved / peak, 4),
+                         "peak_source": peak_src + (" bf16 burst" if tensor else " copy"),
+                         ("algorithmic_flops_per_launch" if tensor else "algorithmic_bytes_per_launch"): work,
+                         "kernel_ms": round(kavg, 5), "traffic": traffic},
+            "e2e": {"value": round(e2e_value, 2), "unit": metric_unit(args.config), "h2d_bytes_per_step": W["h2d"],
                     "d2h_bytes_per_step": W["d2h"], "ms_per_step": round(e2e_ms / args.steps, 5)},
             "gpu_launches": args.steps * W["kernels_per_step"],
             "e2e_gpu_launches": args.steps * W["e2e_kernels_per_step"],

@@ -25,7 +25,7 @@ EXPORTS = (
     "hcu_version", "hcu_last_error", "hcu_create", "hcu_destroy", "hcu_set_stream", "hcu_get_stream",
     "hcu_stream_sync", "hcu_alloc", "hcu_free", "hcu_memset", "hcu_copy_to_device", "hcu_copy_to_host",
     "hcu_device_status", "hcu_inject_failure", "hcu_dispatch", "hcu_attention", "hcu_attention_noalloc", "hcu_kv_append", "hcu_kv_append_rows",
-    "hcu_deltanet_gbeta", "hcu_deltanet_recur", "hcu_deltanet_decode",
+    "hcu_deltanet_gbeta", "hcu_deltanet_recur", "hcu_deltanet_decode", "hcu_swa_prefill",
 )
 
 
@@ -54,6 +54,11 @@ class hcu_deltanet_params(ctypes.Structure):
                 ("HK", ctypes.c_uint32), ("loadState", ctypes.c_uint32), ("batch", ctypes.c_uint32),
                 ("qkv_seq_stride", ctypes.c_uint64), ("gbeta_seq_stride", ctypes.c_uint64),
                 ("state_seq_stride", ctypes.c_uint64), ("core_seq_stride", ctypes.c_uint64)]
+
+
+class hcu_swa_params(ctypes.Structure):
+    _fields_ = [("B", ctypes.c_uint32), ("T", ctypes.c_uint32), ("H", ctypes.c_uint32), ("KV", ctypes.c_uint32),
+                ("D", ctypes.c_uint32), ("window", ctypes.c_uint32), ("out_dtype", ctypes.c_uint32)]
 
 
 _lock = threading.Lock()
@@ -97,6 +102,7 @@ def load(path: str | None = None):
             "hcu_deltanet_gbeta": ([vp, u32, u32, vp, vp, vp, vp, vp], i32),
             "hcu_deltanet_recur": ([vp, ctypes.POINTER(hcu_deltanet_params), vp, vp, vp, vp, vp], i32),
             "hcu_deltanet_decode": ([vp, ctypes.POINTER(hcu_deltanet_params), vp, vp, vp, vp, vp, vp, vp, vp], i32),
+            "hcu_swa_prefill": ([vp, ctypes.POINTER(hcu_swa_params), vp, vp, vp, vp], i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -21,8 +21,8 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from ._lib import (KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueError, check, hcu_attention_params,
-                   hcu_deltanet_params, hcu_kv_cache)
+from ._lib import (DT_BF16, DT_F32, KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueError, check, hcu_attention_params,
+                   hcu_deltanet_params, hcu_kv_cache, hcu_swa_params)
 
 # The reference's op names on this path (src/kernels.ts SHADERS keys).
 SHADERS = ("kv_append_q8", "attention_q8", "deltanet_gbeta", "deltanet_recur")
@@ -210,3 +210,16 @@ class CudaBackend:
         p = self._dn_params(qkv_conv, NK, NV, D, load_state)
         check(self.lib.hcu_deltanet_decode(self._h, ctypes.byref(p), _ptr(qkv_conv), _ptr(a), _ptr(b), _ptr(a_neg),
                                            _ptr(dt_bias), _ptr(state_in), _ptr(core), _ptr(state_out)))
+
+    def swa_prefill(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+                    window: int = 0) -> None:
+        """Causal sliding-window attention over whole prompts: q bf16 [B, T, H, D],
+        k / v bf16 [B, T, KV, D], out bf16 or f32 [B, T, H, D]; window 0 = causal."""
+        self._bind_stream()
+        for t in (q, k, v):
+            if t.dtype != torch.bfloat16 or not t.is_contiguous():
+                raise HachiueError(_lib.HCU_EINVAL, "hachiue: swa_prefill takes contiguous bf16 q / k / v")
+        B, T, H, D = q.shape
+        p = hcu_swa_params(B, T, H, k.shape[2], D, window,
+                           DT_BF16 if out.dtype == torch.bfloat16 else DT_F32)
+        check(self.lib.hcu_swa_prefill(self._h, ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(out)))

@@ -8,7 +8,6 @@
 
 namespace hcu {
 
-constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxSplits = 64;      // key splits per (sequence, KV head, query block)
 constexpr int kMaxUnits = 1 << 16;  // ticket slots at the head of the workspace
 

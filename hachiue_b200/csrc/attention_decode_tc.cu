@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (int j = 0; j < ntiles + 2; ++j) {
       if (j >= 2) {
         const int jo = j - 2, xo = jo & 1;
-        if (!mbar_wait(&o_full[xo], (jo >> 1) & 1, a.status)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_full[xo], (jo >> 1) & 1, a.status))) {  // warp-uniform exit
           aborted = true;
           break;
         }
@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       if (j < ntiles) {
         const int x = j & 1;
-        if (!mbar_wait(&s_full[x], (j >> 1) & 1, a.status)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], (j >> 1) & 1, a.status))) {
           aborted = true;
           break;
         }

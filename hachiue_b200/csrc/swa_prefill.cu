@@ -1,0 +1,421 @@
+// swa_prefill.cu - causal sliding-window attention prefill on tcgen05 (plamo3).
+//
+// Semantics of attention_q8 / runAttentionQ8 over a whole prompt
+// (src/kernels.ts:1341-1426, src/wasm-backend.ts:826-895 with S = T,
+// posBase = 0): query i attends keys j with max(0, i - W + 1) <= j <= i
+// (W = windowSize; W = 0 is full causal), scale 1/sqrt(D), grouped head map
+// kvh = h / (H / KV).  bf16 Q / K / V (RoPE applied), f32 accumulation,
+// bf16 or f32 output.  The reference runs this 8 tokens at a time through the
+// decode kernel (PREFILL_CHUNK, src/engine.ts:29).
+//
+// B200 design (flash-attention on the 5th-gen tensor cores):
+//  * CTA = (sequence, KV head, 128-query tile, pair of query heads of that KV
+//    head).  Both heads use every K / V tile the TMA brings in.
+//  * Per 128-key tile and head: S = Q.K^T (tcgen05.mma, M=N=K=128, Q and K
+//    K-major from 128B-swizzled smem, S in TMEM); the softmax warpgroup of the
+//    head reads its S rows from TMEM (one thread per query row), writes
+//    P = exp2(S*scale - m) as bf16 back into the same TMEM columns, and
+//    O += P.V runs with A = P from TMEM and B = V (MN-major) from smem.
+//  * The two heads ping-pong: while one head's softmax runs, the tensor core
+//    works on the other head's MMAs.
+//  * O stays in TMEM across key tiles.  It is rescaled only when a row's
+//    running max grows by more than 8 (log2 units): until then P is computed
+//    against the stale max, P <= 2^8, which the final O / l cancels exactly.
+//  * Only key tiles that intersect the causal window band are visited; tiles
+//    entirely inside the band skip per-element masking.
+#include "common.cuh"
+#include "context.h"
+#include "tcgen05.cuh"
+
+namespace hcu {
+namespace {
+
+constexpr int SW_THREADS = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 / 6-9 softmax of head 0 / 1
+constexpr int BM = 128, BN = 128, HD = 128;
+constexpr int BOX = BM * 128;                 // [128 rows x 64 bf16] = 16 KB
+constexpr int TILE = 2 * BOX;                 // [128 x 128] bf16 tile
+constexpr int KV_STAGES = 2;
+constexpr int KV_STAGE = 2 * TILE;            // K tile + V tile
+constexpr float RESCALE_LOG2 = 8.f;
+
+struct SwaArgs {
+  int B, T, H, KV, W, G, nqt;
+  float scale_log2;  // log2(e) / sqrt(D)
+  void* out;
+  int out_bf16;
+  uint32_t* status;
+};
+
+// lo in the low 16 bits, hi in the high 16 bits (one cvt.rn.bf16x2.f32).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// 2^x on the SFU (ex2.approx.ftz.f32; 2^-inf = +0).  P is rounded to bf16
+// for the P.V product, far coarser than the instruction's error.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Row max of one 32-column chunk; `lo`..`hi` is the valid column range (all
+// columns when FULL).
+template <bool FULL>
+__device__ __forceinline__ void chunk_max(const uint32_t (&r)[32], int col0, int lo, int hi, float (&mx)[4]) {
+#pragma unroll
+  for (int i = 0; i < 32; i++) {
+    float v = __uint_as_float(r[i]);
+    if (!FULL) v = (col0 + i >= lo && col0 + i <= hi) ? v : -INFINITY;
+    mx[i & 3] = fmaxf(mx[i & 3], v);
+  }
+}
+
+// P for 64 columns (two 32-column chunks) packed as 32 bf16x2 words; adds to
+// the row sum.
+template <bool FULL>
+__device__ __forceinline__ void chunk_p(const uint32_t (&r0)[32], const uint32_t (&r1)[32], int col0, int lo, int hi,
+                                        float scale, float neg_m, float (&ls)[4], uint32_t (&pk)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; i++) {
+    const uint32_t x0 = i < 16 ? r0[2 * i] : r1[2 * i - 32];
+    const uint32_t x1 = i < 16 ? r0[2 * i + 1] : r1[2 * i - 31];
+    float v0 = fmaf(__uint_as_float(x0), scale, neg_m);
+    float v1 = fmaf(__uint_as_float(x1), scale, neg_m);
+    if (!FULL) {
+      const int c = col0 + 2 * i;
+      v0 = (c >= lo && c <= hi) ? v0 : -INFINITY;
+      v1 = (c + 1 >= lo && c + 1 <= hi) ? v1 : -INFINITY;
+    }
+    const float p0 = fast_exp2(v0), p1 = fast_exp2(v1);
+    ls[i & 3] += p0 + p1;
+    pk[i] = pack_bf16x2(p0, p1);
+  }
+}
+
+template <int NHD>
+__global__ void __launch_bounds__(SW_THREADS, 1)
+    swa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const SwaArgs a) {
+  constexpr uint32_t TMEM_COLS = NHD == 2 ? 512 : 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* qsm = smem;                      // [NHD][TILE]
+  uint8_t* kvsm = qsm + NHD * TILE;         // [KV_STAGES][K tile | V tile]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(kvsm + KV_STAGES * KV_STAGE);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 3;
+  uint64_t* s_full = bars + 5;   // [NHD]
+  uint64_t* p_full = bars + 7;   // [NHD]
+  uint64_t* o_done = bars + 9;   // [NHD]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = a.nqt - 1 - (int)blockIdx.x;  // longest tiles first
+  const int m0 = qt * BM;
+  const int hpairs = a.G / NHD;
+  const int g = blockIdx.y / hpairs;
+  const int h0 = g * a.G + (blockIdx.y % hpairs) * NHD;
+  const int b = blockIdx.z;
+  const int kfirst = a.W > 0 ? max(0, m0 - a.W + 1) : 0;
+  const int n_first = (kfirst / BN) * BN;
+  const int n_last = min(m0 + BM - 1, a.T - 1);
+  const int ntiles = (n_last - n_first) / BN + 1;
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < KV_STAGES; i++) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns per head: S (P aliased into its first 64 columns), then O.
+  auto s_col = [](int hd) { return (uint32_t)(hd * 256); };
+  auto o_col = [](int hd) { return (uint32_t)(hd * 256 + 128); };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&tmQ);
+      prefetch_tensormap(&tmK);
+      prefetch_tensormap(&tmV);
+      mbar_arrive_expect_tx(q_full, NHD * TILE);
+      for (int hd = 0; hd < NHD; hd++) {
+        tma_load_4d(qsm + hd * TILE, &tmQ, q_full, 0, h0 + hd, m0, b);
+        tma_load_4d(qsm + hd * TILE + BOX, &tmQ, q_full, 64, h0 + hd, m0, b);
+      }
+      for (int j = 0; j < ntiles; j++) {
+        const int s = j % KV_STAGES;
+        if (j >= KV_STAGES && !mbar_wait(&kv_empty[s], ((j - KV_STAGES) / KV_STAGES) & 1, a.status)) break;
+        uint8_t* st = kvsm + s * KV_STAGE;
+        const int n0 = n_first + j * BN;
+        mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
+        tma_load_4d(st, &tmK, &kv_full[s], 0, g, n0, b);
+        tma_load_4d(st + BOX, &tmK, &kv_full[s], 64, g, n0, b);
+        tma_load_4d(st + TILE, &tmV, &kv_full[s], 0, g, n0, b);
+        tma_load_4d(st + TILE + BOX, &tmV, &kv_full[s], 64, g, n0, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_f16(BM, BN, true, false, false);
+      constexpr uint32_t idesc_pv = idesc_f16(BM, HD, true, false, true);
+      const uint32_t q0 = smem_u32(qsm), kv0 = smem_u32(kvsm);
+      auto qk = [&](int hd, int s) {
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+          const uint64_t ad = smem_desc_sw128(q0 + hd * TILE + (ks >> 2) * BOX + (ks & 3) * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(kv0 + s * KV_STAGE + (ks >> 2) * BOX + (ks & 3) * 32, 16, 1024);
+          mma_f16_ss(tmem + s_col(hd), ad, bd, idesc_qk, ks > 0);
+        }
+        mma_commit(&s_full[hd]);
+      };
+      auto pv = [&](int hd, int s, bool acc) {
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+          const uint64_t bd = smem_desc_sw128(kv0 + s * KV_STAGE + TILE + ks * 2048, BOX, 1024);  // MN-major V
+          mma_f16_ts(tmem + o_col(hd), tmem + s_col(hd) + ks * 8, bd, idesc_pv, (acc || ks > 0) ? 1u : 0u);
+        }
+        mma_commit(&o_done[hd]);
+      };
+      bool ok = mbar_wait(q_full, 0, a.status) && mbar_wait(&kv_full[0], 0, a.status);
+      if (ok) {
+        tc_fence_after();
+        for (int hd = 0; hd < NHD; hd++) qk(hd, 0);
+      }
+      for (int j = 0; ok && j < ntiles; j++) {
+        const int s = j % KV_STAGES;
+        for (int hd = 0; hd < NHD && ok; hd++) {
+          if (!mbar_wait(&p_full[hd], j & 1, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          pv(hd, s, j > 0);
+          if (hd == NHD - 1) mma_commit(&kv_empty[s]);
+          if (j + 1 < ntiles) {
+            const int s1 = (j + 1) % KV_STAGES;
+            if (hd == 0 && !mbar_wait(&kv_full[s1], ((j + 1) / KV_STAGES) & 1, a.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            qk(hd, s1);  // overwrites S / P of this head: ordered after the P.V above
+          }
+        }
+      }
+    }
+  } else if (warp < 2 + 4 * NHD) {
+    // ---------------- softmax of head hd, one thread per query row ----------------
+    const int hd = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int query = m0 + row;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t sc = tmem + lane_off + s_col(hd), oc = tmem + lane_off + o_col(hd);
+    float m_use = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; j++) {
+      const int n0 = n_first + j * BN;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[hd], j & 1, a.status))) {  // warp-uniform exit
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // Pass 1: row max over the tile (masked), then to the log2 domain.
+      const bool full = (n0 + BN - 1 <= m0) && (a.W == 0 || n0 >= m0 + BM - a.W) && (n0 + BN <= a.T);
+      const int lo = (a.W > 0 ? query - a.W + 1 : 0) - n0;  // valid column range of this row
+      const int hi = min(query, a.T - 1) - n0;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 4; c += 2) {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(sc + 32 * c, r0);
+        tmem_ld32(sc + 32 * c + 32, r1);
+        tmem_ld_wait();
+        if (full) {
+          chunk_max<true>(r0, 32 * c, lo, hi, mx4);
+          chunk_max<true>(r1, 32 * c + 32, lo, hi, mx4);
+        } else {
+          chunk_max<false>(r0, 32 * c, lo, hi, mx4);
+          chunk_max<false>(r1, 32 * c + 32, lo, hi, mx4);
+        }
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
+      // The running max grew by more than 2^8 (or this is the first finite
+      // max): move to the new max.  Rows that already accumulated O rescale
+      // it; tcgen05.ld / st are warp-collective, so the whole warp takes the
+      // TMEM round trip when any of its rows needs it (factor 1 elsewhere).
+      const bool move = mx > m_use + RESCALE_LOG2 || (j == 0 && mx > m_use);
+      const bool rescale_o = move && j > 0 && m_use != -INFINITY;
+      const float f = rescale_o ? exp2f(m_use - mx) : 1.f;
+      if (__any_sync(0xffffffffu, rescale_o)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[hd], (j - 1) & 1, a.status))) {  // P.V of tile j-1 landed
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          uint32_t r[32];
+          tmem_ld32(oc + 32 * c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+          tmem_st32(oc + 32 * c, r);
+        }
+        tmem_st_wait();
+      }
+      if (move) {
+        l *= f;
+        m_use = mx;
+      }
+      // Pass 2: P = exp2(S*scale - m) as bf16, written over the S columns
+      // already read (keys 64c..64c+63 land in columns 32c..32c+31).
+      const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        uint32_t r0[32], r1[32], pk[32];
+        tmem_ld32(sc + 64 * c, r0);
+        tmem_ld32(sc + 64 * c + 32, r1);
+        tmem_ld_wait();
+        if (full)
+          chunk_p<true>(r0, r1, 64 * c, lo, hi, a.scale_log2, neg_m, ls, pk);
+        else
+          chunk_p<false>(r0, r1, 64 * c, lo, hi, a.scale_log2, neg_m, ls, pk);
+        tmem_st32(sc + 32 * c, pk);
+      }
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[hd]);
+    }
+    // ---------------- epilogue: O / l (TMEM loads warp-wide, stores per row) ----------------
+    if (ok && !__all_sync(0xffffffffu, mbar_wait(&o_done[hd], (ntiles - 1) & 1, a.status))) ok = false;
+    tc_fence_after();
+    const bool store = query < a.T;
+    const float inv = 1.f / l;
+    const size_t obase = (((size_t)b * a.T + min(query, a.T - 1)) * a.H + (h0 + hd)) * HD;
+#pragma unroll
+    for (int c = 0; c < 4 && ok; c++) {  // ok is warp-uniform
+      uint32_t r[32];
+      tmem_ld32(oc + 32 * c, r);
+      tmem_ld_wait();
+      if (store) {
+        if (a.out_bf16) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + obase + 32 * c);
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
+            dst[i] = w;
+          }
+        } else {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + obase + 32 * c);
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+            dst[i] = make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
+                                 __uint_as_float(r[4 * i + 2]) * inv, __uint_as_float(r[4 * i + 3]) * inv);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+template <int NHD>
+int launch_swa(hcu_context* h, const SwaArgs& args, dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk,
+               const CUtensorMap& tv) {
+  constexpr size_t smem = 1024 + NHD * TILE + KV_STAGES * KV_STAGE + 12 * 8 + 16;
+  auto kern = swa_prefill_kernel<NHD>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                       "hcu_swa_prefill: smem attribute"));
+    attr_done = true;
+  }
+  kern<<<grid, SW_THREADS, smem, h->stream>>>(tq, tk, tv, args);
+  return after_launch("hcu_swa_prefill: launch");
+}
+
+}  // namespace
+}  // namespace hcu
+
+using hcu::fail;
+
+extern "C" int hcu_swa_prefill(hcu_handle h, const hcu_swa_params* p, const void* q, const void* k, const void* v,
+                               void* out) {
+  HCU_TRY(hcu::begin_op(h, "hcu_swa_prefill"));
+  if (!p || !q || !k || !v || !out) return fail(HCU_EINVAL, "hcu_swa_prefill: null argument");
+  const int B = (int)p->B, T = (int)p->T, H = (int)p->H, KV = (int)p->KV, D = (int)p->D;
+  if (B < 1 || T < 1 || H < 1 || KV < 1) return fail(HCU_EINVAL, "hcu_swa_prefill: B, T, H, KV must be positive");
+  if (D != 128) return fail(HCU_EUNSUPPORTED, "hcu_swa_prefill: D=%d (built: 128)", D);
+  if (H % KV) return fail(HCU_EINVAL, "hcu_swa_prefill: H (%d) is not a multiple of KV (%d)", H, KV);
+  if (p->out_dtype != HCU_DT_BF16 && p->out_dtype != HCU_DT_F32)
+    return fail(HCU_EINVAL, "hcu_swa_prefill: out_dtype must be HCU_DT_BF16 or HCU_DT_F32");
+  if (B > 65535) return fail(HCU_EINVAL, "hcu_swa_prefill: B > 65535");
+  if (reinterpret_cast<uintptr_t>(out) % 16) return fail(HCU_EINVAL, "hcu_swa_prefill: out must be 16-byte aligned");
+  const int G = H / KV;
+  const int nhd = (G % 2 == 0) ? 2 : 1;
+  const int nqt = (T + hcu::BM - 1) / hcu::BM;
+  CUtensorMap tq, tk, tv;
+  {
+    uint64_t dims[4] = {128, (uint64_t)H, (uint64_t)T, (uint64_t)B};
+    uint64_t strides[3] = {256, (uint64_t)H * 256, (uint64_t)T * H * 256};
+    uint32_t box[4] = {64, 1, 128, 1};
+    HCU_TRY(hcu::make_tensor_map(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(q), dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  {
+    uint64_t dims[4] = {128, (uint64_t)KV, (uint64_t)T, (uint64_t)B};
+    uint64_t strides[3] = {256, (uint64_t)KV * 256, (uint64_t)T * KV * 256};
+    uint32_t box[4] = {64, 1, 128, 1};
+    HCU_TRY(hcu::make_tensor_map(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(k), dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B));
+    HCU_TRY(hcu::make_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(v), dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  hcu::SwaArgs args{};
+  args.B = B;
+  args.T = T;
+  args.H = H;
+  args.KV = KV;
+  args.W = (int)p->window;
+  args.G = G;
+  args.nqt = nqt;
+  args.scale_log2 = hcu::kLog2e / sqrtf((float)D);
+  args.out = out;
+  args.out_bf16 = p->out_dtype == HCU_DT_BF16;
+  args.status = h->dev_status;
+  dim3 grid((unsigned)nqt, (unsigned)(KV * (G / nhd)), (unsigned)B);
+  if (nhd == 2) return hcu::launch_swa<2>(h, args, grid, tq, tk, tv);
+  return hcu::launch_swa<1>(h, args, grid, tq, tk, tv);
+}

@@ -248,6 +248,22 @@ int hcu_deltanet_decode(hcu_handle h, const hcu_deltanet_params *p, const float 
                         const float *dt_bias, const float *state_in, float *core,
                         float *state_out);
 
+/* Causal sliding-window attention over whole prompts (plamo3 SWA layers):
+ * query i of each sequence attends keys max(0, i - window + 1) .. i
+ * (window = 0: full causal), scale 1/sqrt(D), kvh = h / (H / KV).  These are
+ * the semantics of attention_q8 / runAttentionQ8 with S = T, posBase = 0
+ * (src/kernels.ts:1341-1426, src/wasm-backend.ts:826-895); the reference
+ * feeds prompts through them 8 tokens at a time (src/engine.ts:29).
+ * q bf16 [B, T, H, D]; k, v bf16 [B, T, KV, D] (RoPE applied); out
+ * [B, T, H, D] bf16 or f32.  D = 128.  tcgen05 tensor cores, f32 accumulate. */
+typedef struct {
+  uint32_t B, T, H, KV, D, window;
+  uint32_t out_dtype; /* HCU_DT_BF16 or HCU_DT_F32 */
+} hcu_swa_params;
+
+int hcu_swa_prefill(hcu_handle h, const hcu_swa_params *p, const void *q, const void *k, const void *v,
+                    void *out);
+
 #ifdef __cplusplus
 }
 #endif
