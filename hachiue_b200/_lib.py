@@ -26,6 +26,7 @@ EXPORTS = (
     "hcu_stream_sync", "hcu_alloc", "hcu_free", "hcu_memset", "hcu_copy_to_device", "hcu_copy_to_host",
     "hcu_device_status", "hcu_inject_failure", "hcu_dispatch", "hcu_attention", "hcu_attention_noalloc", "hcu_kv_append", "hcu_kv_append_rows",
     "hcu_deltanet_gbeta", "hcu_deltanet_recur", "hcu_deltanet_decode", "hcu_swa_prefill",
+    "hcu_deltanet_chunked_prefill",
 )
 
 
@@ -59,6 +60,15 @@ class hcu_deltanet_params(ctypes.Structure):
 class hcu_swa_params(ctypes.Structure):
     _fields_ = [("B", ctypes.c_uint32), ("T", ctypes.c_uint32), ("H", ctypes.c_uint32), ("KV", ctypes.c_uint32),
                 ("D", ctypes.c_uint32), ("window", ctypes.c_uint32), ("out_dtype", ctypes.c_uint32)]
+
+
+class hcu_gdn_prefill_params(ctypes.Structure):
+    _fields_ = [("B", ctypes.c_uint32), ("T", ctypes.c_uint32), ("NK", ctypes.c_uint32), ("NV", ctypes.c_uint32),
+                ("D", ctypes.c_uint32), ("load_state", ctypes.c_uint32),
+                ("q_row_stride", ctypes.c_uint64), ("k_row_stride", ctypes.c_uint64),
+                ("v_row_stride", ctypes.c_uint64), ("q_seq_stride", ctypes.c_uint64),
+                ("k_seq_stride", ctypes.c_uint64), ("v_seq_stride", ctypes.c_uint64),
+                ("gb_row_stride", ctypes.c_uint64), ("gb_seq_stride", ctypes.c_uint64)]
 
 
 _lock = threading.Lock()
@@ -103,6 +113,8 @@ def load(path: str | None = None):
             "hcu_deltanet_recur": ([vp, ctypes.POINTER(hcu_deltanet_params), vp, vp, vp, vp, vp], i32),
             "hcu_deltanet_decode": ([vp, ctypes.POINTER(hcu_deltanet_params), vp, vp, vp, vp, vp, vp, vp, vp], i32),
             "hcu_swa_prefill": ([vp, ctypes.POINTER(hcu_swa_params), vp, vp, vp, vp], i32),
+            "hcu_deltanet_chunked_prefill": ([vp, ctypes.POINTER(hcu_gdn_prefill_params), vp, vp, vp, vp, vp, vp,
+                                              vp, vp], i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

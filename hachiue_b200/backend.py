@@ -22,7 +22,7 @@ import torch
 
 from . import _lib
 from ._lib import (DT_BF16, DT_F32, KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueError, check, hcu_attention_params,
-                   hcu_deltanet_params, hcu_kv_cache, hcu_swa_params)
+                   hcu_deltanet_params, hcu_gdn_prefill_params, hcu_kv_cache, hcu_swa_params)
 
 # The reference's op names on this path (src/kernels.ts SHADERS keys).
 SHADERS = ("kv_append_q8", "attention_q8", "deltanet_gbeta", "deltanet_recur")
@@ -223,3 +223,32 @@ class CudaBackend:
         p = hcu_swa_params(B, T, H, k.shape[2], D, window,
                            DT_BF16 if out.dtype == torch.bfloat16 else DT_F32)
         check(self.lib.hcu_swa_prefill(self._h, ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(out)))
+
+    def deltanet_chunked_prefill(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
+                                 beta: torch.Tensor, core: torch.Tensor, state_out: torch.Tensor,
+                                 state_in: torch.Tensor | None = None) -> None:
+        """Gated DeltaNet over whole prompts, 64-token chunks on the tensor cores.
+
+        q, k bf16 [B, T, NK, D]; v bf16 [B, T, NV, D] (token-major views with
+        unit stride inside a head are accepted); g, beta f32 [B, T, NV];
+        core f32 [B, T, NV, D]; states f32 [B, NV, D, D] ([dk][dv]).
+        ``state_in`` None starts from a zero state."""
+        self._bind_stream()
+        B, T, NK, D = q.shape
+        NV = v.shape[2]
+        for t in (q, k, v):
+            if t.dtype != torch.bfloat16 or t.stride(3) != 1 or t.stride(2) != D:
+                raise HachiueError(_lib.HCU_EINVAL, "hachiue: q / k / v must be bf16 with contiguous heads")
+        for t in (g, beta):
+            if t.dtype != torch.float32 or t.stride(2) != 1:
+                raise HachiueError(_lib.HCU_EINVAL, "hachiue: g / beta must be f32 [B, T, NV]")
+        p = hcu_gdn_prefill_params()
+        p.B, p.T, p.NK, p.NV, p.D = B, T, NK, NV, D
+        p.load_state = int(state_in is not None)
+        p.q_row_stride, p.k_row_stride, p.v_row_stride = q.stride(1), k.stride(1), v.stride(1)
+        p.q_seq_stride, p.k_seq_stride, p.v_seq_stride = q.stride(0), k.stride(0), v.stride(0)
+        p.gb_row_stride, p.gb_seq_stride = g.stride(1), g.stride(0)
+        if beta.stride() != g.stride():
+            raise HachiueError(_lib.HCU_EINVAL, "hachiue: g and beta must share strides")
+        check(self.lib.hcu_deltanet_chunked_prefill(self._h, ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(g),
+                                                    _ptr(beta), _ptr(state_in), _ptr(core), _ptr(state_out)))

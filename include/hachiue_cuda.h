@@ -264,6 +264,30 @@ typedef struct {
 int hcu_swa_prefill(hcu_handle h, const hcu_swa_params *p, const void *q, const void *k, const void *v,
                     void *out);
 
+/* Chunked Gated DeltaNet prefill (qwen35 linear-attention layers over whole
+ * prompts): the recurrence of hcu_deltanet_recur / deltanet_recur
+ * (src/kernels.ts:1496-1573, src/wasm-backend.ts:1047-1102) evaluated 64
+ * tokens at a time in WY form on the tensor cores (bf16 operands, f32
+ * accumulation, f32 state carried between chunks).  The reference instead
+ * runs the token-serial scan 8 tokens per call (src/engine.ts:29, :1388).
+ * q, k: bf16 [B, T, NK, D] (token t of sequence b at element
+ * b*q_seq_stride + t*q_row_stride + hk*D); v: bf16 [B, T, NV, D]; V head h
+ * reads QK head h % NK.  g (log decay, <= 0) and beta: f32 at
+ * b*gb_seq_stride + t*gb_row_stride + h (the reference's gbeta buffer
+ * [2, S, NV] is g = gbeta, beta = gbeta + S*NV).  core: f32 [B, T, NV, D];
+ * state_in / state_out: f32 [B, NV, D, D] in [dk][dv] order (may alias).
+ * D = 128.  Strides of 0 select the dense defaults. */
+typedef struct {
+  uint32_t B, T, NK, NV, D, load_state;
+  uint64_t q_row_stride, k_row_stride, v_row_stride;   /* elements between tokens */
+  uint64_t q_seq_stride, k_seq_stride, v_seq_stride;   /* elements between sequences */
+  uint64_t gb_row_stride, gb_seq_stride;
+} hcu_gdn_prefill_params;
+
+int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params *p, const void *q,
+                                 const void *k, const void *v, const float *g, const float *beta,
+                                 const float *state_in, float *core, float *state_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,116 @@
+"""GPU parity of the chunked (WY-form, tensor-core) Gated DeltaNet prefill
+against the oracle's token-serial f32 recurrence (src/wasm-backend.ts
+:1047-1102 semantics).  Tolerance (bf16 tensor-core path): relative L2 <= 1e-2
+and max-abs <= 2e-2 on outputs and final states."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from hachiue_b200 import workloads
+from tests.conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+REL, ABS = 1e-2, 2e-2
+dev = "cuda"
+
+
+def bf16_bits(x):
+    return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+
+def to_dev_bf16(bits):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).to(dev).view(torch.bfloat16)
+
+
+def oracle_head(qb, kb, vb, g, beta, b, h, NK, state0=None):
+    """Token-serial oracle for one (sequence, V head): builds the reference's
+    qkvConv rows for QK head h % NK and that V head."""
+    hk = h % NK
+    q = workloads.bf16_bits_to_f32(qb[b, :, hk])
+    k = workloads.bf16_bits_to_f32(kb[b, :, hk])
+    v = workloads.bf16_bits_to_f32(vb[b, :, h])
+    T, D = q.shape
+    qkv = np.concatenate([q, k, v], 1).astype(np.float32)
+    gb = np.stack([g[b, :, h:h + 1], beta[b, :, h:h + 1]]).astype(np.float32)
+    st = np.zeros((1, D, D), np.float32) if state0 is None else state0[b, h:h + 1].copy()
+    core, st1 = oracle.deltanet_recur(qkv, gb, st, 1, 1, state0 is not None)
+    return core[:, 0], st1[0]
+
+
+def make_inputs(rng, B, T, NK, NV, decay=1.0):
+    q = rng.standard_normal((B, T, NK, 128), dtype=np.float32)
+    k = rng.standard_normal((B, T, NK, 128), dtype=np.float32)
+    v = rng.standard_normal((B, T, NV, 128), dtype=np.float32)
+    a = rng.standard_normal((B, T, NV)).astype(np.float64)
+    g = (-decay * (np.maximum(a, 0) + np.log1p(np.exp(-np.abs(a))))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((B, T, NV))))).astype(np.float32)
+    return bf16_bits(q), bf16_bits(k), bf16_bits(v), g, beta
+
+
+def run(backend, qb, kb, vb, g, beta, state0=None):
+    B, T, NK, _ = qb.shape
+    NV = vb.shape[2]
+    core = torch.full((B, T, NV, 128), float("nan"), device=dev)
+    st = torch.zeros((B, NV, 128, 128), device=dev)
+    sin = None if state0 is None else torch.from_numpy(state0).to(dev)
+    backend.deltanet_chunked_prefill(to_dev_bf16(qb), to_dev_bf16(kb), to_dev_bf16(vb), torch.from_numpy(g).to(dev),
+                                     torch.from_numpy(beta).to(dev), core, st, sin)
+    torch.cuda.synchronize()
+    return core.cpu().numpy(), st.cpu().numpy()
+
+
+@pytest.mark.parametrize("B,T,NK,NV,decay,load", [(1, 64, 1, 2, 1.0, False), (2, 200, 2, 4, 1.0, True),
+                                                  (1, 1000, 1, 2, 1.0, False), (1, 640, 2, 2, 0.02, True),
+                                                  (1, 129, 1, 1, 0.0, False)])
+def test_small_shapes(backend, B, T, NK, NV, decay, load):
+    """One chunk, a partial last chunk, many chunks, weak decay (the state
+    carries across chunks) and no decay at all; zero or loaded initial state."""
+    rng = np.random.default_rng(B + T + NK + NV + int(100 * decay))
+    qb, kb, vb, g, beta = make_inputs(rng, B, T, NK, NV, decay)
+    st0 = (0.02 * rng.standard_normal((B, NV, 128, 128))).astype(np.float32) if load else None
+    core, st = run(backend, qb, kb, vb, g, beta, st0)
+    assert np.isfinite(core).all() and np.isfinite(st).all()
+    for b in range(B):
+        for h in range(NV):
+            rc, rs = oracle_head(qb, kb, vb, g, beta, b, h, NK, st0)
+            assert rel_l2(core[b, :, h], rc) < REL, (b, h, rel_l2(core[b, :, h], rc))
+            assert np.abs(core[b, :, h] - rc).max() < ABS
+            assert rel_l2(st[b, h], rs) < REL
+    assert backend.device_status() == 0
+
+
+def test_agrees_with_recurrent_kernel(backend):
+    """Same inputs through the token-serial CUDA kernel (hcu_deltanet_recur)."""
+    rng = np.random.default_rng(42)
+    B, T, NK, NV = 1, 300, 2, 4
+    qb, kb, vb, g, beta = make_inputs(rng, B, T, NK, NV)
+    core, st = run(backend, qb, kb, vb, g, beta)
+    f = workloads.bf16_bits_to_f32
+    qkv = np.concatenate([f(qb).reshape(B, T, -1), f(kb).reshape(B, T, -1), f(vb).reshape(B, T, -1)], 2)
+    gb = np.stack([g, beta], 1)  # [B, 2, T, NV]
+    core2 = torch.zeros((B, T, NV, 128), device=dev)
+    st2 = torch.zeros((B, NV, 128, 128), device=dev)
+    backend.deltanet_recur(torch.from_numpy(np.ascontiguousarray(qkv)).to(dev),
+                           torch.from_numpy(np.ascontiguousarray(gb)).to(dev), st2, core2, st2, NK, NV, False)
+    torch.cuda.synchronize()
+    assert rel_l2(core, core2.cpu().numpy()) < REL
+    assert rel_l2(st, st2.cpu().numpy()) < REL
+
+
+@pytest.fixture(scope="module")
+def cfg5():
+    return workloads.gdn_prefill_cfg5()
+
+
+def test_cfg5_qwen35_chunked_prefill(backend, cfg5):
+    """Full config 5 (8 x 8192, 16 QK / 32 V heads, zero initial state); the
+    oracle checks all outputs and final states of four (sequence, head) pairs."""
+    w = cfg5
+    core, st = run(backend, w["q"], w["k"], w["v"], w["g"], w["beta"])
+    assert np.isfinite(core).all() and np.isfinite(st).all()
+    for b, h in ((0, 0), (0, 17), (5, 3), (7, 31)):
+        rc, rs = oracle_head(w["q"], w["k"], w["v"], w["g"], w["beta"], b, h, 16)
+        assert rel_l2(core[b, :, h], rc) < REL, (b, h)
+        assert np.abs(core[b, :, h] - rc).max() < ABS
+        assert rel_l2(st[b, h], rs) < REL
