@@ -290,7 +290,53 @@ def setup_cfg3(torch, be, dev):
                 e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg3"), out=out, traffic_key="cfg3")
 
 
-SETUPS = {1: setup_cfg1, 2: setup_cfg2, 3: setup_cfg3, 4: setup_cfg4}
+def setup_cfg5(torch, be, dev):
+    from hachiue_b200 import workloads
+    w = workloads.gdn_prefill_cfg5()
+
+    def bf(x):
+        return torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).to(dev).view(torch.bfloat16)
+
+    q, k, v = bf(w["q"]), bf(w["k"]), bf(w["v"])
+    g = torch.from_numpy(w["g"]).to(dev)
+    beta = torch.from_numpy(w["beta"]).to(dev)
+    core = torch.empty((8, 8192, 32, 128), device=dev)
+    st = torch.empty((8, 32, 128, 128), device=dev)
+
+    def step(i):
+        be.deltanet_chunked_prefill(q, k, v, g, beta, core, st)
+
+    hosts = [torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).pin_memory() for x in (w["q"], w["k"], w["v"])]
+    gh, bh = torch.from_numpy(w["g"]).pin_memory(), torch.from_numpy(w["beta"]).pin_memory()
+    core_h = torch.empty(core.shape).pin_memory()
+    st_h = torch.empty(st.shape).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    gd, bd = torch.empty_like(g), torch.empty_like(beta)
+
+    def e2e_step(i):
+        for dst, src in ((qd, hosts[0]), (kd, hosts[1]), (vd, hosts[2])):
+            dst.view(torch.int16).copy_(src, non_blocking=True)
+        gd.copy_(gh, non_blocking=True)
+        bd.copy_(bh, non_blocking=True)
+        be.deltanet_chunked_prefill(qd, kd, vd, gd, bd, core, st)
+        core_h.copy_(core, non_blocking=True)
+        st_h.copy_(st, non_blocking=True)
+
+    h2d = sum(x.numel() * 2 for x in hosts) + 2 * gh.numel() * 4
+    d2h = core_h.numel() * 4 + st_h.numel() * 4
+    info = dict(workload="cfg5 Qwen3.5 Gated DeltaNet chunked prefill", sequences=8, tokens=8192, qk_heads=16,
+                v_heads=32, d=128, chunk=64, io_dtype="bf16 q/k/v, f32 g/beta, f32 out and final state",
+                l2="inputs 0.56 GB > L2")
+    # Algorithmic work: canonical chunked-WY FLOPs and the bytes that must cross HBM.
+    flops = 65536 * 32 * (10 * 64 * 128 + 6 * 128 * 128)
+    nbytes = 2 * (8 * 8192 * 16 * 128 * 2) + 8 * 8192 * 32 * 128 * 2 + 2 * 8 * 8192 * 32 * 4 \
+        + 8 * 8192 * 32 * 128 * 4 + 8 * 32 * 128 * 128 * 4
+    return dict(step=step, e2e_step=e2e_step, flops=flops, hbm_bytes=nbytes, tokens=8 * 8192, info=info, h2d=h2d,
+                d2h=d2h, kernels_per_step=1, e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg5"), out=core,
+                traffic_key="cfg5")
+
+
+SETUPS = {1: setup_cfg1, 2: setup_cfg2, 3: setup_cfg3, 4: setup_cfg4, 5: setup_cfg5}
 
 
 # ---------------------------------------------------------------------------
@@ -344,6 +390,22 @@ def cpu_sample(kind: str, w: dict, threads: int, budget_s: float = 12.0):
         dt = time.perf_counter() - t0
         flops = n * 4 * 128 * (qe - qs) * 16 * w["window"]
         return flops / dt / 1e12, n * (qe - qs) / dt, f"{n} x 64 queries x 16 heads of cfg3 sequence 0, 1 thread", 1
+    if kind == "cfg5":
+        from hachiue_b200 import workloads as wl
+        T = 2048
+        f = wl.bf16_bits_to_f32
+        qkv = np.concatenate([f(w["q"][0, :T, 0]), f(w["k"][0, :T, 0]), f(w["v"][0, :T, 0])], 1).astype(np.float32)
+        gb = np.stack([w["g"][0, :T, 0:1], w["beta"][0, :T, 0:1]]).astype(np.float32)
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            oracle.deltanet_recur(qkv, gb, np.zeros((1, 128, 128), np.float32), 1, 1, False)
+            n += 1
+            if time.perf_counter() - t0 > min(budget_s, 4.0):
+                break
+        dt = time.perf_counter() - t0
+        flops = n * T * (10 * 64 * 128 + 6 * 128 * 128)
+        return flops / dt / 1e12, n * T / dt, f"{n} x {T} tokens of one (sequence, head) of cfg5, 1 thread", 1
     raise ValueError(kind)
 
 
@@ -360,6 +422,8 @@ def run_reference(args, world, rank):
         w = workloads.decode_cfg1()
     elif args.config == 3:
         w = workloads.swa_cfg3()
+    elif args.config == 5:
+        w = workloads.gdn_prefill_cfg5()
     else:
         w = workloads.gdn_decode_cfg4()
     kind = f"cfg{args.config}"
@@ -393,15 +457,15 @@ def run_reference(args, world, rank):
 
 def metric_name(cfg: int) -> str:
     return {1: "decode attn HBM GB/s", 2: "decode attn HBM GB/s", 3: "SWA prefill TFLOP/s",
-            4: "GDN decode HBM GB/s"}[cfg]
+            4: "GDN decode HBM GB/s", 5: "GDN chunked prefill TFLOP/s"}[cfg]
 
 
 def metric_unit(cfg: int) -> str:
-    return "TFLOP/s" if cfg == 3 else "GB/s"
+    return "TFLOP/s" if cfg in (3, 5) else "GB/s"
 
 
 def dtype_name(cfg: int) -> str:
-    return {1: "f32", 2: "f16", 3: "bf16", 4: "f32"}[cfg]
+    return {1: "f32", 2: "f16", 3: "bf16", 4: "f32", 5: "bf16"}[cfg]
 
 
 # ---------------------------------------------------------------------------
@@ -520,6 +584,13 @@ def main(argv=None):
     if rank == 0:
         traffic = load_traffic(W["traffic_key"])
         peak = peaks["bf16_tflops"] if tensor else peaks["hbm_gbs"]
+        hbm_roof = None
+        if "hbm_bytes" in W:  # tensor work at I/O dtypes whose bytes take longer than its FLOPs
+            gbs = W["hbm_bytes"] / (kavg / 1e3) / 1e9
+            hbm_roof = {"bound": "hbm", "achieved": round(gbs, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": round(gbs / peaks["hbm_gbs"], 4), "algorithmic_bytes_per_launch": W["hbm_bytes"],
+                        "kernel_ms": round(kavg, 5), "traffic": load_traffic(W["traffic_key"]),
+                        "tensor_frac": round(achieved / peaks["bf16_tflops"], 4)}
         line = {
             "metric": metric_name(args.config), "value": round(value, 2), "unit": metric_unit(args.config),
             "n_gpus": world,
@@ -541,6 +612,8 @@ def main(argv=None):
             "clocks": clk,
             "cpu_baseline": cpu,
         }
+        if hbm_roof is not None:
+            line["roofline"] = hbm_roof
         print(json.dumps(line), flush=True)
     be.close()
     if world > 1:

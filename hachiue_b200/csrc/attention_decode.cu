@@ -12,7 +12,7 @@
 //    query heads of the KV head (and up to 16/G queries) are the CTA's R
 //    "rows", so every K/V byte crosses HBM once per call.
 //  * A producer warp streams [TT tokens x Dh] K and V tiles (16 KB each) with
-//    3-D TMA (cp.async.bulk.tensor, no multicast) into a 3-stage mbarrier
+//    3-D TMA tile loads (cp.async.bulk.tensor) into a 3-stage mbarrier
 //    ring; four consumer warps each own a quarter of every tile.
 //  * q.k: each lane owns Dh/32 dimensions; partial dots for 32 (token, row)
 //    pairs are summed across the warp with a transpose-reduce (31 shuffles

@@ -1,8 +1,8 @@
 // common.cuh - shared device helpers for libhachiue_cuda (sm_100a only).
 //
-// PTX wrappers for mbarriers, TMA (cp.async.bulk.tensor, never with
-// .multicast::cluster: these kernels also run in multi-GPU jobs) and bounded
-// waits.  Every wait here gives up after HCU_WAIT_NS nanoseconds of
+// PTX wrappers for mbarriers, TMA tile loads into this CTA's own shared
+// memory (no cluster-wide broadcast form is used: these kernels also run in
+// multi-GPU jobs) and bounded waits.  Every wait here gives up after HCU_WAIT_NS nanoseconds of
 // %globaltimer, records HCU_DEVERR_TIMEOUT in the handle's device status word
 // and lets the caller unwind, so a broken pipeline reports an error instead of
 // hanging the GPU.

@@ -19,8 +19,11 @@
 //
 // One CTA per (sequence, V head, 64-wide block of value columns): the state's
 // value columns evolve independently.  Warp 0 streams K / Q / V chunks with
-// TMA (double-buffered), warp 1 allocates TMEM and issues the MMAs, warps 4-7
-// (one TMEM lane each) do the element-wise work and the solve.
+// TMA (double-buffered), warp 1 allocates TMEM and issues the MMAs.  Two
+// 128-thread warpgroups (one TMEM lane per thread) split the element-wise
+// work so consecutive chunks overlap: warps 4-7 prepare the state-independent
+// part of chunk c+1 (norms, decays, A, (I+A)^-1, QKm) while warps 8-11 run
+// the state-dependent chain of chunk c (R, Delta, outputs, state update).
 #include "common.cuh"
 #include "context.h"
 #include "tcgen05.cuh"
@@ -31,28 +34,29 @@ namespace {
 constexpr int GC = 64;        // chunk length
 constexpr int GD = 128;       // DK = DV
 constexpr int DVB = 64;       // value columns per CTA
-constexpr int GT_THREADS = 256;
+constexpr int GT_THREADS = 384;
 // shared memory layout (bytes)
 constexpr int KQ_BYTES = 32768;  // per buffer: [d-block 0: K rows 0-63 | Q rows 0-63][d-block 1: same]
 constexpr int V_BYTES = 8192;    // per buffer: [64 tokens x 64 values] bf16
+constexpr int AS = 68;           // row stride (floats) of the f32 scratch matrices
 constexpr int OFF_KQ = 0;
 constexpr int OFF_V = OFF_KQ + 2 * KQ_BYTES;
 constexpr int OFF_S0B = OFF_V + 2 * V_BYTES;   // [128 dk x 64 dv] bf16, MN-major B operand
-constexpr int OFF_TB = OFF_S0B + 16384;        // [64 x 64] bf16 (I+A)^-1, K-major A operand
-constexpr int OFF_QKM = OFF_TB + 8192;         // [64 x 64] bf16, K-major A operand
-constexpr int OFF_RB = OFF_QKM + 8192;         // [64 tok x 64 dv] bf16, MN-major B operand
+constexpr int OFF_TB = OFF_S0B + 16384;        // [2][64 x 64] bf16 (I+A)^-1, K-major A operand
+constexpr int OFF_QKM = OFF_TB + 2 * 8192;     // [2][64 x 64] bf16, K-major A operand
+constexpr int OFF_RB = OFF_QKM + 2 * 8192;     // [64 tok x 64 dv] bf16, MN-major B operand
 constexpr int OFF_DB = OFF_RB + 8192;          // Delta
 constexpr int OFF_DSB = OFF_DB + 8192;         // diag(ik exp(g63 - g)) Delta
-constexpr int OFF_AF = OFF_DSB + 8192;         // [64][65] f32 A (and G)
-constexpr int OFF_TF = OFF_AF + 64 * 65 * 4;   // [64][65] f32 (I+A)^-1
-constexpr int OFF_X1 = OFF_TF + 64 * 65 * 4;   // [2][16][17] f32
-constexpr int OFF_X2 = OFF_X1 + 2 * 16 * 17 * 4;  // [32][33] f32
-constexpr int OFF_SC = OFF_X2 + 32 * 33 * 4;   // gam2[64] beta[64] ik[64] iq[64] misc[8]
-constexpr int OFF_BAR = OFF_SC + (4 * 64 + 8) * 4;
-constexpr int NBAR = 13;
+constexpr int OFF_AF = OFF_DSB + 8192;         // [64][AS] f32 A
+constexpr int OFF_TF = OFF_AF + 64 * AS * 4;   // [64][AS] f32 (I+A)^-1
+constexpr int OFF_X1 = OFF_TF + 64 * AS * 4;   // [2][16][20] f32
+constexpr int OFF_X2 = OFF_X1 + 2 * 16 * 20 * 4;  // [32][36] f32
+constexpr int OFF_SC = OFF_X2 + 32 * 36 * 4;   // [2][gam2, beta, ik, iq][64] + misc[16]
+constexpr int OFF_BAR = OFF_SC + (2 * 4 * 64 + 16) * 4;
+constexpr int NBAR = 16;
 constexpr int SMEM_BYTES = OFF_BAR + NBAR * 8 + 16;
-// TMEM columns
-constexpr uint32_t TC_F = 0, TC_X = 64, TC_D = 128, TC_O = 192, TC_S = 256, TMEM_COLS = 512;
+// TMEM columns: [K;Q][K;Q]^T (128), K S0, Q S0, Delta, QKm Delta, state (64 each)
+constexpr uint32_t TC_F = 0, TC_X = 128, TC_QS = 192, TC_DL = 256, TC_O2 = 320, TC_S = 384, TMEM_COLS = 512;
 
 struct GdnArgs {
   int B, T, NK, NV, load_state, nchunks;
@@ -128,45 +132,60 @@ __device__ __forceinline__ void tmem_st64(uint32_t taddr, const float (&x)[64]) 
   tmem_st_wait();
 }
 
+// Value of register-array element `idx` (runtime index) without local memory.
+__device__ __forceinline__ float pick64(const float (&x)[64], int idx) {
+  float v = 0.f;
+#pragma unroll
+  for (int j = 0; j < 64; j++) v = j == idx ? x[j] : v;
+  return v;
+}
+
 __global__ void __launch_bounds__(GT_THREADS, 1)
     gdn_chunked_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const GdnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-  uint64_t* kv_full = bars + 0;   // [2]
-  uint64_t* kv_empty = bars + 2;  // [2]
-  uint64_t* bar_f = bars + 4;     // MMA (f) done
-  uint64_t* bar_a = bars + 5;     // MMA (a) done
-  uint64_t* bar_c = bars + 6;     // MMA (c) done
-  uint64_t* bar_d = bars + 7;     // MMA (d) done
-  uint64_t* bar_e = bars + 8;     // MMA (e) done
-  uint64_t* bar_T = bars + 9;     // (I+A)^-1, QKm, Q' written
-  uint64_t* bar_R = bars + 10;    // R written
-  uint64_t* bar_D = bars + 11;    // Delta copies written, state rescaled
-  uint64_t* bar_s0 = bars + 12;   // S0 (bf16) written
+  uint64_t* kv_full = bars + 0;   // [2] TMA landed
+  uint64_t* kv_empty = bars + 2;  // [2] inputs of a chunk no longer read
+  uint64_t* bar_f = bars + 4;     // (f) [K;Q][K;Q]^T done
+  uint64_t* f_free = bars + 5;    // prep warps have read (f)
+  uint64_t* bar_T = bars + 6;     // [2] prep outputs (scalars, QKm, (I+A)^-1) of a chunk written
+  uint64_t* pfree = bars + 8;     // [2] chain warps done with those prep outputs
+  uint64_t* bar_a = bars + 10;    // (a) K S0, Q S0 done
+  uint64_t* bar_R = bars + 11;    // R written
+  uint64_t* bar_c = bars + 12;    // (c) Delta done
+  uint64_t* bar_D = bars + 13;    // Delta copies written, state rescaled
+  uint64_t* bar_d = bars + 14;    // (d) QKm Delta and (e) state update done
+  uint64_t* bar_s0 = bars + 15;   // bf16 state written (and initial state)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBAR);
   float* Af = reinterpret_cast<float*>(sm + OFF_AF);
   float* Tf = reinterpret_cast<float*>(sm + OFF_TF);
   float* X1 = reinterpret_cast<float*>(sm + OFF_X1);
   float* X2 = reinterpret_cast<float*>(sm + OFF_X2);
-  float* gam2 = reinterpret_cast<float*>(sm + OFF_SC);  // gamma * log2(e)
-  float* betv = gam2 + 64;
-  float* ikv = betv + 64;
-  float* iqv = ikv + 64;
-  float* misc = iqv + 64;
+  float* scal = reinterpret_cast<float*>(sm + OFF_SC);  // [2][4][64]
+  float* misc = scal + 2 * 4 * 64;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int dvb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h % a.NK;
+  const int n = a.nchunks;
 
   if (tid == 0) {
     for (int i = 0; i < 2; i++) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+      mbar_init(&bar_T[i], 4);
+      mbar_init(&pfree[i], 4);
     }
-    for (int i = 4; i <= 8; i++) mbar_init(&bars[i], 1);
-    for (int i = 9; i <= 12; i++) mbar_init(&bars[i], 4);
+    mbar_init(bar_f, 1);
+    mbar_init(f_free, 4);
+    mbar_init(bar_a, 1);
+    mbar_init(bar_R, 4);
+    mbar_init(bar_c, 1);
+    mbar_init(bar_D, 4);
+    mbar_init(bar_d, 1);
+    mbar_init(bar_s0, 4);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -184,7 +203,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       prefetch_tensormap(&tmQ);
       prefetch_tensormap(&tmK);
       prefetch_tensormap(&tmV);
-      for (int c = 0; c < a.nchunks; c++) {
+      for (int c = 0; c < n; c++) {
         const int buf = c & 1;
         if (c >= 2 && !mbar_wait(&kv_empty[buf], ((c - 2) >> 1) & 1, a.status)) break;
         uint8_t* kq = sm + OFF_KQ + buf * KQ_BYTES;
@@ -200,304 +219,300 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t id_f = idesc_f16(128, 64, true, false, false);  // [K;Q] K^T
-      constexpr uint32_t id_kb = idesc_f16(64, 64, true, false, true);   // 64-row A (K-major) x MN-major B
-      constexpr uint32_t id_e = idesc_f16(128, 64, true, true, true);    // K^T (MN-major) x MN-major B
+      constexpr uint32_t id_f = idesc_f16(128, 128, true, false, false);  // [K;Q] [K;Q]^T
+      constexpr uint32_t id_kb = idesc_f16(64, 64, true, false, true);    // 64-row A (K-major) x MN-major B
+      constexpr uint32_t id_e = idesc_f16(128, 64, true, true, true);     // K^T (MN-major) x MN-major B
       const uint32_t s0 = smem_u32(sm);
-      bool ok = true;
-      for (int c = 0; c < a.nchunks && ok; c++) {
-        const int buf = c & 1;
-        const uint32_t kq = s0 + OFF_KQ + buf * KQ_BYTES;
-        ok = mbar_wait(&kv_full[buf], (c >> 1) & 1, a.status);
-        if (!ok) break;
-        tc_fence_after();
-        // (f) D_f = [K; Q] . K^T   (M = 128, N = 64, K = 128)
+      auto issue_f = [&](int c) {
+        const uint32_t kq = s0 + OFF_KQ + (c & 1) * KQ_BYTES;
 #pragma unroll
         for (int ks = 0; ks < 8; ks++) {
-          const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-          mma_f16_ss(tmem + TC_F, smem_desc_sw128(kq + off, 16, 1024), smem_desc_sw128(kq + off, 16, 1024), id_f,
-                     ks > 0);
+          const uint64_t d = smem_desc_sw128(kq + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+          mma_f16_ss(tmem + TC_F, d, d, id_f, ks > 0);
         }
         mma_commit(bar_f);
-        // (a) X = K . S0   (M = 64, N = 64, K = 128)
+      };
+      bool ok = mbar_wait(&kv_full[0], 0, a.status);
+      if (ok) {
+        tc_fence_after();
+        issue_f(0);
+      }
+      for (int c = 0; c < n && ok; c++) {
+        const int buf = c & 1, x = c & 1;
+        const uint32_t kq = s0 + OFF_KQ + buf * KQ_BYTES;
+        // state-independent MMA of the next chunk, once the prep warps hold chunk c's
+        if (c + 1 < n) {
+          ok = mbar_wait(&kv_full[(c + 1) & 1], ((c + 1) >> 1) & 1, a.status) && mbar_wait(f_free, c & 1, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          issue_f(c + 1);
+        }
+        // (a) X = K S0 and QS = Q S0   (M = 64, N = 64, K = 128)
         ok = mbar_wait(bar_s0, c & 1, a.status);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ks++) {
           const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-          mma_f16_ss(tmem + TC_X, smem_desc_sw128(kq + off, 16, 1024),
-                     smem_desc_sw128(s0 + OFF_S0B + ks * 2048, 8192, 1024), id_kb, ks > 0);
+          const uint64_t bd = smem_desc_sw128(s0 + OFF_S0B + ks * 2048, 8192, 1024);
+          mma_f16_ss(tmem + TC_X, smem_desc_sw128(kq + off, 16, 1024), bd, id_kb, ks > 0);
+          mma_f16_ss(tmem + TC_QS, smem_desc_sw128(kq + off + 8192, 16, 1024), bd, id_kb, ks > 0);
         }
         mma_commit(bar_a);
-        // (c) Delta = (I+A)^-1 . R   (M = 64, N = 64, K = 64)
-        ok = mbar_wait(bar_T, c & 1, a.status) && mbar_wait(bar_R, c & 1, a.status);
+        // (c) Delta = (I+A)^-1 R   (M = 64, N = 64, K = 64)
+        ok = mbar_wait(bar_R, c & 1, a.status);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 4; ks++)
-          mma_f16_ss(tmem + TC_D, smem_desc_sw128(s0 + OFF_TB + ks * 32, 16, 1024),
+          mma_f16_ss(tmem + TC_DL, smem_desc_sw128(s0 + OFF_TB + x * 8192 + ks * 32, 16, 1024),
                      smem_desc_sw128(s0 + OFF_RB + ks * 2048, 8192, 1024), id_kb, ks > 0);
         mma_commit(bar_c);
-        // (d) O = Q' . S0 + QKm . Delta   (M = 64, N = 64, K = 128 + 64)
+        // (d) O2 = QKm Delta; (e) S += K^T Dsb   (S pre-scaled by the chain warps)
         ok = mbar_wait(bar_D, c & 1, a.status);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 8; ks++) {
-          const uint32_t off = (ks >> 2) * 16384 + 8192 + (ks & 3) * 32;
-          mma_f16_ss(tmem + TC_O, smem_desc_sw128(kq + off, 16, 1024),
-                     smem_desc_sw128(s0 + OFF_S0B + ks * 2048, 8192, 1024), id_kb, ks > 0);
-        }
-#pragma unroll
-        for (int ks = 0; ks < 4; ks++)
-          mma_f16_ss(tmem + TC_O, smem_desc_sw128(s0 + OFF_QKM + ks * 32, 16, 1024),
-                     smem_desc_sw128(s0 + OFF_DB + ks * 2048, 8192, 1024), id_kb, 1);
-        mma_commit(bar_d);
-        // (e) S += K^T . Dsb   (M = 128, N = 64, K = 64; S pre-scaled by the math warps)
-#pragma unroll
-        for (int ks = 0; ks < 4; ks++)
+        for (int ks = 0; ks < 4; ks++) {
+          mma_f16_ss(tmem + TC_O2, smem_desc_sw128(s0 + OFF_QKM + x * 8192 + ks * 32, 16, 1024),
+                     smem_desc_sw128(s0 + OFF_DB + ks * 2048, 8192, 1024), id_kb, ks > 0);
           mma_f16_ss(tmem + TC_S, smem_desc_sw128(kq + ks * 2048, 16384, 1024),
                      smem_desc_sw128(s0 + OFF_DSB + ks * 2048, 8192, 1024), id_e, 1);
-        mma_commit(bar_e);
+        }
+        mma_commit(bar_d);
         mma_commit(&kv_empty[buf]);
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- element-wise work and the solve (128 threads) ----------------
-    const int q4 = warp - 4;                 // TMEM lane quarter
-    const int t = q4 * 32 + lane;            // 0..127
-    const uint32_t lo = (uint32_t)(q4 * 32) << 16;
-    const int r64 = q4 * 16 + lane;          // row of an M = 64 accumulator (valid when lane < 16)
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------- prep warpgroup: state-independent part of each chunk ----------------
+    const int t = (warp - 4) * 32 + lane;
+    const uint32_t lo = (uint32_t)((warp - 4) * 32) << 16;
     const float inv_sqrt_d = rsqrtf((float)GD);
-    uint8_t* s0b = sm + OFF_S0B;
-    bool ok = true;
-
-    // initial state: TMEM (f32 master) and its bf16 copy
-    {
-      float x[64];
-      if (a.load_state) {
-        const float4* src = reinterpret_cast<const float4*>(
-            a.state_in + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * DVB);
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const float4 v = __ldg(src + i);
-          x[4 * i] = v.x;
-          x[4 * i + 1] = v.y;
-          x[4 * i + 2] = v.z;
-          x[4 * i + 3] = v.w;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; i++) x[i] = 0.f;
-      }
-      tmem_st64(tmem + lo + TC_S, x);
-      store_row64(s0b, t, x);
-      fence_proxy_async();
+    for (int c = 0; c < n; c++) {
+      const int x = c & 1;
+      float* gam2 = scal + x * 256;
+      float* betv = gam2 + 64;
+      float* ikv = gam2 + 128;
+      float* iqv = gam2 + 192;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_f, c & 1, a.status))) break;
+      tc_fence_after();
+      float f[64], dg[64];
+      tmem_ld64(tmem + lo + TC_F, f);         // G row t (t < 64) / P row t-64
+      tmem_ld64(tmem + lo + TC_F + 64, dg);   // K Q^T row / Q Q^T row
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_s0);
-    }
-
-    for (int c = 0; c < a.nchunks && ok; c++) {
-      const int buf = c & 1;
-      const int t0 = c * GC;
-      uint8_t* kq = sm + OFF_KQ + buf * KQ_BYTES;
-      const uint8_t* vt = sm + OFF_V + buf * V_BYTES;
-
-      // ---- (f) landed: G = K K^T (rows 0-63), P = Q K^T (rows 64-127) ----
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_f, c & 1, a.status))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float f[64];
-      tmem_ld64(tmem + lo + TC_F, f);
+      if (lane == 0) mbar_arrive(f_free);
+      const float nrm2 = t < 64 ? pick64(f, t) : pick64(dg, t - 64);  // |k_t|^2 or |q_t-64|^2
       float gi = 0.f, bi = 0.f;
+      const int t0 = c * GC;
+      if (t < 64 && t0 + t < a.T) {
+        const size_t idx = (size_t)b * a.gb_seq + (size_t)(t0 + t) * a.gb_row + h;
+        gi = __ldg(a.g + idx);
+        bi = __ldg(a.beta + idx);
+      }
+      if (c >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pfree[x], ((c - 2) >> 1) & 1, a.status))) break;
       if (t < 64) {
-#pragma unroll
-        for (int j = 0; j < 64; j++) Af[t * 65 + j] = f[j];
-        const int tok = t0 + t;
-        if (tok < a.T) {
-          const size_t gi_idx = (size_t)b * a.gb_seq + (size_t)tok * a.gb_row + h;
-          gi = __ldg(a.g + gi_idx);
-          bi = __ldg(a.beta + gi_idx);
-        }
-        // inclusive scan of g over the chunk (two warps)
         float sc = gi;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const float y = __shfl_up_sync(0xffffffffu, sc, o);
           if (lane >= o) sc += y;
         }
-        if (t == 31) misc[0] = sc;
+        if (t == 31) misc[x] = sc;
         gi = sc;
       }
-      named_bar(1, 128);
+      named_bar(2, 128);
       if (t < 64) {
-        const float gam = gi + (t >= 32 ? misc[0] : 0.f);
-        gam2[t] = gam * kLog2e;
+        gam2[t] = (gi + (t >= 32 ? misc[x] : 0.f)) * kLog2e;
         betv[t] = bi;
-        ikv[t] = rsqrtf(Af[t * 65 + t] + 1e-6f);
+        ikv[t] = rsqrtf(nrm2 + 1e-6f);
       } else {
-        // |q_i|^2 from the Q rows of the tile (both 64-element blocks)
-        const int i = t - 64;
-        float x0[64], x1[64];
-        load_row64(kq, 64 + i, x0);
-        load_row64(kq + 16384, 64 + i, x1);
-        float s2 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 64; j++) s2 = fmaf(x0[j], x0[j], fmaf(x1[j], x1[j], s2));
-        iqv[i] = rsqrtf(s2 + 1e-6f) * inv_sqrt_d;
+        iqv[t - 64] = rsqrtf(nrm2 + 1e-6f) * inv_sqrt_d;
       }
-      named_bar(1, 128);
+      named_bar(2, 128);
       if (t < 64) {
-        // A (strictly lower) in place of G
+        // A (strictly lower), f32
         const float gi2 = gam2[t], cb = betv[t] * ikv[t];
 #pragma unroll
-        for (int j = 0; j < 64; j++)
-          Af[t * 65 + j] = j < t ? cb * ikv[j] * fast_ex2(gi2 - gam2[j]) * f[j] : 0.f;
+        for (int j = 0; j < 64; j++) Af[t * AS + j] = j < t ? cb * ikv[j] * fast_ex2(gi2 - gam2[j]) * f[j] : 0.f;
       } else {
-        // QKm row (lower incl. diagonal) and Q' = diag(Gamma iq) Q
+        // QKm row (lower including the diagonal), bf16
         const int i = t - 64;
         const float gi2 = gam2[i], cq = iqv[i];
-        float x[64];
-#pragma unroll
-        for (int j = 0; j < 64; j++) x[j] = j <= i ? cq * ikv[j] * fast_ex2(gi2 - gam2[j]) * f[j] : 0.f;
-        store_row64(sm + OFF_QKM, i, x);
-        const float sq = fast_ex2(gi2) * cq;
         float y[64];
-        load_row64(kq, 64 + i, y);
 #pragma unroll
-        for (int j = 0; j < 64; j++) y[j] *= sq;
-        store_row64(kq, 64 + i, y);
-        load_row64(kq + 16384, 64 + i, y);
-#pragma unroll
-        for (int j = 0; j < 64; j++) y[j] *= sq;
-        store_row64(kq + 16384, 64 + i, y);
+        for (int j = 0; j < 64; j++) y[j] = j <= i ? cq * ikv[j] * fast_ex2(gi2 - gam2[j]) * f[j] : 0.f;
+        store_row64(sm + OFF_QKM + x * 8192, i, y);
       }
-      named_bar(1, 128);
-
-      // ---- (I + A)^-1: 16x16 diagonal blocks by forward substitution ----
+      named_bar(2, 128);
+      // (I + A)^-1: 16x16 diagonal blocks by forward substitution
       if (t < 64) {
-        const int blk = t >> 4, cc = t & 15, base = blk * 16;
+        const int base = (t >> 4) * 16, cc = t & 15;
         float tc[16];
 #pragma unroll
         for (int r = 0; r < 16; r++) {
           float s = 0.f;
 #pragma unroll
-          for (int j = 0; j < r; j++) s = fmaf(Af[(base + r) * 65 + base + j], tc[j], s);
+          for (int j = 0; j < r; j++) s = fmaf(Af[(base + r) * AS + base + j], tc[j], s);
           tc[r] = r == cc ? 1.f : -s;
         }
 #pragma unroll
-        for (int r = 0; r < 16; r++) Tf[(base + r) * 65 + base + cc] = tc[r];
+        for (int r = 0; r < 16; r++) Tf[(base + r) * AS + base + cc] = tc[r];
       } else {
-        // The block combines below read whole 32x32 blocks: zero the upper
-        // off-diagonal 16x16 blocks (0,1), (2,3) that nothing else writes.
-        const int u = t - 64;  // 0..63
-        for (int e = u; e < 2 * 256; e += 64) {
+        // zero the upper off-diagonal 16x16 blocks (0,1) and (2,3): the
+        // combines below read whole 32x32 blocks
+        for (int e = t - 64; e < 512; e += 64) {
           const int blk = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-          const int rb = blk * 32, cb = blk * 32 + 16;
-          Tf[(rb + r) * 65 + cb + cc] = 0.f;
+          Tf[(blk * 32 + r) * AS + blk * 32 + 16 + cc] = 0.f;
         }
       }
-      named_bar(1, 128);
-      // combine into 32x32 blocks: T[2p+1][2p] = -T[2p+1][2p+1] A[2p+1][2p] T[2p][2p]
+      named_bar(2, 128);
       {
+        // 32x32 blocks: T[2p+1][2p] = -T[2p+1][2p+1] A[2p+1][2p] T[2p][2p]
         const int p = t >> 6, rem = t & 63, r = rem >> 2, c4 = (rem & 3) * 4;
         const int rb = 16 * (2 * p + 1), cb = 16 * (2 * p);
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int k = 0; k < 16; k++) {
-          const float av = Af[(rb + r) * 65 + cb + k];
-#pragma unroll
-          for (int u = 0; u < 4; u++) acc[u] = fmaf(av, Tf[(cb + k) * 65 + cb + c4 + u], acc[u]);
+          const float av = Af[(rb + r) * AS + cb + k];
+          const float4 tv = *reinterpret_cast<const float4*>(&Tf[(cb + k) * AS + cb + c4]);
+          acc.x = fmaf(av, tv.x, acc.x);
+          acc.y = fmaf(av, tv.y, acc.y);
+          acc.z = fmaf(av, tv.z, acc.z);
+          acc.w = fmaf(av, tv.w, acc.w);
         }
-#pragma unroll
-        for (int u = 0; u < 4; u++) X1[(p * 16 + r) * 17 + c4 + u] = acc[u];
-        named_bar(1, 128);
-        float o4[4] = {0.f, 0.f, 0.f, 0.f};
+        *reinterpret_cast<float4*>(&X1[(p * 16 + r) * 20 + c4]) = acc;
+        named_bar(2, 128);
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int k = 0; k < 16; k++) {
-          const float tv = Tf[(rb + r) * 65 + rb + k];
-#pragma unroll
-          for (int u = 0; u < 4; u++) o4[u] = fmaf(tv, X1[(p * 16 + k) * 17 + c4 + u], o4[u]);
+          const float tv = Tf[(rb + r) * AS + rb + k];
+          const float4 xv = *reinterpret_cast<const float4*>(&X1[(p * 16 + k) * 20 + c4]);
+          o.x = fmaf(tv, xv.x, o.x);
+          o.y = fmaf(tv, xv.y, o.y);
+          o.z = fmaf(tv, xv.z, o.z);
+          o.w = fmaf(tv, xv.w, o.w);
         }
-#pragma unroll
-        for (int u = 0; u < 4; u++) Tf[(rb + r) * 65 + cb + c4 + u] = -o4[u];
+        *reinterpret_cast<float4*>(&Tf[(rb + r) * AS + cb + c4]) = make_float4(-o.x, -o.y, -o.z, -o.w);
       }
-      named_bar(1, 128);
-      // combine into 64x64: T[32:64][0:32] = -T[32:64][32:64] A[32:64][0:32] T[0:32][0:32]
+      named_bar(2, 128);
       {
+        // 64x64: T[32:64][0:32] = -T[32:64][32:64] A[32:64][0:32] T[0:32][0:32]
         const int r = t >> 2, c8 = (t & 3) * 8;
         float acc[8];
 #pragma unroll
         for (int u = 0; u < 8; u++) acc[u] = 0.f;
-#pragma unroll 4
+#pragma unroll 8
         for (int k = 0; k < 32; k++) {
-          const float av = Af[(32 + r) * 65 + k];
-#pragma unroll
-          for (int u = 0; u < 8; u++) acc[u] = fmaf(av, Tf[k * 65 + c8 + u], acc[u]);
+          const float av = Af[(32 + r) * AS + k];
+          const float4 t0v = *reinterpret_cast<const float4*>(&Tf[k * AS + c8]);
+          const float4 t1v = *reinterpret_cast<const float4*>(&Tf[k * AS + c8 + 4]);
+          acc[0] = fmaf(av, t0v.x, acc[0]);
+          acc[1] = fmaf(av, t0v.y, acc[1]);
+          acc[2] = fmaf(av, t0v.z, acc[2]);
+          acc[3] = fmaf(av, t0v.w, acc[3]);
+          acc[4] = fmaf(av, t1v.x, acc[4]);
+          acc[5] = fmaf(av, t1v.y, acc[5]);
+          acc[6] = fmaf(av, t1v.z, acc[6]);
+          acc[7] = fmaf(av, t1v.w, acc[7]);
         }
-#pragma unroll
-        for (int u = 0; u < 8; u++) X2[r * 33 + c8 + u] = acc[u];
-        named_bar(1, 128);
+        *reinterpret_cast<float4*>(&X2[r * 36 + c8]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(&X2[r * 36 + c8 + 4]) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        named_bar(2, 128);
 #pragma unroll
         for (int u = 0; u < 8; u++) acc[u] = 0.f;
-#pragma unroll 4
+#pragma unroll 8
         for (int k = 0; k < 32; k++) {
-          const float tv = Tf[(32 + r) * 65 + 32 + k];
-#pragma unroll
-          for (int u = 0; u < 8; u++) acc[u] = fmaf(tv, X2[k * 33 + c8 + u], acc[u]);
+          const float tv = Tf[(32 + r) * AS + 32 + k];
+          const float4 x0 = *reinterpret_cast<const float4*>(&X2[k * 36 + c8]);
+          const float4 x1 = *reinterpret_cast<const float4*>(&X2[k * 36 + c8 + 4]);
+          acc[0] = fmaf(tv, x0.x, acc[0]);
+          acc[1] = fmaf(tv, x0.y, acc[1]);
+          acc[2] = fmaf(tv, x0.z, acc[2]);
+          acc[3] = fmaf(tv, x0.w, acc[3]);
+          acc[4] = fmaf(tv, x1.x, acc[4]);
+          acc[5] = fmaf(tv, x1.y, acc[5]);
+          acc[6] = fmaf(tv, x1.z, acc[6]);
+          acc[7] = fmaf(tv, x1.w, acc[7]);
         }
-#pragma unroll
-        for (int u = 0; u < 8; u++) Tf[(32 + r) * 65 + c8 + u] = -acc[u];
+        *reinterpret_cast<float4*>(&Tf[(32 + r) * AS + c8]) = make_float4(-acc[0], -acc[1], -acc[2], -acc[3]);
+        *reinterpret_cast<float4*>(&Tf[(32 + r) * AS + c8 + 4]) = make_float4(-acc[4], -acc[5], -acc[6], -acc[7]);
       }
-      named_bar(1, 128);
+      named_bar(2, 128);
       if (t < 64) {
-        float x[64];
+        float y[64];
 #pragma unroll
-        for (int j = 0; j < 64; j++) x[j] = j < t ? Tf[t * 65 + j] : (j == t ? 1.f : 0.f);
-        store_row64(sm + OFF_TB, t, x);
+        for (int j = 0; j < 64; j++) y[j] = j < t ? Tf[t * AS + j] : (j == t ? 1.f : 0.f);
+        store_row64(sm + OFF_TB + x * 8192, t, y);
       }
       fence_proxy_async();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_T);
-
-      // ---- (a) landed: R = diag(beta) (V - diag(Gamma ik) X) ----
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_a, c & 1, a.status))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      {
-        float xr[64];
-        tmem_ld64(tmem + lo + TC_X, xr);
-        if (lane < 16) {
-          const int i = r64;
-          float v[64];
-          load_row64(vt, i, v);
-          const float bi2 = betv[i], ci = fast_ex2(gam2[i]) * ikv[i];
+      if (lane == 0) mbar_arrive(&bar_T[x]);
+    }
+  } else if (warp >= 8) {
+    // ---------------- chain warpgroup: state-dependent part of each chunk ----------------
+    const int q4 = warp - 8;
+    const int t = q4 * 32 + lane;            // state row (dk) for M = 128 accumulators
+    const uint32_t lo = (uint32_t)(q4 * 32) << 16;
+    const int r64 = q4 * 16 + lane;          // row of an M = 64 accumulator (valid when lane < 16)
+    uint8_t* s0b = sm + OFF_S0B;
+    {
+      float st[64];
+      if (a.load_state) {
+        const float4* src = reinterpret_cast<const float4*>(
+            a.state_in + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * DVB);
 #pragma unroll
-          for (int j = 0; j < 64; j++) v[j] = bi2 * fmaf(-ci, xr[j], v[j]);
-          store_row64(sm + OFF_RB, i, v);
+        for (int i = 0; i < 16; i++) {
+          const float4 v = __ldg(src + i);
+          st[4 * i] = v.x;
+          st[4 * i + 1] = v.y;
+          st[4 * i + 2] = v.z;
+          st[4 * i + 3] = v.w;
         }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; i++) st[i] = 0.f;
+      }
+      tmem_st64(tmem + lo + TC_S, st);
+      store_row64(s0b, t, st);
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_s0);
+    }
+    for (int c = 0; c < n; c++) {
+      const int x = c & 1;
+      const float* gam2 = scal + x * 256;
+      const float* betv = gam2 + 64;
+      const float* ikv = gam2 + 128;
+      const float* iqv = gam2 + 192;
+      const uint8_t* vt = sm + OFF_V + (c & 1) * V_BYTES;
+      // R = diag(beta) (V - diag(Gamma ik) K S0)
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_a, c & 1, a.status))) break;
+      tc_fence_after();
+      float xr[64];
+      tmem_ld64(tmem + lo + TC_X, xr);
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_T[x], (c >> 1) & 1, a.status))) break;
+      if (lane < 16) {
+        const int i = r64;
+        float v[64];
+        load_row64(vt, i, v);
+        const float bi = betv[i], ci = fast_ex2(gam2[i]) * ikv[i];
+#pragma unroll
+        for (int j = 0; j < 64; j++) v[j] = bi * fmaf(-ci, xr[j], v[j]);
+        store_row64(sm + OFF_RB, i, v);
       }
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_R);
-
-      // ---- (c) landed: Delta copies for (d) and (e); state *= exp(gamma_63) ----
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_c, c & 1, a.status))) {
-        ok = false;
-        break;
-      }
+      // Delta for (d) and (e); state *= exp(gamma_63)
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_c, c & 1, a.status))) break;
       tc_fence_after();
+      const float g63 = gam2[63];
       {
         float dl[64];
-        tmem_ld64(tmem + lo + TC_D, dl);
-        const float g63 = gam2[63];
+        tmem_ld64(tmem + lo + TC_DL, dl);
         if (lane < 16) {
           const int i = r64;
           store_row64(sm + OFF_DB, i, dl);
@@ -517,34 +532,26 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_D);
-
-      // ---- (d) landed: outputs ----
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_d, c & 1, a.status))) {
-        ok = false;
-        break;
-      }
+      // outputs O = diag(Gamma iq) Q S0 + QKm Delta, and the next bf16 state
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_d, c & 1, a.status))) break;
       tc_fence_after();
       {
-        float o[64];
-        tmem_ld64(tmem + lo + TC_O, o);
-        const int tok = t0 + r64;
+        float qs[64], o2[64];
+        tmem_ld64(tmem + lo + TC_QS, qs);
+        tmem_ld64(tmem + lo + TC_O2, o2);
+        const int tok = c * GC + r64;
         if (lane < 16 && tok < a.T) {
+          const float cq = fast_ex2(gam2[r64]) * iqv[r64];
           float4* dst = reinterpret_cast<float4*>(a.core + (((size_t)b * a.T + tok) * a.NV + h) * GD + dvb * DVB);
 #pragma unroll
-          for (int i = 0; i < 16; i++) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          for (int i = 0; i < 16; i++)
+            dst[i] = make_float4(fmaf(cq, qs[4 * i], o2[4 * i]), fmaf(cq, qs[4 * i + 1], o2[4 * i + 1]),
+                                 fmaf(cq, qs[4 * i + 2], o2[4 * i + 2]), fmaf(cq, qs[4 * i + 3], o2[4 * i + 3]));
         }
-      }
-      // ---- (e) landed: new state -> bf16 copy for the next chunk ----
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_e, c & 1, a.status))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      {
         float st[64];
         tmem_ld64(tmem + lo + TC_S, st);
         store_row64(s0b, t, st);
-        if (c == a.nchunks - 1) {
+        if (c == n - 1) {
           float4* dst = reinterpret_cast<float4*>(a.state_out + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * DVB);
 #pragma unroll
           for (int i = 0; i < 16; i++) dst[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
@@ -553,7 +560,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_s0);
+      if (lane == 0) {
+        mbar_arrive(bar_s0);
+        mbar_arrive(&pfree[x]);
+      }
     }
   }
   tc_fence_before();

@@ -1,0 +1,82 @@
+"""Multi-GPU partitioning of the attention hot path (one process per GPU).
+
+The path shards by (sequence, KV / QK head): every unit is independent, so a
+rank computes its units alone and the per-head outputs are joined with one
+all-gather (NCCL over NVLink on GPUs, gloo on CPU).  The reference has no
+multi-device path (one GPUDevice per engine, src/engine.ts:320).
+
+Two partitions are provided:
+  * by sequence (``seq_range``): rank r owns a contiguous range of sequences
+    with all their heads (the benchmark's weak-scaling layout);
+  * by KV head (``kv_head_range``): rank r owns a contiguous range of KV heads
+    of every sequence and the G = H / KV query heads that read them, so each
+    rank stores only its heads' cache.  GDN layers shard by QK head the same
+    way: V heads h and h + NK read QK head h (tiled map), so a rank owning QK
+    heads [a, b) owns V heads {h : h % NK in [a, b)}.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def _split(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous near-equal split of range(n): rank's [lo, hi)."""
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def seq_range(batch: int, world: int, rank: int) -> tuple[int, int]:
+    return _split(batch, world, rank)
+
+
+def kv_head_range(kv_heads: int, world: int, rank: int) -> tuple[int, int]:
+    if kv_heads % world:
+        raise ValueError(f"hachiue: {kv_heads} KV heads do not split over {world} ranks")
+    return _split(kv_heads, world, rank)
+
+
+def v_heads_of_qk_range(nk: int, nv: int, lo: int, hi: int) -> list[int]:
+    """V heads served by QK heads [lo, hi) under the tiled map h % NK."""
+    return [h for h in range(nv) if lo <= h % nk < hi]
+
+
+def gather_seq_shards(local: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather equal sequence shards [b_local, ...] into [world*b_local, ...]."""
+    world = dist.get_world_size(group)
+    out = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+    return out
+
+
+def gather_head_shards(local: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather per-head outputs: local [B, S, H_local, D] (this rank's
+    contiguous head range) -> [B, S, world*H_local, D] on every rank.  The
+    collective moves [world][B, S, H_local, D] (each rank's block contiguous);
+    one local permute restores head order."""
+    world = dist.get_world_size(group)
+    B, S, hl, D = local.shape
+    buf = torch.empty((world, B, S, hl, D), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(buf.view(world * B, S, hl, D), local.contiguous(), group=group)
+    return buf.permute(1, 2, 0, 3, 4).reshape(B, S, world * hl, D)
+
+
+class HeadShardedDecode:
+    """Decode attention with this rank's KV heads: q [B, S, H, Dh] is sliced to
+    the rank's query heads, attention runs on the rank's cache (which holds
+    only its KV heads) and the outputs of all ranks are gathered by head."""
+
+    def __init__(self, backend, H: int, KV: int, group=None):
+        self.be = backend
+        self.group = group
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        self.kv_lo, self.kv_hi = kv_head_range(KV, world, rank)
+        G = H // KV
+        self.h_lo, self.h_hi = self.kv_lo * G, self.kv_hi * G
+
+    def __call__(self, q: torch.Tensor, cache, out_local: torch.Tensor, pos_base, **kw) -> torch.Tensor:
+        ql = q[:, :, self.h_lo:self.h_hi].contiguous()
+        self.be.attention(ql, cache, out_local, pos_base, **kw)
+        return gather_head_shards(out_local, self.group)

@@ -1,0 +1,92 @@
+"""Multi-rank partitioning on CPU: world_size-2 gloo process groups.
+
+Each rank computes its shard with the oracle (the GPU kernels are covered by
+the single-GPU parity tests) and the gathered result must equal the unsharded
+computation exactly: the collective and the re-ordering move bits only."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from hachiue_b200 import dist as hdist
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _attention_inputs(seed=0, B=4, S=2, H=8, KV=4, D=128, T=40):
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((B, S, H, D), dtype=np.float32)
+    k = rng.standard_normal((B * T, KV, D), dtype=np.float32)
+    v = rng.standard_normal((B * T, KV, D), dtype=np.float32)
+    pos = np.full(B, T - S, np.int32)
+    off = (np.arange(B) * T).astype(np.int64)
+    return q, k, v, pos, off
+
+
+def _worker(rank, world, port, mode, result_q):
+    import oracle
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q, k, v, pos, off = _attention_inputs()
+        B, S, H, D = q.shape
+        KV = k.shape[1]
+        if mode == "heads":
+            lo, hi = hdist.kv_head_range(KV, world, rank)
+            G = H // KV
+            ql = np.ascontiguousarray(q[:, :, lo * G:hi * G])
+            kl = np.ascontiguousarray(k[:, lo:hi])
+            vl = np.ascontiguousarray(v[:, lo:hi])
+            local = oracle.attention_batch(ql, kl, vl, pos, off, 0, oracle.KV_F32, threads=1)
+            full = hdist.gather_head_shards(torch.from_numpy(local))
+        else:
+            lo, hi = hdist.seq_range(B, world, rank)
+            local = oracle.attention_batch(np.ascontiguousarray(q[lo:hi]), k, v, pos[lo:hi], off[lo:hi], 0,
+                                           oracle.KV_F32, threads=1)
+            full = hdist.gather_seq_shards(torch.from_numpy(local))
+        if rank == 0:
+            result_q.put(full.numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["heads", "sequences"])
+def test_two_rank_shard_and_gather_matches_unsharded(mode):
+    import oracle
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, result_q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = result_q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    q, k, v, pos, off = _attention_inputs()
+    ref = oracle.attention_batch(q, k, v, pos, off, 0, oracle.KV_F32, threads=1)
+    np.testing.assert_array_equal(got, ref)
+
+
+def test_partitions_cover_everything():
+    for world in (1, 2, 4, 8):
+        seqs = [hdist.seq_range(64, world, r) for r in range(world)]
+        assert seqs[0][0] == 0 and seqs[-1][1] == 64
+        assert all(a[1] == b[0] for a, b in zip(seqs, seqs[1:]))
+        heads = [hdist.kv_head_range(8, world, r) for r in range(world)]
+        assert sum(hi - lo for lo, hi in heads) == 8
+    # GDN: V heads h and h + NK follow their QK head h % NK to the same rank
+    owned = [hdist.v_heads_of_qk_range(16, 32, lo, hi) for lo, hi in (hdist.kv_head_range(16, 4, r) for r in range(4))]
+    assert sorted(sum(owned, [])) == list(range(32))
+    assert all(((h + 16) in o) for o in owned for h in o if h < 16)
+    with pytest.raises(ValueError):
+        hdist.kv_head_range(8, 3, 0)
