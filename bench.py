@@ -332,7 +332,7 @@ def setup_cfg5(torch, be, dev):
     nbytes = 2 * (8 * 8192 * 16 * 128 * 2) + 8 * 8192 * 32 * 128 * 2 + 2 * 8 * 8192 * 32 * 4 \
         + 8 * 8192 * 32 * 128 * 4 + 8 * 32 * 128 * 128 * 4
     return dict(step=step, e2e_step=e2e_step, flops=flops, hbm_bytes=nbytes, tokens=8 * 8192, info=info, h2d=h2d,
-                d2h=d2h, kernels_per_step=1, e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg5"), out=core,
+                d2h=d2h, kernels_per_step=2, e2e_kernels_per_step=2, cpu=dict(w=w, kind="cfg5"), out=core,
                 traffic_key="cfg5")
 
 

@@ -45,6 +45,24 @@ int begin_op(hcu_context* h, const char* op) {
 
 int after_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
 
+int ensure_scratch(hcu_context* h, size_t bytes, const char* what) {
+  if (h->scratch_bytes >= bytes) return HCU_OK;
+  HCU_TRY(check_cuda(cudaStreamSynchronize(h->stream), what));
+  if (h->scratch) {
+    cudaFree(h->scratch);
+    h->scratch = nullptr;
+    h->scratch_bytes = 0;
+  }
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(HCU_ENOMEM, "%s: cannot allocate %zu bytes of scratch", what, bytes);
+  }
+  h->scratch = p;
+  h->scratch_bytes = bytes;
+  return HCU_OK;
+}
+
 int make_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
                     const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                     CUtensorMapSwizzle swizzle) {
@@ -129,6 +147,7 @@ int hcu_destroy(hcu_handle h) {
   cudaStreamSynchronize(h->stream);
   if (h->workspace) cudaFree(h->workspace);
   if (h->dev_status) cudaFree(h->dev_status);
+  if (h->scratch) cudaFree(h->scratch);
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
   delete h;
   return HCU_OK;

@@ -18,6 +18,8 @@ struct hcu_context {
   void* workspace = nullptr;  // split-K partials + counters (zeroed at create)
   size_t workspace_bytes = 0;
   uint32_t* dev_status = nullptr;  // device status word (HCU_DEVERR_*)
+  void* scratch = nullptr;         // large temporaries of the prefill ops, grown on demand
+  size_t scratch_bytes = 0;
   int inject_status = 0;
   int inject_count = 0;
 };
@@ -32,6 +34,9 @@ int check_cuda(cudaError_t e, const char* what);
 int begin_op(hcu_context* h, const char* op);
 // Launch-status check after a kernel launch.
 int after_launch(const char* what);
+// Makes h->scratch at least `bytes` long.  Growing synchronises the handle's
+// stream (queued work may still read the old buffer) and reallocates.
+int ensure_scratch(hcu_context* h, size_t bytes, const char* what);
 
 // Encodes a tiled TMA descriptor (row-major tensor, dims innermost first).
 int make_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,

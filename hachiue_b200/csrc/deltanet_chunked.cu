@@ -8,22 +8,31 @@
 // gamma the in-chunk cumulative sum of g, Gamma = exp(gamma), ik / iq the
 // norm factors (iq includes 1/sqrt(D)) and K, Q, V the raw chunk rows:
 //   A_ij  = beta_i ik_i ik_j exp(gamma_i - gamma_j) (k_i . k_j)    (j < i)
-//   R     = diag(beta) (V - diag(Gamma ik) K S0)
-//   Delta = (I + A)^-1 R                          (the per-token deltas)
-//   O     = diag(Gamma iq) Q S0 + QKm Delta,  QKm_ij = iq_i ik_j exp(gamma_i - gamma_j) (q_i . k_j)  (j <= i)
-//   S1    = exp(gamma_63) S0 + K^T diag(ik_j exp(gamma_63 - gamma_j)) Delta
-// The products run on the tensor cores (bf16 operands, f32 accumulation in
-// TMEM); the state S is kept in f32 in TMEM across chunks (its bf16 copy is
-// the MMA operand); (I + A)^-1 is solved in f32 on the CUDA cores by 16x16
-// diagonal blocks combined twice.
+//   T     = (I + A)^-1,   Tb = T diag(beta)
+//   QKm_ij = iq_i ik_j exp(gamma_i - gamma_j) (q_i . k_j)            (j <= i)
+//   c2 = Gamma ik,  c3 = Gamma iq,  c4 = ik exp(gamma_63 - gamma),  e = exp(gamma_63)
+//   R'    = V - diag(c2) K S0                     (then Delta = Tb R')
+//   O     = diag(c3) Q S0 + (QKm Tb) R'
+//   S1    = e S0 + K^T diag(c4) Tb R'
 //
-// One CTA per (sequence, V head, 64-wide block of value columns): the state's
-// value columns evolve independently.  Warp 0 streams K / Q / V chunks with
-// TMA (double-buffered), warp 1 allocates TMEM and issues the MMAs.  Two
-// 128-thread warpgroups (one TMEM lane per thread) split the element-wise
-// work so consecutive chunks overlap: warps 4-7 prepare the state-independent
-// part of chunk c+1 (norms, decays, A, (I+A)^-1, QKm) while warps 8-11 run
-// the state-dependent chain of chunk c (R, Delta, outputs, state update).
+// Two kernels per slab of chunks:
+//   gdn_prep_kernel  - everything that does not depend on the state, for all
+//     chunks of the slab in parallel: one CTA per (sequence, QK head, chunk)
+//     computes [K;Q][K;Q]^T on the tensor cores once and, per V head that
+//     reads this QK head (one 128-thread warpgroup each), the norms, decays,
+//     A, T (16x16 blocks by substitution on the CUDA cores, combined to 32x32
+//     there and to 64x64 on the tf32 tensor cores), QKm, and writes the
+//     chunk's operand  W = [Tb ; QKm Tb]  (128 x 64 bf16, the second half a
+//     tf32 tensor-core product) and the scalars c2, c3, c4, e to a scratch
+//     buffer.
+//   gdn_chain_kernel - the state recurrence: one CTA per (sequence, V head,
+//     64 value columns) walks the chunks in order with three MMAs per chunk,
+//     [X; QS] = [K; Q] S0,  [Tb R'; O2] = W R',  U = K^T Dsb  (Dsb = c4 Tb R'),
+//     keeping the f32 state in registers (one state row per thread) and its
+//     bf16 copy in shared memory as the next chunk's MMA operand.  Two CTAs
+//     fit per SM.
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "context.h"
 #include "tcgen05.cuh"
@@ -31,43 +40,69 @@
 namespace hcu {
 namespace {
 
-constexpr int GC = 64;        // chunk length
-constexpr int GD = 128;       // DK = DV
-constexpr int DVB = 64;       // value columns per CTA
-constexpr int GT_THREADS = 384;
-// shared memory layout (bytes)
-constexpr int KQ_BYTES = 32768;  // per buffer: [d-block 0: K rows 0-63 | Q rows 0-63][d-block 1: same]
-constexpr int V_BYTES = 8192;    // per buffer: [64 tokens x 64 values] bf16
-constexpr int AS = 68;           // row stride (floats) of the f32 scratch matrices
-constexpr int OFF_KQ = 0;
-constexpr int OFF_V = OFF_KQ + 2 * KQ_BYTES;
-constexpr int OFF_S0B = OFF_V + 2 * V_BYTES;   // [128 dk x 64 dv] bf16, MN-major B operand
-constexpr int OFF_TB = OFF_S0B + 16384;        // [2][64 x 64] bf16 (I+A)^-1, K-major A operand
-constexpr int OFF_QKM = OFF_TB + 2 * 8192;     // [2][64 x 64] bf16, K-major A operand
-constexpr int OFF_RB = OFF_QKM + 2 * 8192;     // [64 tok x 64 dv] bf16, MN-major B operand
-constexpr int OFF_DB = OFF_RB + 8192;          // Delta
-constexpr int OFF_DSB = OFF_DB + 8192;         // diag(ik exp(g63 - g)) Delta
-constexpr int OFF_AF = OFF_DSB + 8192;         // [64][AS] f32 A
-constexpr int OFF_TF = OFF_AF + 64 * AS * 4;   // [64][AS] f32 (I+A)^-1
-constexpr int OFF_X1 = OFF_TF + 64 * AS * 4;   // [2][16][20] f32
-constexpr int OFF_X2 = OFF_X1 + 2 * 16 * 20 * 4;  // [32][36] f32
-constexpr int OFF_SC = OFF_X2 + 32 * 36 * 4;   // [2][gam2, beta, ik, iq][64] + misc[16]
-constexpr int OFF_BAR = OFF_SC + (2 * 4 * 64 + 16) * 4;
-constexpr int NBAR = 16;
-constexpr int SMEM_BYTES = OFF_BAR + NBAR * 8 + 16;
-// TMEM columns: [K;Q][K;Q]^T (128), K S0, Q S0, Delta, QKm Delta, state (64 each)
-constexpr uint32_t TC_F = 0, TC_X = 128, TC_QS = 192, TC_DL = 256, TC_O2 = 320, TC_S = 384, TMEM_COLS = 512;
+constexpr int GC = 64;   // chunk length
+constexpr int GD = 128;  // DK = DV
+constexpr int DVB = 64;  // value columns per chain CTA
+// scratch per (sequence, V head, chunk) unit
+constexpr int W_ELEMS = 128 * 64;  // bf16 operand W = [Tb; QKm Tb]
+constexpr int SC_FLOATS = 4 * 64;  // c2, c3, c4, e (e repeated)
+constexpr size_t UNIT_BYTES = W_ELEMS * 2 + SC_FLOATS * 4;
 
-struct GdnArgs {
-  int B, T, NK, NV, load_state, nchunks;
+// ---------------- prep kernel layout ----------------
+// f32 64 x 64 matrices (A, T) are stored as two 64 x 32 column halves of
+// 128-byte swizzled rows (8 KB each), the tf32 K-major MMA operand layout.
+// TMEM: [K;Q][K;Q]^T in columns 0-127 (whose lanes 64-127 later hold
+// warpgroup w's QKm in columns 64w..64w+63, the A operand of QKm Tb), then per
+// warpgroup 64 columns for the 64x64 combine products and QKm Tb.
+constexpr int PREP_THREADS = 256;
+constexpr int P_OFF_KQ = 0;      // [d-block 0: K rows | Q rows][d-block 1: same], 32 KB; after (f):
+constexpr int P_OFF_U11 = 0;     //   [2 WG] U11 = (T[0:32][0:32])^T f32, 64-row K-major tile (8 KB each)
+constexpr int P_OFF_X2 = 16384;  //   [2 WG] X2^T f32 32 x 32, K-major B operand (4 KB each)
+constexpr int P_OFF_X1 = 24576;  //   [2 WG] X1 f32 [2][16][20] (2560 B each)
+constexpr int P_OFF_WG = 32768;  // [2 WG] A (16 KB), T (16 KB), scalars; A's bytes later stage W
+constexpr int P_WG_STRIDE = 34816;
+constexpr int P_OFF_BAR = P_OFF_WG + 2 * P_WG_STRIDE;
+constexpr int P_NBAR = 8;
+constexpr int P_SMEM = P_OFF_BAR + P_NBAR * 8 + 16;
+static_assert(32768 + (5 * 64 + 16) * 4 <= P_WG_STRIDE, "prep warpgroup region");
+static_assert(P_OFF_X1 + 2 * 2560 <= 32768, "prep X scratch");
+
+// ---------------- chain kernel layout ----------------
+constexpr int CHAIN_THREADS = 192;
+constexpr int C_OFF_KQ = 0;         // [d0: K | Q][d1: K | Q] bf16, A operand of [K;Q] S0
+constexpr int C_OFF_KE = 32768;     // [d0: K][d1: K] bf16, A operand (MN-major) of K^T Dsb
+constexpr int C_OFF_W = 49152;      // W, 128 rows K-major
+constexpr int C_OFF_S0B = 65536;    // [128 dk][64 dv] bf16 state, MN-major B operand
+constexpr int C_OFF_V = 81920;      // [64 tokens][64 values] bf16
+constexpr int C_OFF_RB = 90112;     // R', MN-major B operand
+constexpr int C_OFF_DSB = 98304;    // Dsb, MN-major B operand
+constexpr int C_OFF_SC = 106496;    // [2][4][64] f32
+constexpr int C_OFF_BAR = C_OFF_SC + 2 * SC_FLOATS * 4;
+constexpr int C_NBAR = 18;
+constexpr int C_SMEM = C_OFF_BAR + C_NBAR * 8 + 16;
+// TMEM columns of the chain kernel: P = [X; QS] and later U, Q = [Tb R'; O2]
+constexpr uint32_t TC_P = 0, TC_Q = 64, C_TMEM_COLS = 128;
+
+struct PrepArgs {
+  int T, NK, NV, c0, ns;
   const float* g;
   const float* beta;
   long long gb_row, gb_seq;
+  float* sc;  // [units][4][64]
+  uint32_t* status;
+};
+
+struct ChainArgs {
+  int T, NK, NV, c0, ns, cnt, load_state, v8;
   const float* state_in;
   float* core;
   float* state_out;
   uint32_t* status;
 };
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
 
 __device__ __forceinline__ float fast_ex2(float x) {
   float y;
@@ -80,31 +115,20 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// 8 consecutive f32 values as one 16-byte bf16 chunk.
+__device__ __forceinline__ uint4 pack8(const float* x) {
+  uint4 w;
+  w.x = pack2(x[0], x[1]);
+  w.y = pack2(x[2], x[3]);
+  w.z = pack2(x[4], x[5]);
+  w.w = pack2(x[6], x[7]);
+  return w;
+}
+
 // Writes 64 f32 values as one 128-byte bf16 row of a 128B-swizzled region.
 __device__ __forceinline__ void store_row64(uint8_t* region, int row, const float (&x)[64]) {
 #pragma unroll
-  for (int u = 0; u < 8; u++) {
-    uint4 w;
-    w.x = pack2(x[8 * u + 0], x[8 * u + 1]);
-    w.y = pack2(x[8 * u + 2], x[8 * u + 3]);
-    w.z = pack2(x[8 * u + 4], x[8 * u + 5]);
-    w.w = pack2(x[8 * u + 6], x[8 * u + 7]);
-    *reinterpret_cast<uint4*>(region + sw128_offset(row, 16 * u)) = w;
-  }
-}
-
-// Reads one 128-byte bf16 row (64 values) of a 128B-swizzled region.
-__device__ __forceinline__ void load_row64(const uint8_t* region, int row, float (&x)[64]) {
-#pragma unroll
-  for (int u = 0; u < 8; u++) {
-    const uint4 w = *reinterpret_cast<const uint4*>(region + sw128_offset(row, 16 * u));
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-      x[8 * u + 2 * e] = __uint_as_float(ws[e] << 16);
-      x[8 * u + 2 * e + 1] = __uint_as_float(ws[e] & 0xffff0000u);
-    }
-  }
+  for (int u = 0; u < 8; u++) *reinterpret_cast<uint4*>(region + sw128_offset(row, 16 * u)) = pack8(x + 8 * u);
 }
 
 // 64 TMEM columns of this thread's lane as f32.
@@ -120,76 +144,431 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&x)[64]) {
   }
 }
 
-__device__ __forceinline__ void tmem_st64(uint32_t taddr, const float (&x)[64]) {
-  uint32_t r0[32], r1[32];
-#pragma unroll
-  for (int i = 0; i < 32; i++) {
-    r0[i] = __float_as_uint(x[i]);
-    r1[i] = __float_as_uint(x[32 + i]);
-  }
-  tmem_st32(taddr, r0);
-  tmem_st32(taddr + 32, r1);
-  tmem_st_wait();
+// Float index of element (r, c) of a 64 x 64 f32 matrix held as two swizzled
+// 64 x 32 halves: half c / 32 (2048 floats), row r (32 floats), 16-byte chunk
+// (c % 32) / 4 XOR r % 8.
+__device__ __forceinline__ int swf(int r, int c) {
+  return ((c >> 5) << 11) + (r << 5) + ((((c >> 2) & 7) ^ (r & 7)) << 2) + (c & 3);
 }
 
-// Value of register-array element `idx` (runtime index) without local memory.
-__device__ __forceinline__ float pick64(const float (&x)[64], int idx) {
-  float v = 0.f;
-#pragma unroll
-  for (int j = 0; j < 64; j++) v = j == idx ? x[j] : v;
-  return v;
-}
-
-__global__ void __launch_bounds__(GT_THREADS, 1)
-    gdn_chunked_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, const GdnArgs a) {
+// =====================================================================
+// prep: state-independent operands of every chunk of the slab
+// =====================================================================
+__global__ void __launch_bounds__(PREP_THREADS, 2)
+    gdn_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmW, const PrepArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-  uint64_t* kv_full = bars + 0;   // [2] TMA landed
-  uint64_t* kv_empty = bars + 2;  // [2] inputs of a chunk no longer read
-  uint64_t* bar_f = bars + 4;     // (f) [K;Q][K;Q]^T done
-  uint64_t* f_free = bars + 5;    // prep warps have read (f)
-  uint64_t* bar_T = bars + 6;     // [2] prep outputs (scalars, QKm, (I+A)^-1) of a chunk written
-  uint64_t* pfree = bars + 8;     // [2] chain warps done with those prep outputs
-  uint64_t* bar_a = bars + 10;    // (a) K S0, Q S0 done
-  uint64_t* bar_R = bars + 11;    // R written
-  uint64_t* bar_c = bars + 12;    // (c) Delta done
-  uint64_t* bar_D = bars + 13;    // Delta copies written, state rescaled
-  uint64_t* bar_d = bars + 14;    // (d) QKm Delta and (e) state update done
-  uint64_t* bar_s0 = bars + 15;   // bf16 state written (and initial state)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBAR);
-  float* Af = reinterpret_cast<float*>(sm + OFF_AF);
-  float* Tf = reinterpret_cast<float*>(sm + OFF_TF);
-  float* X1 = reinterpret_cast<float*>(sm + OFF_X1);
-  float* X2 = reinterpret_cast<float*>(sm + OFF_X2);
-  float* scal = reinterpret_cast<float*>(sm + OFF_SC);  // [2][4][64]
-  float* misc = scal + 2 * 4 * 64;
+  uint8_t* sm = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + P_OFF_BAR);
+  uint64_t* bar_kq = bars + 0;   // K / Q chunk landed
+  uint64_t* bar_f = bars + 1;    // [K;Q][K;Q]^T done
+  uint64_t* bar_l3a = bars + 2;  // [2] U11 A21^T done
+  uint64_t* bar_l3b = bars + 4;  // [2] T22 X2 done
+  uint64_t* bar_g = bars + 6;    // [2] QKm Tb done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + P_NBAR);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = blockIdx.x, b = blockIdx.z;
+  const int hk = blockIdx.y % a.NK, pair = blockIdx.y / a.NK;
+  const int t0 = (a.c0 + c) * GC;
+
+  if (tid == 0) {
+    for (int i = 0; i < P_NBAR; i++) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (tid == 0) {
+    prefetch_tensormap(&tmW);
+    mbar_arrive_expect_tx(bar_kq, 32768);
+    tma_load_4d(sm + P_OFF_KQ, &tmK, bar_kq, 0, hk, t0, b);
+    tma_load_4d(sm + P_OFF_KQ + 8192, &tmQ, bar_kq, 0, hk, t0, b);
+    tma_load_4d(sm + P_OFF_KQ + 16384, &tmK, bar_kq, 64, hk, t0, b);
+    tma_load_4d(sm + P_OFF_KQ + 24576, &tmQ, bar_kq, 64, hk, t0, b);
+    if (mbar_wait(bar_kq, 0, a.status)) {
+      tc_fence_after();
+      constexpr uint32_t id_f = idesc_f16(128, 128, true, false, false);
+      const uint32_t kq = smem_u32(sm + P_OFF_KQ);
+#pragma unroll
+      for (int ks = 0; ks < 8; ks++) {
+        const uint64_t d = smem_desc_sw128(kq + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+        mma_f16_ss(tmem, d, d, id_f, ks > 0);
+      }
+      mma_commit(bar_f);
+    }
+  }
+
+  const int wg = warp >> 2, quad = warp & 3, t = quad * 32 + lane;
+  const int h = hk + (2 * pair + wg) * a.NK;
+  const bool active = h < a.NV;
+  {
+    uint8_t* wreg = sm + P_OFF_WG + wg * P_WG_STRIDE;
+    float* Aw = reinterpret_cast<float*>(wreg);            // A, swizzled halves
+    float* Tw = reinterpret_cast<float*>(wreg + 16384);    // T, swizzled halves; later Tb^T
+    float* gam2 = reinterpret_cast<float*>(wreg + 32768);  // gamma * log2(e)
+    float* betv = gam2 + 64;
+    float* ikv = gam2 + 128;
+    float* iqv = gam2 + 192;
+    float* wv = gam2 + 256;  // gam2_j - log2(ik_j)
+    float* misc = gam2 + 320;
+    float* X1 = reinterpret_cast<float*>(sm + P_OFF_X1 + wg * 2560);
+    float* X2T = reinterpret_cast<float*>(sm + P_OFF_X2 + wg * 4096);
+    float* U11 = reinterpret_cast<float*>(sm + P_OFF_U11 + wg * 8192);
+    uint8_t* wst = wreg;  // W staging [Tb; QKm Tb] bf16, 128 swizzled rows (A is dead by then)
+    const uint32_t lo = (uint32_t)(quad * 32) << 16;
+    const uint32_t tl3 = tmem + 128 + 64 * wg;  // 64x64 combine products, later QKm Tb
+    const uint32_t bid = 1 + wg;
+    const size_t unit = ((size_t)b * a.NV + h) * a.ns + c;
+
+    float gi = 0.f, bi = 0.f;
+    if (active && t < 64 && t0 + t < a.T) {
+      const size_t idx = (size_t)b * a.gb_seq + (size_t)(t0 + t) * a.gb_row + h;
+      gi = __ldg(a.g + idx);
+      bi = __ldg(a.beta + idx);
+    }
+    bool ok = active && named_bar_and(bid, 128, mbar_wait(bar_f, 0, a.status));
+    float nrm2 = 0.f, f[64];  // f: G row t (t < 64) or P row t - 64: k_t . k_j / q_i . k_j
+    if (ok) {
+      tc_fence_after();
+      // |k_t|^2 (t < 64) or |q_{t-64}|^2: the diagonal of [K;Q][K;Q]^T, column t
+      uint32_t r[32];
+      tmem_ld32(tmem + lo + quad * 32, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; j++) nrm2 = j == lane ? __uint_as_float(r[j]) : nrm2;
+      tmem_ld64(tmem + lo, f);
+    }
+    // both warpgroups have read [K;Q][K;Q]^T before its columns take QKm
+    tc_fence_before();
+    named_bar(3, PREP_THREADS);
+    if (ok) {
+      tc_fence_after();
+      float sc = gi;
+      if (t < 64) {
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, sc, o);
+          if (lane >= o) sc += y;
+        }
+        if (t == 31) misc[0] = sc;
+      }
+      named_bar(bid, 128);
+      if (t < 64) {
+        const float g2 = (sc + (t >= 32 ? misc[0] : 0.f)) * kLog2e;
+        const float ik = rsqrtf(nrm2 + 1e-6f);
+        gam2[t] = g2;
+        betv[t] = bi;
+        ikv[t] = ik;
+        wv[t] = g2 - __log2f(ik);
+      } else {
+        iqv[t - 64] = rsqrtf(nrm2 + 1e-6f) * rsqrtf((float)GD);
+      }
+      named_bar(bid, 128);
+      // A_tj = 2^(z_t - w_j) f_j with z_t = gam2_t + log2(beta_t ik_t); QKm likewise
+      // with z_i = gam2_i + log2(iq_i).  Entries outside the triangle are selected
+      // away (their exponent may overflow); rows 0-31 only have columns 0-31.
+      if (t < 64) {
+        const float z = gam2[t] + __log2f(betv[t] * ikv[t]);
+#pragma unroll
+        for (int u = 0; u < 16; u++) {
+          if (u >= 8 && quad == 0) break;
+          const float4 w4 = reinterpret_cast<const float4*>(wv)[u];
+          const int j = 4 * u;
+          float4 o;
+          o.x = j + 0 < t ? tf32_round(fast_ex2(z - w4.x) * f[j + 0]) : 0.f;
+          o.y = j + 1 < t ? tf32_round(fast_ex2(z - w4.y) * f[j + 1]) : 0.f;
+          o.z = j + 2 < t ? tf32_round(fast_ex2(z - w4.z) * f[j + 2]) : 0.f;
+          o.w = j + 3 < t ? tf32_round(fast_ex2(z - w4.w) * f[j + 3]) : 0.f;
+          *reinterpret_cast<float4*>(Aw + swf(t, j)) = o;
+        }
+      } else {
+        const int i = t - 64;
+        const float z = gam2[i] + __log2f(iqv[i]);
+        float y[64];
+#pragma unroll
+        for (int u = 0; u < 16; u++) {
+          const float4 w4 = reinterpret_cast<const float4*>(wv)[u];
+          const int j = 4 * u;
+          const bool live = u < 8 || quad == 3;
+          y[j + 0] = live && j + 0 <= i ? tf32_round(fast_ex2(z - w4.x) * f[j + 0]) : 0.f;
+          y[j + 1] = live && j + 1 <= i ? tf32_round(fast_ex2(z - w4.y) * f[j + 1]) : 0.f;
+          y[j + 2] = live && j + 2 <= i ? tf32_round(fast_ex2(z - w4.z) * f[j + 2]) : 0.f;
+          y[j + 3] = live && j + 3 <= i ? tf32_round(fast_ex2(z - w4.w) * f[j + 3]) : 0.f;
+        }
+        // QKm row i: A operand (tf32, from TMEM) of QKm Tb, lane 64 + i
+        uint32_t r0[32], r1[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          r0[j] = __float_as_uint(y[j]);
+          r1[j] = __float_as_uint(y[32 + j]);
+        }
+        tmem_st32(tmem + lo + 64 * wg, r0);
+        tmem_st32(tmem + lo + 64 * wg + 32, r1);
+        tmem_st_wait();
+        tc_fence_before();
+      }
+      named_bar(bid, 128);
+      // (I + A)^-1: 16x16 diagonal blocks by forward substitution.  Thread cc
+      // of a block computes its column, which is also row cc of U = T^T; the
+      // tf32 MMAs below take K-major operands only, so U11 = (T[0:32][0:32])^T
+      // is kept beside T.
+      if (t < 64) {
+        const int base = (t >> 4) * 16, cc = t & 15;
+        float tc[16];
+#pragma unroll
+        for (int r = 0; r < 16; r++) {
+          float s = 0.f;
+#pragma unroll
+          for (int j = 0; j < r; j++) s = fmaf(Aw[swf(base + r, base + j)], tc[j], s);
+          tc[r] = tf32_round(r == cc ? 1.f : -s);
+        }
+#pragma unroll
+        for (int r = 0; r < 16; r++) Tw[swf(base + r, base + cc)] = tc[r];
+        if (base < 32) {
+#pragma unroll
+          for (int u = 0; u < 4; u++)
+            *reinterpret_cast<float4*>(U11 + swf(base + cc, base + 4 * u)) =
+                make_float4(tc[4 * u], tc[4 * u + 1], tc[4 * u + 2], tc[4 * u + 3]);
+        }
+      } else {
+        // zero the upper off-diagonal 16x16 blocks (0,1) and (2,3) of T, and
+        // the matching block of U11: the 32x32 diagonal blocks are read whole
+        for (int e = t - 64; e < 512; e += 64) {
+          const int blk = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+          Tw[swf(blk * 32 + r, blk * 32 + 16 + cc)] = 0.f;
+          if (blk == 0) U11[swf(16 + cc, r)] = 0.f;
+        }
+      }
+      named_bar(bid, 128);
+      {
+        // 32x32 blocks: T[2p+1][2p] = -T[2p+1][2p+1] A[2p+1][2p] T[2p][2p]
+        const int p = t >> 6, rem = t & 63, r = rem >> 2, c4 = (rem & 3) * 4;
+        const int rb = 16 * (2 * p + 1), cb = 16 * (2 * p);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+          const float av = Aw[swf(rb + r, cb + k)];
+          const float4 tv = *reinterpret_cast<const float4*>(Tw + swf(cb + k, cb + c4));
+          acc.x = fmaf(av, tv.x, acc.x);
+          acc.y = fmaf(av, tv.y, acc.y);
+          acc.z = fmaf(av, tv.z, acc.z);
+          acc.w = fmaf(av, tv.w, acc.w);
+        }
+        *reinterpret_cast<float4*>(&X1[(p * 16 + r) * 20 + c4]) = acc;
+        named_bar(bid, 128);
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+          const float tv = Tw[swf(rb + r, rb + k)];
+          const float4 xv = *reinterpret_cast<const float4*>(&X1[(p * 16 + k) * 20 + c4]);
+          o.x = fmaf(tv, xv.x, o.x);
+          o.y = fmaf(tv, xv.y, o.y);
+          o.z = fmaf(tv, xv.z, o.z);
+          o.w = fmaf(tv, xv.w, o.w);
+        }
+        const float4 v = make_float4(tf32_round(-o.x), tf32_round(-o.y), tf32_round(-o.z), tf32_round(-o.w));
+        *reinterpret_cast<float4*>(Tw + swf(rb + r, cb + c4)) = v;
+        if (p == 0) {
+          U11[swf(c4 + 0, rb + r)] = v.x;
+          U11[swf(c4 + 1, rb + r)] = v.y;
+          U11[swf(c4 + 2, rb + r)] = v.z;
+          U11[swf(c4 + 3, rb + r)] = v.w;
+        }
+      }
+      // 64x64 on the tensor cores (tf32, K-major operands):
+      //   X2^T = U11 A[32:64][0:32]^T,  then  T[32:64][0:32] = -T[32:64][32:64] X2.
+      // Both are M = 64 products whose unused rows read padding.
+      fence_proxy_async();
+      named_bar(bid, 128);
+      constexpr uint32_t id_l3 = idesc_tf32(64, 32, false, false);
+      if (t == 0) {
+        tc_fence_after();
+        const uint32_t ub = smem_u32(U11), ab = smem_u32(Aw) + 32 * 128;
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++)
+          mma_tf32_ss(tl3, smem_desc_sw128(ub + ks * 32, 16, 1024), smem_desc_sw128(ab + ks * 32, 16, 1024), id_l3,
+                      ks > 0);
+        mma_commit(&bar_l3a[wg]);
+      }
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_l3a[wg], 0, a.status));
+      if (ok && quad < 2) {
+        tc_fence_after();
+        uint32_t r[32];
+        tmem_ld32(tl3 + lo, r);  // M = 64 rows 0-31 (X2^T): lanes 0-15 of quadrants 0, 1
+        tmem_ld_wait();
+        if (lane < 16) {
+          const int j = 16 * quad + lane;
+#pragma unroll
+          for (int u = 0; u < 8; u++)
+            *reinterpret_cast<float4*>(X2T + j * 32 + ((u ^ (j & 7)) << 2)) =
+                make_float4(tf32_round(__uint_as_float(r[4 * u])), tf32_round(__uint_as_float(r[4 * u + 1])),
+                            tf32_round(__uint_as_float(r[4 * u + 2])), tf32_round(__uint_as_float(r[4 * u + 3])));
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      ok = named_bar_and(bid, 128, ok);
+      if (ok && t == 0) {
+        tc_fence_after();
+        const uint32_t tb = smem_u32(Tw) + 8192, xb = smem_u32(X2T);
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++)
+          mma_tf32_ss(tl3 + 32, smem_desc_sw128(tb + ks * 32, 16, 1024), smem_desc_sw128(xb + ks * 32, 16, 1024),
+                      id_l3, ks > 0);
+        mma_commit(&bar_l3b[wg]);
+      }
+      if (ok && quad >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_l3b[wg], 0, a.status));
+        if (ok) {
+          tc_fence_after();
+          uint32_t r[32];
+          tmem_ld32(tl3 + 32 + lo, r);  // rows 32-63: lanes 0-15 of quadrants 2, 3
+          tmem_ld_wait();
+          if (lane < 16) {
+            const int m = 32 + 16 * (quad - 2) + lane;
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+              *reinterpret_cast<float4*>(Tw + swf(m, 4 * u)) =
+                  make_float4(-__uint_as_float(r[4 * u]), -__uint_as_float(r[4 * u + 1]),
+                              -__uint_as_float(r[4 * u + 2]), -__uint_as_float(r[4 * u + 3]));
+          }
+        }
+      }
+      tc_fence_before();
+      ok = named_bar_and(bid, 128, ok);
+      // Tb = T diag(beta): row t is W row t; its transpose (rows of Tb^T, in
+      // T's place) is the K-major B operand of QKm Tb.
+      float y[64];
+      if (ok && t < 64) {
+#pragma unroll
+        for (int u = 0; u < 16; u++) {
+          const bool live = u < 8 || quad == 1;
+          float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (live) v4 = *reinterpret_cast<const float4*>(Tw + swf(t, 4 * u));
+          const float4 b4 = reinterpret_cast<const float4*>(betv)[u];
+          const float tv[4] = {v4.x, v4.y, v4.z, v4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const int j = 4 * u + e;
+            y[j] = (j < t ? tv[e] : (j == t ? 1.f : 0.f)) * bb[e];
+          }
+        }
+        store_row64(wst, t, y);
+        const float G = fast_ex2(gam2[t]), e63 = fast_ex2(gam2[63]);
+        float* scu = a.sc + unit * SC_FLOATS;
+        scu[t] = G * ikv[t];
+        scu[64 + t] = G * iqv[t];
+        scu[128 + t] = ikv[t] * fast_ex2(gam2[63] - gam2[t]);
+        scu[192 + t] = e63;
+      }
+      named_bar(bid, 128);  // every row of T has been read
+      if (ok && t < 64) {
+#pragma unroll
+        for (int n = 0; n < 64; n++) Tw[swf(n, t)] = tf32_round(y[n]);
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      ok = named_bar_and(bid, 128, ok);
+      if (ok && t == 0) {
+        // QKm Tb (M = 128: rows 64-127 are QKm's, from TMEM lanes 64-127; rows
+        // 0-63 read lanes 0-63 of the same columns and are not used)
+        tc_fence_after();
+        constexpr uint32_t id_g = idesc_tf32(128, 64, false, false);
+        const uint32_t tb = smem_u32(Tw);
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++)
+          mma_tf32_ts(tl3, tmem + 64 * wg + 8 * ks, smem_desc_sw128(tb + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024),
+                      id_g, ks > 0);
+        mma_commit(&bar_g[wg]);
+      }
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_g[wg], 0, a.status));
+      if (ok && quad >= 2) {
+        tc_fence_after();
+        tmem_ld64(tl3 + lo, y);
+        store_row64(wst, t, y);  // W row 64 + i = (QKm Tb) row i
+        fence_proxy_async();
+      }
+      ok = named_bar_and(bid, 128, ok);
+      if (ok && t == 0) {
+        tma_store_2d(&tmW, wst, 0, (int)(unit * 128));
+        tma_store_commit_and_wait_read();
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) {
+    __syncwarp();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// =====================================================================
+// chain: the state recurrence over the chunks of a slab
+// =====================================================================
+__global__ void __launch_bounds__(CHAIN_THREADS, 2)
+    gdn_chain_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmS, const ChainArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C_OFF_BAR);
+  uint64_t* kq_full = bars + 0;
+  uint64_t* kq_empty = bars + 1;  // MMA a done
+  uint64_t* ke_full = bars + 2;
+  uint64_t* ke_empty = bars + 3;  // MMA e done
+  uint64_t* v_full = bars + 4;
+  uint64_t* v_empty = bars + 5;   // R' written
+  uint64_t* w_full = bars + 6;
+  uint64_t* w_empty = bars + 7;   // MMA c done
+  uint64_t* sc_full = bars + 8;   // [2]
+  uint64_t* sc_empty = bars + 10; // [2] chunk finished by the chain warps
+  uint64_t* bar_a = bars + 12;    // [X; QS] in TMEM
+  uint64_t* bar_R = bars + 13;    // R' in shared memory
+  uint64_t* bar_c = bars + 14;    // [Tb R'; O2] in TMEM
+  uint64_t* bar_D = bars + 15;    // Dsb in shared memory, [X; QS] and [Tb R'; O2] read
+  uint64_t* bar_e = bars + 16;    // U in TMEM
+  uint64_t* bar_s0 = bars + 17;   // bf16 state written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C_NBAR);
+  float* scal = reinterpret_cast<float*>(sm + C_OFF_SC);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int dvb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h % a.NK;
-  const int n = a.nchunks;
+  const int n = a.cnt;
+  const size_t unit0 = ((size_t)b * a.NV + h) * a.ns;
 
   if (tid == 0) {
+    mbar_init(kq_full, 1);
+    mbar_init(kq_empty, 1);
+    mbar_init(ke_full, 1);
+    mbar_init(ke_empty, 1);
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 2);
+    mbar_init(w_full, 1);
+    mbar_init(w_empty, 1);
     for (int i = 0; i < 2; i++) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-      mbar_init(&bar_T[i], 4);
-      mbar_init(&pfree[i], 4);
+      mbar_init(&sc_full[i], 1);
+      mbar_init(&sc_empty[i], 4);
     }
-    mbar_init(bar_f, 1);
-    mbar_init(f_free, 4);
     mbar_init(bar_a, 1);
-    mbar_init(bar_R, 4);
+    mbar_init(bar_R, 2);
     mbar_init(bar_c, 1);
     mbar_init(bar_D, 4);
-    mbar_init(bar_d, 1);
+    mbar_init(bar_e, 1);
     mbar_init(bar_s0, 4);
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_alloc(tmem_slot, C_TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -200,370 +579,228 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      prefetch_tensormap(&tmQ);
       prefetch_tensormap(&tmK);
+      prefetch_tensormap(&tmQ);
       prefetch_tensormap(&tmV);
+      prefetch_tensormap(&tmW);
+      prefetch_tensormap(&tmS);
       for (int c = 0; c < n; c++) {
-        const int buf = c & 1;
-        if (c >= 2 && !mbar_wait(&kv_empty[buf], ((c - 2) >> 1) & 1, a.status)) break;
-        uint8_t* kq = sm + OFF_KQ + buf * KQ_BYTES;
-        const int t0 = c * GC;
-        mbar_arrive_expect_tx(&kv_full[buf], KQ_BYTES + V_BYTES);
-        tma_load_4d(kq, &tmK, &kv_full[buf], 0, hk, t0, b);
-        tma_load_4d(kq + 8192, &tmQ, &kv_full[buf], 0, hk, t0, b);
-        tma_load_4d(kq + 16384, &tmK, &kv_full[buf], 64, hk, t0, b);
-        tma_load_4d(kq + 24576, &tmQ, &kv_full[buf], 64, hk, t0, b);
-        tma_load_4d(sm + OFF_V + buf * V_BYTES, &tmV, &kv_full[buf], dvb * DVB, h, t0, b);
+        const int t0 = (a.c0 + c) * GC;
+        const int u = (int)(unit0 + c);
+        const uint32_t pe = (c - 1) & 1;
+        if (c >= 1 && !mbar_wait(kq_empty, pe, a.status)) break;
+        mbar_arrive_expect_tx(kq_full, 32768);
+        tma_load_4d(sm + C_OFF_KQ, &tmK, kq_full, 0, hk, t0, b);
+        tma_load_4d(sm + C_OFF_KQ + 8192, &tmQ, kq_full, 0, hk, t0, b);
+        tma_load_4d(sm + C_OFF_KQ + 16384, &tmK, kq_full, 64, hk, t0, b);
+        tma_load_4d(sm + C_OFF_KQ + 24576, &tmQ, kq_full, 64, hk, t0, b);
+        if (c >= 1 && !mbar_wait(v_empty, pe, a.status)) break;
+        mbar_arrive_expect_tx(v_full, 8192);
+        tma_load_4d(sm + C_OFF_V, &tmV, v_full, dvb * DVB, h, t0, b);
+        if (c >= 2 && !mbar_wait(&sc_empty[c & 1], ((c - 2) >> 1) & 1, a.status)) break;
+        mbar_arrive_expect_tx(&sc_full[c & 1], SC_FLOATS * 4);
+        tma_load_2d(scal + (c & 1) * SC_FLOATS, &tmS, &sc_full[c & 1], 0, u * 4);
+        if (c >= 1 && !mbar_wait(w_empty, pe, a.status)) break;
+        mbar_arrive_expect_tx(w_full, W_ELEMS * 2);
+        tma_load_2d(sm + C_OFF_W, &tmW, w_full, 0, u * 128);
+        if (c >= 1 && !mbar_wait(ke_empty, pe, a.status)) break;
+        mbar_arrive_expect_tx(ke_full, 16384);
+        tma_load_4d(sm + C_OFF_KE, &tmK, ke_full, 0, hk, t0, b);
+        tma_load_4d(sm + C_OFF_KE + 8192, &tmK, ke_full, 64, hk, t0, b);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t id_f = idesc_f16(128, 128, true, false, false);  // [K;Q] [K;Q]^T
-      constexpr uint32_t id_kb = idesc_f16(64, 64, true, false, true);    // 64-row A (K-major) x MN-major B
-      constexpr uint32_t id_e = idesc_f16(128, 64, true, true, true);     // K^T (MN-major) x MN-major B
+      constexpr uint32_t id_n64 = idesc_f16(128, 64, true, false, true);  // K-major A, MN-major B
+      constexpr uint32_t id_e = idesc_f16(128, 64, true, true, true);     // MN-major A (K^T)
       const uint32_t s0 = smem_u32(sm);
-      auto issue_f = [&](int c) {
-        const uint32_t kq = s0 + OFF_KQ + (c & 1) * KQ_BYTES;
-#pragma unroll
-        for (int ks = 0; ks < 8; ks++) {
-          const uint64_t d = smem_desc_sw128(kq + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
-          mma_f16_ss(tmem + TC_F, d, d, id_f, ks > 0);
-        }
-        mma_commit(bar_f);
-      };
-      bool ok = mbar_wait(&kv_full[0], 0, a.status);
-      if (ok) {
-        tc_fence_after();
-        issue_f(0);
-      }
-      for (int c = 0; c < n && ok; c++) {
-        const int buf = c & 1, x = c & 1;
-        const uint32_t kq = s0 + OFF_KQ + buf * KQ_BYTES;
-        // state-independent MMA of the next chunk, once the prep warps hold chunk c's
-        if (c + 1 < n) {
-          ok = mbar_wait(&kv_full[(c + 1) & 1], ((c + 1) >> 1) & 1, a.status) && mbar_wait(f_free, c & 1, a.status);
-          if (!ok) break;
-          tc_fence_after();
-          issue_f(c + 1);
-        }
-        // (a) X = K S0 and QS = Q S0   (M = 64, N = 64, K = 128)
-        ok = mbar_wait(bar_s0, c & 1, a.status);
-        if (!ok) break;
+      for (int c = 0; c < n; c++) {
+        const uint32_t ph = c & 1;
+        // (a) [X; QS] = [K; Q] S0   (M = 128, N = 64, K = 128)
+        if (!mbar_wait(kq_full, ph, a.status) || !mbar_wait(bar_s0, ph, a.status)) break;
         tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 8; ks++) {
-          const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-          const uint64_t bd = smem_desc_sw128(s0 + OFF_S0B + ks * 2048, 8192, 1024);
-          mma_f16_ss(tmem + TC_X, smem_desc_sw128(kq + off, 16, 1024), bd, id_kb, ks > 0);
-          mma_f16_ss(tmem + TC_QS, smem_desc_sw128(kq + off + 8192, 16, 1024), bd, id_kb, ks > 0);
-        }
+        for (int ks = 0; ks < 8; ks++)
+          mma_f16_ss(tmem + TC_P, smem_desc_sw128(s0 + C_OFF_KQ + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
+                     smem_desc_sw128(s0 + C_OFF_S0B + ks * 2048, 8192, 1024), id_n64, ks > 0);
         mma_commit(bar_a);
-        // (c) Delta = (I+A)^-1 R   (M = 64, N = 64, K = 64)
-        ok = mbar_wait(bar_R, c & 1, a.status);
-        if (!ok) break;
+        mma_commit(kq_empty);
+        // (c) [Tb R'; O2] = W R'   (M = 128, N = 64, K = 64)
+        if (!mbar_wait(bar_R, ph, a.status) || !mbar_wait(w_full, ph, a.status)) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 4; ks++)
-          mma_f16_ss(tmem + TC_DL, smem_desc_sw128(s0 + OFF_TB + x * 8192 + ks * 32, 16, 1024),
-                     smem_desc_sw128(s0 + OFF_RB + ks * 2048, 8192, 1024), id_kb, ks > 0);
+          mma_f16_ss(tmem + TC_Q, smem_desc_sw128(s0 + C_OFF_W + ks * 32, 16, 1024),
+                     smem_desc_sw128(s0 + C_OFF_RB + ks * 2048, 8192, 1024), id_n64, ks > 0);
         mma_commit(bar_c);
-        // (d) O2 = QKm Delta; (e) S += K^T Dsb   (S pre-scaled by the chain warps)
-        ok = mbar_wait(bar_D, c & 1, a.status);
-        if (!ok) break;
+        mma_commit(w_empty);
+        // (e) U = K^T Dsb   (M = 128, N = 64, K = 64)
+        if (!mbar_wait(bar_D, ph, a.status) || !mbar_wait(ke_full, ph, a.status)) break;
         tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 4; ks++) {
-          mma_f16_ss(tmem + TC_O2, smem_desc_sw128(s0 + OFF_QKM + x * 8192 + ks * 32, 16, 1024),
-                     smem_desc_sw128(s0 + OFF_DB + ks * 2048, 8192, 1024), id_kb, ks > 0);
-          mma_f16_ss(tmem + TC_S, smem_desc_sw128(kq + ks * 2048, 16384, 1024),
-                     smem_desc_sw128(s0 + OFF_DSB + ks * 2048, 8192, 1024), id_e, 1);
-        }
-        mma_commit(bar_d);
-        mma_commit(&kv_empty[buf]);
+        for (int ks = 0; ks < 4; ks++)
+          mma_f16_ss(tmem + TC_P, smem_desc_sw128(s0 + C_OFF_KE + ks * 2048, 8192, 1024),
+                     smem_desc_sw128(s0 + C_OFF_DSB + ks * 2048, 8192, 1024), id_e, ks > 0);
+        mma_commit(bar_e);
+        mma_commit(ke_empty);
       }
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ---------------- prep warpgroup: state-independent part of each chunk ----------------
-    const int t = (warp - 4) * 32 + lane;
-    const uint32_t lo = (uint32_t)((warp - 4) * 32) << 16;
-    const float inv_sqrt_d = rsqrtf((float)GD);
-    for (int c = 0; c < n; c++) {
-      const int x = c & 1;
-      float* gam2 = scal + x * 256;
-      float* betv = gam2 + 64;
-      float* ikv = gam2 + 128;
-      float* iqv = gam2 + 192;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_f, c & 1, a.status))) break;
-      tc_fence_after();
-      float f[64], dg[64];
-      tmem_ld64(tmem + lo + TC_F, f);         // G row t (t < 64) / P row t-64
-      tmem_ld64(tmem + lo + TC_F + 64, dg);   // K Q^T row / Q Q^T row
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(f_free);
-      const float nrm2 = t < 64 ? pick64(f, t) : pick64(dg, t - 64);  // |k_t|^2 or |q_t-64|^2
-      float gi = 0.f, bi = 0.f;
-      const int t0 = c * GC;
-      if (t < 64 && t0 + t < a.T) {
-        const size_t idx = (size_t)b * a.gb_seq + (size_t)(t0 + t) * a.gb_row + h;
-        gi = __ldg(a.g + idx);
-        bi = __ldg(a.beta + idx);
-      }
-      if (c >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pfree[x], ((c - 2) >> 1) & 1, a.status))) break;
-      if (t < 64) {
-        float sc = gi;
+  } else {
+    // ---------------- chain warps 2-5: TMEM lane quadrant = warp % 4 ----------------
+    const int quad = warp & 3;
+    const int t = quad * 32 + lane;  // state row (dk); row of [K; Q] / W results
+    const uint32_t lo = (uint32_t)(quad * 32) << 16;
+    uint8_t* s0b = sm + C_OFF_S0B;
+    float st[64];
+    if (a.load_state) {
+      const float4* src =
+          reinterpret_cast<const float4*>(a.state_in + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * DVB);
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float y = __shfl_up_sync(0xffffffffu, sc, o);
-          if (lane >= o) sc += y;
+      for (int i = 0; i < 16; i++) {
+        const float4 v = __ldg(src + i);
+        st[4 * i] = v.x;
+        st[4 * i + 1] = v.y;
+        st[4 * i + 2] = v.z;
+        st[4 * i + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; i++) st[i] = 0.f;
+    }
+    store_row64(s0b, t, st);
+    fence_proxy_async();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_s0);
+    bool ok = true;
+    for (int c = 0; c < n && ok; c++) {
+      const uint32_t ph = c & 1;
+      const float* sc = scal + (c & 1) * SC_FLOATS;
+      if (quad < 2) {
+        // R'_t = V_t - c2_t X_t   (token t)
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_a, ph, a.status) && mbar_wait(v_full, ph, a.status) &&
+                                         mbar_wait(&sc_full[c & 1], (c >> 1) & 1, a.status));
+        if (!ok) break;
+        tc_fence_after();
+        const float c2 = sc[t];
+        const uint8_t* vt = sm + C_OFF_V;
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+          uint32_t xr[32];
+          tmem_ld32(tmem + lo + TC_P + 32 * hf, xr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const uint32_t off = sw128_offset(t, 64 * hf + 16 * u);
+            const uint4 vw = *reinterpret_cast<const uint4*>(vt + off);
+            const uint32_t vs[4] = {vw.x, vw.y, vw.z, vw.w};
+            float r[8];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              r[2 * e] = fmaf(-c2, __uint_as_float(xr[8 * u + 2 * e]), bf16_lo(vs[e]));
+              r[2 * e + 1] = fmaf(-c2, __uint_as_float(xr[8 * u + 2 * e + 1]), bf16_hi(vs[e]));
+            }
+            *reinterpret_cast<uint4*>(sm + C_OFF_RB + off) = pack8(r);
+          }
         }
-        if (t == 31) misc[x] = sc;
-        gi = sc;
-      }
-      named_bar(2, 128);
-      if (t < 64) {
-        gam2[t] = (gi + (t >= 32 ? misc[x] : 0.f)) * kLog2e;
-        betv[t] = bi;
-        ikv[t] = rsqrtf(nrm2 + 1e-6f);
-      } else {
-        iqv[t - 64] = rsqrtf(nrm2 + 1e-6f) * inv_sqrt_d;
-      }
-      named_bar(2, 128);
-      if (t < 64) {
-        // A (strictly lower), f32
-        const float gi2 = gam2[t], cb = betv[t] * ikv[t];
+        fence_proxy_async();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar_R);
+          mbar_arrive(v_empty);
+        }
+        // Dsb_t = c4_t (row t of Tb R'), the bf16 operand of the state update
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_c, ph, a.status));
+        if (!ok) break;
+        tc_fence_after();
+        const float c4 = sc[128 + t];
 #pragma unroll
-        for (int j = 0; j < 64; j++) Af[t * AS + j] = j < t ? cb * ikv[j] * fast_ex2(gi2 - gam2[j]) * f[j] : 0.f;
+        for (int hf = 0; hf < 2; hf++) {
+          uint32_t dr[32];
+          tmem_ld32(tmem + lo + TC_Q + 32 * hf, dr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            uint4 w;
+            w.x = pack2(c4 * __uint_as_float(dr[8 * u + 0]), c4 * __uint_as_float(dr[8 * u + 1]));
+            w.y = pack2(c4 * __uint_as_float(dr[8 * u + 2]), c4 * __uint_as_float(dr[8 * u + 3]));
+            w.z = pack2(c4 * __uint_as_float(dr[8 * u + 4]), c4 * __uint_as_float(dr[8 * u + 5]));
+            w.w = pack2(c4 * __uint_as_float(dr[8 * u + 6]), c4 * __uint_as_float(dr[8 * u + 7]));
+            *reinterpret_cast<uint4*>(sm + C_OFF_DSB + sw128_offset(t, 64 * hf + 16 * u)) = w;
+          }
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_D);
       } else {
-        // QKm row (lower including the diagonal), bf16
+        // O_i = c3_i QS_i + O2_i   (token i = t - 64)
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(bar_c, ph, a.status) && mbar_wait(&sc_full[c & 1], (c >> 1) & 1, a.status));
+        if (!ok) break;
+        tc_fence_after();
         const int i = t - 64;
-        const float gi2 = gam2[i], cq = iqv[i];
-        float y[64];
+        const float c3 = sc[64 + i];
+        const int tok = (a.c0 + c) * GC + i;
+        float4* dst = reinterpret_cast<float4*>(a.core + (((size_t)b * a.T + tok) * a.NV + h) * GD + dvb * DVB);
 #pragma unroll
-        for (int j = 0; j < 64; j++) y[j] = j <= i ? cq * ikv[j] * fast_ex2(gi2 - gam2[j]) * f[j] : 0.f;
-        store_row64(sm + OFF_QKM + x * 8192, i, y);
+        for (int hf = 0; hf < 2; hf++) {
+          uint32_t qs[32], o2[32];
+          tmem_ld32(tmem + lo + TC_P + 32 * hf, qs);
+          tmem_ld32(tmem + lo + TC_Q + 32 * hf, o2);
+          tmem_ld_wait();
+          if (hf == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_D);
+          }
+          if (tok < a.T) {
+            float o[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) o[j] = fmaf(c3, __uint_as_float(qs[j]), __uint_as_float(o2[j]));
+            if (a.v8) {
+#pragma unroll
+              for (int u = 0; u < 4; u++)
+                st_global_v8(reinterpret_cast<float*>(dst + 8 * hf + 2 * u), o[8 * u], o[8 * u + 1], o[8 * u + 2],
+                             o[8 * u + 3], o[8 * u + 4], o[8 * u + 5], o[8 * u + 6], o[8 * u + 7]);
+            } else {
+#pragma unroll
+              for (int u = 0; u < 8; u++)
+                dst[8 * hf + u] = make_float4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+            }
+          }
+        }
       }
-      named_bar(2, 128);
-      // (I + A)^-1: 16x16 diagonal blocks by forward substitution
-      if (t < 64) {
-        const int base = (t >> 4) * 16, cc = t & 15;
-        float tc[16];
-#pragma unroll
-        for (int r = 0; r < 16; r++) {
-          float s = 0.f;
-#pragma unroll
-          for (int j = 0; j < r; j++) s = fmaf(Af[(base + r) * AS + base + j], tc[j], s);
-          tc[r] = r == cc ? 1.f : -s;
-        }
-#pragma unroll
-        for (int r = 0; r < 16; r++) Tf[(base + r) * AS + base + cc] = tc[r];
-      } else {
-        // zero the upper off-diagonal 16x16 blocks (0,1) and (2,3): the
-        // combines below read whole 32x32 blocks
-        for (int e = t - 64; e < 512; e += 64) {
-          const int blk = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-          Tf[(blk * 32 + r) * AS + blk * 32 + 16 + cc] = 0.f;
-        }
-      }
-      named_bar(2, 128);
-      {
-        // 32x32 blocks: T[2p+1][2p] = -T[2p+1][2p+1] A[2p+1][2p] T[2p][2p]
-        const int p = t >> 6, rem = t & 63, r = rem >> 2, c4 = (rem & 3) * 4;
-        const int rb = 16 * (2 * p + 1), cb = 16 * (2 * p);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-          const float av = Af[(rb + r) * AS + cb + k];
-          const float4 tv = *reinterpret_cast<const float4*>(&Tf[(cb + k) * AS + cb + c4]);
-          acc.x = fmaf(av, tv.x, acc.x);
-          acc.y = fmaf(av, tv.y, acc.y);
-          acc.z = fmaf(av, tv.z, acc.z);
-          acc.w = fmaf(av, tv.w, acc.w);
-        }
-        *reinterpret_cast<float4*>(&X1[(p * 16 + r) * 20 + c4]) = acc;
-        named_bar(2, 128);
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int k = 0; k < 16; k++) {
-          const float tv = Tf[(rb + r) * AS + rb + k];
-          const float4 xv = *reinterpret_cast<const float4*>(&X1[(p * 16 + k) * 20 + c4]);
-          o.x = fmaf(tv, xv.x, o.x);
-          o.y = fmaf(tv, xv.y, o.y);
-          o.z = fmaf(tv, xv.z, o.z);
-          o.w = fmaf(tv, xv.w, o.w);
-        }
-        *reinterpret_cast<float4*>(&Tf[(rb + r) * AS + cb + c4]) = make_float4(-o.x, -o.y, -o.z, -o.w);
-      }
-      named_bar(2, 128);
-      {
-        // 64x64: T[32:64][0:32] = -T[32:64][32:64] A[32:64][0:32] T[0:32][0:32]
-        const int r = t >> 2, c8 = (t & 3) * 8;
-        float acc[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) acc[u] = 0.f;
-#pragma unroll 8
-        for (int k = 0; k < 32; k++) {
-          const float av = Af[(32 + r) * AS + k];
-          const float4 t0v = *reinterpret_cast<const float4*>(&Tf[k * AS + c8]);
-          const float4 t1v = *reinterpret_cast<const float4*>(&Tf[k * AS + c8 + 4]);
-          acc[0] = fmaf(av, t0v.x, acc[0]);
-          acc[1] = fmaf(av, t0v.y, acc[1]);
-          acc[2] = fmaf(av, t0v.z, acc[2]);
-          acc[3] = fmaf(av, t0v.w, acc[3]);
-          acc[4] = fmaf(av, t1v.x, acc[4]);
-          acc[5] = fmaf(av, t1v.y, acc[5]);
-          acc[6] = fmaf(av, t1v.z, acc[6]);
-          acc[7] = fmaf(av, t1v.w, acc[7]);
-        }
-        *reinterpret_cast<float4*>(&X2[r * 36 + c8]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        *reinterpret_cast<float4*>(&X2[r * 36 + c8 + 4]) = make_float4(acc[4], acc[5], acc[6], acc[7]);
-        named_bar(2, 128);
-#pragma unroll
-        for (int u = 0; u < 8; u++) acc[u] = 0.f;
-#pragma unroll 8
-        for (int k = 0; k < 32; k++) {
-          const float tv = Tf[(32 + r) * AS + 32 + k];
-          const float4 x0 = *reinterpret_cast<const float4*>(&X2[k * 36 + c8]);
-          const float4 x1 = *reinterpret_cast<const float4*>(&X2[k * 36 + c8 + 4]);
-          acc[0] = fmaf(tv, x0.x, acc[0]);
-          acc[1] = fmaf(tv, x0.y, acc[1]);
-          acc[2] = fmaf(tv, x0.z, acc[2]);
-          acc[3] = fmaf(tv, x0.w, acc[3]);
-          acc[4] = fmaf(tv, x1.x, acc[4]);
-          acc[5] = fmaf(tv, x1.y, acc[5]);
-          acc[6] = fmaf(tv, x1.z, acc[6]);
-          acc[7] = fmaf(tv, x1.w, acc[7]);
-        }
-        *reinterpret_cast<float4*>(&Tf[(32 + r) * AS + c8]) = make_float4(-acc[0], -acc[1], -acc[2], -acc[3]);
-        *reinterpret_cast<float4*>(&Tf[(32 + r) * AS + c8 + 4]) = make_float4(-acc[4], -acc[5], -acc[6], -acc[7]);
-      }
-      named_bar(2, 128);
-      if (t < 64) {
-        float y[64];
-#pragma unroll
-        for (int j = 0; j < 64; j++) y[j] = j < t ? Tf[t * AS + j] : (j == t ? 1.f : 0.f);
-        store_row64(sm + OFF_TB + x * 8192, t, y);
-      }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_T[x]);
-    }
-  } else if (warp >= 8) {
-    // ---------------- chain warpgroup: state-dependent part of each chunk ----------------
-    const int q4 = warp - 8;
-    const int t = q4 * 32 + lane;            // state row (dk) for M = 128 accumulators
-    const uint32_t lo = (uint32_t)(q4 * 32) << 16;
-    const int r64 = q4 * 16 + lane;          // row of an M = 64 accumulator (valid when lane < 16)
-    uint8_t* s0b = sm + OFF_S0B;
-    {
-      float st[64];
-      if (a.load_state) {
-        const float4* src = reinterpret_cast<const float4*>(
-            a.state_in + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * DVB);
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const float4 v = __ldg(src + i);
-          st[4 * i] = v.x;
-          st[4 * i + 1] = v.y;
-          st[4 * i + 2] = v.z;
-          st[4 * i + 3] = v.w;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; i++) st[i] = 0.f;
-      }
-      tmem_st64(tmem + lo + TC_S, st);
-      store_row64(s0b, t, st);
-      fence_proxy_async();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_s0);
-    }
-    for (int c = 0; c < n; c++) {
-      const int x = c & 1;
-      const float* gam2 = scal + x * 256;
-      const float* betv = gam2 + 64;
-      const float* ikv = gam2 + 128;
-      const float* iqv = gam2 + 192;
-      const uint8_t* vt = sm + OFF_V + (c & 1) * V_BYTES;
-      // R = diag(beta) (V - diag(Gamma ik) K S0)
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_a, c & 1, a.status))) break;
+      // S1 = e S0 + U, and its bf16 copy for the next chunk
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_e, ph, a.status));
+      if (!ok) break;
       tc_fence_after();
-      float xr[64];
-      tmem_ld64(tmem + lo + TC_X, xr);
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar_T[x], (c >> 1) & 1, a.status))) break;
-      if (lane < 16) {
-        const int i = r64;
-        float v[64];
-        load_row64(vt, i, v);
-        const float bi = betv[i], ci = fast_ex2(gam2[i]) * ikv[i];
+      const float e = sc[192];
 #pragma unroll
-        for (int j = 0; j < 64; j++) v[j] = bi * fmaf(-ci, xr[j], v[j]);
-        store_row64(sm + OFF_RB, i, v);
-      }
-      fence_proxy_async();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_R);
-      // Delta for (d) and (e); state *= exp(gamma_63)
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_c, c & 1, a.status))) break;
-      tc_fence_after();
-      const float g63 = gam2[63];
-      {
-        float dl[64];
-        tmem_ld64(tmem + lo + TC_DL, dl);
-        if (lane < 16) {
-          const int i = r64;
-          store_row64(sm + OFF_DB, i, dl);
-          const float si = ikv[i] * fast_ex2(g63 - gam2[i]);
+      for (int hf = 0; hf < 2; hf++) {
+        uint32_t ur[32];
+        tmem_ld32(tmem + lo + TC_P + 32 * hf, ur);
+        tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 64; j++) dl[j] *= si;
-          store_row64(sm + OFF_DSB, i, dl);
-        }
-        float st[64];
-        tmem_ld64(tmem + lo + TC_S, st);
-        const float dec = fast_ex2(g63);
+        for (int j = 0; j < 32; j++) st[32 * hf + j] = fmaf(e, st[32 * hf + j], __uint_as_float(ur[j]));
 #pragma unroll
-        for (int j = 0; j < 64; j++) st[j] *= dec;
-        tmem_st64(tmem + lo + TC_S, st);
-      }
-      fence_proxy_async();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_D);
-      // outputs O = diag(Gamma iq) Q S0 + QKm Delta, and the next bf16 state
-      if (!__all_sync(0xffffffffu, mbar_wait(bar_d, c & 1, a.status))) break;
-      tc_fence_after();
-      {
-        float qs[64], o2[64];
-        tmem_ld64(tmem + lo + TC_QS, qs);
-        tmem_ld64(tmem + lo + TC_O2, o2);
-        const int tok = c * GC + r64;
-        if (lane < 16 && tok < a.T) {
-          const float cq = fast_ex2(gam2[r64]) * iqv[r64];
-          float4* dst = reinterpret_cast<float4*>(a.core + (((size_t)b * a.T + tok) * a.NV + h) * GD + dvb * DVB);
-#pragma unroll
-          for (int i = 0; i < 16; i++)
-            dst[i] = make_float4(fmaf(cq, qs[4 * i], o2[4 * i]), fmaf(cq, qs[4 * i + 1], o2[4 * i + 1]),
-                                 fmaf(cq, qs[4 * i + 2], o2[4 * i + 2]), fmaf(cq, qs[4 * i + 3], o2[4 * i + 3]));
-        }
-        float st[64];
-        tmem_ld64(tmem + lo + TC_S, st);
-        store_row64(s0b, t, st);
-        if (c == n - 1) {
-          float4* dst = reinterpret_cast<float4*>(a.state_out + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * DVB);
-#pragma unroll
-          for (int i = 0; i < 16; i++) dst[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
-        }
+        for (int u = 0; u < 4; u++)
+          *reinterpret_cast<uint4*>(s0b + sw128_offset(t, 64 * hf + 16 * u)) = pack8(st + 32 * hf + 8 * u);
       }
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(bar_s0);
-        mbar_arrive(&pfree[x]);
+        mbar_arrive(&sc_empty[c & 1]);
       }
+    }
+    if (ok) {
+      float4* dst = reinterpret_cast<float4*>(a.state_out + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * DVB);
+#pragma unroll
+      for (int i = 0; i < 16; i++) dst[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
     }
   }
   tc_fence_before();
@@ -571,7 +808,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1)
   tc_fence_after();
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tmem_dealloc(tmem, C_TMEM_COLS);
   }
 }
 
@@ -589,7 +826,8 @@ extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_
   const long long B = p->B, T = p->T, NK = p->NK, NV = p->NV;
   if (B < 1 || T < 1 || NK < 1 || NV < 1) return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: empty shape");
   if (p->D != hcu::GD) return fail(HCU_EUNSUPPORTED, "hcu_deltanet_chunked_prefill: D=%u (built: 128)", p->D);
-  if (B > 65535 || NV > 65535) return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: B or NV > 65535");
+  if (B > 65535 || NV > 65535 || NK > 65535)
+    return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: B, NK or NV > 65535");
   const long long qrow = p->q_row_stride ? (long long)p->q_row_stride : NK * 128;
   const long long krow = p->k_row_stride ? (long long)p->k_row_stride : NK * 128;
   const long long vrow = p->v_row_stride ? (long long)p->v_row_stride : NV * 128;
@@ -599,7 +837,7 @@ extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_
   if (reinterpret_cast<uintptr_t>(core) % 16 || reinterpret_cast<uintptr_t>(state_out) % 16 ||
       (p->load_state && reinterpret_cast<uintptr_t>(state_in) % 16))
     return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: core / state buffers must be 16-byte aligned");
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, tw, ts;
   {
     uint64_t dims[4] = {128, (uint64_t)NK, (uint64_t)T, (uint64_t)B};
     uint64_t st[3] = {256, (uint64_t)qrow * 2, (uint64_t)qseq * 2};
@@ -617,29 +855,87 @@ extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_
     HCU_TRY(hcu::make_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(v), dims, st, box,
                                  CU_TENSOR_MAP_SWIZZLE_128B));
   }
-  hcu::GdnArgs args{};
-  args.B = (int)B;
-  args.T = (int)T;
-  args.NK = (int)NK;
-  args.NV = (int)NV;
-  args.load_state = p->load_state ? 1 : 0;
-  args.nchunks = (int)((T + hcu::GC - 1) / hcu::GC);
-  args.g = g;
-  args.beta = beta;
-  args.gb_row = p->gb_row_stride ? (long long)p->gb_row_stride : NV;
-  args.gb_seq = p->gb_seq_stride ? (long long)p->gb_seq_stride : T * args.gb_row;
-  args.state_in = state_in;
-  args.core = core;
-  args.state_out = state_out;
-  args.status = h->dev_status;
+  // Scratch: the prep outputs of one slab of chunks (17 KB per sequence, V head
+  // and chunk).  The slab is as long as the scratch budget allows
+  // (HCU_GDN_SCRATCH_MB, default 1 GiB: one slab for 8 x 8192 tokens x 32 heads).
+  const long long nchunks = (T + hcu::GC - 1) / hcu::GC;
+  const long long per_chunk = B * NV * (long long)hcu::UNIT_BYTES;
+  long long budget = 1024ll << 20;
+  if (const char* env = getenv("HCU_GDN_SCRATCH_MB")) {
+    const long long mb = atoll(env);
+    if (mb > 0) budget = mb << 20;
+  }
+  long long ns = budget / per_chunk;
+  if (ns < 1) ns = 1;
+  if (ns > nchunks) ns = nchunks;
+  const long long nslab = (nchunks + ns - 1) / ns;
+  ns = (nchunks + nslab - 1) / nslab;  // even slabs
+  const long long units = B * NV * ns;
+  if (units * 128 > 0x7fffffffll)
+    return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: %lld units per slab exceed the TMA range", units);
+  HCU_TRY(hcu::ensure_scratch(h, (size_t)units * hcu::UNIT_BYTES, "hcu_deltanet_chunked_prefill"));
+  auto* wbuf = reinterpret_cast<__nv_bfloat16*>(h->scratch);  // [units][128][64] bf16
+  auto* sbuf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(h->scratch) + (size_t)units * hcu::W_ELEMS * 2);
+  {
+    uint64_t dims[2] = {64, (uint64_t)units * 128};
+    uint64_t st[1] = {128};
+    uint32_t box[2] = {64, 128};
+    HCU_TRY(hcu::make_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wbuf, dims, st, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B));
+    uint64_t sdims[2] = {64, (uint64_t)units * 4};
+    uint64_t sst[1] = {256};
+    uint32_t sbox[2] = {64, 4};
+    HCU_TRY(hcu::make_tensor_map(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, sbuf, sdims, sst, sbox,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE));
+  }
   static bool attr_done = false;
   if (!attr_done) {
-    HCU_TRY(hcu::check_cuda(cudaFuncSetAttribute(hcu::gdn_chunked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 hcu::SMEM_BYTES + 1024),
+    HCU_TRY(hcu::check_cuda(cudaFuncSetAttribute(hcu::gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 hcu::P_SMEM + 1024),
+                            "hcu_deltanet_chunked_prefill: smem attribute"));
+    HCU_TRY(hcu::check_cuda(cudaFuncSetAttribute(hcu::gdn_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 hcu::C_SMEM + 1024),
                             "hcu_deltanet_chunked_prefill: smem attribute"));
     attr_done = true;
   }
-  hcu::gdn_chunked_kernel<<<dim3(hcu::GD / hcu::DVB, (unsigned)NV, (unsigned)B), hcu::GT_THREADS,
-                            hcu::SMEM_BYTES + 1024, h->stream>>>(tq, tk, tv, args);
-  return hcu::after_launch("hcu_deltanet_chunked_prefill: launch");
+  const long long gb_row = p->gb_row_stride ? (long long)p->gb_row_stride : NV;
+  const long long gb_seq = p->gb_seq_stride ? (long long)p->gb_seq_stride : T * gb_row;
+  const long long npair = ((NV + NK - 1) / NK + 1) / 2;  // V heads per QK head, two per prep CTA
+  if (NK * npair > 65535) return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: too many heads");
+  for (long long s = 0; s < nslab; s++) {
+    const long long c0 = s * ns;
+    const long long cnt = nchunks - c0 < ns ? nchunks - c0 : ns;
+    hcu::PrepArgs pa{};
+    pa.T = (int)T;
+    pa.NK = (int)NK;
+    pa.NV = (int)NV;
+    pa.c0 = (int)c0;
+    pa.ns = (int)ns;
+    pa.g = g;
+    pa.beta = beta;
+    pa.gb_row = gb_row;
+    pa.gb_seq = gb_seq;
+    pa.sc = sbuf;
+    pa.status = h->dev_status;
+    hcu::gdn_prep_kernel<<<dim3((unsigned)cnt, (unsigned)(NK * npair), (unsigned)B), hcu::PREP_THREADS,
+                           hcu::P_SMEM + 1024, h->stream>>>(tq, tk, tw, pa);
+    HCU_TRY(hcu::after_launch("hcu_deltanet_chunked_prefill: prep launch"));
+    hcu::ChainArgs ca{};
+    ca.T = (int)T;
+    ca.NK = (int)NK;
+    ca.NV = (int)NV;
+    ca.c0 = (int)c0;
+    ca.ns = (int)ns;
+    ca.cnt = (int)cnt;
+    ca.load_state = (s > 0 || p->load_state) ? 1 : 0;
+    ca.v8 = reinterpret_cast<uintptr_t>(core) % 32 == 0 ? 1 : 0;
+    ca.state_in = s > 0 ? state_out : state_in;
+    ca.core = core;
+    ca.state_out = state_out;
+    ca.status = h->dev_status;
+    hcu::gdn_chain_kernel<<<dim3(hcu::GD / hcu::DVB, (unsigned)NV, (unsigned)B), hcu::CHAIN_THREADS,
+                            hcu::C_SMEM + 1024, h->stream>>>(tq, tk, tv, tw, ts, ca);
+    HCU_TRY(hcu::after_launch("hcu_deltanet_chunked_prefill: chain launch"));
+  }
+  return HCU_OK;
 }

@@ -38,6 +38,14 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a
          | ((uint32_t)(M >> 4) << 24);               // M / 16
 }
 
+// kind::tf32 instruction descriptor: f32 accumulate, tf32 A/B (format 2), M x N.
+// Only K-major operands are used with it here: an MN-major tf32 operand needs
+// the 32-byte-atom 128B swizzle, not the plain SW128 layout these kernels use.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 // Byte offset of (row, byte_in_row) inside a 128B-swizzled region whose rows
 // are 128 B and whose base is 1024-B aligned (16-byte chunk index XOR row % 8).
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t byte_in_row) {
@@ -74,6 +82,37 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// D (+)= A * B with tf32 operands (K = 8 per instruction) read from shared memory.
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D (+)= A * B with tf32 operands, A read from TMEM (lane = row, one column per
+// element, K = 8 per instruction) and B from shared memory.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// f32 rounded to the nearest tf32 value (10-bit mantissa), so tf32 MMA
+// operands carry rounding rather than truncation error.
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t y;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(y) : "f"(x));
+  return __uint_as_float(y);
 }
 
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread
