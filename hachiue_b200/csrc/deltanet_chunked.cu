@@ -71,7 +71,8 @@ static_assert(P_OFF_X1 + 2 * 2560 <= 32768, "prep X scratch");
 constexpr int CHAIN_THREADS = 192;
 constexpr int C_OFF_KQ = 0;         // [d0: K | Q][d1: K | Q] bf16, A operand of [K;Q] S0
 constexpr int C_OFF_KE = 32768;     // [d0: K][d1: K] bf16, A operand (MN-major) of K^T Dsb
-constexpr int C_OFF_W = 49152;      // W, 128 rows K-major
+constexpr int C_OFF_W = 49152;      // W, 128 rows K-major; after MMA (c) the chunk's f32 outputs
+                                    // [64 tokens][2 x 32 values] (two 128B-swizzled halves) for a TMA store
 constexpr int C_OFF_S0B = 65536;    // [128 dk][64 dv] bf16 state, MN-major B operand
 constexpr int C_OFF_V = 81920;      // [64 tokens][64 values] bf16
 constexpr int C_OFF_RB = 90112;     // R', MN-major B operand
@@ -93,7 +94,7 @@ struct PrepArgs {
 };
 
 struct ChainArgs {
-  int T, NK, NV, c0, ns, cnt, load_state, v8;
+  int T, NK, NV, c0, ns, cnt, load_state;
   const float* state_in;
   float* core;
   float* state_out;
@@ -517,7 +518,8 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
 __global__ void __launch_bounds__(CHAIN_THREADS, 2)
     gdn_chain_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
-                     const __grid_constant__ CUtensorMap tmS, const ChainArgs a) {
+                     const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmO,
+                     const ChainArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C_OFF_BAR);
@@ -528,7 +530,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
   uint64_t* v_full = bars + 4;
   uint64_t* v_empty = bars + 5;   // R' written
   uint64_t* w_full = bars + 6;
-  uint64_t* w_empty = bars + 7;   // MMA c done
+  uint64_t* o_ready = bars + 7;   // MMA c done and the chunk's outputs staged in W's place
   uint64_t* sc_full = bars + 8;   // [2]
   uint64_t* sc_empty = bars + 10; // [2] chunk finished by the chain warps
   uint64_t* bar_a = bars + 12;    // [X; QS] in TMEM
@@ -554,7 +556,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
     mbar_init(v_full, 1);
     mbar_init(v_empty, 2);
     mbar_init(w_full, 1);
-    mbar_init(w_empty, 1);
+    mbar_init(o_ready, 2);
     for (int i = 0; i < 2; i++) {
       mbar_init(&sc_full[i], 1);
       mbar_init(&sc_empty[i], 4);
@@ -584,7 +586,17 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
       prefetch_tensormap(&tmV);
       prefetch_tensormap(&tmW);
       prefetch_tensormap(&tmS);
-      for (int c = 0; c < n; c++) {
+      prefetch_tensormap(&tmO);
+      // outputs of chunk j: staged by the output warps in W's buffer, stored here
+      auto store_outputs = [&](int j) {
+        const int tj = (a.c0 + j) * GC;
+        tma_store_4d(&tmO, sm + C_OFF_W, dvb * DVB, h, tj, b);
+        tma_store_4d(&tmO, sm + C_OFF_W + 8192, dvb * DVB + 32, h, tj, b);
+        tma_store_commit();
+        tma_store_wait_read();
+      };
+      int c = 0;
+      for (; c < n; c++) {
         const int t0 = (a.c0 + c) * GC;
         const int u = (int)(unit0 + c);
         const uint32_t pe = (c - 1) & 1;
@@ -600,7 +612,10 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
         if (c >= 2 && !mbar_wait(&sc_empty[c & 1], ((c - 2) >> 1) & 1, a.status)) break;
         mbar_arrive_expect_tx(&sc_full[c & 1], SC_FLOATS * 4);
         tma_load_2d(scal + (c & 1) * SC_FLOATS, &tmS, &sc_full[c & 1], 0, u * 4);
-        if (c >= 1 && !mbar_wait(w_empty, pe, a.status)) break;
+        if (c >= 1) {
+          if (!mbar_wait(o_ready, pe, a.status)) break;
+          store_outputs(c - 1);
+        }
         mbar_arrive_expect_tx(w_full, W_ELEMS * 2);
         tma_load_2d(sm + C_OFF_W, &tmW, w_full, 0, u * 128);
         if (c >= 1 && !mbar_wait(ke_empty, pe, a.status)) break;
@@ -608,6 +623,8 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
         tma_load_4d(sm + C_OFF_KE, &tmK, ke_full, 0, hk, t0, b);
         tma_load_4d(sm + C_OFF_KE + 8192, &tmK, ke_full, 64, hk, t0, b);
       }
+      if (c == n && n > 0 && mbar_wait(o_ready, (n - 1) & 1, a.status)) store_outputs(n - 1);
+      tma_store_wait_all();
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -634,7 +651,6 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
           mma_f16_ss(tmem + TC_Q, smem_desc_sw128(s0 + C_OFF_W + ks * 32, 16, 1024),
                      smem_desc_sw128(s0 + C_OFF_RB + ks * 2048, 8192, 1024), id_n64, ks > 0);
         mma_commit(bar_c);
-        mma_commit(w_empty);
         // (e) U = K^T Dsb   (M = 128, N = 64, K = 64)
         if (!mbar_wait(bar_D, ph, a.status) || !mbar_wait(ke_full, ph, a.status)) break;
         tc_fence_after();
@@ -678,13 +694,17 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
       const uint32_t ph = c & 1;
       const float* sc = scal + (c & 1) * SC_FLOATS;
       if (quad < 2) {
-        // R'_t = V_t - c2_t X_t   (token t)
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_a, ph, a.status) && mbar_wait(v_full, ph, a.status) &&
-                                         mbar_wait(&sc_full[c & 1], (c >> 1) & 1, a.status));
+        // R'_t = V_t - c2_t X_t   (token t); V's row is read before X lands
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(v_full, ph, a.status) && mbar_wait(&sc_full[c & 1], (c >> 1) & 1, a.status));
+        if (!ok) break;
+        const float c2 = sc[t];
+        uint4 vrow[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) vrow[u] = *reinterpret_cast<const uint4*>(sm + C_OFF_V + sw128_offset(t, 16 * u));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_a, ph, a.status));
         if (!ok) break;
         tc_fence_after();
-        const float c2 = sc[t];
-        const uint8_t* vt = sm + C_OFF_V;
 #pragma unroll
         for (int hf = 0; hf < 2; hf++) {
           uint32_t xr[32];
@@ -693,7 +713,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
 #pragma unroll
           for (int u = 0; u < 4; u++) {
             const uint32_t off = sw128_offset(t, 64 * hf + 16 * u);
-            const uint4 vw = *reinterpret_cast<const uint4*>(vt + off);
+            const uint4 vw = vrow[4 * hf + u];
             const uint32_t vs[4] = {vw.x, vw.y, vw.z, vw.w};
             float r[8];
 #pragma unroll
@@ -743,8 +763,6 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
         tc_fence_after();
         const int i = t - 64;
         const float c3 = sc[64 + i];
-        const int tok = (a.c0 + c) * GC + i;
-        float4* dst = reinterpret_cast<float4*>(a.core + (((size_t)b * a.T + tok) * a.NV + h) * GD + dvb * DVB);
 #pragma unroll
         for (int hf = 0; hf < 2; hf++) {
           uint32_t qs[32], o2[32];
@@ -756,22 +774,19 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_D);
           }
-          if (tok < a.T) {
-            float o[32];
+          // row i of the staged outputs: 32 f32 = one 128-byte swizzled row of half hf
+          uint8_t* orow = sm + C_OFF_W + hf * 8192;
 #pragma unroll
-            for (int j = 0; j < 32; j++) o[j] = fmaf(c3, __uint_as_float(qs[j]), __uint_as_float(o2[j]));
-            if (a.v8) {
-#pragma unroll
-              for (int u = 0; u < 4; u++)
-                st_global_v8(reinterpret_cast<float*>(dst + 8 * hf + 2 * u), o[8 * u], o[8 * u + 1], o[8 * u + 2],
-                             o[8 * u + 3], o[8 * u + 4], o[8 * u + 5], o[8 * u + 6], o[8 * u + 7]);
-            } else {
-#pragma unroll
-              for (int u = 0; u < 8; u++)
-                dst[8 * hf + u] = make_float4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
-            }
-          }
+          for (int u = 0; u < 8; u++)
+            *reinterpret_cast<float4*>(orow + sw128_offset(i, 16 * u)) =
+                make_float4(fmaf(c3, __uint_as_float(qs[4 * u]), __uint_as_float(o2[4 * u])),
+                            fmaf(c3, __uint_as_float(qs[4 * u + 1]), __uint_as_float(o2[4 * u + 1])),
+                            fmaf(c3, __uint_as_float(qs[4 * u + 2]), __uint_as_float(o2[4 * u + 2])),
+                            fmaf(c3, __uint_as_float(qs[4 * u + 3]), __uint_as_float(o2[4 * u + 3])));
         }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_ready);
       }
       // S1 = e S0 + U, and its bf16 copy for the next chunk
       ok = __all_sync(0xffffffffu, mbar_wait(bar_e, ph, a.status));
@@ -837,7 +852,7 @@ extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_
   if (reinterpret_cast<uintptr_t>(core) % 16 || reinterpret_cast<uintptr_t>(state_out) % 16 ||
       (p->load_state && reinterpret_cast<uintptr_t>(state_in) % 16))
     return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: core / state buffers must be 16-byte aligned");
-  CUtensorMap tq, tk, tv, tw, ts;
+  CUtensorMap tq, tk, tv, tw, ts, to;
   {
     uint64_t dims[4] = {128, (uint64_t)NK, (uint64_t)T, (uint64_t)B};
     uint64_t st[3] = {256, (uint64_t)qrow * 2, (uint64_t)qseq * 2};
@@ -853,6 +868,11 @@ extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_
     uint64_t st[3] = {256, (uint64_t)vrow * 2, (uint64_t)vseq * 2};
     uint32_t box[4] = {64, 1, 64, 1};
     HCU_TRY(hcu::make_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(v), dims, st, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B));
+    // outputs core [B][T][NV][128] f32, stored 32 values x 64 tokens at a time
+    uint64_t ost[3] = {512, (uint64_t)NV * 512, (uint64_t)T * NV * 512};
+    uint32_t obox[4] = {32, 1, 64, 1};
+    HCU_TRY(hcu::make_tensor_map(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, core, dims, ost, obox,
                                  CU_TENSOR_MAP_SWIZZLE_128B));
   }
   // Scratch: the prep outputs of one slab of chunks (17 KB per sequence, V head
@@ -928,13 +948,12 @@ extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_
     ca.ns = (int)ns;
     ca.cnt = (int)cnt;
     ca.load_state = (s > 0 || p->load_state) ? 1 : 0;
-    ca.v8 = reinterpret_cast<uintptr_t>(core) % 32 == 0 ? 1 : 0;
     ca.state_in = s > 0 ? state_out : state_in;
     ca.core = core;
     ca.state_out = state_out;
     ca.status = h->dev_status;
     hcu::gdn_chain_kernel<<<dim3(hcu::GD / hcu::DVB, (unsigned)NV, (unsigned)B), hcu::CHAIN_THREADS,
-                            hcu::C_SMEM + 1024, h->stream>>>(tq, tk, tv, tw, ts, ca);
+                            hcu::C_SMEM + 1024, h->stream>>>(tq, tk, tv, tw, ts, to, ca);
     HCU_TRY(hcu::after_launch("hcu_deltanet_chunked_prefill: chain launch"));
   }
   return HCU_OK;
