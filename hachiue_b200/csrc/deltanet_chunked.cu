@@ -49,23 +49,33 @@ constexpr int SC_FLOATS = 4 * 64;  // c2, c3, c4, e (e repeated)
 constexpr size_t UNIT_BYTES = W_ELEMS * 2 + SC_FLOATS * 4;
 
 // ---------------- prep kernel layout ----------------
-// f32 64 x 64 matrices (A, T) are stored as two 64 x 32 column halves of
-// 128-byte swizzled rows (8 KB each), the tf32 K-major MMA operand layout.
+// The CUDA-core phases keep A and T in plain padded f32 arrays; the tf32 MMAs
+// of the 64x64 combine read small 128-byte-swizzled K-major copies (A21, U11,
+// T22), whose M = 64 reads run over 32 neighbouring rows that are not used.
 // TMEM: [K;Q][K;Q]^T in columns 0-127 (whose lanes 64-127 later hold
 // warpgroup w's QKm in columns 64w..64w+63, the A operand of QKm Tb), then per
-// warpgroup 64 columns for the 64x64 combine products and QKm Tb.
+// warpgroup 64 columns for the combine products and QKm Tb.
 constexpr int PREP_THREADS = 256;
-constexpr int P_OFF_KQ = 0;      // [d-block 0: K rows | Q rows][d-block 1: same], 32 KB; after (f):
-constexpr int P_OFF_U11 = 0;     //   [2 WG] U11 = (T[0:32][0:32])^T f32, 64-row K-major tile (8 KB each)
-constexpr int P_OFF_X2 = 16384;  //   [2 WG] X2^T f32 32 x 32, K-major B operand (4 KB each)
-constexpr int P_OFF_X1 = 24576;  //   [2 WG] X1 f32 [2][16][20] (2560 B each)
-constexpr int P_OFF_WG = 32768;  // [2 WG] A (16 KB), T (16 KB), scalars; A's bytes later stage W
-constexpr int P_WG_STRIDE = 34816;
+constexpr int AS = 68;           // row stride (floats) of T
+constexpr int AD = 36;           // row stride (floats) of A's diagonal 32x32 blocks
+constexpr int P_OFF_KQ = 0;      // K / Q chunk (32 KB); after (f) warpgroup w owns bytes [16w, 16w + 16) KB:
+constexpr int P_KQ_U11 = 0;      //   U11 = T[0:32][0:32]^T, 32 swizzled rows
+constexpr int P_KQ_X2T = 4096;   //   X2^T, 32 swizzled rows
+constexpr int P_KQ_X1 = 8192;    //   X1 [2][16][20]
+                                 //   and, once those are read, W = [Tb; QKm Tb] bf16 (128 swizzled rows)
+constexpr int P_OFF_WG = 32768;  // per warpgroup:
+constexpr int P_WG_A21 = 0;      //   A[32:64][0:32], 32 swizzled rows
+constexpr int P_WG_T22 = 4096;   //   T[32:64][32:64], 32 swizzled rows (A21's rows precede it)
+constexpr int P_WG_T = 8192;     //   T [64][AS]; later Tb^T as two swizzled 64 x 32 halves
+constexpr int P_WG_A = 25600;    //   A's diagonal 32x32 blocks [2][32][AD]
+constexpr int P_WG_SC = 34816;   //   gam2, beta, ik, iq, w [64] + misc[16]
+constexpr int P_WG_STRIDE = 36864;
 constexpr int P_OFF_BAR = P_OFF_WG + 2 * P_WG_STRIDE;
 constexpr int P_NBAR = 8;
 constexpr int P_SMEM = P_OFF_BAR + P_NBAR * 8 + 16;
-static_assert(32768 + (5 * 64 + 16) * 4 <= P_WG_STRIDE, "prep warpgroup region");
-static_assert(P_OFF_X1 + 2 * 2560 <= 32768, "prep X scratch");
+static_assert(P_WG_T + 64 * AS * 4 <= P_WG_A && P_WG_A + 2 * 32 * AD * 4 <= P_WG_SC, "prep warpgroup layout");
+static_assert(P_WG_SC + (5 * 64 + 16) * 4 <= P_WG_STRIDE, "prep warpgroup region");
+static_assert(P_KQ_X1 + 2 * 16 * 20 * 4 <= 16384, "prep K/Q reuse");
 
 // ---------------- chain kernel layout ----------------
 constexpr int CHAIN_THREADS = 192;
@@ -211,18 +221,22 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
   const bool active = h < a.NV;
   {
     uint8_t* wreg = sm + P_OFF_WG + wg * P_WG_STRIDE;
-    float* Aw = reinterpret_cast<float*>(wreg);            // A, swizzled halves
-    float* Tw = reinterpret_cast<float*>(wreg + 16384);    // T, swizzled halves; later Tb^T
-    float* gam2 = reinterpret_cast<float*>(wreg + 32768);  // gamma * log2(e)
+    uint8_t* kqh = sm + P_OFF_KQ + wg * 16384;  // this warpgroup's half of the K/Q buffer, after (f)
+    float* A21 = reinterpret_cast<float*>(wreg + P_WG_A21);
+    float* T22 = reinterpret_cast<float*>(wreg + P_WG_T22);
+    float* Tf = reinterpret_cast<float*>(wreg + P_WG_T);
+    float* TbT = Tf;  // swf layout, once T has been read
+    float* Ad = reinterpret_cast<float*>(wreg + P_WG_A);
+    float* gam2 = reinterpret_cast<float*>(wreg + P_WG_SC);  // gamma * log2(e)
     float* betv = gam2 + 64;
     float* ikv = gam2 + 128;
     float* iqv = gam2 + 192;
     float* wv = gam2 + 256;  // gam2_j - log2(ik_j)
     float* misc = gam2 + 320;
-    float* X1 = reinterpret_cast<float*>(sm + P_OFF_X1 + wg * 2560);
-    float* X2T = reinterpret_cast<float*>(sm + P_OFF_X2 + wg * 4096);
-    float* U11 = reinterpret_cast<float*>(sm + P_OFF_U11 + wg * 8192);
-    uint8_t* wst = wreg;  // W staging [Tb; QKm Tb] bf16, 128 swizzled rows (A is dead by then)
+    float* U11 = reinterpret_cast<float*>(kqh + P_KQ_U11);
+    float* X2T = reinterpret_cast<float*>(kqh + P_KQ_X2T);
+    float* X1 = reinterpret_cast<float*>(kqh + P_KQ_X1);
+    uint8_t* wst = kqh;  // W staging
     const uint32_t lo = (uint32_t)(quad * 32) << 16;
     const uint32_t tl3 = tmem + 128 + 64 * wg;  // 64x64 combine products, later QKm Tb
     const uint32_t bid = 1 + wg;
@@ -274,12 +288,11 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       named_bar(bid, 128);
       // A_tj = 2^(z_t - w_j) f_j with z_t = gam2_t + log2(beta_t ik_t); QKm likewise
       // with z_i = gam2_i + log2(iq_i).  Entries outside the triangle are selected
-      // away (their exponent may overflow); rows 0-31 only have columns 0-31.
+      // away (their exponent may overflow).  All values are rounded to tf32.
       if (t < 64) {
         const float z = gam2[t] + __log2f(betv[t] * ikv[t]);
-#pragma unroll
-        for (int u = 0; u < 16; u++) {
-          if (u >= 8 && quad == 0) break;
+        const int r = t & 31;
+        auto a4 = [&](int u) {
           const float4 w4 = reinterpret_cast<const float4*>(wv)[u];
           const int j = 4 * u;
           float4 o;
@@ -287,7 +300,16 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
           o.y = j + 1 < t ? tf32_round(fast_ex2(z - w4.y) * f[j + 1]) : 0.f;
           o.z = j + 2 < t ? tf32_round(fast_ex2(z - w4.z) * f[j + 2]) : 0.f;
           o.w = j + 3 < t ? tf32_round(fast_ex2(z - w4.w) * f[j + 3]) : 0.f;
-          *reinterpret_cast<float4*>(Aw + swf(t, j)) = o;
+          return o;
+        };
+        if (quad == 0) {
+#pragma unroll
+          for (int u = 0; u < 8; u++) *reinterpret_cast<float4*>(Ad + r * AD + 4 * u) = a4(u);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; u++) *reinterpret_cast<float4*>(A21 + r * 32 + ((u ^ (r & 7)) << 2)) = a4(u);
+#pragma unroll
+          for (int u = 8; u < 16; u++) *reinterpret_cast<float4*>(Ad + 32 * AD + r * AD + 4 * (u - 8)) = a4(u);
         }
       } else {
         const int i = t - 64;
@@ -316,35 +338,27 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         tc_fence_before();
       }
       named_bar(bid, 128);
-      // (I + A)^-1: 16x16 diagonal blocks by forward substitution.  Thread cc
-      // of a block computes its column, which is also row cc of U = T^T; the
-      // tf32 MMAs below take K-major operands only, so U11 = (T[0:32][0:32])^T
-      // is kept beside T.
+      // (I + A)^-1: 16x16 diagonal blocks by forward substitution, thread cc of
+      // a block computing its column
       if (t < 64) {
         const int base = (t >> 4) * 16, cc = t & 15;
+        const float* ab = Ad + (base >> 5) * 32 * AD + (base & 31) * (AD + 1);  // A(base, base)
         float tc[16];
 #pragma unroll
         for (int r = 0; r < 16; r++) {
           float s = 0.f;
 #pragma unroll
-          for (int j = 0; j < r; j++) s = fmaf(Aw[swf(base + r, base + j)], tc[j], s);
+          for (int j = 0; j < r; j++) s = fmaf(ab[r * AD + j], tc[j], s);
           tc[r] = tf32_round(r == cc ? 1.f : -s);
         }
 #pragma unroll
-        for (int r = 0; r < 16; r++) Tw[swf(base + r, base + cc)] = tc[r];
-        if (base < 32) {
-#pragma unroll
-          for (int u = 0; u < 4; u++)
-            *reinterpret_cast<float4*>(U11 + swf(base + cc, base + 4 * u)) =
-                make_float4(tc[4 * u], tc[4 * u + 1], tc[4 * u + 2], tc[4 * u + 3]);
-        }
+        for (int r = 0; r < 16; r++) Tf[(base + r) * AS + base + cc] = tc[r];
       } else {
-        // zero the upper off-diagonal 16x16 blocks (0,1) and (2,3) of T, and
-        // the matching block of U11: the 32x32 diagonal blocks are read whole
+        // zero the upper off-diagonal 16x16 blocks (0,1) and (2,3): the 32x32
+        // diagonal blocks are read whole below
         for (int e = t - 64; e < 512; e += 64) {
           const int blk = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-          Tw[swf(blk * 32 + r, blk * 32 + 16 + cc)] = 0.f;
-          if (blk == 0) U11[swf(16 + cc, r)] = 0.f;
+          Tf[(blk * 32 + r) * AS + blk * 32 + 16 + cc] = 0.f;
         }
       }
       named_bar(bid, 128);
@@ -352,11 +366,12 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         // 32x32 blocks: T[2p+1][2p] = -T[2p+1][2p+1] A[2p+1][2p] T[2p][2p]
         const int p = t >> 6, rem = t & 63, r = rem >> 2, c4 = (rem & 3) * 4;
         const int rb = 16 * (2 * p + 1), cb = 16 * (2 * p);
+        const float* arow = Ad + p * 32 * AD + (16 + r) * AD;  // A(rb + r, cb + k) = arow[k]
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int k = 0; k < 16; k++) {
-          const float av = Aw[swf(rb + r, cb + k)];
-          const float4 tv = *reinterpret_cast<const float4*>(Tw + swf(cb + k, cb + c4));
+          const float av = arow[k];
+          const float4 tv = *reinterpret_cast<const float4*>(&Tf[(cb + k) * AS + cb + c4]);
           acc.x = fmaf(av, tv.x, acc.x);
           acc.y = fmaf(av, tv.y, acc.y);
           acc.z = fmaf(av, tv.z, acc.z);
@@ -367,31 +382,39 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int k = 0; k < 16; k++) {
-          const float tv = Tw[swf(rb + r, rb + k)];
+          const float tv = Tf[(rb + r) * AS + rb + k];
           const float4 xv = *reinterpret_cast<const float4*>(&X1[(p * 16 + k) * 20 + c4]);
           o.x = fmaf(tv, xv.x, o.x);
           o.y = fmaf(tv, xv.y, o.y);
           o.z = fmaf(tv, xv.z, o.z);
           o.w = fmaf(tv, xv.w, o.w);
         }
-        const float4 v = make_float4(tf32_round(-o.x), tf32_round(-o.y), tf32_round(-o.z), tf32_round(-o.w));
-        *reinterpret_cast<float4*>(Tw + swf(rb + r, cb + c4)) = v;
-        if (p == 0) {
-          U11[swf(c4 + 0, rb + r)] = v.x;
-          U11[swf(c4 + 1, rb + r)] = v.y;
-          U11[swf(c4 + 2, rb + r)] = v.z;
-          U11[swf(c4 + 3, rb + r)] = v.w;
+        *reinterpret_cast<float4*>(&Tf[(rb + r) * AS + cb + c4]) =
+            make_float4(tf32_round(-o.x), tf32_round(-o.y), tf32_round(-o.z), tf32_round(-o.w));
+      }
+      named_bar(bid, 128);
+      {
+        // swizzled K-major operands of the 64x64 combine: U11 = T[0:32][0:32]^T, T22
+        const int j = t & 31, i0 = (t >> 5) * 8;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const int i = i0 + e;
+          U11[j * 32 + ((((i >> 2) ^ (j & 7))) << 2) + (i & 3)] = Tf[i * AS + j];
         }
+        const int m = t >> 2, cq = (t & 3) * 2;
+        const float4 v0 = *reinterpret_cast<const float4*>(&Tf[(32 + m) * AS + 32 + 4 * cq]);
+        const float4 v1 = *reinterpret_cast<const float4*>(&Tf[(32 + m) * AS + 36 + 4 * cq]);
+        *reinterpret_cast<float4*>(T22 + m * 32 + ((cq ^ (m & 7)) << 2)) = v0;
+        *reinterpret_cast<float4*>(T22 + m * 32 + (((cq + 1) ^ (m & 7)) << 2)) = v1;
       }
       // 64x64 on the tensor cores (tf32, K-major operands):
       //   X2^T = U11 A[32:64][0:32]^T,  then  T[32:64][0:32] = -T[32:64][32:64] X2.
-      // Both are M = 64 products whose unused rows read padding.
       fence_proxy_async();
       named_bar(bid, 128);
       constexpr uint32_t id_l3 = idesc_tf32(64, 32, false, false);
       if (t == 0) {
         tc_fence_after();
-        const uint32_t ub = smem_u32(U11), ab = smem_u32(Aw) + 32 * 128;
+        const uint32_t ub = smem_u32(U11), ab = smem_u32(A21);
 #pragma unroll
         for (int ks = 0; ks < 4; ks++)
           mma_tf32_ss(tl3, smem_desc_sw128(ub + ks * 32, 16, 1024), smem_desc_sw128(ab + ks * 32, 16, 1024), id_l3,
@@ -418,7 +441,8 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       ok = named_bar_and(bid, 128, ok);
       if (ok && t == 0) {
         tc_fence_after();
-        const uint32_t tb = smem_u32(Tw) + 8192, xb = smem_u32(X2T);
+        // A operand rows 32-63 are T22's; rows 0-31 read A21 and are not used
+        const uint32_t tb = smem_u32(A21), xb = smem_u32(X2T);
 #pragma unroll
         for (int ks = 0; ks < 4; ks++)
           mma_tf32_ss(tl3 + 32, smem_desc_sw128(tb + ks * 32, 16, 1024), smem_desc_sw128(xb + ks * 32, 16, 1024),
@@ -436,7 +460,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
             const int m = 32 + 16 * (quad - 2) + lane;
 #pragma unroll
             for (int u = 0; u < 8; u++)
-              *reinterpret_cast<float4*>(Tw + swf(m, 4 * u)) =
+              *reinterpret_cast<float4*>(&Tf[m * AS + 4 * u]) =
                   make_float4(-__uint_as_float(r[4 * u]), -__uint_as_float(r[4 * u + 1]),
                               -__uint_as_float(r[4 * u + 2]), -__uint_as_float(r[4 * u + 3]));
           }
@@ -452,7 +476,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         for (int u = 0; u < 16; u++) {
           const bool live = u < 8 || quad == 1;
           float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (live) v4 = *reinterpret_cast<const float4*>(Tw + swf(t, 4 * u));
+          if (live) v4 = *reinterpret_cast<const float4*>(&Tf[t * AS + 4 * u]);
           const float4 b4 = reinterpret_cast<const float4*>(betv)[u];
           const float tv[4] = {v4.x, v4.y, v4.z, v4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
@@ -471,8 +495,13 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       }
       named_bar(bid, 128);  // every row of T has been read
       if (ok && t < 64) {
+        // Tb^T[n][t] = Tb[t][n] at swf(n, t): eight per-thread bases for n % 8
+        const int tb0 = ((t >> 5) << 11) + (t & 3), tcx = (t >> 2) & 7;
+        int offk[8];
 #pragma unroll
-        for (int n = 0; n < 64; n++) Tw[swf(n, t)] = tf32_round(y[n]);
+        for (int k8 = 0; k8 < 8; k8++) offk[k8] = tb0 + ((tcx ^ k8) << 2);
+#pragma unroll
+        for (int n2 = 0; n2 < 64; n2++) TbT[offk[n2 & 7] + (n2 << 5)] = tf32_round(y[n2]);
       }
       fence_proxy_async();
       tc_fence_before();
@@ -482,7 +511,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         // 0-63 read lanes 0-63 of the same columns and are not used)
         tc_fence_after();
         constexpr uint32_t id_g = idesc_tf32(128, 64, false, false);
-        const uint32_t tb = smem_u32(Tw);
+        const uint32_t tb = smem_u32(TbT);
 #pragma unroll
         for (int ks = 0; ks < 8; ks++)
           mma_tf32_ts(tl3, tmem + 64 * wg + 8 * ks, smem_desc_sw128(tb + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024),
