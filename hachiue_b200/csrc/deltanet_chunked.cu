@@ -95,7 +95,7 @@ constexpr int C_SMEM = C_OFF_BAR + C_NBAR * 8 + 16;
 constexpr uint32_t TC_P = 0, TC_Q = 64, C_TMEM_COLS = 128;
 
 struct PrepArgs {
-  int T, NK, NV, c0, ns;
+  int T, NK, NV, c0, ns, ahead;
   const float* g;
   const float* beta;
   long long gb_row, gb_seq;
@@ -198,6 +198,21 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
 
   if (tid == 0) {
     prefetch_tensormap(&tmW);
+    // warm L2 with the K / Q chunk that the CTA one wave later (a.ahead
+    // blocks further in launch order) will load
+    {
+      const long long lin = blockIdx.x + (long long)gridDim.x * (blockIdx.y + (long long)gridDim.y * blockIdx.z) +
+                            a.ahead;
+      const int cf = (int)(lin % gridDim.x), yf = (int)((lin / gridDim.x) % gridDim.y);
+      const long long bf = lin / ((long long)gridDim.x * gridDim.y);
+      if (bf < gridDim.z) {
+        const int tf = (a.c0 + cf) * GC, hf = yf % a.NK;
+        tma_prefetch_l2_4d(&tmK, 0, hf, tf, (int)bf);
+        tma_prefetch_l2_4d(&tmQ, 0, hf, tf, (int)bf);
+        tma_prefetch_l2_4d(&tmK, 64, hf, tf, (int)bf);
+        tma_prefetch_l2_4d(&tmQ, 64, hf, tf, (int)bf);
+      }
+    }
     mbar_arrive_expect_tx(bar_kq, 32768);
     tma_load_4d(sm + P_OFF_KQ, &tmK, bar_kq, 0, hk, t0, b);
     tma_load_4d(sm + P_OFF_KQ + 8192, &tmQ, bar_kq, 0, hk, t0, b);
@@ -353,12 +368,35 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         }
 #pragma unroll
         for (int r = 0; r < 16; r++) Tf[(base + r) * AS + base + cc] = tc[r];
+        // the swizzled K-major operands of the 64x64 combine: U11 = T[0:32][0:32]^T
+        // (column cc is U11's row base + cc) and T22 = T[32:64][32:64]
+        if (base < 32) {
+          const int j = base + cc;
+#pragma unroll
+          for (int u = 0; u < 4; u++)
+            *reinterpret_cast<float4*>(U11 + j * 32 + ((((base >> 2) + u) ^ (j & 7)) << 2)) =
+                make_float4(tc[4 * u], tc[4 * u + 1], tc[4 * u + 2], tc[4 * u + 3]);
+        } else {
+          const int b2 = base - 32, col = b2 + cc;
+#pragma unroll
+          for (int r = 0; r < 16; r++) {
+            const int m = b2 + r;
+            T22[m * 32 + (((col >> 2) ^ (m & 7)) << 2) + (col & 3)] = tc[r];
+          }
+        }
       } else {
-        // zero the upper off-diagonal 16x16 blocks (0,1) and (2,3): the 32x32
-        // diagonal blocks are read whole below
+        // zero the upper off-diagonal 16x16 blocks (0,1) and (2,3), in T and in
+        // the combine operands: the 32x32 diagonal blocks are read whole below
         for (int e = t - 64; e < 512; e += 64) {
           const int blk = e >> 8, r = (e >> 4) & 15, cc = e & 15;
           Tf[(blk * 32 + r) * AS + blk * 32 + 16 + cc] = 0.f;
+          if (blk == 0) {
+            const int j = 16 + cc;  // U11[16 + cc][r] = T[r][16 + cc]
+            U11[j * 32 + (((r >> 2) ^ (j & 7)) << 2) + (r & 3)] = 0.f;
+          } else {
+            const int col = 16 + cc;  // T22[r][16 + cc]
+            T22[r * 32 + (((col >> 2) ^ (r & 7)) << 2) + (col & 3)] = 0.f;
+          }
         }
       }
       named_bar(bid, 128);
@@ -389,23 +427,21 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
           o.z = fmaf(tv, xv.z, o.z);
           o.w = fmaf(tv, xv.w, o.w);
         }
-        *reinterpret_cast<float4*>(&Tf[(rb + r) * AS + cb + c4]) =
-            make_float4(tf32_round(-o.x), tf32_round(-o.y), tf32_round(-o.z), tf32_round(-o.w));
-      }
-      named_bar(bid, 128);
-      {
-        // swizzled K-major operands of the 64x64 combine: U11 = T[0:32][0:32]^T, T22
-        const int j = t & 31, i0 = (t >> 5) * 8;
+        const float4 v = make_float4(tf32_round(-o.x), tf32_round(-o.y), tf32_round(-o.z), tf32_round(-o.w));
+        *reinterpret_cast<float4*>(&Tf[(rb + r) * AS + cb + c4]) = v;
+        if (p == 0) {
+          // U11[c4 + e][16 + r] = T[16 + r][c4 + e]
+          const int col = 16 + r;
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const int i = i0 + e;
-          U11[j * 32 + ((((i >> 2) ^ (j & 7))) << 2) + (i & 3)] = Tf[i * AS + j];
+          for (int e = 0; e < 4; e++) {
+            const int j = c4 + e;
+            U11[j * 32 + (((col >> 2) ^ (j & 7)) << 2) + (col & 3)] = (&v.x)[e];
+          }
+        } else {
+          // T22[16 + r][c4 .. c4 + 3]
+          const int m = 16 + r;
+          *reinterpret_cast<float4*>(T22 + m * 32 + (((c4 >> 2) ^ (m & 7)) << 2)) = v;
         }
-        const int m = t >> 2, cq = (t & 3) * 2;
-        const float4 v0 = *reinterpret_cast<const float4*>(&Tf[(32 + m) * AS + 32 + 4 * cq]);
-        const float4 v1 = *reinterpret_cast<const float4*>(&Tf[(32 + m) * AS + 36 + 4 * cq]);
-        *reinterpret_cast<float4*>(T22 + m * 32 + ((cq ^ (m & 7)) << 2)) = v0;
-        *reinterpret_cast<float4*>(T22 + m * 32 + (((cq + 1) ^ (m & 7)) << 2)) = v1;
       }
       // 64x64 on the tensor cores (tf32, K-major operands):
       //   X2^T = U11 A[32:64][0:32]^T,  then  T[32:64][0:32] = -T[32:64][32:64] X2.
@@ -960,6 +996,7 @@ extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_
     pa.NV = (int)NV;
     pa.c0 = (int)c0;
     pa.ns = (int)ns;
+    pa.ahead = 2 * h->sm_count;  // two prep CTAs are resident per SM
     pa.g = g;
     pa.beta = beta;
     pa.gb_row = gb_row;

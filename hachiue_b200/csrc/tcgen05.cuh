@@ -107,12 +107,13 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
-// f32 rounded to the nearest tf32 value (10-bit mantissa), so tf32 MMA
-// operands carry rounding rather than truncation error.
+// f32 rounded to the nearest tf32 value (10-bit mantissa, ties away from
+// zero), so tf32 MMA operands carry rounding rather than truncation error.
+// Two integer operations: add half of the dropped 13-bit field, clear it.
+// Infinities stay infinite and finite values that round past the largest
+// tf32 value become infinite, as a rounding conversion would make them.
 __device__ __forceinline__ float tf32_round(float x) {
-  uint32_t y;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(y) : "f"(x));
-  return __uint_as_float(y);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
 }
 
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread
