@@ -364,7 +364,7 @@ def cpu_sample(kind: str, w: dict, threads: int, budget_s: float = 12.0):
         t0 = time.perf_counter()
         n = 0
         while time.perf_counter() - t0 < min(budget_s, 5.0):
-            oracle.attention(w["q"][0], w["k"], w["v"], w["pos_base"])
+            oracle.attention(w["q"], w["k"], w["v"], w["pos_base"])
             n += 1
         dt = time.perf_counter() - t0
         return n * workloads.cfg1_bytes() / dt / 1e9, n / dt, f"{n} cfg1 calls, 1 thread", 1

@@ -30,7 +30,13 @@
 namespace hcu {
 namespace {
 
-constexpr int SW_THREADS = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 / 6-9 softmax of head 0 / 1
+// Warpgroup 0: warp 0 TMA, warp 1 MMA + TMEM (warps 2, 3 idle); warpgroup 1 + hd:
+// softmax of head hd.  With two heads the 384 threads launch with 168
+// registers each (64,512); the control warpgroup drops to 72 and the softmax
+// warpgroups rise to 216: 128 * 72 + 256 * 216 = 64,512.
+__host__ __device__ constexpr int sw_threads(int nhd) { return 128 + 128 * nhd; }
+constexpr uint32_t REG_CTRL = 72, REG_SOFTMAX = 216;
+static_assert(128 * REG_CTRL + 256 * REG_SOFTMAX == 384 * 168, "register split of the two-head kernel");
 constexpr int BM = 128, BN = 128, HD = 128;
 constexpr int BOX = BM * 128;                 // [128 rows x 64 bf16] = 16 KB
 constexpr int TILE = 2 * BOX;                 // [128 x 128] bf16 tile
@@ -60,15 +66,25 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Row max of one 32-column chunk; `lo`..`hi` is the valid column range (all
 // columns when FULL).
 template <bool FULL>
 __device__ __forceinline__ void chunk_max(const uint32_t (&r)[32], int col0, int lo, int hi, float (&mx)[4]) {
 #pragma unroll
-  for (int i = 0; i < 32; i++) {
-    float v = __uint_as_float(r[i]);
-    if (!FULL) v = (col0 + i >= lo && col0 + i <= hi) ? v : -INFINITY;
-    mx[i & 3] = fmaxf(mx[i & 3], v);
+  for (int i = 0; i < 32; i += 2) {
+    float v0 = __uint_as_float(r[i]), v1 = __uint_as_float(r[i + 1]);
+    if (!FULL) {
+      v0 = (col0 + i >= lo && col0 + i <= hi) ? v0 : -INFINITY;
+      v1 = (col0 + i + 1 >= lo && col0 + i + 1 <= hi) ? v1 : -INFINITY;
+    }
+    mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], v0, v1);
   }
 }
 
@@ -95,7 +111,7 @@ __device__ __forceinline__ void chunk_p(const uint32_t (&r0)[32], const uint32_t
 }
 
 template <int NHD>
-__global__ void __launch_bounds__(SW_THREADS, 1)
+__global__ void __launch_bounds__(sw_threads(NHD), 1)
     swa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const SwaArgs a) {
   constexpr uint32_t TMEM_COLS = NHD == 2 ? 512 : 256;
@@ -149,6 +165,8 @@ __global__ void __launch_bounds__(SW_THREADS, 1)
   auto s_col = [](int hd) { return (uint32_t)(hd * 256); };
   auto o_col = [](int hd) { return (uint32_t)(hd * 256 + 128); };
 
+  if (warp < 4) {
+  if (NHD == 2) warpgroup_reg_dealloc<REG_CTRL>();
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
@@ -222,9 +240,11 @@ __global__ void __launch_bounds__(SW_THREADS, 1)
         }
       }
     }
-  } else if (warp < 2 + 4 * NHD) {
+  }
+  } else {
     // ---------------- softmax of head hd, one thread per query row ----------------
-    const int hd = (warp - 2) >> 2;
+    if (NHD == 2) warpgroup_reg_alloc<REG_SOFTMAX>();
+    const int hd = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int query = m0 + row;
@@ -239,24 +259,28 @@ __global__ void __launch_bounds__(SW_THREADS, 1)
         break;
       }
       tc_fence_after();
-      // Pass 1: row max over the tile (masked), then to the log2 domain.
+      // The whole S row (128 columns) is loaded once, with one wait, and kept
+      // in registers for both the row max and P.
       const bool full = (n0 + BN - 1 <= m0) && (a.W == 0 || n0 >= m0 + BM - a.W) && (n0 + BN <= a.T);
       const int lo = (a.W > 0 ? query - a.W + 1 : 0) - n0;  // valid column range of this row
       const int hi = min(query, a.T - 1) - n0;
+      uint32_t s0[32], s1[32], s2[32], s3[32];
+      tmem_ld32(sc, s0);
+      tmem_ld32(sc + 32, s1);
+      tmem_ld32(sc + 64, s2);
+      tmem_ld32(sc + 96, s3);
+      tmem_ld_wait();
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int c = 0; c < 4; c += 2) {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(sc + 32 * c, r0);
-        tmem_ld32(sc + 32 * c + 32, r1);
-        tmem_ld_wait();
-        if (full) {
-          chunk_max<true>(r0, 32 * c, lo, hi, mx4);
-          chunk_max<true>(r1, 32 * c + 32, lo, hi, mx4);
-        } else {
-          chunk_max<false>(r0, 32 * c, lo, hi, mx4);
-          chunk_max<false>(r1, 32 * c + 32, lo, hi, mx4);
-        }
+      if (full) {
+        chunk_max<true>(s0, 0, lo, hi, mx4);
+        chunk_max<true>(s1, 32, lo, hi, mx4);
+        chunk_max<true>(s2, 64, lo, hi, mx4);
+        chunk_max<true>(s3, 96, lo, hi, mx4);
+      } else {
+        chunk_max<false>(s0, 0, lo, hi, mx4);
+        chunk_max<false>(s1, 32, lo, hi, mx4);
+        chunk_max<false>(s2, 64, lo, hi, mx4);
+        chunk_max<false>(s3, 96, lo, hi, mx4);
       }
       const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
       // The running max grew by more than 2^8 (or this is the first finite
@@ -287,21 +311,25 @@ __global__ void __launch_bounds__(SW_THREADS, 1)
         l *= f;
         m_use = mx;
       }
-      // Pass 2: P = exp2(S*scale - m) as bf16, written over the S columns
-      // already read (keys 64c..64c+63 land in columns 32c..32c+31).
+      // P = exp2(S*scale - m) as bf16, written over the S columns already
+      // read (keys 64c..64c+63 land in columns 32c..32c+31).
       const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 2; c++) {
-        uint32_t r0[32], r1[32], pk[32];
-        tmem_ld32(sc + 64 * c, r0);
-        tmem_ld32(sc + 64 * c + 32, r1);
-        tmem_ld_wait();
+      {
+        uint32_t pk[32];
         if (full)
-          chunk_p<true>(r0, r1, 64 * c, lo, hi, a.scale_log2, neg_m, ls, pk);
+          chunk_p<true>(s0, s1, 0, lo, hi, a.scale_log2, neg_m, ls, pk);
         else
-          chunk_p<false>(r0, r1, 64 * c, lo, hi, a.scale_log2, neg_m, ls, pk);
-        tmem_st32(sc + 32 * c, pk);
+          chunk_p<false>(s0, s1, 0, lo, hi, a.scale_log2, neg_m, ls, pk);
+        tmem_st32(sc, pk);
+      }
+      {
+        uint32_t pk[32];
+        if (full)
+          chunk_p<true>(s2, s3, 64, lo, hi, a.scale_log2, neg_m, ls, pk);
+        else
+          chunk_p<false>(s2, s3, 64, lo, hi, a.scale_log2, neg_m, ls, pk);
+        tmem_st32(sc + 32, pk);
       }
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       tmem_st_wait();
@@ -362,7 +390,7 @@ int launch_swa(hcu_context* h, const SwaArgs& args, dim3 grid, const CUtensorMap
                        "hcu_swa_prefill: smem attribute"));
     attr_done = true;
   }
-  kern<<<grid, SW_THREADS, smem, h->stream>>>(tq, tk, tv, args);
+  kern<<<grid, sw_threads(NHD), smem, h->stream>>>(tq, tk, tv, args);
   return after_launch("hcu_swa_prefill: launch");
 }
 

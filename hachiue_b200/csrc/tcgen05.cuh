@@ -116,6 +116,19 @@ __device__ __forceinline__ float tf32_round(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
 }
 
+// Per-warpgroup register budget (all 128 threads of the warpgroup execute it):
+// lower this warpgroup's registers per thread to N, or raise them to N once
+// other warpgroups have released enough.  The budgets must add up to at most
+// the block's registers at launch.
+template <uint32_t N>
+__device__ __forceinline__ void warpgroup_reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void warpgroup_reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread
 // has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
