@@ -62,10 +62,13 @@ def run(backend, qb, kb, vb, g, beta, state0=None):
 
 @pytest.mark.parametrize("B,T,NK,NV,decay,load", [(1, 64, 1, 2, 1.0, False), (2, 200, 2, 4, 1.0, True),
                                                   (1, 1000, 1, 2, 1.0, False), (1, 640, 2, 2, 0.02, True),
-                                                  (1, 129, 1, 1, 0.0, False)])
+                                                  (1, 129, 1, 1, 0.0, False), (1, 256, 1, 2, 4.0, True),
+                                                  (1, 130, 2, 3, 1.0, False)])
 def test_small_shapes(backend, B, T, NK, NV, decay, load):
     """One chunk, a partial last chunk, many chunks, weak decay (the state
-    carries across chunks) and no decay at all; zero or loaded initial state."""
+    carries across chunks), no decay at all and strong decay (in-chunk decay
+    factors far below f32 range); zero or loaded initial state; V heads not a
+    multiple of twice the QK heads."""
     rng = np.random.default_rng(B + T + NK + NV + int(100 * decay))
     qb, kb, vb, g, beta = make_inputs(rng, B, T, NK, NV, decay)
     st0 = (0.02 * rng.standard_normal((B, NV, 128, 128))).astype(np.float32) if load else None
@@ -114,3 +117,19 @@ def test_cfg5_qwen35_chunked_prefill(backend, cfg5):
         assert rel_l2(core[b, :, h], rc) < REL, (b, h)
         assert np.abs(core[b, :, h] - rc).max() < ABS
         assert rel_l2(st[b, h], rs) < REL
+
+
+def test_slabs_carry_the_state(backend, monkeypatch):
+    """A scratch budget of 1 MiB splits 64 chunks into slabs (one prep + chain
+    launch pair each); the state crosses slab boundaries through state_out."""
+    monkeypatch.setenv("HCU_GDN_SCRATCH_MB", "1")
+    rng = np.random.default_rng(7)
+    B, T, NK, NV = 1, 4096, 1, 2
+    qb, kb, vb, g, beta = make_inputs(rng, B, T, NK, NV, 0.05)
+    st0 = (0.02 * rng.standard_normal((B, NV, 128, 128))).astype(np.float32)
+    core, st = run(backend, qb, kb, vb, g, beta, st0)
+    for h in range(NV):
+        rc, rs = oracle_head(qb, kb, vb, g, beta, 0, h, NK, st0)
+        assert rel_l2(core[0, :, h], rc) < REL, (h, rel_l2(core[0, :, h], rc))
+        assert rel_l2(st[0, h], rs) < REL
+    assert backend.device_status() == 0
