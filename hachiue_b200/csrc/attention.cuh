@@ -59,42 +59,94 @@ __device__ __forceinline__ size_t out_index(const AttnArgs& a, const AttnUnit& u
 
 // After every thread of the CTA has written its split's partial
 // (acc, m, l) for unit u: take a ticket; the CTA drawing the last one merges
-// all splits of the unit and re-arms the ticket.  `nthr` threads with ids
-// 0..nthr-1 take part, synchronising on named barrier `barid`.  `scratch`
-// holds >= 3 * kMaxSplits * R floats of shared memory.
-template <int R, int DH>
-__device__ void ticket_merge(const AttnArgs& a, const AttnUnit& u, int tid, int nthr, int barid, float* scratch,
+// all splits of the unit and re-arms the ticket.  NT threads with ids
+// 0..NT-1 take part, synchronising on named barrier `barid`.  `scratch`
+// holds >= kMaxSplits * R floats of shared memory.
+//
+// The merge is latency-bound (a few KB to a few hundred KB read from L2 by
+// one CTA), so every phase keeps many independent loads in flight: one warp
+// per row gathers that row's (m, l) of all splits at once, and each thread
+// accumulates its R*DH/NT output elements over batches of splits whose loads
+// are issued together (about 32 in flight per thread).
+template <int R, int DH, int NT>
+__device__ void ticket_merge(const AttnArgs& a, const AttnUnit& u, int tid, int barid, float* scratch,
                              int* s_last) {
+  static_assert(NT % 32 == 0 && kMaxSplits % 32 == 0, "merge geometry");
   __threadfence();
-  named_bar(barid, nthr);
+  named_bar(barid, NT);
   if (tid == 0) *s_last = (atomicAdd(&a.counters[u.unit], 1) == u.nsplit - 1);
-  named_bar(barid, nthr);
+  named_bar(barid, NT);
   if (!*s_last) return;
   __threadfence();
-  const float* up = a.part + (size_t)u.unit * a.max_splits * R * (DH + 2);
-  float* Ms = scratch;                     // [nsplit][R]
-  float* Ls = scratch + kMaxSplits * R;    // [nsplit][R]
-  float* Ws = scratch + 2 * kMaxSplits * R;
-  for (int i = tid; i < u.nsplit * R; i += nthr) {
-    const float* pp = up + (size_t)i * (DH + 2);
-    Ms[i] = __ldcg(pp + DH);
-    Ls[i] = __ldcg(pp + DH + 1);
-  }
-  named_bar(barid, nthr);
-  for (int r = tid; r < R; r += nthr) {
-    float M = -1e30f;
-    for (int sp = 0; sp < u.nsplit; sp++) M = fmaxf(M, Ms[sp * R + r]);
+  const int n = u.nsplit;
+  constexpr size_t RS = DH + 2;  // floats per (split, row) record
+  const float* up = a.part + (size_t)u.unit * a.max_splits * R * RS;
+  float* Ws = scratch;  // [kMaxSplits][R]: weight of split sp in row r
+  const int warp = tid >> 5, lane = tid & 31;
+  constexpr int SPL = kMaxSplits / 32;  // splits per lane
+  for (int r = warp; r < R; r += NT / 32) {
+    float mv[SPL], lv[SPL];
+#pragma unroll
+    for (int i = 0; i < SPL; i++) {
+      const int sp = lane + 32 * i;
+      const float* pp = up + ((size_t)min(sp, n - 1) * R + r) * RS;
+      mv[i] = __ldcg(pp + DH);
+      lv[i] = __ldcg(pp + DH + 1);
+    }
+#pragma unroll
+    for (int i = 0; i < SPL; i++) {
+      if (lane + 32 * i >= n) {
+        mv[i] = -1e30f;
+        lv[i] = 0.f;
+      }
+    }
+    float M = mv[0];
+#pragma unroll
+    for (int i = 1; i < SPL; i++) M = fmaxf(M, mv[i]);
+    M = warp_max(M);
     float L = 0.f;
-    for (int sp = 0; sp < u.nsplit; sp++) L += Ls[sp * R + r] * exp2f(Ms[sp * R + r] - M);
-    const float inv = 1.f / L;
-    for (int sp = 0; sp < u.nsplit; sp++) Ws[sp * R + r] = exp2f(Ms[sp * R + r] - M) * inv;
+#pragma unroll
+    for (int i = 0; i < SPL; i++) L += lv[i] * exp2f(mv[i] - M);
+    const float inv = 1.f / warp_sum(L);
+#pragma unroll
+    for (int i = 0; i < SPL; i++) {
+      const int sp = lane + 32 * i;
+      if (sp < n) Ws[sp * R + r] = exp2f(mv[i] - M) * inv;
+    }
   }
-  named_bar(barid, nthr);
-  for (int e = tid; e < u.rows_valid * DH; e += nthr) {
-    const int r = e / DH, d = e % DH;
-    float A = 0.f;
-    for (int sp = 0; sp < u.nsplit; sp++) A = fmaf(__ldcg(up + ((size_t)sp * R + r) * (DH + 2) + d), Ws[sp * R + r], A);
-    a.out[out_index(a, u, r, d, DH)] = A;
+  named_bar(barid, NT);
+
+  constexpr int E = R * DH;                   // output elements of the unit
+  constexpr int EPT = (E + NT - 1) / NT;      // elements per thread
+  constexpr int SB = EPT >= 32 ? 1 : 32 / EPT;  // splits per load batch
+  float acc[EPT];
+#pragma unroll
+  for (int k = 0; k < EPT; k++) acc[k] = 0.f;
+  // Loads use clamped (always valid) indices and are unconditional, so the
+  // compiler issues a whole batch before the first use; splits past the end
+  // get weight 0.
+  for (int sp0 = 0; sp0 < n; sp0 += SB) {
+    float x[SB][EPT];
+#pragma unroll
+    for (int j = 0; j < SB; j++)
+#pragma unroll
+      for (int k = 0; k < EPT; k++) {
+        const int sp = min(sp0 + j, n - 1), e = min(tid + k * NT, E - 1), r = e / DH, d = e % DH;
+        x[j][k] = __ldcg(up + ((size_t)sp * R + r) * RS + d);
+      }
+#pragma unroll
+    for (int j = 0; j < SB; j++)
+#pragma unroll
+      for (int k = 0; k < EPT; k++) {
+        const int sp = min(sp0 + j, n - 1), r = min(tid + k * NT, E - 1) / DH;
+        const float wgt = sp0 + j < n ? Ws[sp * R + r] : 0.f;
+        acc[k] = fmaf(x[j][k], wgt, acc[k]);
+      }
+  }
+#pragma unroll
+  for (int k = 0; k < EPT; k++) {
+    const int e = tid + k * NT, r = e / DH, d = e % DH;
+    if (e < E && r < u.rows_valid) a.out[out_index(a, u, r, d, DH)] = acc[k];
   }
   if (tid == 0) a.counters[u.unit] = 0;  // re-arm for the next call
 }

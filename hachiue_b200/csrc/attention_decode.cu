@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   }
   if (u.nsplit == 1) return;
   named_bar(1, NW * 32);  // cb / cm / cl are read above; the merge reuses the stage memory
-  ticket_merge<R, DH>(a, u, tid, NW * 32, 1, reinterpret_cast<float*>(stages), &s_last);
+  ticket_merge<R, DH, NW * 32>(a, u, tid, 1, reinterpret_cast<float*>(stages), &s_last);
   (void)b;
   (void)pb;
 }

@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         part[r * (TC_DH + 2) + TC_DH + 1] = lsum[r];
       }
     }
-    ticket_merge<R, TC_DH>(a, u, t, 128, 1, reinterpret_cast<float*>(stages), s_last);
+    ticket_merge<R, TC_DH, 128>(a, u, t, 1, reinterpret_cast<float*>(stages), s_last);
     return;
   }
   // producer and MMA warps: wait for the softmax warps, then release TMEM

@@ -23,6 +23,8 @@
 //    against the stale max, P <= 2^8, which the final O / l cancels exactly.
 //  * Only key tiles that intersect the causal window band are visited; tiles
 //    entirely inside the band skip per-element masking.
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "context.h"
 #include "tcgen05.cuh"
@@ -46,6 +48,7 @@ constexpr float RESCALE_LOG2 = 8.f;
 
 struct SwaArgs {
   int B, T, H, KV, W, G, nqt;
+  int n_items;       // B * KV * (G / NHD) * nqt work items
   float scale_log2;  // log2(e) / sqrt(D)
   void* out;
   int out_bf16;
@@ -110,6 +113,51 @@ __device__ __forceinline__ void chunk_p(const uint32_t (&r0)[32], const uint32_t
   }
 }
 
+// One work item: a 128-query tile of NHD query heads of one sequence.
+struct SwaItem {
+  int b, g, h0, m0, n_first, ntiles;
+};
+
+// Items are numbered in decreasing cost (query tiles from the last, whose key
+// range is longest, to the first); within a query tile, the head pairs that
+// share a KV head are adjacent, so CTAs running them together share K / V
+// tiles in L2.
+template <int NHD>
+__device__ __forceinline__ SwaItem swa_item(const SwaArgs& a, int idx) {
+  const int hpairs = a.G / NHD;
+  const int per_qt = a.B * a.KV * hpairs;
+  const int qt = a.nqt - 1 - idx / per_qt;
+  int r = idx % per_qt;
+  SwaItem it;
+  it.b = r / (a.KV * hpairs);
+  r %= a.KV * hpairs;
+  it.g = r / hpairs;
+  it.h0 = it.g * a.G + (r % hpairs) * NHD;
+  it.m0 = qt * BM;
+  const int kfirst = a.W > 0 ? max(0, it.m0 - a.W + 1) : 0;
+  it.n_first = (kfirst / BN) * BN;
+  const int n_last = min(it.m0 + BM - 1, a.T - 1);
+  it.ntiles = (n_last - it.n_first) / BN + 1;
+  return it;
+}
+
+// The k-th item of this CTA: rounds of gridDim.x items, walked forwards in
+// even rounds and backwards in odd ones (costs decrease with the index, so
+// every CTA gets a near-equal share of the key tiles).
+__device__ __forceinline__ int swa_item_index(int k) {
+  const int P = (int)gridDim.x, c = (int)blockIdx.x;
+  return k * P + ((k & 1) ? P - 1 - c : c);
+}
+
+// Persistent kernel: one CTA per SM loops over its items.  All barriers run
+// continuously across items; their parities come from item and tile counters
+// that every role advances identically:
+//   q_full / q_empty  once per item (Q of the next item loads as soon as the
+//                     current item's last Q.K^T has read the Q tiles),
+//   kv_full / kv_empty once per key tile, ring index over all items,
+//   s_full / p_full / o_done once per key tile and head,
+//   o_free            once per item and head: the epilogue has moved O out of
+//                     TMEM, so the next item's first P.V may overwrite it.
 template <int NHD>
 __global__ void __launch_bounds__(sw_threads(NHD), 1)
     swa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -121,27 +169,20 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
   uint8_t* kvsm = qsm + NHD * TILE;         // [KV_STAGES][K tile | V tile]
   uint64_t* bars = reinterpret_cast<uint64_t*>(kvsm + KV_STAGES * KV_STAGE);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 3;
-  uint64_t* s_full = bars + 5;   // [NHD]
-  uint64_t* p_full = bars + 7;   // [NHD]
-  uint64_t* o_done = bars + 9;   // [NHD]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* q_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;   // [KV_STAGES]
+  uint64_t* kv_empty = bars + 4;  // [KV_STAGES]
+  uint64_t* s_full = bars + 6;    // [NHD]
+  uint64_t* p_full = bars + 8;    // [NHD]
+  uint64_t* o_done = bars + 10;   // [NHD]
+  uint64_t* o_free = bars + 12;   // [NHD]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qt = a.nqt - 1 - (int)blockIdx.x;  // longest tiles first
-  const int m0 = qt * BM;
-  const int hpairs = a.G / NHD;
-  const int g = blockIdx.y / hpairs;
-  const int h0 = g * a.G + (blockIdx.y % hpairs) * NHD;
-  const int b = blockIdx.z;
-  const int kfirst = a.W > 0 ? max(0, m0 - a.W + 1) : 0;
-  const int n_first = (kfirst / BN) * BN;
-  const int n_last = min(m0 + BM - 1, a.T - 1);
-  const int ntiles = (n_last - n_first) / BN + 1;
 
   if (tid == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < KV_STAGES; i++) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
@@ -150,6 +191,7 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
+      mbar_init(&o_free[i], 4);
     }
     fence_barrier_init();
   }
@@ -173,21 +215,32 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
       prefetch_tensormap(&tmQ);
       prefetch_tensormap(&tmK);
       prefetch_tensormap(&tmV);
-      mbar_arrive_expect_tx(q_full, NHD * TILE);
-      for (int hd = 0; hd < NHD; hd++) {
-        tma_load_4d(qsm + hd * TILE, &tmQ, q_full, 0, h0 + hd, m0, b);
-        tma_load_4d(qsm + hd * TILE + BOX, &tmQ, q_full, 64, h0 + hd, m0, b);
-      }
-      for (int j = 0; j < ntiles; j++) {
-        const int s = j % KV_STAGES;
-        if (j >= KV_STAGES && !mbar_wait(&kv_empty[s], ((j - KV_STAGES) / KV_STAGES) & 1, a.status)) break;
-        uint8_t* st = kvsm + s * KV_STAGE;
-        const int n0 = n_first + j * BN;
-        mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
-        tma_load_4d(st, &tmK, &kv_full[s], 0, g, n0, b);
-        tma_load_4d(st + BOX, &tmK, &kv_full[s], 64, g, n0, b);
-        tma_load_4d(st + TILE, &tmV, &kv_full[s], 0, g, n0, b);
-        tma_load_4d(st + TILE + BOX, &tmV, &kv_full[s], 64, g, n0, b);
+      int kt = 0;  // key tiles loaded, over all items
+      bool ok = true;
+      for (int k = 0; ok; k++) {
+        const int idx = swa_item_index(k);
+        if (idx >= a.n_items) break;
+        const SwaItem it = swa_item<NHD>(a, idx);
+        if (k > 0 && !mbar_wait(q_empty, (k - 1) & 1, a.status)) break;
+        mbar_arrive_expect_tx(q_full, NHD * TILE);
+        for (int hd = 0; hd < NHD; hd++) {
+          tma_load_4d(qsm + hd * TILE, &tmQ, q_full, 0, it.h0 + hd, it.m0, it.b);
+          tma_load_4d(qsm + hd * TILE + BOX, &tmQ, q_full, 64, it.h0 + hd, it.m0, it.b);
+        }
+        for (int j = 0; j < it.ntiles; j++, kt++) {
+          const int s = kt % KV_STAGES;
+          if (kt >= KV_STAGES && !mbar_wait(&kv_empty[s], ((kt - KV_STAGES) / KV_STAGES) & 1, a.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = kvsm + s * KV_STAGE;
+          const int n0 = it.n_first + j * BN;
+          mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
+          tma_load_4d(st, &tmK, &kv_full[s], 0, it.g, n0, it.b);
+          tma_load_4d(st + BOX, &tmK, &kv_full[s], 64, it.g, n0, it.b);
+          tma_load_4d(st + TILE, &tmV, &kv_full[s], 0, it.g, n0, it.b);
+          tma_load_4d(st + TILE + BOX, &tmV, &kv_full[s], 64, it.g, n0, it.b);
+        }
       }
     }
   } else if (warp == 1) {
@@ -213,31 +266,45 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         }
         mma_commit(&o_done[hd]);
       };
-      bool ok = mbar_wait(q_full, 0, a.status) && mbar_wait(&kv_full[0], 0, a.status);
-      if (ok) {
+      int kt = 0;  // key tiles consumed (ring position and per-head tile count)
+      bool ok = true;
+      for (int k = 0; ok; k++) {
+        const int idx = swa_item_index(k);
+        if (idx >= a.n_items) break;
+        const int ntiles = swa_item<NHD>(a, idx).ntiles;
+        if (!mbar_wait(q_full, k & 1, a.status) ||
+            !mbar_wait(&kv_full[kt % KV_STAGES], (kt / KV_STAGES) & 1, a.status))
+          break;
         tc_fence_after();
-        for (int hd = 0; hd < NHD; hd++) qk(hd, 0);
-      }
-      for (int j = 0; ok && j < ntiles; j++) {
-        const int s = j % KV_STAGES;
-        for (int hd = 0; hd < NHD && ok; hd++) {
-          if (!mbar_wait(&p_full[hd], j & 1, a.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          pv(hd, s, j > 0);
-          if (hd == NHD - 1) mma_commit(&kv_empty[s]);
-          if (j + 1 < ntiles) {
-            const int s1 = (j + 1) % KV_STAGES;
-            if (hd == 0 && !mbar_wait(&kv_full[s1], ((j + 1) / KV_STAGES) & 1, a.status)) {
+        // Ordered after the previous item's last P.V of each head (same
+        // issuing thread), which has consumed that head's P.
+        for (int hd = 0; hd < NHD; hd++) qk(hd, kt % KV_STAGES);
+        if (ntiles == 1) mma_commit(q_empty);
+        for (int j = 0; ok && j < ntiles; j++) {
+          const int t = kt + j;
+          const int s = t % KV_STAGES;
+          for (int hd = 0; hd < NHD; hd++) {
+            if (!mbar_wait(&p_full[hd], t & 1, a.status) ||
+                (j == 0 && k > 0 && !mbar_wait(&o_free[hd], (k - 1) & 1, a.status))) {
               ok = false;
               break;
             }
             tc_fence_after();
-            qk(hd, s1);  // overwrites S / P of this head: ordered after the P.V above
+            pv(hd, s, j > 0);
+            if (hd == NHD - 1) mma_commit(&kv_empty[s]);
+            if (j + 1 < ntiles) {
+              const int s1 = (t + 1) % KV_STAGES;
+              if (hd == 0 && !mbar_wait(&kv_full[s1], ((t + 1) / KV_STAGES) & 1, a.status)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              qk(hd, s1);  // overwrites S / P of this head: ordered after the P.V above
+              if (hd == NHD - 1 && j + 2 == ntiles) mma_commit(q_empty);  // the item's last Q.K^T
+            }
           }
         }
+        kt += ntiles;
       }
     }
   }
@@ -247,127 +314,142 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
     const int hd = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int query = m0 + row;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t sc = tmem + lane_off + s_col(hd), oc = tmem + lane_off + o_col(hd);
-    float m_use = -INFINITY, l = 0.f;
+    int kt = 0;  // key tiles processed, over all items
     bool ok = true;
-    for (int j = 0; j < ntiles; j++) {
-      const int n0 = n_first + j * BN;
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[hd], j & 1, a.status))) {  // warp-uniform exit
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // The whole S row (128 columns) is loaded once, with one wait, and kept
-      // in registers for both the row max and P.
-      const bool full = (n0 + BN - 1 <= m0) && (a.W == 0 || n0 >= m0 + BM - a.W) && (n0 + BN <= a.T);
-      const int lo = (a.W > 0 ? query - a.W + 1 : 0) - n0;  // valid column range of this row
-      const int hi = min(query, a.T - 1) - n0;
-      uint32_t s0[32], s1[32], s2[32], s3[32];
-      tmem_ld32(sc, s0);
-      tmem_ld32(sc + 32, s1);
-      tmem_ld32(sc + 64, s2);
-      tmem_ld32(sc + 96, s3);
-      tmem_ld_wait();
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (full) {
-        chunk_max<true>(s0, 0, lo, hi, mx4);
-        chunk_max<true>(s1, 32, lo, hi, mx4);
-        chunk_max<true>(s2, 64, lo, hi, mx4);
-        chunk_max<true>(s3, 96, lo, hi, mx4);
-      } else {
-        chunk_max<false>(s0, 0, lo, hi, mx4);
-        chunk_max<false>(s1, 32, lo, hi, mx4);
-        chunk_max<false>(s2, 64, lo, hi, mx4);
-        chunk_max<false>(s3, 96, lo, hi, mx4);
-      }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
-      // The running max grew by more than 2^8 (or this is the first finite
-      // max): move to the new max.  Rows that already accumulated O rescale
-      // it; tcgen05.ld / st are warp-collective, so the whole warp takes the
-      // TMEM round trip when any of its rows needs it (factor 1 elsewhere).
-      const bool move = mx > m_use + RESCALE_LOG2 || (j == 0 && mx > m_use);
-      const bool rescale_o = move && j > 0 && m_use != -INFINITY;
-      const float f = rescale_o ? exp2f(m_use - mx) : 1.f;
-      if (__any_sync(0xffffffffu, rescale_o)) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[hd], (j - 1) & 1, a.status))) {  // P.V of tile j-1 landed
+    for (int k = 0; ok; k++) {
+      const int idx = swa_item_index(k);
+      if (idx >= a.n_items) break;
+      const SwaItem it = swa_item<NHD>(a, idx);
+      const int m0 = it.m0, query = m0 + row;
+      float m_use = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.ntiles; j++) {
+        const int t = kt + j;
+        const int n0 = it.n_first + j * BN;
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[hd], t & 1, a.status))) {  // warp-uniform exit
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-          uint32_t r[32];
-          tmem_ld32(oc + 32 * c, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-          tmem_st32(oc + 32 * c, r);
+        // The whole S row (128 columns) is loaded once, with one wait, and kept
+        // in registers for both the row max and P.
+        const bool full = (n0 + BN - 1 <= m0) && (a.W == 0 || n0 >= m0 + BM - a.W) && (n0 + BN <= a.T);
+        const int lo = (a.W > 0 ? query - a.W + 1 : 0) - n0;  // valid column range of this row
+        const int hi = min(query, a.T - 1) - n0;
+        uint32_t s0[32], s1[32], s2[32], s3[32];
+        tmem_ld32(sc, s0);
+        tmem_ld32(sc + 32, s1);
+        tmem_ld32(sc + 64, s2);
+        tmem_ld32(sc + 96, s3);
+        tmem_ld_wait();
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (full) {
+          chunk_max<true>(s0, 0, lo, hi, mx4);
+          chunk_max<true>(s1, 32, lo, hi, mx4);
+          chunk_max<true>(s2, 64, lo, hi, mx4);
+          chunk_max<true>(s3, 96, lo, hi, mx4);
+        } else {
+          chunk_max<false>(s0, 0, lo, hi, mx4);
+          chunk_max<false>(s1, 32, lo, hi, mx4);
+          chunk_max<false>(s2, 64, lo, hi, mx4);
+          chunk_max<false>(s3, 96, lo, hi, mx4);
         }
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
+        // The running max grew by more than 2^8 (or this is the first finite
+        // max): move to the new max.  Rows that already accumulated O rescale
+        // it; tcgen05.ld / st are warp-collective, so the whole warp takes the
+        // TMEM round trip when any of its rows needs it (factor 1 elsewhere).
+        const bool move = mx > m_use + RESCALE_LOG2 || (j == 0 && mx > m_use);
+        const bool rescale_o = move && j > 0 && m_use != -INFINITY;
+        const float f = rescale_o ? exp2f(m_use - mx) : 1.f;
+        if (__any_sync(0xffffffffu, rescale_o)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[hd], (t - 1) & 1, a.status))) {  // P.V of tile j-1 landed
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; c++) {
+            uint32_t r[32];
+            tmem_ld32(oc + 32 * c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+            tmem_st32(oc + 32 * c, r);
+          }
+          tmem_st_wait();
+        }
+        if (move) {
+          l *= f;
+          m_use = mx;
+        }
+        // P = exp2(S*scale - m) as bf16, written over the S columns already
+        // read (keys 64c..64c+63 land in columns 32c..32c+31).
+        const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          uint32_t pk[32];
+          if (full)
+            chunk_p<true>(s0, s1, 0, lo, hi, a.scale_log2, neg_m, ls, pk);
+          else
+            chunk_p<false>(s0, s1, 0, lo, hi, a.scale_log2, neg_m, ls, pk);
+          tmem_st32(sc, pk);
+        }
+        {
+          uint32_t pk[32];
+          if (full)
+            chunk_p<true>(s2, s3, 64, lo, hi, a.scale_log2, neg_m, ls, pk);
+          else
+            chunk_p<false>(s2, s3, 64, lo, hi, a.scale_log2, neg_m, ls, pk);
+          tmem_st32(sc + 32, pk);
+        }
+        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
         tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[hd]);
       }
-      if (move) {
-        l *= f;
-        m_use = mx;
-      }
-      // P = exp2(S*scale - m) as bf16, written over the S columns already
-      // read (keys 64c..64c+63 land in columns 32c..32c+31).
-      const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
-      {
-        uint32_t pk[32];
-        if (full)
-          chunk_p<true>(s0, s1, 0, lo, hi, a.scale_log2, neg_m, ls, pk);
-        else
-          chunk_p<false>(s0, s1, 0, lo, hi, a.scale_log2, neg_m, ls, pk);
-        tmem_st32(sc, pk);
-      }
-      {
-        uint32_t pk[32];
-        if (full)
-          chunk_p<true>(s2, s3, 64, lo, hi, a.scale_log2, neg_m, ls, pk);
-        else
-          chunk_p<false>(s2, s3, 64, lo, hi, a.scale_log2, neg_m, ls, pk);
-        tmem_st32(sc + 32, pk);
-      }
-      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      tmem_st_wait();
+      // ---------------- epilogue: O / l ----------------
+      // O comes out of TMEM in one go (128 registers; the S registers are
+      // dead here), then o_free lets the next item's first P.V overwrite it
+      // while this warp normalises and stores.
+      if (ok && !__all_sync(0xffffffffu, mbar_wait(&o_done[hd], (kt + it.ntiles - 1) & 1, a.status))) ok = false;
+      if (!ok) break;  // warp-uniform
+      tc_fence_after();
+      uint32_t o[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; c++) tmem_ld32(oc + 32 * c, o[c]);
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[hd]);
-    }
-    // ---------------- epilogue: O / l (TMEM loads warp-wide, stores per row) ----------------
-    if (ok && !__all_sync(0xffffffffu, mbar_wait(&o_done[hd], (ntiles - 1) & 1, a.status))) ok = false;
-    tc_fence_after();
-    const bool store = query < a.T;
-    const float inv = 1.f / l;
-    const size_t obase = (((size_t)b * a.T + min(query, a.T - 1)) * a.H + (h0 + hd)) * HD;
+      if (lane == 0) mbar_arrive(&o_free[hd]);
+      if (query < a.T) {
+        const float inv = 1.f / l;
+        const size_t obase = (((size_t)it.b * a.T + query) * a.H + (it.h0 + hd)) * HD;
 #pragma unroll
-    for (int c = 0; c < 4 && ok; c++) {  // ok is warp-uniform
-      uint32_t r[32];
-      tmem_ld32(oc + 32 * c, r);
-      tmem_ld_wait();
-      if (store) {
-        if (a.out_bf16) {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + obase + 32 * c);
+        for (int c = 0; c < 4; c++) {
+          if (a.out_bf16) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + obase + 32 * c);
 #pragma unroll
-          for (int i = 0; i < 4; i++) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
-            dst[i] = w;
+            for (int i = 0; i < 4; i++) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(o[c][8 * i + 0]) * inv, __uint_as_float(o[c][8 * i + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(o[c][8 * i + 2]) * inv, __uint_as_float(o[c][8 * i + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(o[c][8 * i + 4]) * inv, __uint_as_float(o[c][8 * i + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(o[c][8 * i + 6]) * inv, __uint_as_float(o[c][8 * i + 7]) * inv);
+              dst[i] = w;
+            }
+          } else {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + obase + 32 * c);
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+              dst[i] = make_float4(__uint_as_float(o[c][4 * i]) * inv, __uint_as_float(o[c][4 * i + 1]) * inv,
+                                   __uint_as_float(o[c][4 * i + 2]) * inv, __uint_as_float(o[c][4 * i + 3]) * inv);
           }
-        } else {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + obase + 32 * c);
-#pragma unroll
-          for (int i = 0; i < 8; i++)
-            dst[i] = make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
-                                 __uint_as_float(r[4 * i + 2]) * inv, __uint_as_float(r[4 * i + 3]) * inv);
         }
       }
+      kt += it.ntiles;
     }
   }
   tc_fence_before();
@@ -380,15 +462,23 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
 }
 
 template <int NHD>
-int launch_swa(hcu_context* h, const SwaArgs& args, dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk,
+int launch_swa(hcu_context* h, const SwaArgs& args, const CUtensorMap& tq, const CUtensorMap& tk,
                const CUtensorMap& tv) {
-  constexpr size_t smem = 1024 + NHD * TILE + KV_STAGES * KV_STAGE + 12 * 8 + 16;
+  constexpr size_t smem = 1024 + NHD * TILE + KV_STAGES * KV_STAGE + 16 * 8 + 16;
   auto kern = swa_prefill_kernel<NHD>;
   static bool attr_done = false;
   if (!attr_done) {
     HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "hcu_swa_prefill: smem attribute"));
     attr_done = true;
+  }
+  // One CTA per SM (the shared memory admits no second), never more CTAs than
+  // items.  HCU_SWA_CTAS caps the grid (tests use it to give every CTA a long
+  // chain of items on small shapes).
+  int grid = args.n_items < h->sm_count ? args.n_items : h->sm_count;
+  if (const char* env = getenv("HCU_SWA_CTAS")) {
+    const int c = atoi(env);
+    if (c > 0 && c < grid) grid = c;
   }
   kern<<<grid, sw_threads(NHD), smem, h->stream>>>(tq, tk, tv, args);
   return after_launch("hcu_swa_prefill: launch");
@@ -443,7 +533,9 @@ extern "C" int hcu_swa_prefill(hcu_handle h, const hcu_swa_params* p, const void
   args.out = out;
   args.out_bf16 = p->out_dtype == HCU_DT_BF16;
   args.status = h->dev_status;
-  dim3 grid((unsigned)nqt, (unsigned)(KV * (G / nhd)), (unsigned)B);
-  if (nhd == 2) return hcu::launch_swa<2>(h, args, grid, tq, tk, tv);
-  return hcu::launch_swa<1>(h, args, grid, tq, tk, tv);
+  const long long n_items = (long long)B * KV * (G / nhd) * nqt;
+  if (n_items > (1LL << 30)) return fail(HCU_EINVAL, "hcu_swa_prefill: B x H x T/128 too large");
+  args.n_items = (int)n_items;
+  if (nhd == 2) return hcu::launch_swa<2>(h, args, tq, tk, tv);
+  return hcu::launch_swa<1>(h, args, tq, tk, tv);
 }
