@@ -71,19 +71,64 @@ def load_traffic(key: str):
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+    """Samples SM clocks and clock-event (throttle) reasons while the timed
+    region runs.  NVML is polled every ~2 ms from a thread (read-only queries),
+    so even a timed region of a few milliseconds gets samples; `mark_start` /
+    `mark_end` bracket the region and only samples inside it are reported.
+    Falls back to `nvidia-smi -lms 100` when NVML is unavailable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASON_NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.lines = []
         self.thread = None
+        self.samples = []  # (perf_counter, sm_mhz, reasons)
+        self.max_mhz = None
+        self.window = [None, None]
+        self._stop = threading.Event()
+        self.source = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            prop = torch.cuda.get_device_properties(self.gpu)
+            bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def start(self):
+        try:
+            nv, h = self._nvml_handle()
+            bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+
+            def poll():
+                while not self._stop.is_set():
+                    t = time.perf_counter()
+                    try:
+                        sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    except Exception:
+                        break
+                    self.samples.append((t, sm, {n for n, b in bits.items() if r & b}))
+                    time.sleep(0.002)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            self.source = "nvml"
+            return
+        except Exception:
+            pass
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -91,40 +136,53 @@ class ClockSampler:
         except Exception:
             self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.source = "nvidia-smi"
+
+        def read():
+            for line in self.proc.stdout:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm, self.max_mhz = float(parts[1]), float(parts[2])
+                except ValueError:
+                    continue
+                self.samples.append((time.perf_counter(), sm,
+                                     {n for n, v in zip(self.REASON_NAMES, parts[5:9]) if v.lower() == "active"}))
+
+        self.thread = threading.Thread(target=read, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def wait_ready(self, timeout: float = 10.0):
+        """Returns once the first sample arrived (nvidia-smi starts slowly)."""
+        t0 = time.perf_counter()
+        while self.thread is not None and not self.samples and time.perf_counter() - t0 < timeout:
+            time.sleep(0.01)
+
+    def mark_start(self):
+        self.window[0] = time.perf_counter()
+
+    def mark_end(self):
+        self.window[1] = time.perf_counter()
 
     def stop(self):
-        if self.proc is None:
+        if self.thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        if self.thread:
-            self.thread.join(timeout=2)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
+        self._stop.set()
+        if self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        self.thread.join(timeout=5)
+        t0, t1 = self.window
+        inside = [x for x in self.samples if t0 is not None and t1 is not None and t0 <= x[0] <= t1]
+        if not inside:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = set().union(*(x[2] for x in inside))
+        return {"sm_mhz": statistics.median(x[1] for x in inside), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(inside), "source": self.source}
 
 
 def dist_setup(args):
@@ -518,10 +576,11 @@ def main(argv=None):
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     clocks = ClockSampler(local)
     clocks.start()
-    time.sleep(0.3)
+    clocks.wait_ready()
     barrier()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    clocks.mark_start()
     t_start.record(stream)
     for i in range(args.steps):
         kev[i][0].record(stream)
@@ -531,6 +590,7 @@ def main(argv=None):
             dist.all_gather_into_tensor(gather_out, W["out"])
     t_end.record(stream)
     barrier()
+    clocks.mark_end()
     clk = clocks.stop()
     total_ms = t_start.elapsed_time(t_end)
     kernel_ms = [a.elapsed_time(b) for a, b in kev]

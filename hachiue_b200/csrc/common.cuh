@@ -69,13 +69,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread until the phase completes or
+// `hint_ns` passes, instead of returning at once: a waiting warp then takes
+// no issue slots from the warps that share its scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on phase `parity` of `bar`.  Returns false (and sets the device
-// status word) if the phase did not complete within HCU_WAIT_NS.
+// status word) if the phase did not complete within HCU_WAIT_NS.  Each poll
+// sleeps up to 1 ms.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     if (globaltimer() - t0 > HCU_WAIT_NS) {
       if (status) atomicOr(status, HCU_DEVERR_TIMEOUT);
       return false;

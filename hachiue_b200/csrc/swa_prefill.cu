@@ -45,6 +45,7 @@ constexpr int TILE = 2 * BOX;                 // [128 x 128] bf16 tile
 constexpr int KV_STAGES = 2;
 constexpr int KV_STAGE = 2 * TILE;            // K tile + V tile
 constexpr float RESCALE_LOG2 = 8.f;
+constexpr int kSwaPolyPairs = 0;  // of every 8 column pairs, exponentials on the FMA pipe
 
 struct SwaArgs {
   int B, T, H, KV, W, G, nqt;
@@ -76,6 +77,19 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
+// Sets the scores of columns outside this row's valid range lo..hi (tile
+// column indices) to -inf, in one 32-column chunk starting at column C0.
+// Chunks that every row of the warp keeps whole are skipped (a warp vote), so
+// only the one or two chunks a causal diagonal or window edge cuts through
+// pay a compare and select per element.
+template <int C0>
+__device__ __forceinline__ void mask_chunk(uint32_t (&r)[32], int lo, int hi) {
+  if (__all_sync(0xffffffffu, lo <= C0 && hi >= C0 + 31)) return;
+  const int a = lo - C0, b = hi - C0;
+#pragma unroll
+  for (int i = 0; i < 32; i++) r[i] = (i >= a && i <= b) ? r[i] : 0xff800000u;  // -inf
+}
+
 // Row max of one 32-column chunk; `lo`..`hi` is the valid column range (all
 // columns when FULL).
 template <bool FULL>
@@ -91,24 +105,76 @@ __device__ __forceinline__ void chunk_max(const uint32_t (&r)[32], int col0, int
   }
 }
 
+// Packed f32x2 arithmetic (sm_100): one instruction for two lanes of a
+// 64-bit register pair, half the issue slots of two scalar instructions.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x for two values on the FMA pipe, so that part of the exponentials
+// bypasses the SFU (16 results per clock per SM, the softmax's bottleneck).
+// x = j + f with j = round(x) (adding 1.5 * 2^23 rounds to nearest and leaves
+// j in the low mantissa bits), 2^f from a cubic in f on [-0.5, 0.5] fitted
+// for least maximum relative error (7.5e-5, far below the 2^-9 of the bf16
+// that P is rounded to), and 2^j added into the exponent field.  x is first
+// clamped at -125 so the result stays a normal float (masked scores give
+// about 2^-125 instead of 0, which no f32 row sum or P.V product can see).
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& p0, float& p1) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  constexpr float C0 = 0.99992812f, C1 = 0.69326097f, C2 = 0.24261054f, C3 = 0.05517132f;
+  const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t t = add2(x, f2_pack(kRound, kRound));
+  const uint64_t f = fma2(add2(t, f2_pack(-kRound, -kRound)), f2_pack(-1.f, -1.f), x);
+  uint64_t q = fma2(f2_pack(C3, C3), f, f2_pack(C2, C2));
+  q = fma2(q, f, f2_pack(C1, C1));
+  q = fma2(q, f, f2_pack(C0, C0));
+  float q0, q1, t0, t1;
+  f2_unpack(q, q0, q1);
+  f2_unpack(t, t0, t1);
+  p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+  p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
+}
+
 // P for 64 columns (two 32-column chunks) packed as 32 bf16x2 words; adds to
-// the row sum.
-template <bool FULL>
+// the row sum (two packed accumulators).  NPOLY of every 8 column pairs take
+// the FMA-pipe exponential, the rest the SFU.
+template <bool FULL, int NPOLY>
 __device__ __forceinline__ void chunk_p(const uint32_t (&r0)[32], const uint32_t (&r1)[32], int col0, int lo, int hi,
-                                        float scale, float neg_m, float (&ls)[4], uint32_t (&pk)[32]) {
+                                        uint64_t scale2, uint64_t negm2, uint64_t (&ls2)[2], uint32_t (&pk)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; i++) {
     const uint32_t x0 = i < 16 ? r0[2 * i] : r1[2 * i - 32];
     const uint32_t x1 = i < 16 ? r0[2 * i + 1] : r1[2 * i - 31];
-    float v0 = fmaf(__uint_as_float(x0), scale, neg_m);
-    float v1 = fmaf(__uint_as_float(x1), scale, neg_m);
+    float v0, v1;
+    f2_unpack(fma2(f2_pack(__uint_as_float(x0), __uint_as_float(x1)), scale2, negm2), v0, v1);
     if (!FULL) {
       const int c = col0 + 2 * i;
       v0 = (c >= lo && c <= hi) ? v0 : -INFINITY;
       v1 = (c + 1 >= lo && c + 1 <= hi) ? v1 : -INFINITY;
     }
-    const float p0 = fast_exp2(v0), p1 = fast_exp2(v1);
-    ls[i & 3] += p0 + p1;
+    float p0, p1;
+    if ((i & 7) < NPOLY) {
+      exp2_poly2(v0, v1, p0, p1);
+    } else {
+      p0 = fast_exp2(v0);
+      p1 = fast_exp2(v1);
+    }
+    ls2[i & 1] = add2(ls2[i & 1], f2_pack(p0, p1));
     pk[i] = pack_bf16x2(p0, p1);
   }
 }
@@ -158,7 +224,7 @@ __device__ __forceinline__ int swa_item_index(int k) {
 //   s_full / p_full / o_done once per key tile and head,
 //   o_free            once per item and head: the epilogue has moved O out of
 //                     TMEM, so the next item's first P.V may overwrite it.
-template <int NHD>
+template <int NHD, int NPOLY>
 __global__ void __launch_bounds__(sw_threads(NHD), 1)
     swa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const SwaArgs a) {
@@ -176,7 +242,8 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
   uint64_t* p_full = bars + 8;    // [NHD]
   uint64_t* o_done = bars + 10;   // [NHD]
   uint64_t* o_free = bars + 12;   // [NHD]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* p_half = bars + 14;   // [NHD]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -192,6 +259,7 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
       mbar_init(&o_free[i], 4);
+      mbar_init(&p_half[i], 4);
     }
     fence_barrier_init();
   }
@@ -258,13 +326,15 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         }
         mma_commit(&s_full[hd]);
       };
-      auto pv = [&](int hd, int s, bool acc) {
+      // P.V in two halves of 64 keys (k-steps 0-3, 4-7): the first runs
+      // while the softmax still computes the second half of P.
+      auto pv_half = [&](int hd, int s, int half, bool acc) {
 #pragma unroll
-        for (int ks = 0; ks < 8; ks++) {
+        for (int i = 0; i < 4; i++) {
+          const int ks = 4 * half + i;
           const uint64_t bd = smem_desc_sw128(kv0 + s * KV_STAGE + TILE + ks * 2048, BOX, 1024);  // MN-major V
           mma_f16_ts(tmem + o_col(hd), tmem + s_col(hd) + ks * 8, bd, idesc_pv, (acc || ks > 0) ? 1u : 0u);
         }
-        mma_commit(&o_done[hd]);
       };
       int kt = 0;  // key tiles consumed (ring position and per-head tile count)
       bool ok = true;
@@ -284,13 +354,20 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
           const int t = kt + j;
           const int s = t % KV_STAGES;
           for (int hd = 0; hd < NHD; hd++) {
-            if (!mbar_wait(&p_full[hd], t & 1, a.status) ||
+            if (!mbar_wait(&p_half[hd], t & 1, a.status) ||
                 (j == 0 && k > 0 && !mbar_wait(&o_free[hd], (k - 1) & 1, a.status))) {
               ok = false;
               break;
             }
             tc_fence_after();
-            pv(hd, s, j > 0);
+            pv_half(hd, s, 0, j > 0);
+            if (!mbar_wait(&p_full[hd], t & 1, a.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            pv_half(hd, s, 1, true);
+            mma_commit(&o_done[hd]);
             if (hd == NHD - 1) mma_commit(&kv_empty[s]);
             if (j + 1 < ntiles) {
               const int s1 = (t + 1) % KV_STAGES;
@@ -343,18 +420,17 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         tmem_ld32(sc + 64, s2);
         tmem_ld32(sc + 96, s3);
         tmem_ld_wait();
-        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (full) {
-          chunk_max<true>(s0, 0, lo, hi, mx4);
-          chunk_max<true>(s1, 32, lo, hi, mx4);
-          chunk_max<true>(s2, 64, lo, hi, mx4);
-          chunk_max<true>(s3, 96, lo, hi, mx4);
-        } else {
-          chunk_max<false>(s0, 0, lo, hi, mx4);
-          chunk_max<false>(s1, 32, lo, hi, mx4);
-          chunk_max<false>(s2, 64, lo, hi, mx4);
-          chunk_max<false>(s3, 96, lo, hi, mx4);
+        if (!full) {  // tile cut by the causal diagonal, the window edge or T
+          mask_chunk<0>(s0, lo, hi);
+          mask_chunk<32>(s1, lo, hi);
+          mask_chunk<64>(s2, lo, hi);
+          mask_chunk<96>(s3, lo, hi);
         }
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        chunk_max<true>(s0, 0, lo, hi, mx4);
+        chunk_max<true>(s1, 32, lo, hi, mx4);
+        chunk_max<true>(s2, 64, lo, hi, mx4);
+        chunk_max<true>(s3, 96, lo, hi, mx4);
         const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
         // The running max grew by more than 2^8 (or this is the first finite
         // max): move to the new max.  Rows that already accumulated O rescale
@@ -387,24 +463,29 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         // P = exp2(S*scale - m) as bf16, written over the S columns already
         // read (keys 64c..64c+63 land in columns 32c..32c+31).
         const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint64_t scale2 = f2_pack(a.scale_log2, a.scale_log2), negm2 = f2_pack(neg_m, neg_m);
+        uint64_t ls2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
         {
           uint32_t pk[32];
-          if (full)
-            chunk_p<true>(s0, s1, 0, lo, hi, a.scale_log2, neg_m, ls, pk);
-          else
-            chunk_p<false>(s0, s1, 0, lo, hi, a.scale_log2, neg_m, ls, pk);
+          chunk_p<true, NPOLY>(s0, s1, 0, lo, hi, scale2, negm2, ls2, pk);
           tmem_st32(sc, pk);
         }
+        // Keys 0..63 of P are in TMEM: the first half of P.V may start.
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_half[hd]);
         {
           uint32_t pk[32];
-          if (full)
-            chunk_p<true>(s2, s3, 64, lo, hi, a.scale_log2, neg_m, ls, pk);
-          else
-            chunk_p<false>(s2, s3, 64, lo, hi, a.scale_log2, neg_m, ls, pk);
+          chunk_p<true, NPOLY>(s2, s3, 64, lo, hi, scale2, negm2, ls2, pk);
           tmem_st32(sc + 32, pk);
         }
-        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        {
+          float a0, a1, b0, b1;
+          f2_unpack(ls2[0], a0, a1);
+          f2_unpack(ls2[1], b0, b1);
+          l += (a0 + a1) + (b0 + b1);
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -465,7 +546,7 @@ template <int NHD>
 int launch_swa(hcu_context* h, const SwaArgs& args, const CUtensorMap& tq, const CUtensorMap& tk,
                const CUtensorMap& tv) {
   constexpr size_t smem = 1024 + NHD * TILE + KV_STAGES * KV_STAGE + 16 * 8 + 16;
-  auto kern = swa_prefill_kernel<NHD>;
+  auto kern = swa_prefill_kernel<NHD, kSwaPolyPairs>;
   static bool attr_done = false;
   if (!attr_done) {
     HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
