@@ -30,6 +30,11 @@ SHADERS = ("kv_append_q8", "attention_q8", "deltanet_gbeta", "deltanet_recur")
 _DTYPE_OF_FORMAT = {KV_F32: torch.float32, KV_F16: torch.float16, KV_BF16: torch.bfloat16, KV_Q8_0: torch.int8}
 
 
+def _current_raw_stream(index: int) -> int:
+    f = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    return f(index) if f is not None else torch.cuda.current_stream(index).cuda_stream
+
+
 def _ptr(t: torch.Tensor | None) -> int | None:
     if t is None:
         return None
@@ -70,7 +75,17 @@ class KVCache:
         return self.k.shape[0]
 
     def c_struct(self) -> hcu_kv_cache:
-        return hcu_kv_cache(self.fmt, self.rows, _ptr(self.k), _ptr(self.v), _ptr(self.k_scale), _ptr(self.v_scale))
+        """The C view of the cache, rebuilt only when a tensor changed (a
+        decode step calls this once per layer)."""
+        key = (self.fmt, self.k.data_ptr(), self.v.data_ptr(), self.k.shape[0],
+               None if self.k_scale is None else self.k_scale.data_ptr(),
+               None if self.v_scale is None else self.v_scale.data_ptr())
+        cached = self.__dict__.get("_c_struct")
+        if cached is None or cached[0] != key:
+            cached = (key, hcu_kv_cache(self.fmt, self.rows, _ptr(self.k), _ptr(self.v), _ptr(self.k_scale),
+                                        _ptr(self.v_scale)))
+            self.__dict__["_c_struct"] = cached
+        return cached[1]
 
 
 class CudaBackend:
@@ -84,6 +99,8 @@ class CudaBackend:
         h = ctypes.c_void_p()
         check(self.lib.hcu_create(self.device.index, workspace_bytes, ctypes.byref(h)))
         self._h = h
+        self._stream = None  # the stream last bound to the handle
+        self._attn_params = hcu_attention_params()
 
     # -- lifecycle -----------------------------------------------------------
     def close(self) -> None:
@@ -98,8 +115,12 @@ class CudaBackend:
             pass
 
     def _bind_stream(self) -> None:
-        s = torch.cuda.current_stream(self.device).cuda_stream
-        check(self.lib.hcu_set_stream(self._h, ctypes.c_void_p(s)))
+        """Binds the handle to the device's current torch stream (a ctypes
+        call only when the stream changed since the last op)."""
+        s = _current_raw_stream(self.device.index)
+        if s != self._stream:
+            check(self.lib.hcu_set_stream(self._h, ctypes.c_void_p(s)))
+            self._stream = s
 
     def sync(self) -> None:
         self._bind_stream()
@@ -157,7 +178,7 @@ class CudaBackend:
         B = q.shape[0] if batched else 1
         S, H, Dh = q.shape[-3:]
         KV = kv_heads or cache.k.shape[1]
-        p = hcu_attention_params()
+        p = self._attn_params  # every field is set below
         p.S, p.H, p.KV, p.Dh = S, H, KV, Dh
         p.windowSize = window_size
         p.batch = B
