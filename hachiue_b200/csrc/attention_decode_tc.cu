@@ -17,7 +17,8 @@
 // live in TMEM: two S buffers and two O buffers, so the QK^T MMA of tile j+1
 // and the P.V MMA of tile j-1 overlap the softmax of tile j.
 //
-// Warp roles (192 threads): warp 0 issues TMA (3-stage, 64 KB per stage),
+// Warp roles (192 threads): warp 0 issues TMA (K tiles into a 2-slot ring,
+// V tiles into a 1-slot ring, 32 KB per slot),
 // warp 1 allocates TMEM and issues MMAs (one thread), warps 2-5 (128 threads,
 // one TMEM lane each) run the online softmax and accumulate each tile's O^T
 // into registers (thread = head-dim index), rescaled by the running max.
@@ -28,11 +29,16 @@ namespace hcu {
 namespace {
 
 constexpr int TC_THREADS = 192;
-constexpr int TC_NST = 3;
 constexpr int TC_TT = kTcTile;              // 128 tokens per tile
 constexpr int TC_DH = 128;
 constexpr int BOX_BYTES = TC_TT * 128;      // [128 tokens x 64 elements x 2 B]
-constexpr int STAGE_BYTES = 4 * BOX_BYTES;  // K lo, K hi, V lo, V hi
+constexpr int HALF_BYTES = 2 * BOX_BYTES;   // one K or V tile: lo and hi 64-element boxes
+// K runs a tile ahead of V: a K slot frees as soon as Q.K^T has read it, the
+// V slot only after P.V.  3 x 32 KB of ring (plus Q / P staging) lets two CTAs
+// share an SM for NC = 16, so one CTA's start-up and split merge overlap the
+// other's streaming.
+constexpr int TC_KST = 2, TC_VST = 1;
+constexpr int RING_BYTES = (TC_KST + TC_VST) * HALF_BYTES;
 constexpr float PSCALE = 256.f;             // q and p are scaled by 2^8 before splitting
 
 // x ~= sum of NT 16-bit terms, largest first.
@@ -76,7 +82,7 @@ __device__ __forceinline__ void st_u16(uint8_t* base, uint32_t off, uint16_t v) 
 }
 
 template <bool BF16, int R, int NC>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(TC_THREADS, NC == 16 ? 2 : 1)
     attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                           const AttnArgs a) {
   constexpr int NT = BF16 ? 3 : 2;
@@ -87,12 +93,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stages = smem;
-  uint8_t* qs = stages + TC_NST * STAGE_BYTES;  // [2 blocks][NC rows x 128 B]
+  uint8_t* stages = smem;                       // K slots, then the V slot
+  uint8_t* vslot = stages + TC_KST * HALF_BYTES;
+  uint8_t* qs = stages + RING_BYTES;            // [2 blocks][NC rows x 128 B]
   uint8_t* ps = qs + 2 * QS_BLK;                // [2 buffers][2 blocks][NC rows x 128 B]
   uint64_t* bars = reinterpret_cast<uint64_t*>(ps + 4 * QS_BLK);
-  uint64_t* kv_full = bars;
-  uint64_t* kv_empty = bars + 3;
+  uint64_t* k_full = bars;                      // [TC_KST]
+  uint64_t* k_empty = bars + 2;                 // [TC_KST]
+  uint64_t* v_full = bars + 4;
+  uint64_t* v_empty = bars + 5;
   uint64_t* s_full = bars + 6;
   uint64_t* s_free = bars + 8;
   uint64_t* p_full = bars + 10;
@@ -114,10 +123,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int ntiles = (u.k_hi - u.k_lo + TC_TT - 1) / TC_TT;
 
   if (tid == 0) {
-    for (int i = 0; i < 3; i++) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+    for (int i = 0; i < TC_KST; i++) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
     }
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
     for (int i = 0; i < 2; i++) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4);
@@ -166,16 +177,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (lane == 0) {
       prefetch_tensormap(&tmK);
       prefetch_tensormap(&tmV);
-      for (int it = 0; it < ntiles; ++it) {
-        const int s = it % TC_NST, rnd = it / TC_NST;
-        if (rnd > 0 && !mbar_wait(&kv_empty[s], (rnd - 1) & 1, a.status)) break;
-        uint8_t* st = stages + s * STAGE_BYTES;
+      auto load_k = [&](int it) {  // K of tile it, after Q.K^T(it - TC_KST) read its slot
+        const int s = it % TC_KST, rnd = it / TC_KST;
+        if (rnd > 0 && !mbar_wait(&k_empty[s], (rnd - 1) & 1, a.status)) return false;
+        uint8_t* st = stages + s * HALF_BYTES;
         const int row = (int)(u.roff + u.k_lo + it * TC_TT);
-        mbar_arrive_expect_tx(&kv_full[s], STAGE_BYTES);
-        tma_load_3d(st, &tmK, &kv_full[s], 0, u.g, row);
-        tma_load_3d(st + BOX_BYTES, &tmK, &kv_full[s], 64, u.g, row);
-        tma_load_3d(st + 2 * BOX_BYTES, &tmV, &kv_full[s], 0, u.g, row);
-        tma_load_3d(st + 3 * BOX_BYTES, &tmV, &kv_full[s], 64, u.g, row);
+        mbar_arrive_expect_tx(&k_full[s], HALF_BYTES);
+        tma_load_3d(st, &tmK, &k_full[s], 0, u.g, row);
+        tma_load_3d(st + BOX_BYTES, &tmK, &k_full[s], 64, u.g, row);
+        return true;
+      };
+      if (ntiles > 0 && load_k(0)) {
+        for (int it = 0; it < ntiles; ++it) {
+          if (it + 1 < ntiles && !load_k(it + 1)) break;
+          // V of tile it, after P.V(it - 1) read the slot
+          if (it > 0 && !mbar_wait(v_empty, (it - 1) & 1, a.status)) break;
+          const int row = (int)(u.roff + u.k_lo + it * TC_TT);
+          mbar_arrive_expect_tx(v_full, HALF_BYTES);
+          tma_load_3d(vslot, &tmV, v_full, 0, u.g, row);
+          tma_load_3d(vslot + BOX_BYTES, &tmV, v_full, 64, u.g, row);
+        }
       }
     }
   } else if (warp == 1) {
@@ -186,11 +207,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t st0 = smem_u32(stages), qs0 = smem_u32(qs), ps0 = smem_u32(ps);
       for (int j = 0; j <= ntiles; ++j) {
         if (j < ntiles) {
-          const int s = j % TC_NST, x = j & 1;
-          if (!mbar_wait(&kv_full[s], (j / TC_NST) & 1, a.status)) break;
+          const int s = j % TC_KST, x = j & 1;
+          if (!mbar_wait(&k_full[s], (j / TC_KST) & 1, a.status)) break;
           if (j >= 2 && !mbar_wait(&s_free[x], ((j - 2) >> 1) & 1, a.status)) break;
           tc_fence_after();
-          const uint32_t kb = st0 + s * STAGE_BYTES;
+          const uint32_t kb = st0 + s * HALF_BYTES;
 #pragma unroll
           for (int ks = 0; ks < 8; ks++) {
             const uint64_t ad = smem_desc_sw128(kb + (ks >> 2) * BOX_BYTES + (ks & 3) * 32, 16, 1024);
@@ -198,13 +219,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mma_f16_ss(tmem + S_COL + x * NC, ad, bd, idesc_qk, ks > 0);
           }
           mma_commit(&s_full[x]);
+          mma_commit(&k_empty[s]);
         }
         if (j >= 1) {
-          const int jp = j - 1, sp = jp % TC_NST, xp = jp & 1;
+          const int jp = j - 1, xp = jp & 1;
+          // V(jp) landed (the softmax also waits for it before zeroing rows of a partial tile)
+          if (!mbar_wait(v_full, jp & 1, a.status)) break;
           if (!mbar_wait(&p_full[xp], (jp >> 1) & 1, a.status)) break;
           if (jp >= 2 && !mbar_wait(&o_free[xp], ((jp - 2) >> 1) & 1, a.status)) break;
           tc_fence_after();
-          const uint32_t vb = st0 + sp * STAGE_BYTES + 2 * BOX_BYTES;
+          const uint32_t vb = st0 + TC_KST * HALF_BYTES;
           const uint32_t pb = ps0 + xp * 2 * QS_BLK;
 #pragma unroll
           for (int ks = 0; ks < 8; ks++) {
@@ -213,7 +237,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mma_f16_ss(tmem + O_COL + xp * NC, ad, bd, idesc_pv, ks > 0);
           }
           mma_commit(&o_full[xp]);
-          mma_commit(&kv_empty[sp]);
+          mma_commit(v_empty);
         }
       }
     }
@@ -293,10 +317,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < NT; k++) st_u16(pbuf, sw128_offset(k * R + r, (t & 63) * 2), tm[k]);
         }
+        if (u.k_lo + j * TC_TT + TC_TT > u.k_hi) {  // partial tile (uniform for the CTA)
+          // V(j) must have landed before its rows are overwritten.  P.V(j - 1)
+          // completing first (its own O buffer, one phase in flight) means the
+          // one V slot holds no earlier tile, so the wait for V(j) is exact.
+          const int jm = j - 1;
+          const bool okw = (jm < 0 || mbar_wait(&o_full[jm & 1], (jm >> 1) & 1, a.status)) &&
+                           mbar_wait(v_full, j & 1, a.status);
+          if (!__all_sync(0xffffffffu, okw)) {
+            aborted = true;
+            break;
+          }
+        }
         if (key >= u.k_hi) {
           // Rows past this split's keys may hold anything (another sequence,
           // unwritten cache): zero this token's V row so 0 * V stays 0.
-          uint8_t* vrow = stages + (j % TC_NST) * STAGE_BYTES + 2 * BOX_BYTES + t * 128;
+          uint8_t* vrow = vslot + t * 128;
 #pragma unroll
           for (int c = 0; c < 8; c++) {
             reinterpret_cast<uint4*>(vrow)[c] = make_uint4(0, 0, 0, 0);
@@ -355,7 +391,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 template <bool BF16, int R, int NC>
 int launch(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap& tk, const CUtensorMap& tv) {
   constexpr int QS_BLK = NC * 128;
-  constexpr size_t smem = 1024 + TC_NST * STAGE_BYTES + 6 * QS_BLK + 16 * 8 + 16 + (2 * 4 * R + 4 * R) * 4;
+  constexpr size_t smem = 1024 + RING_BYTES + 6 * QS_BLK + 16 * 8 + 16 + (2 * 4 * R + 4 * R) * 4;
   auto kern = attn_decode_tc_kernel<BF16, R, NC>;
   static bool attr_done = false;
   if (!attr_done) {
