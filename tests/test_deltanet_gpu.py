@@ -82,3 +82,28 @@ def test_segments_batched(backend, S, load):
     torch.cuda.synchronize()
     assert rel_l2(core.cpu().numpy(), ref_core) < TOL
     assert rel_l2(st_out.cpu().numpy(), ref_st) < TOL
+
+
+def test_single_token_items_chain(backend):
+    """S = 1 runs on the persistent step kernel (two CTAs per SM, the next
+    item's state prefetched by bulk copy): 80 sequences x 4 V heads = 320
+    items give some CTAs two items, through the non-fused entry point with a
+    loaded state."""
+    rng = np.random.default_rng(77)
+    B, S, NK, NV, D = 80, 1, 2, 4, 128
+    conv = 2 * NK * D + NV * D
+    qkv = rng.standard_normal((B, S, conv), dtype=np.float32)
+    a = rng.standard_normal((B, S, NV), dtype=np.float32)
+    b = rng.standard_normal((B, S, NV), dtype=np.float32)
+    a_neg = -np.ones(NV, np.float32)
+    dtb = np.zeros(NV, np.float32)
+    st0 = (0.02 * rng.standard_normal((B, NV, D, D))).astype(np.float32)
+    gb = np.stack([oracle.deltanet_gbeta(a[i], b[i], a_neg, dtb) for i in range(B)])
+    ref_core, ref_st = oracle.deltanet_recur_batch(qkv, gb, st0, NK, NV, True)
+    st_out = torch.zeros((B, NV, D, D), device=dev)
+    core = torch.zeros((B, S, NV, D), device=dev)
+    backend.deltanet_recur(T(qkv), T(gb), T(st0), core, st_out, NK, NV, True)
+    torch.cuda.synchronize()
+    assert rel_l2(core.cpu().numpy(), ref_core) < TOL
+    assert rel_l2(st_out.cpu().numpy(), ref_st) < TOL
+    assert backend.device_status() == 0
