@@ -26,7 +26,7 @@ EXPORTS = (
     "hcu_stream_sync", "hcu_alloc", "hcu_free", "hcu_memset", "hcu_copy_to_device", "hcu_copy_to_host",
     "hcu_device_status", "hcu_inject_failure", "hcu_dispatch", "hcu_attention", "hcu_attention_noalloc", "hcu_kv_append", "hcu_kv_append_rows",
     "hcu_deltanet_gbeta", "hcu_deltanet_recur", "hcu_deltanet_decode", "hcu_swa_prefill",
-    "hcu_deltanet_chunked_prefill",
+    "hcu_deltanet_chunked_prefill", "hcu_conv1d_causal", "hcu_deltanet_norm_gate", "hcu_gdn_layer_step",
 )
 
 
@@ -55,6 +55,20 @@ class hcu_deltanet_params(ctypes.Structure):
                 ("HK", ctypes.c_uint32), ("loadState", ctypes.c_uint32), ("batch", ctypes.c_uint32),
                 ("qkv_seq_stride", ctypes.c_uint64), ("gbeta_seq_stride", ctypes.c_uint64),
                 ("state_seq_stride", ctypes.c_uint64), ("core_seq_stride", ctypes.c_uint64)]
+
+
+class hcu_conv1d_params(ctypes.Structure):
+    _fields_ = [("S", ctypes.c_uint32), ("C", ctypes.c_uint32), ("K", ctypes.c_uint32), ("loadState", ctypes.c_uint32),
+                ("batch", ctypes.c_uint32), ("x_seq_stride", ctypes.c_uint64), ("y_seq_stride", ctypes.c_uint64),
+                ("state_seq_stride", ctypes.c_uint64)]
+
+
+class hcu_gdn_step_params(ctypes.Structure):
+    _fields_ = [("H", ctypes.c_uint32), ("HK", ctypes.c_uint32), ("DK", ctypes.c_uint32), ("DV", ctypes.c_uint32),
+                ("K", ctypes.c_uint32), ("loadState", ctypes.c_uint32), ("batch", ctypes.c_uint32),
+                ("eps", ctypes.c_float), ("qkv_seq_stride", ctypes.c_uint64), ("conv_seq_stride", ctypes.c_uint64),
+                ("ab_seq_stride", ctypes.c_uint64), ("z_seq_stride", ctypes.c_uint64),
+                ("state_seq_stride", ctypes.c_uint64), ("out_seq_stride", ctypes.c_uint64)]
 
 
 class hcu_swa_params(ctypes.Structure):
@@ -115,6 +129,9 @@ def load(path: str | None = None):
             "hcu_swa_prefill": ([vp, ctypes.POINTER(hcu_swa_params), vp, vp, vp, vp], i32),
             "hcu_deltanet_chunked_prefill": ([vp, ctypes.POINTER(hcu_gdn_prefill_params), vp, vp, vp, vp, vp, vp,
                                               vp, vp], i32),
+            "hcu_conv1d_causal": ([vp, ctypes.POINTER(hcu_conv1d_params), vp, vp, vp, vp, vp], i32),
+            "hcu_deltanet_norm_gate": ([vp, u32, u32, ctypes.c_float, vp, vp, vp, vp], i32),
+            "hcu_gdn_layer_step": ([vp, ctypes.POINTER(hcu_gdn_step_params)] + [vp] * 13, i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -22,10 +22,11 @@ import torch
 
 from . import _lib
 from ._lib import (DT_BF16, DT_F32, KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueError, check, hcu_attention_params,
-                   hcu_deltanet_params, hcu_gdn_prefill_params, hcu_kv_cache, hcu_swa_params)
+                   hcu_conv1d_params, hcu_deltanet_params, hcu_gdn_prefill_params, hcu_gdn_step_params, hcu_kv_cache,
+                   hcu_swa_params)
 
 # The reference's op names on this path (src/kernels.ts SHADERS keys).
-SHADERS = ("kv_append_q8", "attention_q8", "deltanet_gbeta", "deltanet_recur")
+SHADERS = ("kv_append_q8", "attention_q8", "deltanet_gbeta", "deltanet_recur", "conv1d_causal", "deltanet_norm_gate")
 
 _DTYPE_OF_FORMAT = {KV_F32: torch.float32, KV_F16: torch.float16, KV_BF16: torch.bfloat16, KV_Q8_0: torch.int8}
 
@@ -231,6 +232,47 @@ class CudaBackend:
         p = self._dn_params(qkv_conv, NK, NV, D, load_state)
         check(self.lib.hcu_deltanet_decode(self._h, ctypes.byref(p), _ptr(qkv_conv), _ptr(a), _ptr(b), _ptr(a_neg),
                                            _ptr(dt_bias), _ptr(state_in), _ptr(core), _ptr(state_out)))
+
+    def conv1d_causal(self, x: torch.Tensor, w: torch.Tensor, state_in: torch.Tensor, y: torch.Tensor,
+                      state_out: torch.Tensor, load_state: bool = True) -> None:
+        """conv1d_causal + SiLU: x, y f32 [(B,) S, C]; w f32 [C, K]; conv states
+        f32 [(B,) K-1, C] (state_in may be state_out)."""
+        self._bind_stream()
+        p = hcu_conv1d_params()
+        p.batch = x.shape[0] if x.dim() == 3 else 1
+        p.S, p.C = x.shape[-2], x.shape[-1]
+        p.K = w.shape[1]
+        p.loadState = int(bool(load_state))
+        check(self.lib.hcu_conv1d_causal(self._h, ctypes.byref(p), _ptr(x), _ptr(w), _ptr(state_in), _ptr(y),
+                                         _ptr(state_out)))
+
+    def deltanet_norm_gate(self, core: torch.Tensor, z: torch.Tensor, gamma: torch.Tensor, y: torch.Tensor,
+                           eps: float) -> None:
+        """Gated RMSNorm over rows of DV: core, z, y f32 [..., DV]; gamma f32 [DV]."""
+        self._bind_stream()
+        DV = gamma.shape[0]
+        check(self.lib.hcu_deltanet_norm_gate(self._h, core.numel() // DV, DV, float(eps), _ptr(core), _ptr(z),
+                                              _ptr(gamma), _ptr(y)))
+
+    def gdn_layer_step(self, qkv_mixed: torch.Tensor, conv_w: torch.Tensor, conv_in: torch.Tensor,
+                       conv_out: torch.Tensor, a: torch.Tensor, b: torch.Tensor, a_neg: torch.Tensor,
+                       dt_bias: torch.Tensor, z: torch.Tensor, gamma: torch.Tensor, state_in: torch.Tensor,
+                       state_out: torch.Tensor, out: torch.Tensor, NK: int, NV: int, eps: float,
+                       load_state: bool = True, D: int = 128) -> None:
+        """One GDN layer step for one token per sequence, fused (conv1d_causal,
+        g / beta, recurrence, gated RMSNorm): qkv_mixed f32 [B, C]; conv_w f32
+        [C, 4]; conv states f32 [B, 3, C] (in and out different); a, b f32
+        [B, NV]; z f32 [B, NV*D]; gamma f32 [D]; states f32 [B, NV, D, D];
+        out f32 [B, NV*D]."""
+        self._bind_stream()
+        p = hcu_gdn_step_params()
+        p.batch = qkv_mixed.shape[0] if qkv_mixed.dim() == 2 else 1
+        p.H, p.HK, p.DK, p.DV, p.K = NV, NK, D, D, conv_w.shape[1]
+        p.loadState = int(bool(load_state))
+        p.eps = float(eps)
+        check(self.lib.hcu_gdn_layer_step(self._h, ctypes.byref(p), _ptr(qkv_mixed), _ptr(conv_w), _ptr(conv_in),
+                                          _ptr(conv_out), _ptr(a), _ptr(b), _ptr(a_neg), _ptr(dt_bias), _ptr(z),
+                                          _ptr(gamma), _ptr(state_in), _ptr(state_out), _ptr(out)))
 
     def swa_prefill(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
                     window: int = 0) -> None:

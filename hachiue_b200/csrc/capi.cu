@@ -276,6 +276,26 @@ int hcu_dispatch(hcu_handle h, const char* shader, const uint32_t words[8], void
                               static_cast<const float*>(buffers[2]), static_cast<float*>(buffers[3]),
                               static_cast<float*>(buffers[4]));
   }
+  if (!strcmp(shader, "conv1d_causal")) {
+    HCU_TRY(need(5));
+    hcu_conv1d_params p{};
+    p.S = words[0];
+    p.C = words[1];
+    p.K = words[2];
+    p.loadState = words[3];
+    p.batch = 1;
+    return hcu_conv1d_causal(h, &p, static_cast<const float*>(buffers[0]), static_cast<const float*>(buffers[1]),
+                             static_cast<const float*>(buffers[2]), static_cast<float*>(buffers[3]),
+                             static_cast<float*>(buffers[4]));
+  }
+  if (!strcmp(shader, "deltanet_norm_gate")) {
+    HCU_TRY(need(4));
+    float eps;
+    memcpy(&eps, &words[2], sizeof(float));  // mkUniform writes rmsEps as an f32 word (src/engine.ts:1398)
+    return hcu_deltanet_norm_gate(h, words[0], words[1], eps, static_cast<const float*>(buffers[0]),
+                                  static_cast<const float*>(buffers[1]), static_cast<const float*>(buffers[2]),
+                                  static_cast<float*>(buffers[3]));
+  }
   return fail(HCU_EINVAL, "missing pipeline %s", shader);
 }
 

@@ -45,7 +45,20 @@ struct DnArgs {
   int S, H, HK, load_state;
   long long qkv_stride, gbeta_stride, ab_stride, state_stride, core_stride;
   uint32_t* status;  // device status word (bounded waits of the step kernel)
+  // Layer step only (conv1d_causal before, deltanet_norm_gate after the recurrence):
+  // qkv holds the pre-conv mix [C]; conv state [K-1][C] in / out (ping-pong);
+  // z [H*DV] gate; gamma [DV]; out [H*DV] the gated RMSNorm of the core row.
+  const float* conv_w;
+  const float* conv_in;
+  float* conv_out;
+  const float* z;
+  const float* gamma;
+  float* out;
+  float eps;
+  long long conv_stride, z_stride, out_stride;
 };
+
+constexpr int LAYER_K = 4;  // conv1d width of the fused layer step (qwen35 convKernel)
 
 __device__ __forceinline__ void gbeta_f64(float a, float dtb, float aneg, float bb, float* g, float* beta) {
   const double x = (double)a + (double)dtb;
@@ -191,13 +204,22 @@ __global__ void __launch_bounds__(DN_THREADS, 2) deltanet_recur_kernel(const DnA
 // memory by bulk copy, with the next q / k / v and a / b in registers, so the
 // SM's HBM stream does not pause for the reductions and barriers of an update.
 // The arithmetic is the per-token body of deltanet_recur_kernel.
-template <bool FUSED>
+//
+// LAYER adds the layer's neighbours of the recurrence (src/engine.ts:1358-1400)
+// to the same pass: the causal conv1d + SiLU of the token's q / k / v channels
+// from the pre-conv mix and the conv state (conv1d_causal, src/kernels.ts:
+// 1431-1466), and the gated RMSNorm of the output row (deltanet_norm_gate,
+// src/kernels.ts:1578-1611), so neither qkvConv nor core makes an HBM round
+// trip.  Each item writes the new conv state of its V channels; the q / k
+// channels of QK head hk are written by the item of V head hk.
+template <bool FUSED, bool LAYER>
 __global__ void __launch_bounds__(DN_THREADS, 2) deltanet_step_kernel(const DnArgs p, int n_items) {
   extern __shared__ __align__(16) float sstate[];  // [128][128] f32: the next item's state
   __shared__ float qs[DN_D], ks[DN_D];
   __shared__ float red_k[8][DN_D], red_q[8][DN_D];
   __shared__ float sdelta[DN_D];
   __shared__ float scal[6];  // ik, iq, k.q (raw), exp(g), beta
+  __shared__ float nrm[4];   // LAYER: partial sums of squares of the output row
   __shared__ uint64_t full;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -218,16 +240,36 @@ __global__ void __launch_bounds__(DN_THREADS, 2) deltanet_step_kernel(const DnAr
     for (int c = 0; c < 4; c++) bulk_load(sstate + c * (DN_D * DN_D / 4), src + c * (DN_D * DN_D / 4), STATE_BYTES / 4, &full);
   };
   struct Small {
-    float x;       // q (tid < 128) or k (tid >= 128) element
-    float v;       // v element (tid < 128)
+    float x;       // q (tid < 128) or k (tid >= 128) element (LAYER: pre-conv)
+    float v;       // v element (tid < 128) (LAYER: pre-conv)
     float ga, gb;  // thread 0: a, b (fused) or g, beta
+    // LAYER: conv taps and state of the two channels, and the gate element
+    float wx[LAYER ? LAYER_K : 1], wv[LAYER ? LAYER_K : 1];
+    float cx[LAYER ? LAYER_K - 1 : 1], cv[LAYER ? LAYER_K - 1 : 1];
+    float z;
   };
+  const long long conv_c = 2 * key_dim + (long long)p.H * DN_D;  // channels of the conv
   auto load_small = [&](int it, Small& I) {
     const int h = it % p.H, bidx = it / p.H, hk = h % p.HK;
     const float* row = p.qkv + bidx * p.qkv_stride;
-    I.x = tid < DN_D ? __ldg(row + (long long)hk * DN_D + tid)
-                     : __ldg(row + key_dim + (long long)hk * DN_D + (tid - DN_D));
-    I.v = tid < DN_D ? __ldg(row + 2 * key_dim + (long long)h * DN_D + tid) : 0.f;
+    const long long chx = tid < DN_D ? (long long)hk * DN_D + tid : key_dim + (long long)hk * DN_D + (tid - DN_D);
+    const long long chv = 2 * key_dim + (long long)h * DN_D + (tid & (DN_D - 1));
+    I.x = __ldg(row + chx);
+    I.v = tid < DN_D ? __ldg(row + chv) : 0.f;
+    if constexpr (LAYER) {
+#pragma unroll
+      for (int j = 0; j < LAYER_K; j++) {
+        I.wx[j] = __ldg(p.conv_w + chx * LAYER_K + j);
+        I.wv[j] = tid < DN_D ? __ldg(p.conv_w + chv * LAYER_K + j) : 0.f;
+      }
+      const float* cs = p.conv_in + bidx * p.conv_stride;
+#pragma unroll
+      for (int j = 0; j < LAYER_K - 1; j++) {
+        I.cx[j] = p.load_state ? __ldg(cs + j * conv_c + chx) : 0.f;
+        I.cv[j] = p.load_state && tid < DN_D ? __ldg(cs + j * conv_c + chv) : 0.f;
+      }
+      I.z = tid < DN_D ? __ldg(p.z + bidx * p.z_stride + (long long)h * DN_D + tid) : 0.f;
+    }
     I.ga = I.gb = 0.f;
     if (tid == 0) {
       if constexpr (FUSED) {
@@ -267,7 +309,34 @@ __global__ void __launch_bounds__(DN_THREADS, 2) deltanet_step_kernel(const DnAr
 #pragma unroll
       for (int i = 0; i < 16; i++) st[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (tid < DN_D) qs[tid] = cur.x; else ks[tid - DN_D] = cur.x;
+    float xval = cur.x, vval = cur.v;
+    if constexpr (LAYER) {
+      // conv1d_causal for this token: ext rows 0..K-2 = conv state, row K-1 = x
+      float ax = 0.f, av = 0.f;
+#pragma unroll
+      for (int j = 0; j < LAYER_K - 1; j++) {
+        ax = fmaf(cur.wx[j], cur.cx[j], ax);
+        av = fmaf(cur.wv[j], cur.cv[j], av);
+      }
+      ax = fmaf(cur.wx[LAYER_K - 1], cur.x, ax);
+      av = fmaf(cur.wv[LAYER_K - 1], cur.v, av);
+      xval = ax / (1.f + expf(-ax));
+      vval = av / (1.f + expf(-av));
+      // new conv state: rows shift up by one, the token's mix becomes row K-2
+      const int hk = h % p.HK;
+      float* cs = p.conv_out + bidx * p.conv_stride;
+      const long long chx = tid < DN_D ? (long long)hk * DN_D + tid : key_dim + (long long)hk * DN_D + (tid - DN_D);
+      const long long chv = 2 * key_dim + (long long)h * DN_D + tid;
+      if (h == hk) {
+#pragma unroll
+        for (int j = 0; j < LAYER_K - 1; j++) cs[j * conv_c + chx] = j + 1 < LAYER_K - 1 ? cur.cx[j + 1] : cur.x;
+      }
+      if (tid < DN_D) {
+#pragma unroll
+        for (int j = 0; j < LAYER_K - 1; j++) cs[j * conv_c + chv] = j + 1 < LAYER_K - 1 ? cur.cv[j + 1] : cur.v;
+      }
+    }
+    if (tid < DN_D) qs[tid] = xval; else ks[tid - DN_D] = xval;
     if (tid == 0) {
       float g = cur.ga, beta = cur.gb;
       if constexpr (FUSED) gbeta_f64(cur.ga, p.dt_bias[h], p.a_neg[h], cur.gb, &g, &beta);
@@ -297,6 +366,7 @@ __global__ void __launch_bounds__(DN_THREADS, 2) deltanet_step_kernel(const DnAr
     __syncthreads();
     const float ik = scal[0], iq = scal[1], gt = scal[3], bt = scal[4];
     const float kq = scal[2] * ik * iq;  // k^ . q^
+    float orow = 0.f;                    // output element of thread tid < 128
     float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = pk;
 #pragma unroll
     for (int i = 0; i < 16; i++) {
@@ -325,11 +395,26 @@ __global__ void __launch_bounds__(DN_THREADS, 2) deltanet_step_kernel(const DnAr
         kvd += red_k[w][tid];
         qd += red_q[w][tid];
       }
-      const float delta = (cur.v - kvd) * bt;
+      const float delta = (vval - kvd) * bt;
       sdelta[tid] = delta;
-      p.core[bidx * p.core_stride + (long long)h * DN_D + tid] = fmaf(delta, kq, qd);
+      orow = fmaf(delta, kq, qd);
+      if constexpr (LAYER) {
+        const float sq = warp_sum(orow * orow);
+        if (lane == 0) nrm[warp] = sq;
+      } else {
+        p.core[bidx * p.core_stride + (long long)h * DN_D + tid] = orow;
+      }
     }
     __syncthreads();
+    if constexpr (LAYER) {
+      // deltanet_norm_gate: y = gamma * o / sqrt(mean(o^2) + eps) * silu(z)
+      if (tid < DN_D) {
+        const float inv = rsqrtf(((nrm[0] + nrm[1]) + (nrm[2] + nrm[3])) * (1.f / DN_D) + p.eps);
+        const float zz = cur.z;
+        p.out[bidx * p.out_stride + (long long)h * DN_D + tid] =
+            __ldg(p.gamma + tid) * (orow * inv) * (zz / (1.f + expf(-zz)));
+      }
+    }
     const float4 d4 = *reinterpret_cast<const float4*>(&sdelta[lane * 4]);
     float4* dst = reinterpret_cast<float4*>(p.state_out + bidx * p.state_stride + (long long)h * DN_D * DN_D);
 #pragma unroll
@@ -356,22 +441,95 @@ int launch_dn(hcu_context* h, const hcu_deltanet_params* p, DnArgs a, bool fused
     constexpr int smem = DN_D * DN_D * 4;
     static bool attr_done = false;
     if (!attr_done) {
-      HCU_TRY(check_cuda(cudaFuncSetAttribute(deltanet_step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              smem), "deltanet: smem attribute"));
-      HCU_TRY(check_cuda(cudaFuncSetAttribute(deltanet_step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              smem), "deltanet: smem attribute"));
+      HCU_TRY(check_cuda(cudaFuncSetAttribute(deltanet_step_kernel<true, false>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                         "deltanet: smem attribute"));
+      HCU_TRY(check_cuda(cudaFuncSetAttribute(deltanet_step_kernel<false, false>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                         "deltanet: smem attribute"));
       attr_done = true;
     }
     if (fused)
-      deltanet_step_kernel<true><<<grid, DN_THREADS, smem, h->stream>>>(a, (int)n);
+      deltanet_step_kernel<true, false><<<grid, DN_THREADS, smem, h->stream>>>(a, (int)n);
     else
-      deltanet_step_kernel<false><<<grid, DN_THREADS, smem, h->stream>>>(a, (int)n);
+      deltanet_step_kernel<false, false><<<grid, DN_THREADS, smem, h->stream>>>(a, (int)n);
   } else if (fused) {
     deltanet_recur_kernel<true><<<dim3(p->H, batch), DN_THREADS, 0, h->stream>>>(a);
   } else {
     deltanet_recur_kernel<false><<<dim3(p->H, batch), DN_THREADS, 0, h->stream>>>(a);
   }
   return HCU_OK;
+}
+
+// conv1d_causal (src/kernels.ts:1431-1466; JS src/wasm-backend.ts:1003-1031):
+// y[t][c] = silu(sum_j w[c][j] * ext(t + j, c)) with ext rows 0..K-2 the conv
+// state (zeros when !loadState) followed by the S input rows.  One thread per
+// (sequence, token, channel); f32 arithmetic like the WGSL.
+struct ConvArgs {
+  const float* x;
+  const float* w;
+  const float* state_in;
+  float* y;
+  float* state_out;
+  int S, C, K, load_state;
+  long long x_stride, y_stride, state_stride;
+};
+
+__device__ __forceinline__ float conv_ext(const ConvArgs& a, int b, int m, int c) {
+  if (m + 1 < a.K) return a.load_state ? a.state_in[b * a.state_stride + (long long)m * a.C + c] : 0.f;
+  return a.x[b * a.x_stride + (long long)(m - (a.K - 1)) * a.C + c];
+}
+
+__global__ void __launch_bounds__(256) conv1d_kernel(const ConvArgs a) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long n = (long long)a.S * a.C;
+  if (i >= n) return;
+  const int b = blockIdx.y;
+  const int c = (int)(i % a.C), t = (int)(i / a.C);
+  float acc = 0.f;
+  for (int j = 0; j < a.K; j++) acc = fmaf(__ldg(a.w + (long long)c * a.K + j), conv_ext(a, b, t + j, c), acc);
+  a.y[b * a.y_stride + i] = acc / (1.f + expf(-acc));
+}
+
+// The new conv state: the last K-1 rows of the extended sequence.  One thread
+// per (sequence, channel) reads all of them before writing any, so the state
+// may be updated in place (the output kernel, launched first on the same
+// stream, has finished reading the old rows).
+constexpr int CONV_KMAX = 8;
+__global__ void __launch_bounds__(256) conv1d_state_kernel(const ConvArgs a) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= a.C) return;
+  const int b = blockIdx.y;
+  float v[CONV_KMAX - 1];
+#pragma unroll
+  for (int sk = 0; sk < CONV_KMAX - 1; sk++)
+    if (sk < a.K - 1) v[sk] = conv_ext(a, b, a.S + sk, c);
+#pragma unroll
+  for (int sk = 0; sk < CONV_KMAX - 1; sk++)
+    if (sk < a.K - 1) a.state_out[b * a.state_stride + (long long)sk * a.C + c] = v[sk];
+}
+
+// deltanet_norm_gate (src/kernels.ts:1578-1611; JS src/wasm-backend.ts:
+// 1104-1117): per row, y = gamma * core / sqrt(mean(core^2) + eps) * silu(z).
+// One warp per row.
+__global__ void __launch_bounds__(256) norm_gate_kernel(const float* __restrict__ core, const float* __restrict__ z,
+                                                        const float* __restrict__ gamma, float* __restrict__ y,
+                                                        int rows, int DV, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long r = (long long)blockIdx.x * 8 + warp;
+  if (r >= rows) return;
+  const float* c = core + r * DV;
+  float s = 0.f;
+  for (int i = lane; i < DV; i += 32) {
+    const float v = c[i];
+    s = fmaf(v, v, s);
+  }
+  s = warp_sum(s);
+  const float inv = rsqrtf(s / (float)DV + eps);
+  for (int i = lane; i < DV; i += 32) {
+    const float zz = z[r * DV + i];
+    y[r * DV + i] = __ldg(gamma + i) * (c[i] * inv) * (zz / (1.f + expf(-zz)));
+  }
 }
 
 int check_dn(const hcu_deltanet_params* p, const char* op) {
@@ -454,4 +612,107 @@ extern "C" int hcu_deltanet_decode(hcu_handle h, const hcu_deltanet_params* p, c
   args.core = core;
   HCU_TRY(launch_dn(h, p, args, true));
   return hcu::after_launch("hcu_deltanet_decode");
+}
+
+extern "C" int hcu_conv1d_causal(hcu_handle h, const hcu_conv1d_params* p, const float* x, const float* w,
+                                 const float* state_in, float* y, float* state_out) {
+  HCU_TRY(hcu::begin_op(h, "hcu_conv1d_causal"));
+  if (!p || !x || !w || !y || !state_out || (p->loadState && !state_in))
+    return fail(HCU_EINVAL, "hcu_conv1d_causal: null argument");
+  if (p->S < 1 || p->C < 1 || p->K < 1 || p->K > (uint32_t)CONV_KMAX)
+    return fail(HCU_EINVAL, "hcu_conv1d_causal: need S, C >= 1 and 1 <= K <= %d", CONV_KMAX);
+  const int batch = p->batch ? (int)p->batch : 1;
+  if (batch > 65535) return fail(HCU_EINVAL, "hcu_conv1d_causal: batch > 65535");
+  const long long n = (long long)p->S * p->C;
+  if (n > 0x3fffffffLL) return fail(HCU_EINVAL, "hcu_conv1d_causal: S x C too large");
+  ConvArgs a{};
+  a.x = x;
+  a.w = w;
+  a.state_in = state_in;
+  a.y = y;
+  a.state_out = state_out;
+  a.S = (int)p->S;
+  a.C = (int)p->C;
+  a.K = (int)p->K;
+  a.load_state = p->loadState ? 1 : 0;
+  a.x_stride = p->x_seq_stride ? (long long)p->x_seq_stride : n;
+  a.y_stride = p->y_seq_stride ? (long long)p->y_seq_stride : n;
+  a.state_stride = p->state_seq_stride ? (long long)p->state_seq_stride : (long long)(p->K - 1) * p->C;
+  conv1d_kernel<<<dim3((unsigned)((n + 255) / 256), (unsigned)batch), 256, 0, h->stream>>>(a);
+  HCU_TRY(hcu::after_launch("hcu_conv1d_causal"));
+  if (p->K > 1) {
+    conv1d_state_kernel<<<dim3((unsigned)((p->C + 255) / 256), (unsigned)batch), 256, 0, h->stream>>>(a);
+    HCU_TRY(hcu::after_launch("hcu_conv1d_causal: state"));
+  }
+  return HCU_OK;
+}
+
+extern "C" int hcu_deltanet_norm_gate(hcu_handle h, uint32_t rows, uint32_t DV, float eps, const float* core,
+                                      const float* z, const float* gamma, float* y) {
+  HCU_TRY(hcu::begin_op(h, "hcu_deltanet_norm_gate"));
+  if (!core || !z || !gamma || !y) return fail(HCU_EINVAL, "hcu_deltanet_norm_gate: null buffer");
+  if (rows < 1 || DV < 1 || rows > 0x3fffffffu) return fail(HCU_EINVAL, "hcu_deltanet_norm_gate: bad rows / DV");
+  norm_gate_kernel<<<(rows + 7) / 8, 256, 0, h->stream>>>(core, z, gamma, y, (int)rows, (int)DV, eps);
+  return hcu::after_launch("hcu_deltanet_norm_gate");
+}
+
+extern "C" int hcu_gdn_layer_step(hcu_handle h, const hcu_gdn_step_params* p, const float* qkv_mixed,
+                                  const float* conv_w, const float* conv_state_in, float* conv_state_out,
+                                  const float* a, const float* b, const float* a_neg, const float* dt_bias,
+                                  const float* z, const float* gamma, const float* state_in, float* state_out,
+                                  float* out) {
+  HCU_TRY(hcu::begin_op(h, "hcu_gdn_layer_step"));
+  if (!p || !qkv_mixed || !conv_w || !conv_state_out || !a || !b || !a_neg || !dt_bias || !z || !gamma ||
+      !state_out || !out || (p->loadState && (!state_in || !conv_state_in)))
+    return fail(HCU_EINVAL, "hcu_gdn_layer_step: null buffer");
+  if (p->DK != DN_D || p->DV != DN_D)
+    return fail(HCU_EUNSUPPORTED, "hcu_gdn_layer_step: DK=%u DV=%u (built: %d)", p->DK, p->DV, DN_D);
+  if (p->K != (uint32_t)LAYER_K) return fail(HCU_EUNSUPPORTED, "hcu_gdn_layer_step: K=%u (built: %d)", p->K, LAYER_K);
+  if (p->H < 1 || p->HK < 1 || p->H < p->HK)
+    return fail(HCU_EINVAL, "hcu_gdn_layer_step: need H >= HK >= 1 (every QK head's conv state has a writer)");
+  if (p->loadState && conv_state_in == conv_state_out)
+    return fail(HCU_EINVAL, "hcu_gdn_layer_step: conv state in and out must be different buffers (ping-pong)");
+  const int batch = p->batch ? (int)p->batch : 1;
+  if (batch > 65535) return fail(HCU_EINVAL, "hcu_gdn_layer_step: batch > 65535");
+  HCU_TRY(check_align(state_out, "stateOut", "hcu_gdn_layer_step"));
+  if (p->loadState) HCU_TRY(check_align(state_in, "stateIn", "hcu_gdn_layer_step"));
+  const long long C = 2LL * p->HK * DN_D + (long long)p->H * DN_D;
+  DnArgs args{};
+  args.qkv = qkv_mixed;
+  args.a = a;
+  args.b = b;
+  args.a_neg = a_neg;
+  args.dt_bias = dt_bias;
+  args.state_in = state_in;
+  args.state_out = state_out;
+  args.S = 1;
+  args.H = (int)p->H;
+  args.HK = (int)p->HK;
+  args.load_state = p->loadState ? 1 : 0;
+  args.qkv_stride = p->qkv_seq_stride ? (long long)p->qkv_seq_stride : C;
+  args.ab_stride = p->ab_seq_stride ? (long long)p->ab_seq_stride : p->H;
+  args.state_stride = p->state_seq_stride ? (long long)p->state_seq_stride : (long long)p->H * DN_D * DN_D;
+  args.conv_w = conv_w;
+  args.conv_in = conv_state_in;
+  args.conv_out = conv_state_out;
+  args.conv_stride = p->conv_seq_stride ? (long long)p->conv_seq_stride : (LAYER_K - 1) * C;
+  args.z = z;
+  args.z_stride = p->z_seq_stride ? (long long)p->z_seq_stride : (long long)p->H * DN_D;
+  args.gamma = gamma;
+  args.out = out;
+  args.out_stride = p->out_seq_stride ? (long long)p->out_seq_stride : (long long)p->H * DN_D;
+  args.eps = p->eps;
+  args.status = h->dev_status;
+  const long long n = (long long)batch * p->H;
+  const int grid = (int)(n < 2LL * h->sm_count ? n : 2LL * h->sm_count);
+  constexpr int smem = DN_D * DN_D * 4;
+  static bool attr_done = false;
+  if (!attr_done) {
+    HCU_TRY(hcu::check_cuda(cudaFuncSetAttribute(deltanet_step_kernel<true, true>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                            "hcu_gdn_layer_step: smem attribute"));
+    attr_done = true;
+  }
+  deltanet_step_kernel<true, true><<<grid, DN_THREADS, smem, h->stream>>>(args, (int)n);
+  return hcu::after_launch("hcu_gdn_layer_step");
 }

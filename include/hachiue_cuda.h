@@ -122,6 +122,11 @@ int hcu_inject_failure(hcu_handle h, int status, int n);
  *   "deltanet_recur" words [S, H, DK, DV, HK, loadState]        (kernels.ts:1496)
  *                    buffers [qkvConv f32, gbeta f32, stateIn f32, core f32,
  *                             stateOut f32]   (stateIn == stateOut allowed)
+ *   "conv1d_causal"  words [S, C, K, loadState]                 (kernels.ts:1431)
+ *                    buffers [x f32, w f32, stateIn f32, y f32, stateOut f32]
+ *                    (stateIn == stateOut allowed)
+ *   "deltanet_norm_gate" words [rows, DV, eps (f32 bits), 0]   (kernels.ts:1578)
+ *                    buffers [core f32, z f32, gamma f32, y f32]
  *
  * Q8 scales are stored as in the JS backend (amax/127, wasm-backend.ts:815),
  * not the WGSL's amax (kernels.ts:1333); a cache written by this library is
@@ -247,6 +252,61 @@ int hcu_deltanet_decode(hcu_handle h, const hcu_deltanet_params *p, const float 
                         const float *a, const float *b, const float *a_neg,
                         const float *dt_bias, const float *state_in, float *core,
                         float *state_out);
+
+/* Causal depthwise conv1d of width K plus SiLU, with its conv state:
+ * conv1d_causal (src/kernels.ts:1431-1466; JS src/wasm-backend.ts:1003-1031).
+ * x f32 [batch, S, C]; w f32 [C, K]; state f32 [batch, K-1, C], read when
+ * loadState and then replaced by the last K-1 rows of the extended sequence
+ * (state_in == state_out updates in place); y f32 [batch, S, C] with
+ * y[t][c] = silu(sum_j w[c][j] * ext(t + j, c)).  Strides are per sequence, in
+ * elements (0 = dense).  1 <= K <= 8. */
+typedef struct {
+  uint32_t S, C, K, loadState;
+  uint32_t batch;                 /* 0 or 1: single sequence */
+  uint64_t x_seq_stride;          /* default S * C */
+  uint64_t y_seq_stride;          /* default S * C */
+  uint64_t state_seq_stride;      /* default (K - 1) * C */
+} hcu_conv1d_params;
+
+int hcu_conv1d_causal(hcu_handle h, const hcu_conv1d_params *p, const float *x, const float *w,
+                      const float *state_in, float *y, float *state_out);
+
+/* Gated RMSNorm of the recurrence output: y = gamma * core /
+ * sqrt(mean(core^2) + eps) * silu(z) per row of DV (deltanet_norm_gate,
+ * src/kernels.ts:1578-1611; JS src/wasm-backend.ts:1104-1117).  core, z, y
+ * f32 [rows, DV]; gamma f32 [DV]. */
+int hcu_deltanet_norm_gate(hcu_handle h, uint32_t rows, uint32_t DV, float eps, const float *core,
+                           const float *z, const float *gamma, float *y);
+
+/* One Gated DeltaNet layer step for one token per sequence (decode), fused:
+ * conv1d_causal on the pre-conv mix, g / beta, the delta-rule update and the
+ * gated RMSNorm, i.e. the dispatches at src/engine.ts:1367-1396 between the
+ * qkv / gate GEMVs and the ssm_out GEMV, with neither qkvConv nor core
+ * leaving the chip.
+ * qkv_mixed f32 [batch, C] (C = 2*HK*DK + H*DV, the attn_qkv GEMV output);
+ * conv_w f32 [C, K]; conv state f32 [batch, K-1, C], in and out different
+ * buffers (the engine's ping-pong, src/engine.ts:1371-1376); a, b f32
+ * [batch, H]; aNeg, dtBias f32 [H]; z f32 [batch, H*DV] (the attn_gate GEMV
+ * output); gamma f32 [DV] (ssm_norm); state f32 [batch, H, DK, DV], in place
+ * allowed; out f32 [batch, H*DV] (the input of ssm_out).  K = 4,
+ * DK = DV = 128, H >= HK. */
+typedef struct {
+  uint32_t H, HK, DK, DV, K, loadState;
+  uint32_t batch;                 /* 0 or 1: single sequence */
+  float eps;                      /* rmsEps */
+  uint64_t qkv_seq_stride;        /* default C */
+  uint64_t conv_seq_stride;       /* default (K - 1) * C */
+  uint64_t ab_seq_stride;         /* default H */
+  uint64_t z_seq_stride;          /* default H * DV */
+  uint64_t state_seq_stride;      /* default H * DK * DV */
+  uint64_t out_seq_stride;        /* default H * DV */
+} hcu_gdn_step_params;
+
+int hcu_gdn_layer_step(hcu_handle h, const hcu_gdn_step_params *p, const float *qkv_mixed,
+                       const float *conv_w, const float *conv_state_in, float *conv_state_out,
+                       const float *a, const float *b, const float *a_neg, const float *dt_bias,
+                       const float *z, const float *gamma, const float *state_in, float *state_out,
+                       float *out);
 
 /* Causal sliding-window attention over whole prompts (plamo3 SWA layers):
  * query i of each sequence attends keys max(0, i - window + 1) .. i

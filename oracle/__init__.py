@@ -56,6 +56,8 @@ def lib():
             L.oracle_deltanet_recur_batch.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i64, i64,
                                                       i64, i64, i32]
             L.oracle_f16_to_f64.argtypes = [ctypes.c_uint16]
+            L.oracle_conv1d_causal.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32]
+            L.oracle_deltanet_norm_gate.argtypes = [vp, vp, vp, vp, i32, i32, ctypes.c_float]
             L.oracle_f16_to_f64.restype = ctypes.c_double
             _ = f
             _lib = L
@@ -138,6 +140,53 @@ def deltanet_gbeta(a: np.ndarray, b: np.ndarray, a_neg: np.ndarray, dt_bias: np.
     out = np.zeros((2, S, NV), np.float32)
     lib().oracle_deltanet_gbeta(_p(a), _p(b), _p(a_neg), _p(dt_bias), _p(out), S, NV)
     return out
+
+
+def conv1d_causal(qkv_mixed: np.ndarray, conv_w: np.ndarray, conv_state: np.ndarray, load_state: bool = True):
+    """Causal conv1d + SiLU (src/wasm-backend.ts:1003-1031): qkv_mixed f32
+    [S, C], conv_w f32 [C, K], conv_state f32 [K-1, C].  Returns (qkv_conv
+    [S, C], new conv_state); the input state is not modified."""
+    S, C = qkv_mixed.shape
+    K = conv_w.shape[1]
+    st = np.array(conv_state, dtype=np.float32, copy=True, order="C")
+    out = np.zeros((S, C), np.float32)
+    lib().oracle_conv1d_causal(_p(np.ascontiguousarray(qkv_mixed, np.float32)),
+                               _p(np.ascontiguousarray(conv_w, np.float32)), _p(st), _p(out), S, C, K,
+                               int(load_state))
+    return out, st
+
+
+def deltanet_norm_gate(core: np.ndarray, z: np.ndarray, gamma: np.ndarray, eps: float) -> np.ndarray:
+    """Gated RMSNorm (src/wasm-backend.ts:1104-1117): core, z f32 [rows, DV],
+    gamma f32 [DV] -> y f32 [rows, DV]."""
+    DV = gamma.shape[0]
+    c = np.ascontiguousarray(core, np.float32).reshape(-1, DV)
+    zz = np.ascontiguousarray(z, np.float32).reshape(-1, DV)
+    y = np.zeros_like(c)
+    lib().oracle_deltanet_norm_gate(_p(c), _p(zz), _p(np.ascontiguousarray(gamma, np.float32)), _p(y), c.shape[0],
+                                    DV, float(eps))
+    return y.reshape(core.shape)
+
+
+def gdn_layer_step(qkv_mixed, conv_w, conv_state, a, b, a_neg, dt_bias, z, gamma, eps, state, NK: int, NV: int,
+                   load_state: bool = True):
+    """One Gated DeltaNet layer step for one token per sequence, as the engine
+    dispatches it between the qkv / gate GEMVs and ssm_out (src/engine.ts
+    :1367-1398; JS src/wasm-backend.ts:1003-1117): conv1d_causal, g / beta,
+    the recurrence, the gated RMSNorm.  qkv_mixed [B, C]; conv_w [C, K];
+    conv_state [B, K-1, C]; a, b [B, NV]; z [B, NV*D]; gamma [D]; state
+    [B, NV, D, D].  Returns (out [B, NV*D], new conv_state, new state)."""
+    B = qkv_mixed.shape[0]
+    D = state.shape[-1]
+    out = np.zeros((B, NV * D), np.float32)
+    conv_new = np.zeros_like(conv_state, dtype=np.float32)
+    st_new = np.zeros_like(state, dtype=np.float32)
+    for i in range(B):
+        qkv_conv, conv_new[i] = conv1d_causal(qkv_mixed[i][None], conv_w, conv_state[i], load_state)
+        gb = deltanet_gbeta(a[i][None], b[i][None], a_neg, dt_bias)
+        core, st_new[i] = deltanet_recur(qkv_conv, gb, state[i], NK, NV, load_state)
+        out[i] = deltanet_norm_gate(core.reshape(NV, D), z[i].reshape(NV, D), gamma, eps).reshape(-1)
+    return out, conv_new, st_new
 
 
 def deltanet_recur(qkv_conv: np.ndarray, gbeta: np.ndarray, state: np.ndarray, NK: int, NV: int,

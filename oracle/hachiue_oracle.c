@@ -429,3 +429,58 @@ void oracle_deltanet_recur_batch(const float *qkvConv, const float *gbeta, float
                        qkvStride, gbStride, stStride, coreStride};
   parallel_for(batch, threads, recur_batch_body, &c);
 }
+
+/* ------------------------------------------------------------------------ */
+/* Causal depthwise conv1d + SiLU with its conv state                        */
+/* (src/wasm-backend.ts:1003-1031; WGSL twin conv1d_causal,                  */
+/* src/kernels.ts:1431-1466).                                               */
+/*                                                                          */
+/* qkvMixed f32 [S, C]; convW f32 [C, K]; convState f32 [K-1, C], read when  */
+/* loadState and replaced in place by the last K-1 rows of the extended      */
+/* sequence; qkvConv f32 [S, C] = silu(sum_j w[c][j] * ext(t + j, c)).        */
+/* ------------------------------------------------------------------------ */
+static inline double conv_ext(const float *qkvMixed, const float *convState, int m, int c, int C, int K,
+                              int loadState) {
+  if (m + 1 < K) return loadState ? (double)convState[(long)m * C + c] : 0.0;
+  return (double)qkvMixed[(long)(m - (K - 1)) * C + c];
+}
+
+void oracle_conv1d_causal(const float *qkvMixed, const float *convW, float *convState, float *qkvConv, int S,
+                          int C, int K, int loadState) {
+  for (int t = 0; t < S; t++) {
+    for (int c = 0; c < C; c++) {
+      double acc = 0.0;
+      for (int j = 0; j < K; j++)
+        acc += (double)convW[(long)c * K + j] * conv_ext(qkvMixed, convState, t + j, c, C, K, loadState);
+      qkvConv[(long)t * C + c] = fround(acc / (1.0 + exp(-acc)));
+    }
+  }
+  float *next = (float *)malloc(sizeof(float) * (size_t)(K - 1) * (size_t)C);
+  for (int sk = 0; sk < K - 1; sk++)
+    for (int c = 0; c < C; c++)
+      next[(long)sk * C + c] = fround(conv_ext(qkvMixed, convState, S + sk, c, C, K, loadState));
+  memcpy(convState, next, sizeof(float) * (size_t)(K - 1) * (size_t)C);
+  free(next);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Gated RMSNorm y = gamma * rmsnorm(core) * silu(z)                         */
+/* (src/wasm-backend.ts:1104-1117; WGSL twin deltanet_norm_gate,             */
+/* src/kernels.ts:1578-1611).  core, z, y f32 [rows, DV]; gamma f32 [DV].    */
+/* ------------------------------------------------------------------------ */
+void oracle_deltanet_norm_gate(const float *core, const float *z, const float *gamma, float *y, int rows, int DV,
+                               float eps) {
+  for (int r = 0; r < rows; r++) {
+    const long base = (long)r * DV;
+    double sumSq = 0.0;
+    for (int i = 0; i < DV; i++) {
+      const double c = core[base + i];
+      sumSq += c * c;
+    }
+    const double inv = 1.0 / sqrt(sumSq / DV + (double)eps);
+    for (int i = 0; i < DV; i++) {
+      const double zz = z[base + i];
+      y[base + i] = fround((double)gamma[i] * ((double)core[base + i] * inv) * (zz / (1.0 + exp(-zz))));
+    }
+  }
+}

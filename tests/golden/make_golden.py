@@ -71,6 +71,48 @@ def gdn_case(rng, S, NK, NV, D, load_state):
                 core=core, new_state=new_state, meta=np.array([S, NK, NV, D, int(load_state)], np.int64))
 
 
+def conv1d_case(rng, S, C, K, load_state):
+    x = rng.standard_normal((S, C), dtype=np.float32)
+    w = (rng.standard_normal((C, K), dtype=np.float32) * np.float32(0.5)).astype(np.float32)
+    state = rng.standard_normal((K - 1, C), dtype=np.float32)
+    y, new_state = oracle.conv1d_causal(x, w, state, load_state)
+    return dict(x=x, w=w, state=state, y=y, new_state=new_state, meta=np.array([S, C, K, int(load_state)], np.int64))
+
+
+def norm_gate_case(rng, rows, DV, eps):
+    core = rng.standard_normal((rows, DV), dtype=np.float32)
+    z = rng.standard_normal((rows, DV), dtype=np.float32)
+    gamma = (1 + rng.standard_normal(DV, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    y = oracle.deltanet_norm_gate(core, z, gamma, eps)
+    return dict(core=core, z=z, gamma=gamma, y=y, eps=np.array([eps], np.float32),
+                meta=np.array([rows, DV], np.int64))
+
+
+def gdn_layer_case(rng, B, NK, NV, D, K, load_state, eps):
+    C = 2 * NK * D + NV * D
+    d = dict(
+        qkv=rng.standard_normal((B, C), dtype=np.float32),
+        conv_w=(rng.standard_normal((C, K), dtype=np.float32) * np.float32(0.5)).astype(np.float32),
+        conv_state=rng.standard_normal((B, K - 1, C), dtype=np.float32),
+        a=rng.standard_normal((B, NV), dtype=np.float32),
+        b=rng.standard_normal((B, NV), dtype=np.float32),
+        a_neg=(-np.exp(rng.standard_normal(NV, dtype=np.float32) * np.float32(0.5))).astype(np.float32),
+        dt_bias=(rng.standard_normal(NV, dtype=np.float32) * np.float32(0.5)).astype(np.float32),
+        z=rng.standard_normal((B, NV * D), dtype=np.float32),
+        gamma=(1 + rng.standard_normal(D, dtype=np.float32) * np.float32(0.1)).astype(np.float32),
+        state=(rng.standard_normal((B, NV, D, D), dtype=np.float32) * np.float32(0.02)).astype(np.float32),
+    )
+    if not load_state:  # unused: zeros keep the fixture small
+        d["state"][:] = 0
+        d["conv_state"][:] = 0
+    out, conv_new, st_new = oracle.gdn_layer_step(d["qkv"], d["conv_w"], d["conv_state"], d["a"], d["b"],
+                                                  d["a_neg"], d["dt_bias"], d["z"], d["gamma"], eps, d["state"],
+                                                  NK, NV, load_state)
+    d.update(out=out, new_conv_state=conv_new, new_state=st_new, eps=np.array([eps], np.float32),
+             meta=np.array([B, NK, NV, D, K, int(load_state)], np.int64))
+    return d
+
+
 def main():
     rng = np.random.default_rng(20240601)
     cases = {
@@ -83,6 +125,12 @@ def main():
         "attn_bf16_batch": attention_dense_case(rng, oracle.KV_BF16, 2, 4, 4, 128, [33, 45]),
         "gdn_decode": gdn_case(rng, 1, 1, 2, 128, True),
         "gdn_segment_fresh": gdn_case(rng, 8, 1, 2, 128, False),
+        # the layer's neighbours of the recurrence (conv1d_causal, deltanet_norm_gate, and the fused step)
+        "conv1d_segment": conv1d_case(rng, 5, 96, 4, True),
+        "conv1d_fresh": conv1d_case(rng, 2, 64, 4, False),
+        "norm_gate": norm_gate_case(rng, 6, 128, 1e-6),
+        "gdn_layer_step": gdn_layer_case(rng, 2, 1, 2, 128, 4, True, 1e-6),
+        "gdn_layer_fresh": gdn_layer_case(rng, 1, 1, 3, 128, 4, False, 1e-6),
     }
     for name, arrays in cases.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)

@@ -38,6 +38,22 @@ def test_golden_reproduces(name):
         fmt, B, S, H, KV, Dh, W = (int(x) for x in d["meta"])
         out = oracle.attention_batch(d["q"], d["k"], d["v"], d["pos"], d["off"], W, fmt)
         np.testing.assert_array_equal(out, d["out"])
+    elif name.startswith("conv1d"):
+        S, C, K, ls = (int(x) for x in d["meta"])
+        y, st = oracle.conv1d_causal(d["x"], d["w"], d["state"], bool(ls))
+        np.testing.assert_array_equal(y, d["y"])
+        np.testing.assert_array_equal(st, d["new_state"])
+    elif name == "norm_gate":
+        y = oracle.deltanet_norm_gate(d["core"], d["z"], d["gamma"], float(d["eps"][0]))
+        np.testing.assert_array_equal(y, d["y"])
+    elif name.startswith("gdn_layer"):
+        B, NK, NV, D, K, ls = (int(x) for x in d["meta"])
+        out, conv_new, st_new = oracle.gdn_layer_step(d["qkv"], d["conv_w"], d["conv_state"], d["a"], d["b"],
+                                                      d["a_neg"], d["dt_bias"], d["z"], d["gamma"],
+                                                      float(d["eps"][0]), d["state"], NK, NV, bool(ls))
+        np.testing.assert_array_equal(out, d["out"])
+        np.testing.assert_array_equal(conv_new, d["new_conv_state"])
+        np.testing.assert_array_equal(st_new, d["new_state"])
     else:
         S, NK, NV, D, ls = (int(x) for x in d["meta"])
         gb = oracle.deltanet_gbeta(d["a"], d["b"], d["a_neg"], d["dt_bias"])
@@ -183,3 +199,40 @@ def test_batch_drivers_match_single_calls():
     for b in range(3):
         ref = oracle.attention(q[b], k[off[b]:off[b] + lens[b]], v[off[b]:off[b] + lens[b]], lens[b] - 1)
         np.testing.assert_array_equal(out[b], ref)
+
+
+@pytest.mark.parametrize("load", [True, False])
+def test_conv1d_matches_closed_form(load):
+    """conv1d_causal against a dense numpy f64 form: the extended sequence is
+    the conv state (or zeros) followed by the inputs; each output is the SiLU
+    of a K-tap dot; the new state is the last K-1 extended rows."""
+    rng = np.random.default_rng(3 + load)
+    S, C, K = 6, 40, 4
+    x = rng.standard_normal((S, C), dtype=np.float32)
+    w = rng.standard_normal((C, K), dtype=np.float32)
+    st = rng.standard_normal((K - 1, C), dtype=np.float32)
+    y, ns = oracle.conv1d_causal(x, w, st, load)
+    ext = np.concatenate([st if load else np.zeros_like(st), x], 0).astype(np.float64)
+    acc = np.stack([sum(w[:, j].astype(np.float64) * ext[t + j] for j in range(K)) for t in range(S)])
+    np.testing.assert_allclose(y, acc / (1 + np.exp(-acc)), rtol=1e-6, atol=1e-6)
+    np.testing.assert_array_equal(ns, ext[S:].astype(np.float32))
+    # a 1-token step shifts the state by one row and appends the token
+    y1, ns1 = oracle.conv1d_causal(x[:1], w, st, True)
+    np.testing.assert_array_equal(ns1, np.concatenate([st[1:], x[:1]], 0))
+
+
+def test_norm_gate_matches_closed_form():
+    rng = np.random.default_rng(9)
+    core = rng.standard_normal((5, 128), dtype=np.float32)
+    z = rng.standard_normal((5, 128), dtype=np.float32)
+    gamma = rng.standard_normal(128, dtype=np.float32)
+    y = oracle.deltanet_norm_gate(core, z, gamma, 1e-6)
+    c = core.astype(np.float64)
+    ref = gamma * c / np.sqrt((c * c).mean(1, keepdims=True) + np.float64(np.float32(1e-6))) * (z / (1 + np.exp(-z.astype(np.float64))))
+    np.testing.assert_allclose(y, ref, rtol=1e-6, atol=1e-6)
+    # known answer: a row of equal values normalises to 1 (eps aside), silu(0) = 0
+    one = oracle.deltanet_norm_gate(np.full((1, 128), 3.0, np.float32), np.full((1, 128), 20.0, np.float32),
+                                    np.ones(128, np.float32), 0.0)
+    np.testing.assert_allclose(one, np.full((1, 128), 20.0 / (1 + np.exp(-20.0))), rtol=1e-7)
+    zero = oracle.deltanet_norm_gate(core[:1], np.zeros((1, 128), np.float32), gamma, 1e-6)
+    np.testing.assert_array_equal(zero, np.zeros((1, 128), np.float32))
