@@ -394,7 +394,60 @@ def setup_cfg5(torch, be, dev):
                 traffic_key="cfg5")
 
 
-SETUPS = {1: setup_cfg1, 2: setup_cfg2, 3: setup_cfg3, 4: setup_cfg4, 5: setup_cfg5}
+def setup_cfg6(torch, be, dev):
+    """Configuration 4 as a whole GDN layer step (conv1d + g/beta + recurrence
+    + gated RMSNorm in one kernel).  The unfused sequence of the reference's
+    dispatches (conv1d_causal, the recurrence with g/beta fused, norm_gate:
+    four launches) runs on the same inputs as the comparison arm."""
+    from hachiue_b200 import workloads
+    w = workloads.gdn_layer_cfg6()
+    NK, NV, D = w["NK"], w["NV"], w["D"]
+    B = w["qkv"].shape[0]
+    copies = 2  # 2 x 268 MB of state > L2
+    T = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    states = [T(w["state"]) for _ in range(copies)]
+    conv = [T(w["conv_state"]), T(w["conv_state"])]  # ping-pong, as the engine
+    qkv, conv_w, a, b, z, gamma = T(w["qkv"]), T(w["conv_w"]), T(w["a"]), T(w["b"]), T(w["z"]), T(w["gamma"])
+    an, dtb = T(w["a_neg"]), T(w["dt_bias"])
+    out = torch.zeros((B, NV * D), device=dev)
+    qkv_conv = torch.zeros_like(qkv)
+    core = torch.zeros((B, 1, NV, D), device=dev)
+
+    def step(i):
+        st = states[i % copies]
+        be.gdn_layer_step(qkv, conv_w, conv[i & 1], conv[(i + 1) & 1], a, b, an, dtb, z, gamma, st, st, out, NK, NV,
+                          w["eps"])
+
+    def unfused(i):
+        st = states[i % copies]
+        be.conv1d_causal(qkv[:, None], conv_w, conv[i & 1], qkv_conv[:, None], conv[(i + 1) & 1])
+        be.deltanet_decode(qkv_conv[:, None], a[:, None], b[:, None], an, dtb, st, core, st, NK, NV)
+        be.deltanet_norm_gate(core, z, gamma, out, w["eps"])
+
+    hs = {k: torch.from_numpy(np.ascontiguousarray(w[k])).pin_memory() for k in ("qkv", "a", "b", "z")}
+    out_h = torch.empty(out.shape).pin_memory()
+    dd = {k: torch.empty_like(v, device=dev) for k, v in hs.items()}
+
+    def e2e_step(i):
+        for k in hs:
+            dd[k].copy_(hs[k], non_blocking=True)
+        st = states[i % copies]
+        be.gdn_layer_step(dd["qkv"], conv_w, conv[i & 1], conv[(i + 1) & 1], dd["a"], dd["b"], an, dtb, dd["z"],
+                          gamma, st, st, out, NK, NV, w["eps"])
+        out_h.copy_(out, non_blocking=True)
+
+    info = dict(workload="cfg6 = cfg4 as a whole Qwen3.5 GDN layer step (conv1d K=4 + g/beta + recurrence + "
+                         "gated RMSNorm, fused)", sequences=B, qk_heads=NK, v_heads=NV, d=D,
+                state="f32 [64,32,128,128] in place, conv state f32 [64,3,8192] ping-pong",
+                l2="rotates 2 state copies (> L2)")
+    return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg6_bytes(), tokens=B, info=info,
+                h2d=sum(v.numel() * 4 for v in hs.values()), d2h=out_h.numel() * 4, kernels_per_step=1,
+                e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg6"), out=out, traffic_key="cfg6",
+                alt=dict(name="unfused: conv1d_causal (2 kernels) + recurrence with g/beta + norm_gate",
+                         step=unfused, kernels_per_step=4))
+
+
+SETUPS = {1: setup_cfg1, 2: setup_cfg2, 3: setup_cfg3, 4: setup_cfg4, 5: setup_cfg5, 6: setup_cfg6}
 
 
 # ---------------------------------------------------------------------------
@@ -433,6 +486,13 @@ def cpu_sample(kind: str, w: dict, threads: int, budget_s: float = 12.0):
         oracle.deltanet_recur_batch(w["qkv"][:B], gb, w["state"][:B], w["NK"], w["NV"], True, threads=threads)
         dt = time.perf_counter() - t0
         return workloads.cfg4_bytes(B=B) / dt / 1e9, B / dt, f"{B} of 64 sequences of cfg4 on {threads} threads", threads
+    if kind == "cfg6":
+        B = 8
+        t0 = time.perf_counter()
+        oracle.gdn_layer_step(w["qkv"][:B], w["conv_w"], w["conv_state"][:B], w["a"][:B], w["b"][:B], w["a_neg"],
+                              w["dt_bias"], w["z"][:B], w["gamma"], w["eps"], w["state"][:B], w["NK"], w["NV"], True)
+        dt = time.perf_counter() - t0
+        return workloads.cfg6_bytes(B=B) / dt / 1e9, B / dt, f"{B} of 64 sequences of cfg6, 1 thread", 1
     if kind == "cfg3":
         from hachiue_b200 import workloads as wl
         qs, qe = 3000, 3064
@@ -482,6 +542,8 @@ def run_reference(args, world, rank):
         w = workloads.swa_cfg3()
     elif args.config == 5:
         w = workloads.gdn_prefill_cfg5()
+    elif args.config == 6:
+        w = workloads.gdn_layer_cfg6()
     else:
         w = workloads.gdn_decode_cfg4()
     kind = f"cfg{args.config}"
@@ -515,7 +577,7 @@ def run_reference(args, world, rank):
 
 def metric_name(cfg: int) -> str:
     return {1: "decode attn HBM GB/s", 2: "decode attn HBM GB/s", 3: "SWA prefill TFLOP/s",
-            4: "GDN decode HBM GB/s", 5: "GDN chunked prefill TFLOP/s"}[cfg]
+            4: "GDN decode HBM GB/s", 5: "GDN chunked prefill TFLOP/s", 6: "GDN layer step HBM GB/s"}[cfg]
 
 
 def metric_unit(cfg: int) -> str:
@@ -523,7 +585,7 @@ def metric_unit(cfg: int) -> str:
 
 
 def dtype_name(cfg: int) -> str:
-    return {1: "f32", 2: "f16", 3: "bf16", 4: "f32", 5: "bf16"}[cfg]
+    return {1: "f32", 2: "f16", 3: "bf16", 4: "f32", 5: "bf16", 6: "f32"}[cfg]
 
 
 # ---------------------------------------------------------------------------
@@ -632,6 +694,24 @@ def main(argv=None):
         e2e_ms = float(t.item())
     e2e_value = world * work / (e2e_ms / args.steps / 1e3) / scale
 
+    # ---- comparison arm of the same workload (device-resident, as `value`) ----
+    alt = None
+    if "alt" in W:
+        for i in range(args.warmup):
+            W["alt"]["step"](i)
+        barrier()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for i in range(args.steps):
+            W["alt"]["step"](i)
+        a1.record(stream)
+        barrier()
+        alt_ms = a0.elapsed_time(a1) / args.steps
+        alt = {"name": W["alt"]["name"], "ms_per_step": round(alt_ms, 5),
+               "value": round(world * work / (alt_ms / 1e3) / scale, 2), "unit": metric_unit(args.config),
+               "gpu_launches_per_step": W["alt"]["kernels_per_step"]}
+
     peaks, peak_src = load_peaks()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -672,6 +752,8 @@ def main(argv=None):
             "clocks": clk,
             "cpu_baseline": cpu,
         }
+        if alt is not None:
+            line["comparison"] = alt
         if hbm_roof is not None:
             line["roofline"] = hbm_roof
         print(json.dumps(line), flush=True)

@@ -10,6 +10,9 @@ same values.  "N(0, 0.02)" is read as standard deviation 0.02.
   cfg3  PLaMo-3 SWA prefill: 8 x 4096, H=16, KV=4, Dh=128, W=1024, bf16
   cfg4  Qwen3.5 GDN decode step: 64 seqs, NK=16, NV=32, D=128, f32 state
   cfg5  Qwen3.5 GDN chunked prefill: 8 x 8192, NK=16, NV=32, D=128, bf16 in
+  cfg6  cfg4 as a whole layer step: conv1d (K=4) + g/beta + recurrence + gated
+        RMSNorm around it (not a BASELINE.json configuration: the fused
+        neighbours of the recurrence)
 """
 from __future__ import annotations
 
@@ -122,3 +125,26 @@ def cfg1_bytes(T=1024, H=16, KV=8, Dh=128) -> int:
 def cfg4_bytes(B=64, NK=16, NV=32, D=128) -> int:
     """state read + write, q, k, v, out (f32), a, b (f32)."""
     return 2 * B * NV * D * D * 4 + B * (2 * NK * D + NV * D) * 4 + B * NV * D * 4 + 2 * B * NV * 4
+
+
+def gdn_layer_cfg6(seed: int = 6, batch: int = 64, NK: int = 16, NV: int = 32, D: int = 128, K: int = 4):
+    """Configuration 4's shapes through the layer's neighbours: the pre-conv
+    mix qkv_mixed [B, C] (C = 2*NK*D + NV*D), conv weights [C, K] ~ N(0, 0.5),
+    conv state [B, K-1, C], a / b [B, NV] (aNeg = -1, dtBias = 0), the gate z
+    [B, NV*D], the norm weight gamma [D] ~ 1 + N(0, 0.1), eps 1e-6, state
+    [B, NV, D, D] ~ N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+    C = 2 * NK * D + NV * D
+    return dict(qkv=_normal(rng, (batch, C)), conv_w=_normal(rng, (C, K), std=0.5),
+                conv_state=_normal(rng, (batch, K - 1, C)), a=_normal(rng, (batch, NV)), b=_normal(rng, (batch, NV)),
+                z=_normal(rng, (batch, NV * D)), gamma=(1 + _normal(rng, (D,), std=0.1)).astype(np.float32),
+                state=_normal(rng, (batch, NV, D, D), std=0.02), a_neg=-np.ones(NV, np.float32),
+                dt_bias=np.zeros(NV, np.float32), eps=1e-6, NK=NK, NV=NV, D=D, K=K)
+
+
+def cfg6_bytes(B=64, NK=16, NV=32, D=128, K=4) -> int:
+    """state read + write, pre-conv mix, conv state read + write, conv
+    weights, a / b, gate z, output, norm weight, aNeg / dtBias (f32)."""
+    C = 2 * NK * D + NV * D
+    return (2 * B * NV * D * D * 4 + B * C * 4 + 2 * B * (K - 1) * C * 4 + C * K * 4 + 2 * B * NV * 4
+            + 2 * B * NV * D * 4 + D * 4 + 2 * NV * 4)
