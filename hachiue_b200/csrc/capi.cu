@@ -291,7 +291,7 @@ int hcu_dispatch(hcu_handle h, const char* shader, const uint32_t words[8], void
   if (!strcmp(shader, "deltanet_norm_gate")) {
     HCU_TRY(need(4));
     float eps;
-    memcpy(&eps, &words[2], sizeof(float));  // mkUniform writes rmsEps as an f32 word (src/engine.ts:1398)
+    memcpy(&eps, &words[2], sizeof(float));  // mkUniform writes rmsEps as an f32 word (src/engine.ts:1399)
     return hcu_deltanet_norm_gate(h, words[0], words[1], eps, static_cast<const float*>(buffers[0]),
                                   static_cast<const float*>(buffers[1]), static_cast<const float*>(buffers[2]),
                                   static_cast<float*>(buffers[3]));

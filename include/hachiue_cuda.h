@@ -280,12 +280,12 @@ int hcu_deltanet_norm_gate(hcu_handle h, uint32_t rows, uint32_t DV, float eps, 
 
 /* One Gated DeltaNet layer step for one token per sequence (decode), fused:
  * conv1d_causal on the pre-conv mix, g / beta, the delta-rule update and the
- * gated RMSNorm, i.e. the dispatches at src/engine.ts:1367-1396 between the
+ * gated RMSNorm, i.e. the dispatches at src/engine.ts:1366-1400 between the
  * qkv / gate GEMVs and the ssm_out GEMV, with neither qkvConv nor core
  * leaving the chip.
  * qkv_mixed f32 [batch, C] (C = 2*HK*DK + H*DV, the attn_qkv GEMV output);
  * conv_w f32 [C, K]; conv state f32 [batch, K-1, C], in and out different
- * buffers (the engine's ping-pong, src/engine.ts:1371-1376); a, b f32
+ * buffers (the engine's ping-pong, src/engine.ts:1359-1372); a, b f32
  * [batch, H]; aNeg, dtBias f32 [H]; z f32 [batch, H*DV] (the attn_gate GEMV
  * output); gamma f32 [DV] (ssm_norm); state f32 [batch, H, DK, DV], in place
  * allowed; out f32 [batch, H*DV] (the input of ssm_out).  K = 4,

@@ -172,7 +172,7 @@ def gdn_layer_step(qkv_mixed, conv_w, conv_state, a, b, a_neg, dt_bias, z, gamma
                    load_state: bool = True):
     """One Gated DeltaNet layer step for one token per sequence, as the engine
     dispatches it between the qkv / gate GEMVs and ssm_out (src/engine.ts
-    :1367-1398; JS src/wasm-backend.ts:1003-1117): conv1d_causal, g / beta,
+    :1366-1400; JS src/wasm-backend.ts:1003-1117): conv1d_causal, g / beta,
     the recurrence, the gated RMSNorm.  qkv_mixed [B, C]; conv_w [C, K];
     conv_state [B, K-1, C]; a, b [B, NV]; z [B, NV*D]; gamma [D]; state
     [B, NV, D, D].  Returns (out [B, NV*D], new conv_state, new state)."""

@@ -2,7 +2,7 @@
 against the oracle: conv1d_causal (src/kernels.ts:1431-1466), deltanet_norm_gate
 (src/kernels.ts:1578-1611), through the reference's op names and the typed API,
 and the fused single-token layer step (conv1d + g / beta + recurrence + gated
-RMSNorm, src/engine.ts:1367-1398) at the configuration-4 shape.
+RMSNorm, src/engine.ts:1366-1400) at the configuration-4 shape.
 
 Tolerance (fp32): relative L2 <= 1e-4; conv states moved without arithmetic are
 bit-exact."""
