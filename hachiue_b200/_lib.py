@@ -27,6 +27,7 @@ EXPORTS = (
     "hcu_device_status", "hcu_inject_failure", "hcu_dispatch", "hcu_attention", "hcu_attention_noalloc", "hcu_kv_append", "hcu_kv_append_rows",
     "hcu_deltanet_gbeta", "hcu_deltanet_recur", "hcu_deltanet_decode", "hcu_swa_prefill",
     "hcu_deltanet_chunked_prefill", "hcu_conv1d_causal", "hcu_deltanet_norm_gate", "hcu_gdn_layer_step",
+    "hcu_rmsnorm", "hcu_rope", "hcu_split_q_gate", "hcu_sigmoid_gate", "hcu_attn_prologue",
 )
 
 
@@ -47,6 +48,13 @@ class hcu_attention_params(ctypes.Structure):
     _fields_ = [("S", ctypes.c_uint32), ("H", ctypes.c_uint32), ("KV", ctypes.c_uint32), ("Dh", ctypes.c_uint32),
                 ("posBase", ctypes.c_uint32), ("windowSize", ctypes.c_uint32), ("batch", ctypes.c_uint32),
                 ("max_context", ctypes.c_uint32), ("pos_base", ctypes.c_void_p),
+                ("kv_row_offset", ctypes.c_void_p), ("seq_row_stride", ctypes.c_uint64), ("gate", ctypes.c_void_p)]
+
+
+class hcu_attn_prologue_params(ctypes.Structure):
+    _fields_ = [("S", ctypes.c_uint32), ("H", ctypes.c_uint32), ("KV", ctypes.c_uint32), ("Dh", ctypes.c_uint32),
+                ("rotaryDim", ctypes.c_uint32), ("posBase", ctypes.c_uint32), ("batch", ctypes.c_uint32),
+                ("split_gate", ctypes.c_uint32), ("eps", ctypes.c_float), ("pos_base", ctypes.c_void_p),
                 ("kv_row_offset", ctypes.c_void_p), ("seq_row_stride", ctypes.c_uint64)]
 
 
@@ -132,6 +140,12 @@ def load(path: str | None = None):
             "hcu_conv1d_causal": ([vp, ctypes.POINTER(hcu_conv1d_params), vp, vp, vp, vp, vp], i32),
             "hcu_deltanet_norm_gate": ([vp, u32, u32, ctypes.c_float, vp, vp, vp, vp], i32),
             "hcu_gdn_layer_step": ([vp, ctypes.POINTER(hcu_gdn_step_params)] + [vp] * 13, i32),
+            "hcu_rmsnorm": ([vp, u32, u32, ctypes.c_float, u32, vp, vp, vp], i32),
+            "hcu_rope": ([vp, u32, u32, u32, u32, u32, vp, vp, vp], i32),
+            "hcu_split_q_gate": ([vp, u32, u32, u32, vp, vp, vp], i32),
+            "hcu_sigmoid_gate": ([vp, ctypes.c_uint64, vp, vp], i32),
+            "hcu_attn_prologue": ([vp, ctypes.POINTER(hcu_attn_prologue_params)] + [vp] * 9
+                                  + [ctypes.POINTER(hcu_kv_cache)], i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -22,11 +22,12 @@ import torch
 
 from . import _lib
 from ._lib import (DT_BF16, DT_F32, KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueError, check, hcu_attention_params,
-                   hcu_conv1d_params, hcu_deltanet_params, hcu_gdn_prefill_params, hcu_gdn_step_params, hcu_kv_cache,
+                   hcu_attn_prologue_params, hcu_conv1d_params, hcu_deltanet_params, hcu_gdn_prefill_params, hcu_gdn_step_params, hcu_kv_cache,
                    hcu_swa_params)
 
 # The reference's op names on this path (src/kernels.ts SHADERS keys).
-SHADERS = ("kv_append_q8", "attention_q8", "deltanet_gbeta", "deltanet_recur", "conv1d_causal", "deltanet_norm_gate")
+SHADERS = ("kv_append_q8", "attention_q8", "deltanet_gbeta", "deltanet_recur", "conv1d_causal", "deltanet_norm_gate",
+           "rmsnorm", "rope", "split_q_gate", "sigmoid_gate")
 
 _DTYPE_OF_FORMAT = {KV_F32: torch.float32, KV_F16: torch.float16, KV_BF16: torch.bfloat16, KV_Q8_0: torch.int8}
 
@@ -169,11 +170,12 @@ class CudaBackend:
 
     def attention(self, q: torch.Tensor, cache: KVCache, out: torch.Tensor, pos_base, window_size: int = 0,
                   kv_heads: int | None = None, kv_row_offset: torch.Tensor | None = None,
-                  max_context: int = 0, seq_row_stride: int = 0) -> None:
+                  max_context: int = 0, seq_row_stride: int = 0, gate: torch.Tensor | None = None) -> None:
         """GQA attention of q [S, H, Dh] (or [B, S, H, Dh]) over ``cache``.
 
         ``pos_base`` is an int (single sequence) or an int32 CUDA tensor [B];
-        batched sequences read cache rows ``kv_row_offset[b] + j``."""
+        batched sequences read cache rows ``kv_row_offset[b] + j``.  ``gate``
+        (shaped like ``out``) applies the qwen35 output gate out *= sigmoid(gate)."""
         self._bind_stream()
         batched = q.dim() == 4
         B = q.shape[0] if batched else 1
@@ -194,8 +196,50 @@ class CudaBackend:
         p.max_context = max_context
         p.kv_row_offset = _ptr(kv_row_offset)
         p.seq_row_stride = seq_row_stride
+        p.gate = _ptr(gate)
         kv = cache.c_struct()
         check(self.lib.hcu_attention(self._h, ctypes.byref(p), _ptr(q), ctypes.byref(kv), _ptr(out)))
+
+    def attn_prologue(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm: torch.Tensor,
+                      k_norm: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, q_out: torch.Tensor,
+                      cache: KVCache, pos_base, eps: float, rotary_dim: int, gate_out: torch.Tensor | None = None,
+                      kv_row_offset: torch.Tensor | None = None, seq_row_stride: int = 0) -> None:
+        """Fused split / q-k RMSNorm / RoPE / K-V append: q f32 [(B,) S, H, Dh]
+        (or [(B,) S, H, 2*Dh] with ``gate_out``, the qwen35 doubled
+        projection); k, v f32 [(B,) S, KV, Dh]; q_out [(B,) S, H, Dh]."""
+        self._bind_stream()
+        batched = k.dim() == 4
+        p = hcu_attn_prologue_params()
+        p.batch = k.shape[0] if batched else 1
+        p.S, p.KV, p.Dh = k.shape[-3], k.shape[-2], k.shape[-1]
+        p.H = q.shape[-2]
+        p.rotaryDim = rotary_dim
+        p.split_gate = int(gate_out is not None)
+        p.eps = float(eps)
+        if isinstance(pos_base, torch.Tensor):
+            p.posBase, p.pos_base = 0, _ptr(pos_base)
+        else:
+            p.posBase, p.pos_base = int(pos_base), None
+        p.kv_row_offset = _ptr(kv_row_offset)
+        p.seq_row_stride = seq_row_stride
+        kv = cache.c_struct()
+        check(self.lib.hcu_attn_prologue(self._h, ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm),
+                                         _ptr(k_norm), _ptr(cos), _ptr(sin), _ptr(q_out), _ptr(gate_out),
+                                         ctypes.byref(kv)))
+
+    def rmsnorm(self, x: torch.Tensor, gamma: torch.Tensor, y: torch.Tensor, eps: float,
+                add_unit_offset: bool = False) -> None:
+        """rmsnorm over rows of gamma's length."""
+        self._bind_stream()
+        dim = gamma.shape[0]
+        check(self.lib.hcu_rmsnorm(self._h, x.numel() // dim, dim, float(eps), int(add_unit_offset), _ptr(x),
+                                   _ptr(gamma), _ptr(y)))
+
+    def rope(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, rotary_dim: int, pos_base: int) -> None:
+        """RoPE in place on x f32 [S, heads, head_dim]."""
+        self._bind_stream()
+        S, heads, hd = x.shape
+        check(self.lib.hcu_rope(self._h, S, heads, hd, rotary_dim, pos_base, _ptr(cos), _ptr(sin), _ptr(x)))
 
     def deltanet_gbeta(self, a: torch.Tensor, b: torch.Tensor, a_neg: torch.Tensor, dt_bias: torch.Tensor,
                        out: torch.Tensor) -> None:

@@ -24,6 +24,7 @@ struct AttnArgs {
   float* part;     // [units, max_splits, R, DH + 2]: acc[DH], m (log2), l
   int* counters;   // [kMaxUnits] split-merge tickets, 0 between calls
   uint32_t* status;
+  const float* gate;  // null, or [B, S, H, Dh]: out *= sigmoid(gate) (qwen35 sigmoid_gate)
 };
 
 // Per-CTA geometry shared by both kernels.
@@ -55,6 +56,14 @@ __device__ __forceinline__ AttnUnit attn_unit(const AttnArgs& a, int split) {
 __device__ __forceinline__ size_t out_index(const AttnArgs& a, const AttnUnit& u, int r, int d, int DH) {
   const int qi = u.q0 + r / a.G, h = u.g * a.G + r % a.G;
   return (((size_t)u.b * a.S + qi) * a.H + h) * DH + d;
+}
+
+// Writes one output element, times sigmoid(gate) when the call carries the
+// qwen35 output gate (sigmoid_gate, src/kernels.ts:1249-1262: att * (1 / (1 +
+// exp(-gate)))).
+__device__ __forceinline__ void store_out(const AttnArgs& a, size_t idx, float v) {
+  if (a.gate) v *= 1.f / (1.f + expf(-a.gate[idx]));
+  a.out[idx] = v;
 }
 
 // After every thread of the CTA has written its split's partial
@@ -146,7 +155,7 @@ __device__ void ticket_merge(const AttnArgs& a, const AttnUnit& u, int tid, int 
 #pragma unroll
   for (int k = 0; k < EPT; k++) {
     const int e = tid + k * NT, r = e / DH, d = e % DH;
-    if (e < E && r < u.rows_valid) a.out[out_index(a, u, r, d, DH)] = acc[k];
+    if (e < E && r < u.rows_valid) store_out(a, out_index(a, u, r, d, DH), acc[k]);
   }
   if (tid == 0) a.counters[u.unit] = 0;  // re-arm for the next call
 }

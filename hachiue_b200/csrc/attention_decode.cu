@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       A += cb[(w * R + r) * DH + d] * f;
     }
     if (u.nsplit == 1) {
-      if (r < rows_valid) a.out[out_index(a, u, r, d, DH)] = A / L;
+      if (r < rows_valid) store_out(a, out_index(a, u, r, d, DH), A / L);
     } else {
       part[r * (DH + 2) + d] = A;
       if (d == 0) {
@@ -562,6 +562,7 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   args.counters = static_cast<int*>(h->workspace);
   args.part = reinterpret_cast<float*>(static_cast<char*>(h->workspace) + cnt_bytes);
   args.status = h->dev_status;
+  args.gate = p->gate;
   dim3 grid((unsigned)max_splits, (unsigned)KV, (unsigned)(batch * nqb));
   if (use_tc) return hcu::launch_attn_tc(h, fmt, R, args, grid, tk, tv);
   switch (fmt) {

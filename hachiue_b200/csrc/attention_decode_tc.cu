@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(TC_THREADS, NC == 16 ? 2 : 1)
     if (u.nsplit == 1) {
 #pragma unroll
       for (int r = 0; r < R; r++)
-        if (r < u.rows_valid) a.out[out_index(a, u, r, t, TC_DH)] = acc[r] / lsum[r];
+        if (r < u.rows_valid) store_out(a, out_index(a, u, r, t, TC_DH), acc[r] / lsum[r]);
       return;
     }
     float* part = a.part + ((size_t)u.unit * a.max_splits + split) * R * (TC_DH + 2);

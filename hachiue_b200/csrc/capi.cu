@@ -296,6 +296,27 @@ int hcu_dispatch(hcu_handle h, const char* shader, const uint32_t words[8], void
                                   static_cast<const float*>(buffers[1]), static_cast<const float*>(buffers[2]),
                                   static_cast<float*>(buffers[3]));
   }
+  if (!strcmp(shader, "rmsnorm")) {
+    HCU_TRY(need(3));
+    float eps;
+    memcpy(&eps, &words[2], sizeof(float));  // f32 uniform word (src/engine.ts:1104)
+    return hcu_rmsnorm(h, words[0], words[1], eps, words[3], static_cast<const float*>(buffers[0]),
+                       static_cast<const float*>(buffers[1]), static_cast<float*>(buffers[2]));
+  }
+  if (!strcmp(shader, "rope")) {
+    HCU_TRY(need(3));
+    return hcu_rope(h, words[0], words[1], words[2], words[3], words[4], static_cast<const float*>(buffers[0]),
+                    static_cast<const float*>(buffers[1]), static_cast<float*>(buffers[2]));
+  }
+  if (!strcmp(shader, "split_q_gate")) {
+    HCU_TRY(need(3));
+    return hcu_split_q_gate(h, words[0], words[1], words[2], static_cast<const float*>(buffers[0]),
+                            static_cast<float*>(buffers[1]), static_cast<float*>(buffers[2]));
+  }
+  if (!strcmp(shader, "sigmoid_gate")) {
+    HCU_TRY(need(2));
+    return hcu_sigmoid_gate(h, words[0], static_cast<const float*>(buffers[0]), static_cast<float*>(buffers[1]));
+  }
   return fail(HCU_EINVAL, "missing pipeline %s", shader);
 }
 

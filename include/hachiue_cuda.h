@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define HCU_ABI_VERSION 1
+#define HCU_ABI_VERSION 2  /* 2: hcu_attention_params.gate */
 
 /* Status codes. */
 #define HCU_OK 0
@@ -127,6 +127,14 @@ int hcu_inject_failure(hcu_handle h, int status, int n);
  *                    (stateIn == stateOut allowed)
  *   "deltanet_norm_gate" words [rows, DV, eps (f32 bits), 0]   (kernels.ts:1578)
  *                    buffers [core f32, z f32, gamma f32, y f32]
+ *   "rmsnorm"        words [rows, D, eps (f32 bits), addUnitOffset] (kernels.ts:324)
+ *                    buffers [x f32, gamma f32, y f32]
+ *   "rope"           words [S, H, Dh, rotaryDim, posBase]       (kernels.ts:1120)
+ *                    buffers [cos f32, sin f32, x f32 (rotated in place)]
+ *   "split_q_gate"   words [S, H, Dh]                           (kernels.ts:1155)
+ *                    buffers [qg f32, q f32, gate f32]
+ *   "sigmoid_gate"   words [N]                                  (kernels.ts:1249)
+ *                    buffers [gate f32, att f32 (gated in place)]
  *
  * Q8 scales are stored as in the JS backend (amax/127, wasm-backend.ts:815),
  * not the WGSL's amax (kernels.ts:1333); a cache written by this library is
@@ -165,6 +173,8 @@ typedef struct {
   const int32_t *pos_base;      /* device [batch] or NULL: posBase for every sequence */
   const int64_t *kv_row_offset; /* device [batch] or NULL: b * seq_row_stride */
   uint64_t seq_row_stride;      /* rows per sequence when kv_row_offset is NULL */
+  const float *gate;            /* device [batch, S, H, Dh] or NULL: out *= sigmoid(gate), the qwen35
+                                   attention output gate (sigmoid_gate, src/kernels.ts:1249-1262) */
 } hcu_attention_params;
 
 /* out[b, qi, h, :] = softmax_j(q . k_j / sqrt(Dh)) . v_j with the grouped head
@@ -252,6 +262,50 @@ int hcu_deltanet_decode(hcu_handle h, const hcu_deltanet_params *p, const float 
                         const float *a, const float *b, const float *a_neg,
                         const float *dt_bias, const float *state_in, float *core,
                         float *state_out);
+
+/* The full-attention layer's neighbours of the KV append and the attention
+ * (src/engine.ts:1408-1458; JS src/wasm-backend.ts:1125-1157), with the
+ * reference's arithmetic (f64, rounded to f32 where the JS stores):
+ *   hcu_rmsnorm:      y = x / sqrt(mean(x^2) + eps) * (gamma or 1 + gamma) per
+ *                     row of dim (rmsnorm, kernels.ts:324-355);
+ *   hcu_rope:         x [S, heads, head_dim] rotated in place at positions
+ *                     posBase + s, pairs (i, i + rotary_dim/2), tables
+ *                     [pos][rotary_dim/2] (rope, kernels.ts:1120-1150);
+ *   hcu_split_q_gate: qg [S, H, 2*Dh] -> q, gate [S, H, Dh] (kernels.ts:1155);
+ *   hcu_sigmoid_gate: att[i] *= 1 / (1 + exp(-gate[i])) (kernels.ts:1249). */
+int hcu_rmsnorm(hcu_handle h, uint32_t rows, uint32_t dim, float eps, uint32_t add_unit_offset,
+                const float *x, const float *gamma, float *y);
+int hcu_rope(hcu_handle h, uint32_t S, uint32_t heads, uint32_t head_dim, uint32_t rotary_dim,
+             uint32_t posBase, const float *cos_tab, const float *sin_tab, float *x);
+int hcu_split_q_gate(hcu_handle h, uint32_t S, uint32_t H, uint32_t Dh, const float *qg, float *q,
+                     float *gate);
+int hcu_sigmoid_gate(hcu_handle h, uint64_t n, const float *gate, float *att);
+
+/* The attention prologue of a full-attention layer, fused: split_q_gate
+ * (qwen35), the per-head q / k RMSNorm, RoPE, and the append of K (normed and
+ * rotated) and V to the cache, for S tokens of each of `batch` sequences.
+ * Sequence b's tokens sit at positions pos_base[b] + s (or posBase) and cache
+ * rows kv_row_offset[b] + pos (or b * seq_row_stride + pos), as in
+ * hcu_attention.  q f32 [batch, S, H, Dh] (split_gate: [batch, S, H, 2*Dh],
+ * the attn_q GEMV output with the gate in the second half); k, v f32
+ * [batch, S, KV, Dh]; q_norm, k_norm f32 [Dh]; cos / sin f32
+ * [positions, rotaryDim / 2]; q_out f32 [batch, S, H, Dh]; gate_out f32
+ * [batch, S, H, Dh] (split_gate only).  A Q8_0 cache receives exactly what
+ * appendKvQ8 of the same rows would write.  Dh 128 or 256; rotaryDim a
+ * multiple of 64, at most Dh. */
+typedef struct {
+  uint32_t S, H, KV, Dh, rotaryDim, posBase;
+  uint32_t batch;               /* 0 or 1: single sequence */
+  uint32_t split_gate;          /* 1: qwen35 doubled q projection */
+  float eps;                    /* rmsEps */
+  const int32_t *pos_base;      /* device [batch] or NULL */
+  const int64_t *kv_row_offset; /* device [batch] or NULL */
+  uint64_t seq_row_stride;
+} hcu_attn_prologue_params;
+
+int hcu_attn_prologue(hcu_handle h, const hcu_attn_prologue_params *p, const float *q, const float *k,
+                      const float *v, const float *q_norm, const float *k_norm, const float *cos_tab,
+                      const float *sin_tab, float *q_out, float *gate_out, const hcu_kv_cache *kv);
 
 /* Causal depthwise conv1d of width K plus SiLU, with its conv state:
  * conv1d_causal (src/kernels.ts:1431-1466; JS src/wasm-backend.ts:1003-1031).

@@ -58,6 +58,9 @@ def lib():
             L.oracle_f16_to_f64.argtypes = [ctypes.c_uint16]
             L.oracle_conv1d_causal.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32]
             L.oracle_deltanet_norm_gate.argtypes = [vp, vp, vp, vp, i32, i32, ctypes.c_float]
+            L.oracle_rmsnorm.argtypes = [vp, vp, vp, i32, i32, ctypes.c_float, i32]
+            L.oracle_rope.argtypes = [vp, i32, i32, i32, i32, i32, vp, vp]
+            L.oracle_sigmoid_gate.argtypes = [vp, vp, i64]
             L.oracle_f16_to_f64.restype = ctypes.c_double
             _ = f
             _lib = L
@@ -166,6 +169,78 @@ def deltanet_norm_gate(core: np.ndarray, z: np.ndarray, gamma: np.ndarray, eps: 
     lib().oracle_deltanet_norm_gate(_p(c), _p(zz), _p(np.ascontiguousarray(gamma, np.float32)), _p(y), c.shape[0],
                                     DV, float(eps))
     return y.reshape(core.shape)
+
+
+def rmsnorm(x: np.ndarray, gamma: np.ndarray, eps: float, add_unit_offset: bool = False) -> np.ndarray:
+    """runRmsNorm (src/wasm-backend.ts:427-444) over rows of gamma's length."""
+    dim = gamma.shape[0]
+    xx = np.ascontiguousarray(x, np.float32).reshape(-1, dim)
+    y = np.zeros_like(xx)
+    lib().oracle_rmsnorm(_p(xx), _p(np.ascontiguousarray(gamma, np.float32)), _p(y), xx.shape[0], dim, float(eps),
+                         int(add_unit_offset))
+    return y.reshape(np.shape(x))
+
+
+def rope(x: np.ndarray, rotary_dim: int, pos_base: int, cos_tab: np.ndarray, sin_tab: np.ndarray) -> np.ndarray:
+    """applyRope (src/wasm-backend.ts:767-791) on x [S, heads, head_dim];
+    returns the rotated copy."""
+    S, nh, hd = x.shape
+    y = np.array(x, dtype=np.float32, copy=True, order="C")
+    lib().oracle_rope(_p(y), S, nh, hd, rotary_dim, pos_base, _p(np.ascontiguousarray(cos_tab, np.float32)),
+                      _p(np.ascontiguousarray(sin_tab, np.float32)))
+    return y
+
+
+def sigmoid_gate(gate: np.ndarray, att: np.ndarray) -> np.ndarray:
+    """att * sigmoid(gate) (src/wasm-backend.ts:1152-1157); returns the product."""
+    y = np.array(att, dtype=np.float32, copy=True, order="C")
+    lib().oracle_sigmoid_gate(_p(np.ascontiguousarray(gate, np.float32)), _p(y), y.size)
+    return y
+
+
+def rope_tables(rotary_dim: int, max_pos: int, theta: float, factor: float = 1.0, orig_max_pos: int = 4096,
+                beta_fast: float = 32.0, beta_slow: float = 1.0):
+    """cos / sin tables [max_pos, rotary_dim / 2] f32 as buildRopeTables makes
+    them (src/engine.ts:261-311): f64 inverse frequencies theta^(-2i/rotary_dim),
+    blended toward freq / factor by YaRN's linear ramp when factor > 1, and
+    cos / sin of pos * inv_freq scaled by 0.1 ln(factor) + 1."""
+    half = rotary_dim >> 1
+    mscale = 0.1 * np.log(factor) + 1.0 if factor > 1.0 else 1.0
+    i = np.arange(half, dtype=np.float64)
+    freq = 1.0 / np.power(float(theta), 2.0 * i / rotary_dim)
+    if factor > 1.0:
+        def corr_dim(n_rot):
+            return rotary_dim * np.log(orig_max_pos / (n_rot * 2.0 * np.pi)) / (2.0 * np.log(theta))
+        low = max(0.0, corr_dim(beta_fast))
+        high = min(half - 1.0, corr_dim(beta_slow))
+        if low == high:
+            high += 0.001
+        ramp = np.clip((i - low) / (high - low), 0.0, 1.0)
+        inv = freq / factor * ramp + freq * (1.0 - ramp)
+    else:
+        inv = freq
+    angle = np.arange(max_pos, dtype=np.float64)[:, None] * inv[None, :]
+    return (np.cos(angle) * mscale).astype(np.float32), (np.sin(angle) * mscale).astype(np.float32)
+
+
+def attn_layer_step(q, k, v, q_norm, k_norm, eps, cos_tab, sin_tab, rotary_dim: int, pos_base: int, kq, ks, vq, vs,
+                    gate=None):
+    """One full-attention layer step of one sequence between the q / k / v
+    GEMVs and attn_output, as src/wasm-backend.ts:1125-1157 (and the engine's
+    dispatches, src/engine.ts:1408-1458) run it: per-head q / k RMSNorm, RoPE
+    at positions pos_base.., the Q8_0 append of K and V (the caches are updated
+    in place), attention_q8, and for qwen35 the sigmoid gate.  q [S, H, Dh];
+    k, v [S, KV, Dh]; gate [S, H, Dh] or None.  Returns (q_normed, out)."""
+    S, H, Dh = q.shape
+    KV = k.shape[1]
+    qn = rope(rmsnorm(q, q_norm, eps), rotary_dim, pos_base, cos_tab, sin_tab)
+    kn = rope(rmsnorm(k, k_norm, eps), rotary_dim, pos_base, cos_tab, sin_tab)
+    append_kv_q8(kn, kq, ks, pos_base)
+    append_kv_q8(np.ascontiguousarray(v, np.float32), vq, vs, pos_base)
+    out = attention(qn, kq, vq, pos_base, 0, KV_Q8_0, ks, vs)
+    if gate is not None:
+        out = sigmoid_gate(gate, out)
+    return qn, out
 
 
 def gdn_layer_step(qkv_mixed, conv_w, conv_state, a, b, a_neg, dt_bias, z, gamma, eps, state, NK: int, NV: int,

@@ -484,3 +484,56 @@ void oracle_deltanet_norm_gate(const float *core, const float *z, const float *g
     }
   }
 }
+
+/* ------------------------------------------------------------------------ */
+/* RMSNorm y = x / sqrt(mean(x^2) + eps) * gamma per row of `dim`            */
+/* (runRmsNorm, src/wasm-backend.ts:427-444; WGSL twin rmsnorm,              */
+/* src/kernels.ts:324-355, whose addUnitOffset adds 1 to gamma).             */
+/* ------------------------------------------------------------------------ */
+void oracle_rmsnorm(const float *x, const float *gamma, float *y, int rows, int dim, float eps, int addUnitOffset) {
+  for (int r = 0; r < rows; r++) {
+    const long base = (long)r * dim;
+    double sumSq = 0.0;
+    for (int i = 0; i < dim; i++) {
+      const double v = x[base + i];
+      sumSq += v * v;
+    }
+    const double inv = 1.0 / sqrt(sumSq / dim + (double)eps);
+    for (int i = 0; i < dim; i++) {
+      const double g = addUnitOffset ? 1.0 + (double)gamma[i] : (double)gamma[i];
+      y[base + i] = fround((double)x[base + i] * inv * g);
+    }
+  }
+}
+
+/* ------------------------------------------------------------------------ */
+/* RoPE in place on x [S, nHeads, headDim] at positions posBase + s, rotating */
+/* the pairs (i, i + rotaryDim/2) with cos / sin tables [pos][rotaryDim/2]    */
+/* (applyRope, src/wasm-backend.ts:767-791; WGSL twin rope,                  */
+/* src/kernels.ts:1120-1150).                                               */
+/* ------------------------------------------------------------------------ */
+void oracle_rope(float *x, int S, int nHeads, int headDim, int rotaryDim, int posBase, const float *cosTab,
+                 const float *sinTab) {
+  const int halfRot = rotaryDim >> 1;
+  for (int s = 0; s < S; s++) {
+    const long csBase = (long)(posBase + s) * halfRot;
+    for (int h = 0; h < nHeads; h++) {
+      const long base = ((long)s * nHeads + h) * headDim;
+      for (int pair = 0; pair < halfRot; pair++) {
+        const double c = cosTab[csBase + pair], sn = sinTab[csBase + pair];
+        const double v0 = x[base + pair], v1 = x[base + pair + halfRot];
+        x[base + pair] = fround(v0 * c - v1 * sn);
+        x[base + pair + halfRot] = fround(v1 * c + v0 * sn);
+      }
+    }
+  }
+}
+
+/* ------------------------------------------------------------------------ */
+/* qwen35 attention output gate: att *= 1 / (1 + exp(-gate)) in place        */
+/* (src/wasm-backend.ts:1152-1157; WGSL twin sigmoid_gate,                   */
+/* src/kernels.ts:1249-1262).                                               */
+/* ------------------------------------------------------------------------ */
+void oracle_sigmoid_gate(const float *gate, float *att, long n) {
+  for (long i = 0; i < n; i++) att[i] = fround((double)att[i] * (1.0 / (1.0 + exp(-(double)gate[i]))));
+}

@@ -174,7 +174,7 @@ def test_errors_are_reported(backend):
         backend.attention(torch.zeros((1, 4, 64), device=dev), KVCache.allocate(8, 2, 64, KV_F32),
                           torch.zeros((1, 4, 64), device=dev), 3)
     with pytest.raises(HachiueError, match="missing pipeline"):
-        backend.dispatch("rope", [1, 2, 3], [out])
+        backend.dispatch("gemv_q4_k", [1, 2, 3], [out])
     backend.inject_failure(5, 1)
     with pytest.raises(HachiueError, match="injected"):
         backend.attention(torch.zeros((1, 4, 128), device=dev), cache, out, 3)
