@@ -447,7 +447,63 @@ def setup_cfg6(torch, be, dev):
                          step=unfused, kernels_per_step=4))
 
 
-SETUPS = {1: setup_cfg1, 2: setup_cfg2, 3: setup_cfg3, 4: setup_cfg4, 5: setup_cfg5, 6: setup_cfg6}
+def setup_cfg7(torch, be, dev):
+    """Configuration 1 as a whole qwen3 attention layer step on the reference's
+    Q8_0 cache: the fused prologue (q / k RMSNorm + RoPE + K / V append) and
+    the attention, two launches.  The comparison arm is the engine's dispatch
+    sequence (src/engine.ts:1419-1453) through the reference's op names:
+    rmsnorm x2, rope x2, kv_append_q8 x2, attention_q8, seven launches."""
+    from hachiue_b200 import KV_Q8_0, workloads
+    from hachiue_b200.backend import KVCache, f32_word
+    w = workloads.attn_layer_cfg7()
+    H, KV, Dh, rot, pos, eps = w["H"], w["KV"], w["Dh"], w["rot"], w["pos"], w["eps"]
+    T = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    half = rot // 2
+    inv = 1.0 / np.power(w["theta"], 2.0 * np.arange(half) / rot)
+    ang = np.arange(pos + 1)[:, None] * inv[None, :]
+    cos, sin = T(np.cos(ang).astype(np.float32)), T(np.sin(ang).astype(np.float32))
+    cache = KVCache(KV_Q8_0, T(w["kq"]), T(w["vq"]), T(w["ks"]), T(w["vs"]))
+    q, k, v, qn, kn = T(w["q"]), T(w["k"]), T(w["v"]), T(w["q_norm"]), T(w["k_norm"])
+    q_out = torch.zeros_like(q)
+    out = torch.zeros_like(q)
+    qn_buf, kn_buf = torch.zeros_like(q), torch.zeros_like(k)
+
+    def step(i):
+        be.attn_prologue(q, k, v, qn, kn, cos, sin, q_out, cache, pos, eps, rot)
+        be.attention(q_out, cache, out, pos)
+
+    def unfused(i):
+        be.dispatch("rmsnorm", [H, Dh, f32_word(eps), 0], [q, qn, qn_buf])
+        be.dispatch("rmsnorm", [KV, Dh, f32_word(eps), 0], [k, kn, kn_buf])
+        be.dispatch("rope", [1, H, Dh, rot, pos], [cos, sin, qn_buf])
+        be.dispatch("rope", [1, KV, Dh, rot, pos], [cos, sin, kn_buf])
+        be.dispatch("kv_append_q8", [1, KV, Dh, pos], [kn_buf, cache.k, cache.k_scale])
+        be.dispatch("kv_append_q8", [1, KV, Dh, pos], [v, cache.v, cache.v_scale])
+        be.dispatch("attention_q8", [1, H, KV, Dh, pos, 0], [qn_buf, cache.k, cache.k_scale, cache.v,
+                                                             cache.v_scale, out])
+
+    hs = {name: torch.from_numpy(np.ascontiguousarray(w[name])).pin_memory() for name in ("q", "k", "v")}
+    dd = {name: torch.empty_like(t, device=dev) for name, t in hs.items()}
+    out_h = torch.empty(out.shape).pin_memory()
+
+    def e2e_step(i):
+        for name in hs:
+            dd[name].copy_(hs[name], non_blocking=True)
+        be.attn_prologue(dd["q"], dd["k"], dd["v"], qn, kn, cos, sin, q_out, cache, pos, eps, rot)
+        be.attention(q_out, cache, out, pos)
+        out_h.copy_(out, non_blocking=True)
+
+    info = dict(workload="cfg7 = cfg1 as a whole qwen3 attention layer step (q/k RMSNorm + RoPE + Q8_0 K/V "
+                         "append + attention, fused prologue)", q_heads=H, kv_heads=KV, head_dim=Dh,
+                context=pos + 1, kv_dtype="Q8_0 (the reference's cache format)", l2="1.2 MB, L2-resident")
+    return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg7_bytes(), tokens=1, info=info,
+                h2d=sum(t.numel() * 4 for t in hs.values()), d2h=out_h.numel() * 4, kernels_per_step=2,
+                e2e_kernels_per_step=2, cpu=dict(w=w, kind="cfg7"), out=out, traffic_key="cfg7",
+                alt=dict(name="unfused: the engine's dispatch sequence (rmsnorm x2, rope x2, kv_append_q8 x2, "
+                              "attention_q8)", step=unfused, kernels_per_step=7))
+
+
+SETUPS = {1: setup_cfg1, 2: setup_cfg2, 3: setup_cfg3, 4: setup_cfg4, 5: setup_cfg5, 6: setup_cfg6, 7: setup_cfg7}
 
 
 # ---------------------------------------------------------------------------
@@ -493,6 +549,17 @@ def cpu_sample(kind: str, w: dict, threads: int, budget_s: float = 12.0):
                               w["dt_bias"], w["z"][:B], w["gamma"], w["eps"], w["state"][:B], w["NK"], w["NV"], True)
         dt = time.perf_counter() - t0
         return workloads.cfg6_bytes(B=B) / dt / 1e9, B / dt, f"{B} of 64 sequences of cfg6, 1 thread", 1
+    if kind == "cfg7":
+        cos, sin = oracle.rope_tables(w["rot"], w["pos"] + 1, w["theta"])
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < min(budget_s, 5.0):
+            kq, ks, vq, vs = w["kq"].copy(), w["ks"].copy(), w["vq"].copy(), w["vs"].copy()
+            oracle.attn_layer_step(w["q"], w["k"], w["v"], w["q_norm"], w["k_norm"], w["eps"], cos, sin, w["rot"],
+                                   w["pos"], kq, ks, vq, vs)
+            n += 1
+        dt = time.perf_counter() - t0
+        return n * workloads.cfg7_bytes() / dt / 1e9, n / dt, f"{n} cfg7 layer steps, 1 thread", 1
     if kind == "cfg3":
         from hachiue_b200 import workloads as wl
         qs, qe = 3000, 3064
@@ -544,6 +611,8 @@ def run_reference(args, world, rank):
         w = workloads.gdn_prefill_cfg5()
     elif args.config == 6:
         w = workloads.gdn_layer_cfg6()
+    elif args.config == 7:
+        w = workloads.attn_layer_cfg7()
     else:
         w = workloads.gdn_decode_cfg4()
     kind = f"cfg{args.config}"
@@ -577,7 +646,8 @@ def run_reference(args, world, rank):
 
 def metric_name(cfg: int) -> str:
     return {1: "decode attn HBM GB/s", 2: "decode attn HBM GB/s", 3: "SWA prefill TFLOP/s",
-            4: "GDN decode HBM GB/s", 5: "GDN chunked prefill TFLOP/s", 6: "GDN layer step HBM GB/s"}[cfg]
+            4: "GDN decode HBM GB/s", 5: "GDN chunked prefill TFLOP/s", 6: "GDN layer step HBM GB/s",
+            7: "attention layer step HBM GB/s"}[cfg]
 
 
 def metric_unit(cfg: int) -> str:
@@ -585,7 +655,7 @@ def metric_unit(cfg: int) -> str:
 
 
 def dtype_name(cfg: int) -> str:
-    return {1: "f32", 2: "f16", 3: "bf16", 4: "f32", 5: "bf16", 6: "f32"}[cfg]
+    return {1: "f32", 2: "f16", 3: "bf16", 4: "f32", 5: "bf16", 6: "f32", 7: "q8_0 cache, f32 math"}[cfg]
 
 
 # ---------------------------------------------------------------------------

@@ -13,6 +13,9 @@ same values.  "N(0, 0.02)" is read as standard deviation 0.02.
   cfg6  cfg4 as a whole layer step: conv1d (K=4) + g/beta + recurrence + gated
         RMSNorm around it (not a BASELINE.json configuration: the fused
         neighbours of the recurrence)
+  cfg7  cfg1 as a whole attention layer step on the reference's Q8_0 cache:
+        q / k RMSNorm + RoPE + K / V append + attention (not a BASELINE.json
+        configuration: the fused neighbours of the append and the attention)
 """
 from __future__ import annotations
 
@@ -148,3 +151,28 @@ def cfg6_bytes(B=64, NK=16, NV=32, D=128, K=4) -> int:
     C = 2 * NK * D + NV * D
     return (2 * B * NV * D * D * 4 + B * C * 4 + 2 * B * (K - 1) * C * 4 + C * K * 4 + 2 * B * NV * 4
             + 2 * B * NV * D * 4 + D * 4 + 2 * NV * 4)
+
+
+def attn_layer_cfg7(seed: int = 7, H: int = 16, KV: int = 8, Dh: int = 128, context: int = 1024, theta: float = 1e6):
+    """Configuration 1's shapes as a qwen3 attention layer step: q [1, H, Dh],
+    k, v [1, KV, Dh] ~ N(0, 1) (the GEMV outputs), q / k norm weights ~ 1 +
+    N(0, 0.1), and a Q8_0 cache whose first context-1 rows hold random int8
+    values with scales ~ |N(0, 0.02)|; the step appends row context-1."""
+    rng = np.random.default_rng(seed)
+    rows = context
+    kq = rng.integers(-127, 128, (rows, KV, Dh), dtype=np.int8)
+    vq = rng.integers(-127, 128, (rows, KV, Dh), dtype=np.int8)
+    ks = np.abs(_normal(rng, (rows, KV, Dh // 32), std=0.02))
+    vs = np.abs(_normal(rng, (rows, KV, Dh // 32), std=0.02))
+    return dict(q=_normal(rng, (1, H, Dh)), k=_normal(rng, (1, KV, Dh)), v=_normal(rng, (1, KV, Dh)),
+                q_norm=(1 + _normal(rng, (Dh,), std=0.1)).astype(np.float32),
+                k_norm=(1 + _normal(rng, (Dh,), std=0.1)).astype(np.float32),
+                kq=kq, ks=ks, vq=vq, vs=vs, pos=context - 1, rot=Dh, theta=theta, eps=1e-6, H=H, KV=KV, Dh=Dh)
+
+
+def cfg7_bytes(H=16, KV=8, Dh=128, context=1024) -> int:
+    """Q8_0 K and V read (int8 + f32 scale per 32), q / k / v in, q_out write
+    and read, the appended K / V rows, norm weights, one RoPE row, out."""
+    cache = 2 * context * KV * (Dh + Dh // 32 * 4)
+    io = (H + 2 * KV) * Dh * 4 + 2 * H * Dh * 4 + 2 * KV * (Dh + Dh // 32 * 4) + 2 * Dh * 4 + Dh * 4 + H * Dh * 4
+    return cache + io
