@@ -113,6 +113,30 @@ def gdn_layer_case(rng, B, NK, NV, D, K, load_state, eps):
     return d
 
 
+def attn_layer_case(rng, S, H, KV, Dh, rot, pos, split, eps):
+    """The full-attention layer step of one sequence (src/wasm-backend.ts
+    :1125-1157) on a Q8_0 cache that holds `pos` earlier rows."""
+    rows = pos + S
+    qg = rng.standard_normal((S, H, 2 * Dh if split else Dh), dtype=np.float32)
+    k = rng.standard_normal((S, KV, Dh), dtype=np.float32)
+    v = rng.standard_normal((S, KV, Dh), dtype=np.float32)
+    qn = (1 + rng.standard_normal(Dh, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    kn = (1 + rng.standard_normal(Dh, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    kq, ks = np.zeros((rows, KV, Dh), np.int8), np.zeros((rows, KV, Dh // 32), np.float32)
+    vq, vs = kq.copy(), ks.copy()
+    if pos:
+        oracle.append_kv_q8(rng.standard_normal((pos, KV, Dh), dtype=np.float32), kq, ks, 0)
+        oracle.append_kv_q8(rng.standard_normal((pos, KV, Dh), dtype=np.float32), vq, vs, 0)
+    cos, sin = oracle.rope_tables(rot, rows, 1e6)
+    d = dict(qg=qg, k=k, v=v, qn=qn, kn=kn, kq0=kq.copy(), ks0=ks.copy(), vq0=vq.copy(), vs0=vs.copy(), cos=cos,
+             sin=sin, eps=np.array([eps], np.float32), meta=np.array([S, H, KV, Dh, rot, pos, int(split)], np.int64))
+    q = np.ascontiguousarray(qg[..., :Dh]) if split else qg
+    gate = np.ascontiguousarray(qg[..., Dh:]) if split else None
+    q_out, out = oracle.attn_layer_step(q, k, v, qn, kn, eps, cos, sin, rot, pos, kq, ks, vq, vs, gate=gate)
+    d.update(q_out=q_out, out=out, kq=kq, ks=ks, vq=vq, vs=vs)
+    return d
+
+
 def main():
     rng = np.random.default_rng(20240601)
     cases = {
@@ -131,6 +155,9 @@ def main():
         "norm_gate": norm_gate_case(rng, 6, 128, 1e-6),
         "gdn_layer_step": gdn_layer_case(rng, 2, 1, 2, 128, 4, True, 1e-6),
         "gdn_layer_fresh": gdn_layer_case(rng, 1, 1, 3, 128, 4, False, 1e-6),
+        # the full-attention layer's neighbours (q/k RMSNorm, RoPE, Q8_0 append, sigmoid gate)
+        "attn_layer_qwen3": attn_layer_case(rng, 2, 8, 4, 128, 128, 40, False, 1e-6),
+        "attn_layer_qwen35": attn_layer_case(rng, 1, 4, 2, 256, 64, 30, True, 1e-6),
     }
     for name, arrays in cases.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)

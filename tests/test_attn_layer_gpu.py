@@ -157,3 +157,23 @@ def test_batched_prologue_and_gated_tensor_core_attention(backend):
         ref = oracle.sigmoid_gate(q[b, :, :, Dh:], ref)
         assert rel_l2(oo[b], ref) < TOL
     assert backend.device_status() == 0
+
+
+@pytest.mark.parametrize("name", ["attn_layer_qwen3", "attn_layer_qwen35"])
+def test_layer_step_golden(backend, name):
+    """The committed fixtures (oracle outputs): fused prologue + gated attention."""
+    import os
+    d = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", name + ".npz")))
+    S, H, KV, Dh, rot, pos, split = (int(x) for x in d["meta"])
+    cache = KVCache(KV_Q8_0, T(d["kq0"]), T(d["vq0"]), T(d["ks0"]), T(d["vs0"]))
+    q_out = torch.zeros((S, H, Dh), device=dev)
+    gate_out = torch.zeros((S, H, Dh), device=dev) if split else None
+    backend.attn_prologue(T(d["qg"]), T(d["k"]), T(d["v"]), T(d["qn"]), T(d["kn"]), T(d["cos"]), T(d["sin"]), q_out,
+                          cache, pos, float(d["eps"][0]), rot, gate_out=gate_out)
+    out = torch.zeros((S, H, Dh), device=dev)
+    backend.attention(q_out, cache, out, pos, gate=gate_out)
+    torch.cuda.synchronize()
+    assert rel_l2(q_out.cpu().numpy(), d["q_out"]) < TIGHT
+    for t, key in ((cache.k, "kq"), (cache.k_scale, "ks"), (cache.v, "vq"), (cache.v_scale, "vs")):
+        np.testing.assert_array_equal(t.cpu().numpy(), d[key])
+    assert rel_l2(out.cpu().numpy(), d["out"]) < TOL

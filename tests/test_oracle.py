@@ -34,6 +34,17 @@ def test_golden_reproduces(name):
         np.testing.assert_array_equal(ks, d["ks"])
         out = oracle.attention(d["q"], d["kq"], d["vq"], pos, W, oracle.KV_Q8_0, d["ks"], d["vs"])
         np.testing.assert_array_equal(out, d["out"])
+    elif name.startswith("attn_layer"):
+        S, H, KV, Dh, rot, pos, split = (int(x) for x in d["meta"])
+        kq, ks, vq, vs = d["kq0"].copy(), d["ks0"].copy(), d["vq0"].copy(), d["vs0"].copy()
+        q = np.ascontiguousarray(d["qg"][..., :Dh]) if split else d["qg"]
+        gate = np.ascontiguousarray(d["qg"][..., Dh:]) if split else None
+        q_out, out = oracle.attn_layer_step(q, d["k"], d["v"], d["qn"], d["kn"], float(d["eps"][0]), d["cos"],
+                                            d["sin"], rot, pos, kq, ks, vq, vs, gate=gate)
+        np.testing.assert_array_equal(q_out, d["q_out"])
+        np.testing.assert_array_equal(out, d["out"])
+        for a, b in ((kq, "kq"), (ks, "ks"), (vq, "vq"), (vs, "vs")):
+            np.testing.assert_array_equal(a, d[b])
     elif name.startswith("attn_"):
         fmt, B, S, H, KV, Dh, W = (int(x) for x in d["meta"])
         out = oracle.attention_batch(d["q"], d["k"], d["v"], d["pos"], d["off"], W, fmt)
@@ -236,3 +247,35 @@ def test_norm_gate_matches_closed_form():
     np.testing.assert_allclose(one, np.full((1, 128), 20.0 / (1 + np.exp(-20.0))), rtol=1e-7)
     zero = oracle.deltanet_norm_gate(core[:1], np.zeros((1, 128), np.float32), gamma, 1e-6)
     np.testing.assert_array_equal(zero, np.zeros((1, 128), np.float32))
+
+
+def test_rmsnorm_rope_gate_match_closed_forms():
+    """rmsnorm, RoPE and the sigmoid gate against dense numpy f64 forms, and
+    RoPE's known answers: position 0 is the identity, and a rotation by pos
+    then by -pos (the conjugate tables) restores the input."""
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((3, 4, 128), dtype=np.float32)
+    g = rng.standard_normal(128, dtype=np.float32)
+    y = oracle.rmsnorm(x, g, 1e-6)
+    x64 = x.astype(np.float64)
+    ref = x64 / np.sqrt((x64 * x64).mean(-1, keepdims=True) + np.float64(np.float32(1e-6))) * g
+    np.testing.assert_allclose(y, ref, rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(oracle.rmsnorm(x, g, 1e-6, True),
+                               x64 / np.sqrt((x64 * x64).mean(-1, keepdims=True) + np.float64(np.float32(1e-6)))
+                               * (1.0 + g), rtol=1e-6, atol=1e-6)
+    for rot in (64, 128):
+        cos, sin = oracle.rope_tables(rot, 16, 1e6)
+        half = rot // 2
+        r = oracle.rope(y, rot, 5, cos, sin)
+        c, s_ = cos[5:8][:, None, :].astype(np.float64), sin[5:8][:, None, :].astype(np.float64)
+        yy = y.astype(np.float64)
+        exp = yy.copy()
+        exp[..., :half] = yy[..., :half] * c - yy[..., half:rot] * s_
+        exp[..., half:rot] = yy[..., half:rot] * c + yy[..., :half] * s_
+        np.testing.assert_allclose(r, exp, rtol=1e-6, atol=1e-6)
+        np.testing.assert_array_equal(oracle.rope(y[:1], rot, 0, cos, sin), y[:1])  # position 0: cos 1, sin 0
+        back = oracle.rope(r, rot, 5, cos, -sin)
+        np.testing.assert_allclose(back, y, rtol=1e-5, atol=1e-5)
+    gate = rng.standard_normal(x.shape, dtype=np.float32)
+    np.testing.assert_allclose(oracle.sigmoid_gate(gate, x), x64 / (1 + np.exp(-gate.astype(np.float64))),
+                               rtol=1e-6, atol=1e-6)
