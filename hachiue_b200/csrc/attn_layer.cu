@@ -117,7 +117,7 @@ template <>
 __device__ __forceinline__ __nv_bfloat16 to_cache<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 
 template <int NJ, int HJ>  // Dh / 32 elements per lane; rotaryDim / 64 = partner register distance
-__global__ void __launch_bounds__(256) attn_prologue_kernel(const ProArgs a) {
+__global__ void __launch_bounds__(128) attn_prologue_kernel(const ProArgs a) {
   constexpr int Dh = NJ * 32;
   const int s = blockIdx.x, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -125,15 +125,26 @@ __global__ void __launch_bounds__(256) attn_prologue_kernel(const ProArgs a) {
   const long long row = (a.row_off ? a.row_off[b] : (long long)b * a.seq_row_stride) + pos;
   const long long tok = (long long)b * a.S + s;
   const int nrows = a.H + 2 * a.KV;
-  for (int r = warp; r < nrows; r += 8) {
+  // one warp per row: the rows' dependent chains (loads, f64 reductions) run side by side
+  for (int r = blockIdx.z * 4 + warp; r < nrows; r += 4 * gridDim.z) {
     const int kind = r < a.H ? 0 : (r < a.H + a.KV ? 1 : 2);  // q, k, v
     const int head = kind == 0 ? r : (kind == 1 ? r - a.H : r - a.H - a.KV);
     const float* src = kind == 0 ? a.q + (tok * a.H + head) * (long long)(a.split ? 2 * Dh : Dh)
                                  : (kind == 1 ? a.k : a.v) + (tok * a.KV + head) * (long long)Dh;
-    float x[NJ];
+    float x[NJ], wv[NJ], cv[HJ], sv[HJ];
 #pragma unroll
     for (int j = 0; j < NJ; j++) x[j] = src[lane + 32 * j];
     if (kind < 2) {
+      // the norm weights and this position's RoPE row are loaded with the row
+      const float* w = kind == 0 ? a.qn_w : a.kn_w;
+      const long long cs = (long long)pos * (32 * HJ);
+#pragma unroll
+      for (int j = 0; j < NJ; j++) wv[j] = w[lane + 32 * j];
+#pragma unroll
+      for (int j = 0; j < HJ; j++) {
+        cv[j] = a.cos_tab[cs + lane + 32 * j];
+        sv[j] = a.sin_tab[cs + lane + 32 * j];
+      }
       // runRmsNorm: inv = 1 / sqrt(sum x^2 / Dh + eps), y = x * inv * gamma, stored f32
       double sq = 0.0;
 #pragma unroll
@@ -141,15 +152,12 @@ __global__ void __launch_bounds__(256) attn_prologue_kernel(const ProArgs a) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
       const double inv = 1.0 / sqrt(sq / Dh + a.eps);
-      const float* w = kind == 0 ? a.qn_w : a.kn_w;
 #pragma unroll
-      for (int j = 0; j < NJ; j++) x[j] = (float)__dmul_rn(__dmul_rn((double)x[j], inv), (double)w[lane + 32 * j]);
+      for (int j = 0; j < NJ; j++) x[j] = (float)__dmul_rn(__dmul_rn((double)x[j], inv), (double)wv[j]);
       // applyRope: pairs (e, e + half), half = 32 HJ, sit in one lane (registers j, j + HJ)
-      const long long cs = (long long)pos * (32 * HJ);
 #pragma unroll
       for (int j = 0; j < HJ; j++) {
-        const int e = lane + 32 * j;
-        const double c = a.cos_tab[cs + e], sn = a.sin_tab[cs + e];
+        const double c = cv[j], sn = sv[j];
         const double v0 = x[j], v1 = x[j + HJ];
         x[j] = (float)__dsub_rn(__dmul_rn(v0, c), __dmul_rn(v1, sn));
         x[j + HJ] = (float)__dadd_rn(__dmul_rn(v1, c), __dmul_rn(v0, sn));
@@ -288,15 +296,18 @@ extern "C" int hcu_attn_prologue(hcu_handle h, const hcu_attn_prologue_params* p
   a.pos_default = (int)p->posBase;
   a.split = p->split_gate ? 1 : 0;
   a.fmt = fmt;
-  const dim3 grid(p->S, (unsigned)batch);
+  // (token, sequence, group of four q / k / v rows)
+  const long long nrows = (long long)p->H + 2ll * p->KV;
+  if (nrows > 4ll * 65535) return fail(HCU_EINVAL, "hcu_attn_prologue: too many heads");
+  const dim3 grid(p->S, (unsigned)batch, (unsigned)((nrows + 3) / 4));
   const int hj = (int)p->rotaryDim / 64;
   if (Dh == 128) {
-    if (hj == 1) attn_prologue_kernel<4, 1><<<grid, 256, 0, h->stream>>>(a);
-    else attn_prologue_kernel<4, 2><<<grid, 256, 0, h->stream>>>(a);
+    if (hj == 1) attn_prologue_kernel<4, 1><<<grid, 128, 0, h->stream>>>(a);
+    else attn_prologue_kernel<4, 2><<<grid, 128, 0, h->stream>>>(a);
   } else {
-    if (hj == 1) attn_prologue_kernel<8, 1><<<grid, 256, 0, h->stream>>>(a);
-    else if (hj == 2) attn_prologue_kernel<8, 2><<<grid, 256, 0, h->stream>>>(a);
-    else attn_prologue_kernel<8, 4><<<grid, 256, 0, h->stream>>>(a);
+    if (hj == 1) attn_prologue_kernel<8, 1><<<grid, 128, 0, h->stream>>>(a);
+    else if (hj == 2) attn_prologue_kernel<8, 2><<<grid, 128, 0, h->stream>>>(a);
+    else attn_prologue_kernel<8, 4><<<grid, 128, 0, h->stream>>>(a);
   }
   return hcu::after_launch("hcu_attn_prologue");
 }

@@ -665,6 +665,18 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
         const int t0 = (a.c0 + c) * GC;
         const int u = (int)(unit0 + c);
         const uint32_t pe = (c - 1) & 1;
+        if (c + 1 < n) {
+          // warm L2 with the next chunk's tiles: its loads below are issued only
+          // when this chunk frees the buffers, a chunk's time before they are needed
+          const int t1 = t0 + GC;
+          tma_prefetch_l2_4d(&tmK, 0, hk, t1, b);
+          tma_prefetch_l2_4d(&tmK, 64, hk, t1, b);
+          tma_prefetch_l2_4d(&tmQ, 0, hk, t1, b);
+          tma_prefetch_l2_4d(&tmQ, 64, hk, t1, b);
+          tma_prefetch_l2_4d(&tmV, dvb * DVB, h, t1, b);
+          tma_prefetch_l2_2d(&tmW, 0, (u + 1) * 128);
+          tma_prefetch_l2_2d(&tmS, 0, (u + 1) * 4);
+        }
         if (c >= 1 && !mbar_wait(kq_empty, pe, a.status)) break;
         mbar_arrive_expect_tx(kq_full, 32768);
         tma_load_4d(sm + C_OFF_KQ, &tmK, kq_full, 0, hk, t0, b);
