@@ -26,7 +26,7 @@ EXPORTS = (
     "hcu_stream_sync", "hcu_alloc", "hcu_free", "hcu_memset", "hcu_copy_to_device", "hcu_copy_to_host",
     "hcu_device_status", "hcu_inject_failure", "hcu_dispatch", "hcu_attention", "hcu_attention_noalloc", "hcu_kv_append", "hcu_kv_append_rows",
     "hcu_deltanet_gbeta", "hcu_deltanet_recur", "hcu_deltanet_decode", "hcu_swa_prefill",
-    "hcu_deltanet_chunked_prefill", "hcu_conv1d_causal", "hcu_deltanet_norm_gate", "hcu_gdn_layer_step",
+    "hcu_deltanet_chunked_prefill", "hcu_deltanet_chunked_prefill_snap", "hcu_conv1d_causal", "hcu_deltanet_norm_gate", "hcu_gdn_layer_step",
     "hcu_rmsnorm", "hcu_rope", "hcu_split_q_gate", "hcu_sigmoid_gate", "hcu_attn_prologue",
 )
 
@@ -137,6 +137,8 @@ def load(path: str | None = None):
             "hcu_swa_prefill": ([vp, ctypes.POINTER(hcu_swa_params), vp, vp, vp, vp], i32),
             "hcu_deltanet_chunked_prefill": ([vp, ctypes.POINTER(hcu_gdn_prefill_params), vp, vp, vp, vp, vp, vp,
                                               vp, vp], i32),
+            "hcu_deltanet_chunked_prefill_snap": ([vp, ctypes.POINTER(hcu_gdn_prefill_params), vp, vp, vp, vp, vp,
+                                                   vp, vp, vp, u32, vp], i32),
             "hcu_conv1d_causal": ([vp, ctypes.POINTER(hcu_conv1d_params), vp, vp, vp, vp, vp], i32),
             "hcu_deltanet_norm_gate": ([vp, u32, u32, ctypes.c_float, vp, vp, vp, vp], i32),
             "hcu_gdn_layer_step": ([vp, ctypes.POINTER(hcu_gdn_step_params)] + [vp] * 13, i32),

@@ -333,13 +333,16 @@ class CudaBackend:
 
     def deltanet_chunked_prefill(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
                                  beta: torch.Tensor, core: torch.Tensor, state_out: torch.Tensor,
-                                 state_in: torch.Tensor | None = None) -> None:
+                                 state_in: torch.Tensor | None = None, snapshots: torch.Tensor | None = None,
+                                 snap_every: int = 0) -> None:
         """Gated DeltaNet over whole prompts, 64-token chunks on the tensor cores.
 
         q, k bf16 [B, T, NK, D]; v bf16 [B, T, NV, D] (token-major views with
         unit stride inside a head are accepted); g, beta f32 [B, T, NV];
         core f32 [B, T, NV, D]; states f32 [B, NV, D, D] ([dk][dv]).
-        ``state_in`` None starts from a zero state."""
+        ``state_in`` None starts from a zero state.  With ``snapshots`` f32
+        [B, T // (64 * snap_every), NV, D, D], snapshot j receives the state
+        after token 64 * snap_every * (j + 1) (for prefix reuse)."""
         self._bind_stream()
         B, T, NK, D = q.shape
         NV = v.shape[2]
@@ -357,5 +360,15 @@ class CudaBackend:
         p.gb_row_stride, p.gb_seq_stride = g.stride(1), g.stride(0)
         if beta.stride() != g.stride():
             raise HachiueError(_lib.HCU_EINVAL, "hachiue: g and beta must share strides")
+        if snapshots is not None:
+            n_snap = T // (64 * snap_every) if snap_every > 0 else 0
+            if (snapshots.dtype != torch.float32 or not snapshots.is_contiguous()
+                    or tuple(snapshots.shape) != (B, n_snap, NV, D, D)):
+                raise HachiueError(_lib.HCU_EINVAL,
+                                   f"hachiue: snapshots must be contiguous f32 [{B}, {n_snap}, {NV}, {D}, {D}]")
+            check(self.lib.hcu_deltanet_chunked_prefill_snap(
+                self._h, ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state_in),
+                _ptr(core), _ptr(state_out), snap_every, _ptr(snapshots)))
+            return
         check(self.lib.hcu_deltanet_chunked_prefill(self._h, ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(g),
                                                     _ptr(beta), _ptr(state_in), _ptr(core), _ptr(state_out)))

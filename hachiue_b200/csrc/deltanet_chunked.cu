@@ -109,6 +109,11 @@ struct ChainArgs {
   float* core;
   float* state_out;
   uint32_t* status;
+  // state snapshots (prefix reuse): snapshot j = the state after token
+  // 64 * snap_every * (j + 1), f32 [B][snap_count][NV][D][D]; null for none
+  float* snap;
+  int snap_every;
+  long long snap_count;
 };
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -888,6 +893,15 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
         mbar_arrive(bar_s0);
         mbar_arrive(&sc_empty[c & 1]);
       }
+      if (a.snap && (a.c0 + c + 1) % a.snap_every == 0) {
+        const long long j = (a.c0 + c + 1) / a.snap_every - 1;  // < snap_count: the chunk is full
+        if (j < a.snap_count) {
+          float4* dst = reinterpret_cast<float4*>(
+              a.snap + ((((size_t)b * a.snap_count + j) * a.NV + h) * GD + t) * GD + dvb * DVB);
+#pragma unroll
+          for (int i = 0; i < 16; i++) dst[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+        }
+      }
     }
     if (ok) {
       float4* dst = reinterpret_cast<float4*>(a.state_out + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * DVB);
@@ -909,10 +923,11 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
 
 using hcu::fail;
 
-extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q,
-                                            const void* k, const void* v, const float* g, const float* beta,
-                                            const float* state_in, float* core, float* state_out) {
-  HCU_TRY(hcu::begin_op(h, "hcu_deltanet_chunked_prefill"));
+namespace {
+
+int chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q, const void* k, const void* v,
+                    const float* g, const float* beta, const float* state_in, float* core, float* state_out,
+                    uint32_t snap_every, float* snapshots) {
   if (!p || !q || !k || !v || !g || !beta || !core || !state_out || (p->load_state && !state_in))
     return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: null argument");
   const long long B = p->B, T = p->T, NK = p->NK, NV = p->NV;
@@ -927,8 +942,10 @@ extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_
   const long long kseq = p->k_seq_stride ? (long long)p->k_seq_stride : T * krow;
   const long long vseq = p->v_seq_stride ? (long long)p->v_seq_stride : T * vrow;
   if (reinterpret_cast<uintptr_t>(core) % 16 || reinterpret_cast<uintptr_t>(state_out) % 16 ||
-      (p->load_state && reinterpret_cast<uintptr_t>(state_in) % 16))
+      (p->load_state && reinterpret_cast<uintptr_t>(state_in) % 16) ||
+      reinterpret_cast<uintptr_t>(snapshots) % 16)
     return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: core / state buffers must be 16-byte aligned");
+  const long long snap_count = snap_every ? T / (hcu::GC * (long long)snap_every) : 0;
   CUtensorMap tq, tk, tv, tw, ts, to;
   {
     uint64_t dims[4] = {128, (uint64_t)NK, (uint64_t)T, (uint64_t)B};
@@ -1030,9 +1047,31 @@ extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_
     ca.core = core;
     ca.state_out = state_out;
     ca.status = h->dev_status;
+    ca.snap = snap_count > 0 ? snapshots : nullptr;
+    ca.snap_every = (int)snap_every;
+    ca.snap_count = snap_count;
     hcu::gdn_chain_kernel<<<dim3(hcu::GD / hcu::DVB, (unsigned)NV, (unsigned)B), hcu::CHAIN_THREADS,
                             hcu::C_SMEM + 1024, h->stream>>>(tq, tk, tv, tw, ts, to, ca);
     HCU_TRY(hcu::after_launch("hcu_deltanet_chunked_prefill: chain launch"));
   }
   return HCU_OK;
+}
+
+}  // namespace
+
+extern "C" int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q,
+                                            const void* k, const void* v, const float* g, const float* beta,
+                                            const float* state_in, float* core, float* state_out) {
+  HCU_TRY(hcu::begin_op(h, "hcu_deltanet_chunked_prefill"));
+  return chunked_prefill(h, p, q, k, v, g, beta, state_in, core, state_out, 0, nullptr);
+}
+
+extern "C" int hcu_deltanet_chunked_prefill_snap(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q,
+                                                 const void* k, const void* v, const float* g, const float* beta,
+                                                 const float* state_in, float* core, float* state_out,
+                                                 uint32_t snap_every, float* snapshots) {
+  HCU_TRY(hcu::begin_op(h, "hcu_deltanet_chunked_prefill_snap"));
+  if (!snap_every || !snapshots)
+    return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill_snap: snap_every must be >= 1 and snapshots non-null");
+  return chunked_prefill(h, p, q, k, v, g, beta, state_in, core, state_out, snap_every, snapshots);
 }

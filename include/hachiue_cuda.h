@@ -402,6 +402,22 @@ int hcu_deltanet_chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params *p, 
                                  const void *k, const void *v, const float *g, const float *beta,
                                  const float *state_in, float *core, float *state_out);
 
+/* The same prefill, also writing state snapshots for prefix reuse.  The engine
+ * resets a hybrid (GDN) model's cache whenever a new prompt diverges from the
+ * token history, because it keeps no GDN state but the latest
+ * (src/engine.ts:1580-1584); with snapshots taken every snap_every chunks it can
+ * instead restore the last snapshot at or before the common prefix (as
+ * state_in of the next call) and prefill only from there.
+ * Snapshot j (0 <= j < T / (64 * snap_every)) is the state after token
+ * 64 * snap_every * (j + 1): f32 [B, n_snap, NV, D, D], [dk][dv] order, 16-byte
+ * aligned.  The snapshots and state_out equal, bit for bit, the state_out of a
+ * call over that prefix; a call that resumes from a snapshot reproduces the
+ * remaining outputs bit for bit. */
+int hcu_deltanet_chunked_prefill_snap(hcu_handle h, const hcu_gdn_prefill_params *p, const void *q,
+                                      const void *k, const void *v, const float *g, const float *beta,
+                                      const float *state_in, float *core, float *state_out,
+                                      uint32_t snap_every, float *snapshots);
+
 #ifdef __cplusplus
 }
 #endif

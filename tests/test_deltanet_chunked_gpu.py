@@ -133,3 +133,67 @@ def test_slabs_carry_the_state(backend, monkeypatch):
         assert rel_l2(core[0, :, h], rc) < REL, (h, rel_l2(core[0, :, h], rc))
         assert rel_l2(st[0, h], rs) < REL
     assert backend.device_status() == 0
+
+
+def test_state_snapshots_for_prefix_reuse(backend):
+    """Snapshots every 4 chunks: each equals, bit for bit, the final state of a
+    prefill over that prefix; resuming from a snapshot reproduces the rest of
+    the full prefill's outputs and its final state bit for bit (the restore
+    path that lets a hybrid model keep a diverging prompt's common prefix,
+    where the reference resets, src/engine.ts:1580-1584)."""
+    rng = np.random.default_rng(77)
+    B, T, NK, NV, every = 2, 1000, 2, 4, 4
+    qb, kb, vb, g, beta = make_inputs(rng, B, T, NK, NV, 0.5)
+    st0 = (0.02 * rng.standard_normal((B, NV, 128, 128))).astype(np.float32)
+    q, k, v = to_dev_bf16(qb), to_dev_bf16(kb), to_dev_bf16(vb)
+    gd, bd = torch.from_numpy(g).to(dev), torch.from_numpy(beta).to(dev)
+    s0 = torch.from_numpy(st0).to(dev)
+    n_snap = T // (64 * every)
+    assert n_snap == 3
+    core = torch.full((B, T, NV, 128), float("nan"), device=dev)
+    st = torch.zeros((B, NV, 128, 128), device=dev)
+    snaps = torch.full((B, n_snap, NV, 128, 128), float("nan"), device=dev)
+    backend.deltanet_chunked_prefill(q, k, v, gd, bd, core, st, s0, snapshots=snaps, snap_every=every)
+    # the plain entry point gives the same outputs
+    core_plain = torch.empty_like(core)
+    st_plain = torch.empty_like(st)
+    backend.deltanet_chunked_prefill(q, k, v, gd, bd, core_plain, st_plain, s0)
+    torch.cuda.synchronize()
+    assert torch.equal(core, core_plain) and torch.equal(st, st_plain)
+    for j in range(n_snap):
+        Tp = 64 * every * (j + 1)
+        c_p = torch.empty((B, Tp, NV, 128), device=dev)
+        s_p = torch.empty_like(st)
+        backend.deltanet_chunked_prefill(q[:, :Tp], k[:, :Tp], v[:, :Tp], gd[:, :Tp], bd[:, :Tp], c_p, s_p, s0)
+        torch.cuda.synchronize()
+        assert torch.equal(snaps[:, j], s_p), j
+        assert torch.equal(c_p, core[:, :Tp]), j
+    # resume after snapshot 1 (token 512) and finish the prompt
+    t1 = 64 * every * 2
+    c_r = torch.empty((B, T - t1, NV, 128), device=dev)
+    s_r = torch.empty_like(st)
+    backend.deltanet_chunked_prefill(q[:, t1:], k[:, t1:], v[:, t1:], gd[:, t1:], bd[:, t1:], c_r, s_r,
+                                     snaps[:, 1].contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(c_r, core[:, t1:])
+    assert torch.equal(s_r, st)
+    # and against the oracle, one head
+    rc, rs = oracle_head(qb, kb, vb, g, beta, 1, 3, NK, st0)
+    assert rel_l2(core[1, :, 3].cpu().numpy(), rc) < REL
+    assert backend.device_status() == 0
+
+
+def test_snapshot_arguments_are_checked(backend):
+    from hachiue_b200._lib import HachiueError
+    rng = np.random.default_rng(5)
+    qb, kb, vb, g, beta = make_inputs(rng, 1, 256, 1, 2)
+    core = torch.empty((1, 256, 2, 128), device=dev)
+    st = torch.empty((1, 2, 128, 128), device=dev)
+    with pytest.raises(HachiueError):  # wrong snapshot count for T = 256, every = 2
+        backend.deltanet_chunked_prefill(to_dev_bf16(qb), to_dev_bf16(kb), to_dev_bf16(vb),
+                                         torch.from_numpy(g).to(dev), torch.from_numpy(beta).to(dev), core, st,
+                                         snapshots=torch.empty((1, 3, 2, 128, 128), device=dev), snap_every=2)
+    with pytest.raises(HachiueError):  # snap_every 0 with a buffer: refused by the C entry point
+        backend.deltanet_chunked_prefill(to_dev_bf16(qb), to_dev_bf16(kb), to_dev_bf16(vb),
+                                         torch.from_numpy(g).to(dev), torch.from_numpy(beta).to(dev), core, st,
+                                         snapshots=torch.empty((1, 0, 2, 128, 128), device=dev), snap_every=0)
