@@ -396,12 +396,12 @@ int launch_t(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap&
   using C = Cfg<FMT, DH>;
   auto kern = attn_decode_kernel<FMT, DH, R>;
   const size_t smem = NST * C::STAGE_BYTES + 2 * NST * sizeof(uint64_t) + NW * C::TPW * R * sizeof(float);
-  static bool attr_done = false;  // per instantiation
-  if (!attr_done) {
+  static std::atomic<uint64_t> attr_done{0};  // per device
+  HCU_TRY(once_per_device(attr_done, h->device, [&]() -> int {
     HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "hcu_attention: smem attribute"));
-    attr_done = true;
-  }
+    return HCU_OK;
+  }));
   kern<<<grid, NTHREADS, smem, h->stream>>>(tk, tv, tks, tvs, args);
   return after_launch("hcu_attention: launch");
 }

@@ -393,12 +393,12 @@ int launch(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap& t
   constexpr int QS_BLK = NC * 128;
   constexpr size_t smem = 1024 + RING_BYTES + 6 * QS_BLK + 16 * 8 + 16 + (2 * 4 * R + 4 * R) * 4;
   auto kern = attn_decode_tc_kernel<BF16, R, NC>;
-  static bool attr_done = false;
-  if (!attr_done) {
+  static std::atomic<uint64_t> attr_done{0};  // per device
+  HCU_TRY(once_per_device(attr_done, h->device, [&]() -> int {
     HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "hcu_attention: tc smem attribute"));
-    attr_done = true;
-  }
+    return HCU_OK;
+  }));
   kern<<<grid, TC_THREADS, smem, h->stream>>>(tk, tv, args);
   return after_launch("hcu_attention: tc launch");
 }

@@ -6,6 +6,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "hachiue_cuda.h"
@@ -34,6 +35,17 @@ int check_cuda(cudaError_t e, const char* what);
 int begin_op(hcu_context* h, const char* op);
 // Launch-status check after a kernel launch.
 int after_launch(const char* what);
+// Kernel attributes such as the dynamic shared-memory limit belong to a
+// device: a call site sets them once per device, recorded in `done` (one bit
+// per device id; ids of 64 and above set them on every call).
+template <typename F>
+int once_per_device(std::atomic<uint64_t>& done, int device, F&& set) {
+  const uint64_t bit = (device >= 0 && device < 64) ? (1ull << device) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return HCU_OK;
+  const int rc = set();
+  if (rc == HCU_OK && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return rc;
+}
 // Makes h->scratch at least `bytes` long.  Growing synchronises the handle's
 // stream (queued work may still read the old buffer) and reallocates.
 int ensure_scratch(hcu_context* h, size_t bytes, const char* what);

@@ -439,16 +439,16 @@ int launch_dn(hcu_context* h, const hcu_deltanet_params* p, DnArgs a, bool fused
     if (n > 0x7fffffffLL) return fail(HCU_EINVAL, "deltanet: batch x H too large");
     const int grid = (int)(n < 2LL * h->sm_count ? n : 2LL * h->sm_count);  // two CTAs per SM
     constexpr int smem = DN_D * DN_D * 4;
-    static bool attr_done = false;
-    if (!attr_done) {
+    static std::atomic<uint64_t> attr_done{0};  // per device
+    HCU_TRY(once_per_device(attr_done, h->device, [&]() -> int {
       HCU_TRY(check_cuda(cudaFuncSetAttribute(deltanet_step_kernel<true, false>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                          "deltanet: smem attribute"));
       HCU_TRY(check_cuda(cudaFuncSetAttribute(deltanet_step_kernel<false, false>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                          "deltanet: smem attribute"));
-      attr_done = true;
-    }
+      return HCU_OK;
+    }));
     if (fused)
       deltanet_step_kernel<true, false><<<grid, DN_THREADS, smem, h->stream>>>(a, (int)n);
     else
@@ -706,13 +706,13 @@ extern "C" int hcu_gdn_layer_step(hcu_handle h, const hcu_gdn_step_params* p, co
   const long long n = (long long)batch * p->H;
   const int grid = (int)(n < 2LL * h->sm_count ? n : 2LL * h->sm_count);
   constexpr int smem = DN_D * DN_D * 4;
-  static bool attr_done = false;
-  if (!attr_done) {
+  static std::atomic<uint64_t> attr_done{0};  // per device
+  HCU_TRY(hcu::once_per_device(attr_done, h->device, [&]() -> int {
     HCU_TRY(hcu::check_cuda(cudaFuncSetAttribute(deltanet_step_kernel<true, true>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                             "hcu_gdn_layer_step: smem attribute"));
-    attr_done = true;
-  }
+    return HCU_OK;
+  }));
   deltanet_step_kernel<true, true><<<grid, DN_THREADS, smem, h->stream>>>(args, (int)n);
   return hcu::after_launch("hcu_gdn_layer_step");
 }

@@ -1002,16 +1002,16 @@ int chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q
     HCU_TRY(hcu::make_tensor_map(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, sbuf, sdims, sst, sbox,
                                  CU_TENSOR_MAP_SWIZZLE_NONE));
   }
-  static bool attr_done = false;
-  if (!attr_done) {
+  static std::atomic<uint64_t> attr_done{0};  // per device
+  HCU_TRY(hcu::once_per_device(attr_done, h->device, [&]() -> int {
     HCU_TRY(hcu::check_cuda(cudaFuncSetAttribute(hcu::gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  hcu::P_SMEM + 1024),
                             "hcu_deltanet_chunked_prefill: smem attribute"));
     HCU_TRY(hcu::check_cuda(cudaFuncSetAttribute(hcu::gdn_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  hcu::C_SMEM + 1024),
                             "hcu_deltanet_chunked_prefill: smem attribute"));
-    attr_done = true;
-  }
+    return HCU_OK;
+  }));
   const long long gb_row = p->gb_row_stride ? (long long)p->gb_row_stride : NV;
   const long long gb_seq = p->gb_seq_stride ? (long long)p->gb_seq_stride : T * gb_row;
   const long long npair = ((NV + NK - 1) / NK + 1) / 2;  // V heads per QK head, two per prep CTA

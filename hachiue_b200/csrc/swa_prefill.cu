@@ -547,12 +547,12 @@ int launch_swa(hcu_context* h, const SwaArgs& args, const CUtensorMap& tq, const
                const CUtensorMap& tv) {
   constexpr size_t smem = 1024 + NHD * TILE + KV_STAGES * KV_STAGE + 16 * 8 + 16;
   auto kern = swa_prefill_kernel<NHD, kSwaPolyPairs>;
-  static bool attr_done = false;
-  if (!attr_done) {
+  static std::atomic<uint64_t> attr_done{0};  // per device
+  HCU_TRY(once_per_device(attr_done, h->device, [&]() -> int {
     HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "hcu_swa_prefill: smem attribute"));
-    attr_done = true;
-  }
+    return HCU_OK;
+  }));
   // One CTA per SM (the shared memory admits no second), never more CTAs than
   // items.  HCU_SWA_CTAS caps the grid (tests use it to give every CTA a long
   // chain of items on small shapes).
