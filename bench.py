@@ -177,12 +177,22 @@ class ClockSampler:
                 self.proc.kill()
         self.thread.join(timeout=5)
         t0, t1 = self.window
-        inside = [x for x in self.samples if t0 is not None and t1 is not None and t0 <= x[0] <= t1]
+        if t0 is None or t1 is None:
+            return None
+        inside = [x for x in self.samples if t0 <= x[0] <= t1]
+        window = "timed region"
+        if not inside:
+            # a region shorter than the polling period: the samples just before
+            # and just after it bracket it
+            before = [x for x in self.samples if x[0] < t0]
+            after = [x for x in self.samples if x[0] > t1]
+            inside = before[-1:] + after[:1]
+            window = "bracketing samples (timed region shorter than the polling period)"
         if not inside:
             return None
         reasons = set().union(*(x[2] for x in inside))
         return {"sm_mhz": statistics.median(x[1] for x in inside), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(reasons), "samples": len(inside), "source": self.source}
+                "reasons": sorted(reasons), "samples": len(inside), "source": self.source, "window": window}
 
 
 def dist_setup(args):
@@ -265,10 +275,12 @@ def setup_cfg1(torch, be, dev):
         out_host.copy_(out, non_blocking=True)
 
     info = dict(workload="cfg1 Qwen3-1.7B GQA decode attention", q_heads=16, kv_heads=8, head_dim=128, context=1024,
-                kv_dtype="f32", l2=f"rotates {copies} cache copies (> L2)")
+                kv_dtype="f32", l2=f"rotates {copies} cache copies (> L2)",
+                launch="device-resident warm-up and timed steps each run as one CUDA graph of the op calls; "
+                       "e2e calls the API directly")
     return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg1_bytes(), tokens=1, info=info,
                 h2d=q_host.numel() * 4, d2h=out_host.numel() * 4, kernels_per_step=1, e2e_kernels_per_step=1,
-                cpu=dict(w=w, kind="cfg1"), out=out, traffic_key="cfg1")
+                cpu=dict(w=w, kind="cfg1"), out=out, traffic_key="cfg1", graph_period=copies)
 
 
 def setup_cfg4(torch, be, dev):
@@ -499,12 +511,14 @@ def setup_cfg7(torch, be, dev):
 
     info = dict(workload="cfg7 = cfg1 as a whole qwen3 attention layer step (q/k RMSNorm + RoPE + Q8_0 K/V "
                          "append + attention, fused prologue)", q_heads=H, kv_heads=KV, head_dim=Dh,
-                context=pos + 1, kv_dtype="Q8_0 (the reference's cache format)", l2=f"rotates {copies} cache copies (> L2)")
+                context=pos + 1, kv_dtype="Q8_0 (the reference's cache format)", l2=f"rotates {copies} cache copies (> L2)",
+                launch="device-resident warm-up and timed steps (and the comparison arm's) each run as one CUDA "
+                       "graph of the op calls; e2e calls the API directly")
     return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg7_bytes(), tokens=1, info=info,
                 h2d=sum(t.numel() * 4 for t in hs.values()), d2h=out_h.numel() * 4, kernels_per_step=2,
                 e2e_kernels_per_step=2, cpu=dict(w=w, kind="cfg7"), out=out, traffic_key="cfg7",
                 alt=dict(name="unfused: the engine's dispatch sequence (rmsnorm x2, rope x2, kv_append_q8 x2, "
-                              "attention_q8)", step=unfused, kernels_per_step=7))
+                              "attention_q8)", step=unfused, kernels_per_step=7), graph_period=copies)
 
 
 SETUPS = {1: setup_cfg1, 2: setup_cfg2, 3: setup_cfg3, 4: setup_cfg4, 5: setup_cfg5, 6: setup_cfg6, 7: setup_cfg7}
@@ -694,10 +708,32 @@ def main(argv=None):
     if world > 1:
         gather_out = torch.empty((world,) + tuple(W["out"].shape), device=dev, dtype=W["out"].dtype)
 
-    def full_step(i):
-        W["step"](i)
+    def gather(i):
         if world > 1:
             dist.all_gather_into_tensor(gather_out, W["out"])
+
+    def drain():
+        pass
+
+    def full_step(i):
+        W["step"](i)
+        gather(i)
+
+    # Latency-bound configurations (one sequence, a few launches of ~10 us) run
+    # their device-resident steps as CUDA graphs, as a serving loop would: the
+    # timed graph holds exactly the K timed steps (the warm-up graph the W
+    # warm-up steps), so the launches are not paced by Python.  Single GPU only.
+    graph_mode = bool(W.get("graph_period")) and world == 1
+
+    def capture(fn, n):
+        for i in range(min(n, W["graph_period"])):  # every input variant once, outside capture
+            fn(i)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                fn(i)
+        return g
 
     def barrier():
         if world > 1:
@@ -705,8 +741,13 @@ def main(argv=None):
         torch.cuda.synchronize(dev)
 
     # ---- device-resident timing ----
-    for i in range(args.warmup):
-        full_step(i)
+    if graph_mode:
+        g_warm, g_timed = capture(W["step"], args.warmup), capture(W["step"], args.steps)
+        g_warm.replay()
+    else:
+        for i in range(args.warmup):
+            full_step(i)
+    drain()
     barrier()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -718,18 +759,23 @@ def main(argv=None):
     t_end = torch.cuda.Event(enable_timing=True)
     clocks.mark_start()
     t_start.record(stream)
-    for i in range(args.steps):
-        kev[i][0].record(stream)
-        W["step"](i)
-        kev[i][1].record(stream)
-        if world > 1:
-            dist.all_gather_into_tensor(gather_out, W["out"])
+    if graph_mode:
+        g_timed.replay()
+    else:
+        for i in range(args.steps):
+            kev[i][0].record(stream)
+            W["step"](i)
+            kev[i][1].record(stream)
+            gather(i)
+    drain()
     t_end.record(stream)
     barrier()
     clocks.mark_end()
     clk = clocks.stop()
     total_ms = t_start.elapsed_time(t_end)
-    kernel_ms = [a.elapsed_time(b) for a, b in kev]
+    # in a graph the steps run back to back: a step's average duration is the
+    # whole replay's over K (gaps between launches included)
+    kernel_ms = [total_ms / args.steps] * args.steps if graph_mode else [a.elapsed_time(b) for a, b in kev]
     if world > 1:
         t = torch.tensor([total_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -749,16 +795,16 @@ def main(argv=None):
     # ---- end to end through the public API (host buffers) ----
     for i in range(args.warmup):
         W["e2e_step"](i)
-        if world > 1:
-            dist.all_gather_into_tensor(gather_out, W["out"])
+        gather(i)
+    drain()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
         W["e2e_step"](i)
-        if world > 1:
-            dist.all_gather_into_tensor(gather_out, W["out"])
+        gather(i)
+    drain()
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1)
@@ -771,14 +817,21 @@ def main(argv=None):
     # ---- comparison arm of the same workload (device-resident, as `value`) ----
     alt = None
     if "alt" in W:
-        for i in range(args.warmup):
-            W["alt"]["step"](i)
+        if graph_mode:
+            ga_warm, ga_timed = capture(W["alt"]["step"], args.warmup), capture(W["alt"]["step"], args.steps)
+            ga_warm.replay()
+        else:
+            for i in range(args.warmup):
+                W["alt"]["step"](i)
         barrier()
         a0 = torch.cuda.Event(enable_timing=True)
         a1 = torch.cuda.Event(enable_timing=True)
         a0.record(stream)
-        for i in range(args.steps):
-            W["alt"]["step"](i)
+        if graph_mode:
+            ga_timed.replay()
+        else:
+            for i in range(args.steps):
+                W["alt"]["step"](i)
         a1.record(stream)
         barrier()
         alt_ms = a0.elapsed_time(a1) / args.steps
