@@ -218,13 +218,17 @@ int hcu_attention_noalloc(const hcu_attention_params *p, const float *q, const h
 /* Append S rows of K or V (f32 [S, KV, Dh]) at cache row posBase in `format`.
  * For Q8_0 this is appendKvQ8 (src/wasm-backend.ts:793-824) bit for bit:
  * scale = amax/127 stored as f32, q = clamp(Math.round(x*127/amax), +-127).
- * `data` is K or V of an hcu_kv_cache, `scale` its scale array (Q8_0 only). */
+ * `data` is K or V of an hcu_kv_cache, `scale` its scale array (Q8_0 only).
+ * The call does not know the cache's length: the caller keeps posBase + S
+ * within it, as the engine does by allocating maxSeqLen rows up front
+ * (src/engine.ts:483-492).  (The Python host checks it against KVCache.rows.) */
 int hcu_kv_append(hcu_handle h, uint32_t S, uint32_t KV, uint32_t Dh, uint32_t posBase,
                   uint32_t format, const float *src, void *data, float *scale);
 
 /* Batched decode form of hcu_kv_append: source row i (f32 [n, KV, Dh]) goes to
  * cache row dst_rows[i] (device int64 array), e.g. one new token per sequence
- * of a packed batch.  Same per-row arithmetic as hcu_kv_append. */
+ * of a packed batch.  Same per-row arithmetic as hcu_kv_append; every
+ * dst_rows[i] must be a row of the cache. */
 int hcu_kv_append_rows(hcu_handle h, uint32_t n, uint32_t KV, uint32_t Dh, uint32_t format,
                        const float *src, const int64_t *dst_rows, void *data, float *scale);
 
