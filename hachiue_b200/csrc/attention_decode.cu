@@ -46,6 +46,18 @@ struct Cfg {
 
 
 
+// Four int8 values packed in a word, as exact f32 values, without the
+// int-to-float conversion instruction (a quarter-rate pipe): with its sign bit
+// flipped, each byte b + 128 becomes the low mantissa byte of 2^23, and
+// subtracting 2^23 + 128 leaves b.
+__device__ __forceinline__ void s8x4_to_f32(uint32_t w, float* f) {
+  const uint32_t u = w ^ 0x80808080u;
+  f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.f;
+  f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.f;
+  f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.f;
+  f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.f;
+}
+
 // Loads the lane's DPL elements of tile row `row` as f32 (Q8_0: times the
 // block scale, like `kQ * kS` in wasm-backend.ts:861-866).
 template <int FMT, int DH>
@@ -91,17 +103,14 @@ __device__ __forceinline__ void load_row(const uint8_t* tile, const float* scale
     const int8_t* p = reinterpret_cast<const int8_t*>(tile + (size_t)row * DH) + lane * DPL;
     const float s = scales[row * (DH / 32) + (lane * DPL) / 32];
     if constexpr (DPL == 4) {
-      char4 x = *reinterpret_cast<const char4*>(p);
-      v[0] = (float)x.x * s;
-      v[1] = (float)x.y * s;
-      v[2] = (float)x.z * s;
-      v[3] = (float)x.w * s;
+      s8x4_to_f32(*reinterpret_cast<const uint32_t*>(p), v);
     } else {
-      int2 xx = *reinterpret_cast<const int2*>(p);
-      const int8_t* b = reinterpret_cast<const int8_t*>(&xx);
-#pragma unroll
-      for (int i = 0; i < 8; i++) v[i] = (float)b[i] * s;
+      const uint2 xx = *reinterpret_cast<const uint2*>(p);
+      s8x4_to_f32(xx.x, v);
+      s8x4_to_f32(xx.y, v + 4);
     }
+#pragma unroll
+    for (int i = 0; i < DPL; i++) v[i] *= s;
   }
 }
 
