@@ -31,7 +31,12 @@ using namespace hcu;
 
 constexpr int NW = 4;                   // consumer warps
 constexpr int NTHREADS = (NW + 1) * 32; // + 1 TMA producer warp
-constexpr int NST = 3;                  // pipeline stages
+// Pipeline stages and CTAs per SM: with few rows per CTA, three CTAs of two
+// stages share an SM (more warps to hide load and shared-memory latency);
+// with more rows the registers allow two CTAs of three stages.
+__host__ __device__ constexpr bool three_ctas(int R, int DH) { return R <= 2 || (R <= 4 && DH == 128); }
+__host__ __device__ constexpr int ctas_per_sm(int R, int DH) { return three_ctas(R, DH) ? 3 : 2; }
+__host__ __device__ constexpr int stages_for(int R, int DH) { return three_ctas(R, DH) ? 2 : 3; }
 
 template <int FMT, int DH>
 struct Cfg {
@@ -140,12 +145,12 @@ __device__ __forceinline__ void treduce(float (&v)[N], int lane) {
 }
 
 template <int FMT, int DH, int R>
-__global__ void __launch_bounds__(NTHREADS, 2)
+__global__ void __launch_bounds__(NTHREADS, ctas_per_sm(R, DH))
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const __grid_constant__ CUtensorMap tmKs, const __grid_constant__ CUtensorMap tmVs,
                        const AttnArgs a) {
   using C = Cfg<FMT, DH>;
-  constexpr int TT = C::TT, TPW = C::TPW, DPL = C::DPL;
+  constexpr int TT = C::TT, TPW = C::TPW, DPL = C::DPL, NST = stages_for(R, DH);
   constexpr int TG = (32 / R) < TPW ? (32 / R > 0 ? 32 / R : 1) : TPW;  // tokens per reduce group
   constexpr int NV = TG * R;                                            // values per reduce
   constexpr int NPL = NV >= 32 ? NV / 32 : 1;                           // results per lane
@@ -156,7 +161,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * C::STAGE_BYTES);
   uint64_t* empty = full + NST;
   float* sc_all = reinterpret_cast<float*>(empty + NST);
-  __shared__ int s_last;
+  int* s_last = reinterpret_cast<int*>(sc_all + NW * TPW * R);  // in the dynamic memory: no static padding
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -322,6 +327,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
 
     // ---- acc += p . V over the warp's valid rows ----
     const int tcount = min(TPW, k_hi - wk0);
+    constexpr int PV_UNROLL = R <= 4 ? 4 : 1;  // more rows leave no registers to unroll with
+#pragma unroll PV_UNROLL
     for (int t = 0; t < tcount; t++) {
       float vvec[DPL];
       load_row<FMT, DH>(vtile, vscale, wrow0 + t, lane, vvec);
@@ -391,7 +398,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   }
   if (u.nsplit == 1) return;
   named_bar(1, NW * 32);  // cb / cm / cl are read above; the merge reuses the stage memory
-  ticket_merge<R, DH, NW * 32>(a, u, tid, 1, reinterpret_cast<float*>(stages), &s_last);
+  ticket_merge<R, DH, NW * 32>(a, u, tid, 1, reinterpret_cast<float*>(stages), s_last);
   (void)b;
   (void)pb;
 }
@@ -404,7 +411,11 @@ int launch_t(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap&
              const CUtensorMap& tks, const CUtensorMap& tvs) {
   using C = Cfg<FMT, DH>;
   auto kern = attn_decode_kernel<FMT, DH, R>;
-  const size_t smem = NST * C::STAGE_BYTES + 2 * NST * sizeof(uint64_t) + NW * C::TPW * R * sizeof(float);
+  constexpr int NST = stages_for(R, DH);
+  const size_t smem = NST * C::STAGE_BYTES + 2 * NST * sizeof(uint64_t) + NW * C::TPW * R * sizeof(float) + 16;
+  // the per-warp partials and the split merge reuse the stage buffers
+  static_assert((NW * R * DH + 2 * NW * R) * 4 <= NST * C::STAGE_BYTES && kMaxSplits * R * 4 <= NST * C::STAGE_BYTES,
+                "merge buffers exceed the stage memory");
   static std::atomic<uint64_t> attr_done{0};  // per device
   HCU_TRY(once_per_device(attr_done, h->device, [&]() -> int {
     HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
