@@ -213,3 +213,34 @@ def test_tensor_core_and_cuda_core_paths(backend, monkeypatch, impl, fmt, H, KV,
     ref = oracle.attention(q, kk, vv, pos, W, fmt)
     assert rel_l2(out.cpu().numpy(), ref) < TOL
     assert backend.device_status() == 0
+
+
+@pytest.mark.parametrize("H,KV,S,pos,W", [(32, 8, 1, 4000, 0), (16, 4, 3, 700, 0), (8, 2, 5, 1000, 300),
+                                          (4, 4, 1, 129, 0), (16, 2, 1, 2049, 0), (12, 3, 2, 63, 17),
+                                          (16, 8, 1, 1023, 0)])
+def test_q8_cache_rows_past_the_context(backend, H, KV, S, pos, W):
+    """Q8_0 caches (the engine's format) against runAttentionQ8 over GQA groups
+    1-8, S > 1, windows and tile-edge lengths, with the rows past the context
+    holding arbitrary int8 values and NaN scales: they must never reach the
+    output."""
+    rng = np.random.default_rng(7 * H + KV + S + pos + W)
+    rows = pos + S
+    q = rng.standard_normal((S, H, 128), dtype=np.float32)
+    kf = rng.standard_normal((rows, KV, 128), dtype=np.float32)
+    vf = rng.standard_normal((rows, KV, 128), dtype=np.float32)
+    cache = KVCache.allocate(rows + 200, KV, 128, KV_Q8_0)
+    cache.k.copy_(torch.from_numpy(rng.integers(-127, 128, cache.k.shape, dtype=np.int8)))
+    cache.v.copy_(torch.from_numpy(rng.integers(-127, 128, cache.v.shape, dtype=np.int8)))
+    cache.k_scale.fill_(float("nan"))
+    cache.v_scale.fill_(float("nan"))
+    backend.kv_append(T(kf), cache, "k", 0)
+    backend.kv_append(T(vf), cache, "v", 0)
+    out = torch.zeros((S, H, 128), device=dev)
+    backend.attention(T(q), cache, out, pos, W)
+    torch.cuda.synchronize()
+    kq, vq = cache.k[:rows].cpu().numpy(), cache.v[:rows].cpu().numpy()
+    ks, vs = cache.k_scale[:rows].cpu().numpy(), cache.v_scale[:rows].cpu().numpy()
+    ref = oracle.attention(q, kq, vq, pos, W, KV_Q8_0, ks, vs)
+    assert np.isfinite(out.cpu().numpy()).all()
+    assert rel_l2(out.cpu().numpy(), ref) < TOL
+    assert backend.device_status() == 0
