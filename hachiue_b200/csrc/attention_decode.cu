@@ -499,13 +499,15 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
                 (long long)p->posBase + S);
   if (kv->rows == 0 || kv->rows > 0x7fffffffu) return fail(HCU_EINVAL, "hcu_attention: bad cache row count");
 
-  // Key splits: about 8 CTAs per SM over the whole call, at most kMaxSplits
-  // per unit, each a whole number of tiles.
+  // Key splits: about 8 CTAs per SM over the whole call for the tensor-core
+  // kernel, 24 for the CUDA-core one (three resident per SM, and shorter
+  // splits balance its uneven sequences: cfg2's Q8_0 shapes 289 -> 259 us),
+  // at most kMaxSplits per unit, each a whole number of tiles.
   const int TT = use_tc ? hcu::kTcTile : tile_tokens(fmt, Dh);
   const long long units = (long long)batch * KV * nqb;
   if (units > kMaxUnits)
     return fail(HCU_EINVAL, "hcu_attention: batch x KV x query blocks = %lld > %d", units, kMaxUnits);
-  long long target = 8LL * h->sm_count;
+  long long target = (use_tc ? 8LL : 24LL) * h->sm_count;
   long long want_splits = (target + units - 1) / units;
   if (want_splits < 1) want_splits = 1;
   long long chunk = (max_range + want_splits - 1) / want_splits;
