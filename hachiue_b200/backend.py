@@ -138,6 +138,12 @@ class CudaBackend:
         """Make the next ``n`` op calls fail on the host with ``status``."""
         check(self.lib.hcu_inject_failure(self._h, status, n))
 
+    def selftest_wait_timeout(self) -> None:
+        """Launch a kernel whose bounded wait runs out (about 2 s): it records
+        the timeout bit in the device status word and returns."""
+        self._bind_stream()
+        check(self.lib.hcu_selftest_wait_timeout(self._h))
+
     # -- the reference's seam --------------------------------------------------
     def dispatch(self, shader_name: str, words, buffers) -> None:
         """engine.dispatch(): ``words`` are up to eight u32 uniform words (use

@@ -104,6 +104,14 @@ int hcu_device_status(hcu_handle h, uint32_t *status, int clear);
  * with `status` on the host before launching anything (0 disables). */
 int hcu_inject_failure(hcu_handle h, int status, int n);
 
+/* Failure-detection self-test (no counterpart in the reference, whose device
+ * failures surface as onDeviceLost, src/engine.ts:641-643): launches one warp
+ * that waits on a pipeline barrier nothing ever signals, through the bounded
+ * wait every kernel here uses.  After about 2 s the wait gives up, sets bit 1
+ * (timeout) in the handle's device status word and the kernel returns: no
+ * fault, and the context stays usable.  Read it with hcu_device_status. */
+int hcu_selftest_wait_timeout(hcu_handle h);
+
 /* ------------------------------------------------------------------------ */
 /* The reference's dispatch seam                                              */
 /* ------------------------------------------------------------------------ */

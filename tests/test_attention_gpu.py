@@ -244,3 +244,23 @@ def test_q8_cache_rows_past_the_context(backend, H, KV, S, pos, W):
     assert np.isfinite(out.cpu().numpy()).all()
     assert rel_l2(out.cpu().numpy(), ref) < TOL
     assert backend.device_status() == 0
+
+
+def test_bounded_wait_reports_a_timeout(backend):
+    """A device-side wait that nothing ends gives up after its time limit,
+    records the timeout bit in the status word and returns: the host reads
+    it, and the next call runs normally (no fault, no hang)."""
+    assert backend.device_status() == 0
+    backend.selftest_wait_timeout()
+    assert backend.device_status() == 1  # HCU_DEVERR_TIMEOUT, cleared by the read
+    assert backend.device_status() == 0
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal((1, 4, 128), dtype=np.float32)
+    k = rng.standard_normal((40, 2, 128), dtype=np.float32)
+    v = rng.standard_normal((40, 2, 128), dtype=np.float32)
+    cache = KVCache(KV_F32, T(k), T(v))
+    out = torch.zeros((1, 4, 128), device=dev)
+    backend.attention(T(q), cache, out, 39)
+    torch.cuda.synchronize()
+    assert rel_l2(out.cpu().numpy(), oracle.attention(q, k, v, 39)) < TOL
+    assert backend.device_status() == 0
