@@ -80,3 +80,42 @@ class HeadShardedDecode:
         ql = q[:, :, self.h_lo:self.h_hi].contiguous()
         self.be.attention(ql, cache, out_local, pos_base, **kw)
         return gather_head_shards(out_local, self.group)
+
+
+class PeerLost(RuntimeError):
+    """A rank stopped taking steps: raised on the host before the next
+    collective, instead of blocking in it."""
+
+
+class StepWatch:
+    """Host-side failure detection between steps.  Every rank posts ``step`` to
+    the process group's store after finishing a step's launches; before the
+    next collective, ``check(step)`` waits (up to ``timeout_s``) for every
+    peer's post of that step and raises :class:`PeerLost` naming the ranks
+    that never posted.  A rank therefore leaves only between steps, with none
+    of its kernels or collectives in flight, and its peers learn of it on the
+    host rather than inside a collective."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 5.0, prefix: str = "hachiue/step"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = timeout_s, prefix
+
+    def _key(self, rank: int, step: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def post(self, step: int) -> None:
+        self.store.set(self._key(self.rank, step), "1")
+
+    def check(self, step: int) -> None:
+        import time
+        keys = [self._key(r, step) for r in range(self.world) if r != self.rank]
+        deadline = time.monotonic() + self.timeout_s
+        missing = keys
+        while True:
+            missing = [k for k in missing if not self.store.check([k])]
+            if not missing or time.monotonic() > deadline:
+                break
+            time.sleep(0.01)
+        if missing:
+            lost = sorted(int(k.rsplit("/", 1)[1]) for k in missing)
+            raise PeerLost(f"hachiue: rank(s) {lost} did not finish step {step} within {self.timeout_s} s")

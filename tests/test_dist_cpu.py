@@ -3,6 +3,7 @@
 Each rank computes its shard with the oracle (the GPU kernels are covered by
 the single-GPU parity tests) and the gathered result must equal the unsharded
 computation exactly: the collective and the re-ordering move bits only."""
+import datetime
 import os
 import socket
 
@@ -90,3 +91,58 @@ def test_partitions_cover_everything():
     assert all(((h + 16) in o) for o in owned for h in o if h < 16)
     with pytest.raises(ValueError):
         hdist.kv_head_range(8, 3, 0)
+
+
+def _watch_worker(rank, world, port, fail_rank, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=30))
+    dist.init_process_group("gloo", rank=rank, world_size=world, store=dist.PrefixStore("pg", store))
+    watch = hdist.StepWatch(store, rank, world, timeout_s=2.0)
+    out = torch.zeros(world)
+    try:
+        for step in range(4):
+            if rank == fail_rank and step == 2:
+                raise RuntimeError("rank failed between steps")  # leaves with nothing in flight
+            watch.post(step)
+            watch.check(step)  # every peer finished this step's work: the collective may start
+            dist.all_gather_into_tensor(out, torch.full((1,), float(rank + step)))
+        result_q.put((rank, "done", out.tolist()))
+    except hdist.PeerLost as e:
+        result_q.put((rank, "peer_lost", str(e)))
+    except RuntimeError as e:
+        result_q.put((rank, "raised", str(e)))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_a_rank_that_leaves_is_reported_not_waited_for():
+    """Host-side failure detection with 2 gloo ranks: rank 1 raises between
+    steps; rank 0 learns of it from the store before its next all-gather and
+    raises PeerLost naming rank 1 instead of blocking."""
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_watch_worker, args=(r, 2, port, 1, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict((r, (kind, msg)) for r, kind, msg in (q.get(timeout=120) for _ in range(2)))
+    for p in ps:
+        p.join(timeout=60)
+    assert got[1][0] == "raised"
+    assert got[0][0] == "peer_lost" and "[1]" in got[0][1] and "step 2" in got[0][1]
+
+
+def test_step_watch_without_failures():
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_watch_worker, args=(r, 2, port, -1, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict((r, (kind, msg)) for r, kind, msg in (q.get(timeout=120) for _ in range(2)))
+    for p in ps:
+        p.join(timeout=60)
+    assert got[0] == ("done", [3.0, 4.0]) and got[1] == ("done", [3.0, 4.0])
