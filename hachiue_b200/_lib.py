@@ -24,7 +24,8 @@ STATUS_NAMES = {
 EXPORTS = (
     "hcu_version", "hcu_last_error", "hcu_create", "hcu_destroy", "hcu_set_stream", "hcu_get_stream",
     "hcu_stream_sync", "hcu_alloc", "hcu_free", "hcu_memset", "hcu_copy_to_device", "hcu_copy_to_host",
-    "hcu_device_status", "hcu_inject_failure", "hcu_selftest_wait_timeout", "hcu_dispatch", "hcu_attention", "hcu_attention_noalloc", "hcu_kv_append", "hcu_kv_append_rows",
+    "hcu_device_status", "hcu_inject_failure", "hcu_selftest_wait_timeout", "hcu_comm_create", "hcu_comm_destroy",
+    "hcu_allgather", "hcu_dispatch", "hcu_attention", "hcu_attention_noalloc", "hcu_kv_append", "hcu_kv_append_rows",
     "hcu_deltanet_gbeta", "hcu_deltanet_recur", "hcu_deltanet_decode", "hcu_swa_prefill",
     "hcu_deltanet_chunked_prefill", "hcu_deltanet_chunked_prefill_snap", "hcu_conv1d_causal", "hcu_deltanet_norm_gate", "hcu_gdn_layer_step",
     "hcu_rmsnorm", "hcu_rope", "hcu_split_q_gate", "hcu_sigmoid_gate", "hcu_attn_prologue",
@@ -126,6 +127,9 @@ def load(path: str | None = None):
             "hcu_device_status": ([vp, ctypes.POINTER(u32), i32], i32),
             "hcu_inject_failure": ([vp, i32, i32], i32),
             "hcu_selftest_wait_timeout": ([vp], i32),
+            "hcu_comm_create": ([i32, ctypes.POINTER(i32), ctypes.POINTER(vp)], i32),
+            "hcu_comm_destroy": ([vp], i32),
+            "hcu_allgather": ([vp, ctypes.POINTER(vp), ctypes.POINTER(vp), sz, ctypes.POINTER(vp)], i32),
             "hcu_dispatch": ([vp, ctypes.c_char_p, ctypes.POINTER(u32), ctypes.POINTER(vp), i32], i32),
             "hcu_attention": ([vp, ctypes.POINTER(hcu_attention_params), vp, ctypes.POINTER(hcu_kv_cache), vp], i32),
             "hcu_attention_noalloc": ([ctypes.POINTER(hcu_attention_params), vp, ctypes.POINTER(hcu_kv_cache), vp,

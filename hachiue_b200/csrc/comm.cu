@@ -1,0 +1,123 @@
+// comm.cu - single-process multi-GPU collectives for hosts that cannot run
+// one process per GPU.  The reference's host is one Node process driving one
+// GPUDevice (src/engine.ts:320); a multi-GPU 'cuda' backend under Node has
+// to drive every GPU from that process, so the all-gather that joins the
+// per-rank outputs of the sharded path (hachiue_b200/dist.py does the same with
+// torch.distributed, one process per GPU) runs here on one NCCL communicator
+// per device made by ncclCommInitAll, in one ncclGroupStart / ncclGroupEnd.
+//
+// NCCL is opened at the first hcu_comm_create with dlopen("libnccl.so.2"), not
+// linked: a process that already holds an NCCL (torch's, for instance) shares
+// it, and a library user who never creates a communicator never loads one.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <mutex>
+
+#include "context.h"
+
+struct hcu_comm_s {
+  int n = 0;
+  int devices[HCU_COMM_MAX_DEVICES] = {};
+  ncclComm_t comms[HCU_COMM_MAX_DEVICES] = {};
+};
+
+namespace {
+
+using hcu::fail;
+
+struct NcclApi {
+  decltype(&ncclCommInitAll) init_all = nullptr;
+  decltype(&ncclCommDestroy) destroy = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclGroupStart) group_start = nullptr;
+  decltype(&ncclGroupEnd) group_end = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+  bool ok = false;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!lib) return;
+    api.init_all = reinterpret_cast<decltype(api.init_all)>(dlsym(lib, "ncclCommInitAll"));
+    api.destroy = reinterpret_cast<decltype(api.destroy)>(dlsym(lib, "ncclCommDestroy"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(lib, "ncclAllGather"));
+    api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(lib, "ncclGroupStart"));
+    api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(lib, "ncclGroupEnd"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(lib, "ncclGetErrorString"));
+    api.ok = api.init_all && api.destroy && api.all_gather && api.group_start && api.group_end && api.error_string;
+  });
+  return api;
+}
+
+int check_nccl(ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return HCU_OK;
+  return fail(HCU_ENCCL, "%s: %s", what, nccl().error_string(r));
+}
+
+}  // namespace
+
+extern "C" int hcu_comm_create(int n, const int* devices, hcu_comm* comm) {
+  if (!comm || !devices) return fail(HCU_EINVAL, "hcu_comm_create: null argument");
+  *comm = nullptr;
+  if (n < 1 || n > HCU_COMM_MAX_DEVICES) return fail(HCU_EINVAL, "hcu_comm_create: %d devices (1..%d)", n,
+                                                     HCU_COMM_MAX_DEVICES);
+  int count = 0;
+  HCU_TRY(hcu::check_cuda(cudaGetDeviceCount(&count), "hcu_comm_create: cudaGetDeviceCount"));
+  for (int i = 0; i < n; i++) {
+    if (devices[i] < 0 || devices[i] >= count)
+      return fail(HCU_EINVAL, "hcu_comm_create: device %d of %d", devices[i], count);
+    for (int j = 0; j < i; j++)
+      if (devices[j] == devices[i]) return fail(HCU_EINVAL, "hcu_comm_create: device %d listed twice", devices[i]);
+  }
+  const NcclApi& api = nccl();
+  if (!api.ok) return fail(HCU_ENCCL, "hcu_comm_create: libnccl.so.2 could not be opened");
+  hcu_comm c = new (std::nothrow) hcu_comm_s;
+  if (!c) return fail(HCU_ENOMEM, "hcu_comm_create: out of host memory");
+  c->n = n;
+  for (int i = 0; i < n; i++) c->devices[i] = devices[i];
+  const int st = check_nccl(api.init_all(c->comms, n, c->devices), "hcu_comm_create: ncclCommInitAll");
+  if (st != HCU_OK) {
+    delete c;
+    return st;
+  }
+  *comm = c;
+  return HCU_OK;
+}
+
+extern "C" int hcu_comm_destroy(hcu_comm comm) {
+  if (!comm) return HCU_OK;
+  int st = HCU_OK;
+  for (int i = 0; i < comm->n; i++) {
+    const int r = check_nccl(nccl().destroy(comm->comms[i]), "hcu_comm_destroy: ncclCommDestroy");
+    if (st == HCU_OK) st = r;
+  }
+  delete comm;
+  return st;
+}
+
+extern "C" int hcu_allgather(hcu_comm comm, void* const* send, void* const* recv, size_t bytes,
+                             void* const* streams) {
+  if (!comm || !send || !recv || !streams) return fail(HCU_EINVAL, "hcu_allgather: null argument");
+  for (int i = 0; i < comm->n; i++)
+    if (!send[i] || !recv[i]) return fail(HCU_EINVAL, "hcu_allgather: null buffer of rank %d", i);
+  if (bytes == 0) return HCU_OK;
+  const NcclApi& api = nccl();
+  int prev = 0;
+  HCU_TRY(hcu::check_cuda(cudaGetDevice(&prev), "hcu_allgather: cudaGetDevice"));
+  HCU_TRY(check_nccl(api.group_start(), "hcu_allgather: ncclGroupStart"));
+  int st = HCU_OK;
+  for (int i = 0; i < comm->n && st == HCU_OK; i++) {
+    st = hcu::check_cuda(cudaSetDevice(comm->devices[i]), "hcu_allgather: cudaSetDevice");
+    if (st == HCU_OK)
+      st = check_nccl(api.all_gather(send[i], recv[i], bytes, ncclInt8, comm->comms[i],
+                                     static_cast<cudaStream_t>(streams[i])),
+                      "hcu_allgather: ncclAllGather");
+  }
+  const int end = check_nccl(api.group_end(), "hcu_allgather: ncclGroupEnd");
+  cudaSetDevice(prev);
+  return st != HCU_OK ? st : end;
+}

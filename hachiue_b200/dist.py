@@ -119,3 +119,49 @@ class StepWatch:
         if missing:
             lost = sorted(int(k.rsplit("/", 1)[1]) for k in missing)
             raise PeerLost(f"hachiue: rank(s) {lost} did not finish step {step} within {self.timeout_s} s")
+
+
+class DeviceComm:
+    """One process driving several GPUs (as a Node host of the reference
+    would): a communicator over ``devices`` (hcu_comm_create, ncclCommInitAll)
+    and the path's all-gather (hcu_allgather) on each device's current torch
+    stream.  Rank i is ``devices[i]``."""
+
+    def __init__(self, devices):
+        import ctypes
+        from . import _lib
+        self._ct, self.lib = ctypes, _lib.load()
+        self.devices = [int(d) for d in devices]
+        n = len(self.devices)
+        h = ctypes.c_void_p()
+        _lib.check(self.lib.hcu_comm_create(n, (ctypes.c_int * n)(*self.devices), ctypes.byref(h)))
+        self._c = h
+
+    def all_gather(self, sends: list[torch.Tensor], recvs: list[torch.Tensor]) -> None:
+        """recvs[i][r] = sends[r] for every rank: sends[i] on devices[i],
+        recvs[i] of shape (n,) + sends[i].shape, same dtype."""
+        from . import _lib
+        ct, n = self._ct, len(self.devices)
+        if len(sends) != n or len(recvs) != n:
+            raise _lib.HachiueError(_lib.HCU_EINVAL, f"hachiue: all_gather takes {n} send and receive buffers")
+        nbytes = sends[0].numel() * sends[0].element_size()
+        for i, (s, r) in enumerate(zip(sends, recvs)):
+            if (s.device.index != self.devices[i] or r.device.index != self.devices[i] or not s.is_contiguous()
+                    or not r.is_contiguous() or s.numel() * s.element_size() != nbytes
+                    or r.numel() * r.element_size() != n * nbytes):
+                raise _lib.HachiueError(_lib.HCU_EINVAL, f"hachiue: all_gather buffers of rank {i}")
+        streams = [torch.cuda.current_stream(d).cuda_stream for d in self.devices]
+        vp = ct.c_void_p
+        _lib.check(self.lib.hcu_allgather(self._c, (vp * n)(*[s.data_ptr() for s in sends]),
+                                          (vp * n)(*[r.data_ptr() for r in recvs]), nbytes, (vp * n)(*streams)))
+
+    def close(self) -> None:
+        if getattr(self, "_c", None):
+            self.lib.hcu_comm_destroy(self._c)
+            self._c = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -100,6 +100,23 @@ int hcu_copy_to_host(hcu_handle h, void *host_dst, const void *device_src, size_
  * synchronises the stream.  `clear` resets it. */
 int hcu_device_status(hcu_handle h, uint32_t *status, int clear);
 
+/* Single-process multi-GPU: the reference drives one GPUDevice from one Node
+ * process (src/engine.ts:320), so a multi-GPU host of this library drives
+ * every GPU from one process.  A communicator over
+ * `n` of this process's devices (ncclCommInitAll; NCCL is opened with dlopen
+ * at the first call, fails with HCU_ENCCL if absent).  Rank i is devices[i]. */
+#define HCU_COMM_MAX_DEVICES 16
+typedef struct hcu_comm_s *hcu_comm;
+int hcu_comm_create(int n, const int *devices, hcu_comm *comm);
+int hcu_comm_destroy(hcu_comm comm);
+
+/* All-gather of the sharded path's per-rank outputs, the one collective of
+ * the multi-GPU layout: rank i sends `bytes` from send[i] (device memory of
+ * devices[i]) and receives every rank's block, rank-major, into recv[i]
+ * (n * bytes).  streams[i] is a CUDA stream of devices[i] (NULL: its default
+ * stream); the call enqueues and returns. */
+int hcu_allgather(hcu_comm comm, void *const *send, void *const *recv, size_t bytes, void *const *streams);
+
 /* Test hook for failure detection: the next `n` op calls on this handle fail
  * with `status` on the host before launching anything (0 disables). */
 int hcu_inject_failure(hcu_handle h, int status, int n);
