@@ -108,6 +108,8 @@ int hcu_device_status(hcu_handle h, uint32_t *status, int clear);
 #define HCU_COMM_MAX_DEVICES 16
 typedef struct hcu_comm_s *hcu_comm;
 int hcu_comm_create(int n, const int *devices, hcu_comm *comm);
+/* Destroy once every all-gather enqueued on the communicator has completed
+ * (synchronise its streams first). */
 int hcu_comm_destroy(hcu_comm comm);
 
 /* All-gather of the sharded path's per-rank outputs, the one collective of
