@@ -1,31 +1,47 @@
 """Benchmark of the hachiue attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+                    [--no-secondary] [--no-cpu-baseline]
 
-Prints ONE JSON line (rank 0).  The default workload is configuration 2 of the
-benchmark set: Qwen3-8B-shape batched GQA decode attention, 64 sequences,
-32 query / 8 KV heads, head_dim 128, per-sequence contexts U[512, 8192]
-(seed 1), f16 KV cache, f32 q / out.  A step is one decode-attention pass over
-the whole batch.  Other configurations (--config 1, 4) are available for
-profiling; their parity is covered by the tests.
+Prints ONE JSON line (rank 0).
+
+Headline (``value``): configuration 2 of the benchmark set, Qwen3-8B-shape
+batched GQA decode attention (64 sequences, 32 query / 8 KV heads, head_dim
+128, per-sequence contexts U[512, 8192] from seed 1, f16 KV cache, f32 q /
+out).  A step is one decode-attention pass over the whole batch; ``value`` is
+its algorithmic HBM GB/s with the inputs resident.  ``e2e`` is the same metric
+through the public API with host buffers: every step copies its q and its new
+K / V rows from pinned host memory, appends the rows, runs the attention and
+reads the output back (hachiue_b200.pipeline.HostPipeline overlaps step i+1's
+copies with step i's kernels, as a serving loop does).
+
+``secondary`` (one GPU, default run): the other benchmark configurations in
+the same run, each with its own value, roofline (algorithmic work per launch,
+kernel time, fraction of MEASURED_PEAKS.json), clocks, e2e and CPU sample:
+cfg1 (Qwen3-1.7B decode, f32 cache), cfg3 (PLaMo-3 SWA prefill, bf16, tensor
+roofline), cfg4 (Qwen3.5 GDN decode step), cfg5 (Qwen3.5 GDN chunked prefill)
+and cfg2_q8 (cfg2's shapes on the reference's own Q8_0 cache format).
+``--config N`` (1-7, or 2q8) makes configuration N the headline instead.
+
+Multi-GPU (torchrun, one process per GPU): the headline is weak scaling (each
+rank owns its own 64-sequence batch; the per-head outputs of all ranks are
+all-gathered every step through this library's NCCL communicator,
+hcu_comm_init_rank / hcu_allgather, overlapped with the next step).  The
+``strong`` block measures one configuration's fixed work split over the N
+GPUs: cfg2 by KV head and cfg5 by QK head (V heads h and h + NK together),
+with the all-gather's time and share measured by CUDA events.
 
 Timing: CUDA events on the launching stream, W untimed warm-up steps, K timed
-steps bracketed by barrier + synchronize, max over ranks.  The config-2 working
-set (1.1 GB of K/V) is larger than L2 (126 MB), so no flush is needed; the
-smaller configurations rotate through enough input copies to exceed L2.
+steps bracketed by barrier + synchronize, max over ranks.  cfg2, cfg2_q8, cfg3
+and cfg5 read more than L2 (126 MB) per step; cfg1 and cfg4 rotate input
+copies to exceed it.  Clocks are sampled (NVML, read-only) during each timed
+region.
 
-``value`` is aggregate algorithmic HBM GB/s of the attention kernel over all
-ranks (inputs resident in HBM); ``e2e`` is the same metric through the public
-``CudaBackend`` API with the step's inputs (q and the step's new K/V rows)
-copied from pinned host memory, the K/V append, the attention and the output
-read back every step.  Multi-GPU (torchrun) is weak scaling: each rank owns its
-own 64-sequence batch, and the per-head outputs of all ranks are all-gathered
-over NCCL every step.
-
-``--impl reference`` times the reference algorithm on the host cores instead:
-the reference is TypeScript and cannot run here, so this arm runs the C
-restatement in oracle/ (its JS-semantics port), multi-threaded over sequences,
-on a bounded sample of the same workload.
+``--impl reference`` times the reference algorithm on the host cores: the
+reference is TypeScript with no JS runtime on the box, so its JS-semantics C
+restatement (oracle/) runs, multi-threaded over sequences, on a bounded
+sample of the same workload, and also in the reference's own setting (one
+thread over a Q8_0 cache), reported beside it.
 """
 from __future__ import annotations
 
@@ -88,7 +104,6 @@ class ClockSampler:
         self.thread = None
         self.samples = []  # (perf_counter, sm_mhz, reasons)
         self.max_mhz = None
-        self.window = [None, None]
         self._stop = threading.Event()
         self.source = None
 
@@ -159,31 +174,15 @@ class ClockSampler:
         while self.thread is not None and not self.samples and time.perf_counter() - t0 < timeout:
             time.sleep(0.01)
 
-    def mark_start(self):
-        self.window[0] = time.perf_counter()
-
-    def mark_end(self):
-        self.window[1] = time.perf_counter()
-
-    def stop(self):
+    def summary(self, t0: float, t1: float):
+        """Median SM clock, max clock and the throttle reasons seen between
+        perf_counter marks t0 and t1 (the samples just outside a window
+        shorter than the polling period when none fall inside)."""
         if self.thread is None:
-            return None
-        self._stop.set()
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-        self.thread.join(timeout=5)
-        t0, t1 = self.window
-        if t0 is None or t1 is None:
             return None
         inside = [x for x in self.samples if t0 <= x[0] <= t1]
         window = "timed region"
         if not inside:
-            # a region shorter than the polling period: the samples just before
-            # and just after it bracket it
             before = [x for x in self.samples if x[0] < t0]
             after = [x for x in self.samples if x[0] > t1]
             inside = before[-1:] + after[:1]
@@ -194,6 +193,18 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(x[1] for x in inside), "sm_max_mhz": self.max_mhz,
                 "reasons": sorted(reasons), "samples": len(inside), "source": self.source, "window": window}
 
+    def stop(self):
+        if self.thread is None:
+            return
+        self._stop.set()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        self.thread.join(timeout=5)
+
 
 def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -202,54 +213,143 @@ def dist_setup(args):
     return world, rank, local
 
 
+
+
+# ---------------------------------------------------------------------------
+# workload descriptions (no GPU: shared by both arms, so their `config` match)
+# ---------------------------------------------------------------------------
+def config_info(cfg: str) -> dict:
+    from hachiue_b200 import workloads
+    if cfg == "1":
+        return dict(workload="cfg1 Qwen3-1.7B GQA decode attention", q_heads=16, kv_heads=8, head_dim=128,
+                    context=1024, kv_dtype="f32", l2="rotates 32 cache copies (> L2)",
+                    launch="device-resident warm-up and timed steps each run as one CUDA graph of the op calls; "
+                           "e2e calls the API directly")
+    if cfg in ("2", "2q8"):
+        lens = workloads.cfg2_lens()
+        return dict(workload="cfg2 Qwen3-8B batched GQA decode attention" + (" on a Q8_0 cache" if cfg == "2q8" else ""),
+                    sequences=64, q_heads=32, kv_heads=8, head_dim=128,
+                    kv_dtype="Q8_0 (int8 + f32 scale per 32, the reference's cache format)" if cfg == "2q8" else "f16",
+                    context="U[512,8192] seed 1", sum_context=int(lens.sum()),
+                    l2=("inputs (0.63 GB K/V) larger than L2" if cfg == "2q8" else "inputs (1.1 GB K/V) larger than L2"))
+    if cfg == "3":
+        return dict(workload="cfg3 PLaMo-3 sliding-window causal attention prefill", sequences=8, tokens=4096,
+                    q_heads=16, kv_heads=4, head_dim=128, window=1024, io_dtype="bf16 in, bf16 out",
+                    l2="inputs 201 MB > L2")
+    if cfg == "4":
+        return dict(workload="cfg4 Qwen3.5 Gated DeltaNet decode step", sequences=64, qk_heads=16, v_heads=32, d=128,
+                    state="f32 [64,32,128,128]", l2="rotates 2 state copies (> L2)")
+    if cfg == "5":
+        return dict(workload="cfg5 Qwen3.5 Gated DeltaNet chunked prefill", sequences=8, tokens=8192, qk_heads=16,
+                    v_heads=32, d=128, chunk=64, io_dtype="bf16 q/k/v, f32 g/beta, f32 out and final state",
+                    l2="inputs 0.56 GB > L2")
+    if cfg == "6":
+        return dict(workload="cfg6 = cfg4 as a whole Qwen3.5 GDN layer step (conv1d K=4 + g/beta + recurrence + "
+                             "gated RMSNorm, fused)", sequences=64, qk_heads=16, v_heads=32, d=128,
+                    state="f32 [64,32,128,128] in place, conv state f32 [64,3,8192] ping-pong",
+                    l2="rotates 2 state copies (> L2)")
+    if cfg == "7":
+        return dict(workload="cfg7 = cfg1 as a whole qwen3 attention layer step (q/k RMSNorm + RoPE + Q8_0 K/V "
+                             "append + attention, fused prologue)", q_heads=16, kv_heads=8, head_dim=128,
+                    context=1024, kv_dtype="Q8_0 (the reference's cache format)", l2="rotates 64 cache copies (> L2)",
+                    launch="device-resident warm-up and timed steps (and the comparison arm's) each run as one CUDA "
+                           "graph of the op calls; e2e calls the API directly")
+    raise ValueError(cfg)
+
+
+def metric_name(cfg: str) -> str:
+    return {"1": "decode attn HBM GB/s", "2": "decode attn HBM GB/s", "2q8": "decode attn (Q8_0 cache) HBM GB/s",
+            "3": "SWA prefill TFLOP/s", "4": "GDN decode HBM GB/s", "5": "GDN chunked prefill TFLOP/s",
+            "6": "GDN layer step HBM GB/s", "7": "attention layer step HBM GB/s"}[cfg]
+
+
+def metric_unit(cfg: str) -> str:
+    return "TFLOP/s" if cfg in ("3", "5") else "GB/s"
+
+
+def dtype_name(cfg: str) -> str:
+    return {"1": "f32", "2": "f16", "2q8": "q8_0 cache, f32 math", "3": "bf16", "4": "f32", "5": "bf16",
+            "6": "f32", "7": "q8_0 cache, f32 math"}[cfg]
+
+
 # ---------------------------------------------------------------------------
 # workloads (device side)
 # ---------------------------------------------------------------------------
-def setup_cfg2(torch, be, dev):
-    from hachiue_b200 import KV_F16, workloads
-    from hachiue_b200.backend import KVCache
+def _cfg2_device(torch, dev):
+    """cfg2's inputs on the device: f16 K / V packed [sum T, 8, 128], q, the
+    per-sequence positions and row offsets."""
+    from hachiue_b200 import workloads
     w = workloads.decode_cfg2()
-    k = torch.from_numpy(w["k"].view(np.int16)).to(dev).view(torch.float16)
-    v = torch.from_numpy(w["v"].view(np.int16)).to(dev).view(torch.float16)
-    cache = KVCache(KV_F16, k, v)
-    q = torch.from_numpy(w["q"]).to(dev)
-    out = torch.zeros_like(q)
-    pos = torch.from_numpy(w["pos_base"]).to(dev)
-    off = torch.from_numpy(w["row_offset"]).to(dev)
-    maxc = int(w["lens"].max())
-    nbytes = workloads.cfg2_bytes(w["lens"])
+    return dict(w=w, k=torch.from_numpy(w["k"].view(np.int16)).to(dev).view(torch.float16),
+                v=torch.from_numpy(w["v"].view(np.int16)).to(dev).view(torch.float16),
+                q=torch.from_numpy(w["q"]).to(dev), pos=torch.from_numpy(w["pos_base"]).to(dev),
+                off=torch.from_numpy(w["row_offset"]).to(dev), maxc=int(w["lens"].max()))
 
-    def step(i):
-        be.attention(q, cache, out, pos, 0, kv_row_offset=off, max_context=maxc)
 
-    # e2e: the user-facing decode step through the public API with host buffers.
-    B, KV, Dh = 64, 8, 128
+def _decode_e2e(torch, be, dev, cache, d, B=64, H=32, KV=8, Dh=128):
+    """The user-facing decode step through the public API with host buffers:
+    q and the step's new K / V rows (one per sequence, at its last position,
+    already counted in its length) copied from pinned host memory, the rows
+    appended in one launch, the attention over the whole context, and the
+    output read back, pipelined over two slots (HostPipeline)."""
+    from hachiue_b200.pipeline import HostPipeline
+    w = d["w"]
     q_host = torch.from_numpy(w["q"]).pin_memory()
     kv_new_host = torch.from_numpy(
         np.random.default_rng(99).standard_normal((2, B, KV, Dh), dtype=np.float32)).pin_memory()
     out_host = torch.empty_like(q_host).pin_memory()
-    q_dev = torch.empty_like(q)
-    kv_new_dev = torch.empty((2, B, KV, Dh), device=dev)
-    # the step appends one row per sequence at its last position (rows already
-    # counted in lens), then runs attention over the full context
     last_rows = torch.from_numpy(w["row_offset"] + w["lens"] - 1).to(dev)
+    pipe = HostPipeline(dev, [(tuple(q_host.shape), torch.float32), (tuple(kv_new_host.shape), torch.float32)],
+                        [(tuple(out_host.shape), torch.float32)])
+
+    def compute(ins, outs):
+        be.kv_append_rows_kv(ins[1][0], ins[1][1], cache, last_rows)
+        be.attention(ins[0], cache, outs[0], d["pos"], 0, kv_row_offset=d["off"], max_context=d["maxc"])
 
     def e2e_step(i):
-        q_dev.copy_(q_host, non_blocking=True)
-        kv_new_dev.copy_(kv_new_host, non_blocking=True)
-        be.kv_append_rows(kv_new_dev[0], cache, "k", last_rows)
-        be.kv_append_rows(kv_new_dev[1], cache, "v", last_rows)
-        be.attention(q_dev, cache, out, pos, 0, kv_row_offset=off, max_context=maxc)
-        out_host.copy_(out, non_blocking=True)
+        pipe.submit([q_host, kv_new_host], [out_host], compute)
 
-    h2d = q_host.numel() * 4 + kv_new_host.numel() * 4
-    d2h = out_host.numel() * 4
-    info = dict(workload="cfg2 Qwen3-8B batched GQA decode attention", sequences=64, q_heads=32, kv_heads=8,
-                head_dim=128, kv_dtype="f16", context="U[512,8192] seed 1", sum_context=int(w["lens"].sum()),
-                l2="inputs (1.1 GB K/V) larger than L2")
-    cpu = dict(w=w, kind="cfg2")
-    return dict(step=step, e2e_step=e2e_step, bytes=nbytes, tokens=64, info=info, h2d=h2d, d2h=d2h,
-                kernels_per_step=1, e2e_kernels_per_step=3, cpu=cpu, out=out, traffic_key="cfg2")
+    return dict(e2e_step=e2e_step, e2e_begin=pipe.begin, e2e_end=pipe.drain,
+                h2d=q_host.numel() * 4 + kv_new_host.numel() * 4, d2h=out_host.numel() * 4, e2e_kernels_per_step=2,
+                e2e_note="HostPipeline: two slots; step i+1's H2D and step i-1's D2H overlap step i's kernels")
+
+
+def setup_cfg2(torch, be, dev, d=None):
+    from hachiue_b200 import KV_F16, workloads
+    from hachiue_b200.backend import KVCache
+    d = d or _cfg2_device(torch, dev)
+    cache = KVCache(KV_F16, d["k"], d["v"])
+    outs = [torch.zeros_like(d["q"]) for _ in range(2)]  # step i writes outs[i % 2] (the gather reads it)
+
+    def step(i):
+        be.attention(d["q"], cache, outs[i & 1], d["pos"], 0, kv_row_offset=d["off"], max_context=d["maxc"])
+
+    W = dict(step=step, bytes=workloads.cfg2_bytes(d["w"]["lens"]), tokens=64, info=config_info("2"),
+             kernels_per_step=1, cpu=dict(w=d["w"], kind="cfg2"), outs=outs, traffic_key="cfg2", dev_inputs=d)
+    W.update(_decode_e2e(torch, be, dev, cache, d))
+    return W
+
+
+def setup_cfg2q8(torch, be, dev, d=None):
+    """cfg2's sequences, contexts and values on the reference's Q8_0 cache
+    (appendKvQ8 of the same f16 values, done on the device)."""
+    from hachiue_b200 import KV_Q8_0, workloads
+    from hachiue_b200.backend import KVCache
+    d = d or _cfg2_device(torch, dev)
+    rows, KV, Dh = d["k"].shape
+    cache = KVCache.allocate(rows, KV, Dh, KV_Q8_0, device=dev)
+    for src, which in ((d["k"], "k"), (d["v"], "v")):
+        be.kv_append(src.float(), cache, which, 0)
+    torch.cuda.synchronize(dev)
+    outs = [torch.zeros_like(d["q"]) for _ in range(2)]
+
+    def step(i):
+        be.attention(d["q"], cache, outs[i & 1], d["pos"], 0, kv_row_offset=d["off"], max_context=d["maxc"])
+
+    W = dict(step=step, bytes=workloads.cfg2_q8_bytes(d["w"]["lens"]), tokens=64, info=config_info("2q8"),
+             kernels_per_step=1, cpu=dict(w=d["w"], kind="cfg2q8", cache=cache), outs=outs, traffic_key="cfg2q8")
+    W.update(_decode_e2e(torch, be, dev, cache, d))
+    return W
 
 
 def setup_cfg1(torch, be, dev):
@@ -274,11 +374,7 @@ def setup_cfg1(torch, be, dev):
         be.attention(q_dev, caches[i % copies], out, w["pos_base"])
         out_host.copy_(out, non_blocking=True)
 
-    info = dict(workload="cfg1 Qwen3-1.7B GQA decode attention", q_heads=16, kv_heads=8, head_dim=128, context=1024,
-                kv_dtype="f32", l2=f"rotates {copies} cache copies (> L2)",
-                launch="device-resident warm-up and timed steps each run as one CUDA graph of the op calls; "
-                       "e2e calls the API directly")
-    return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg1_bytes(), tokens=1, info=info,
+    return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg1_bytes(), tokens=1, info=config_info("1"),
                 h2d=q_host.numel() * 4, d2h=out_host.numel() * 4, kernels_per_step=1, e2e_kernels_per_step=1,
                 cpu=dict(w=w, kind="cfg1"), out=out, traffic_key="cfg1", graph_period=copies)
 
@@ -314,18 +410,9 @@ def setup_cfg4(torch, be, dev):
         be.deltanet_decode(qkv_d, a_d, b_d, an, dtb, st, core, st, NK, NV)
         core_h.copy_(core, non_blocking=True)
 
-    info = dict(workload="cfg4 Qwen3.5 Gated DeltaNet decode step", sequences=64, qk_heads=16, v_heads=32, d=128,
-                state="f32 [64,32,128,128]", l2="rotates 2 state copies (> L2)")
-    return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg4_bytes(), tokens=64, info=info,
+    return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg4_bytes(), tokens=64, info=config_info("4"),
                 h2d=(qkv_h.numel() + a_h.numel() + b_h.numel()) * 4, d2h=core_h.numel() * 4, kernels_per_step=1,
                 e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg4"), out=core, traffic_key="cfg4")
-
-
-def swa_flops(T=4096, W=1024, B=8, H=16, D=128) -> int:
-    """Algorithmic FLOPs of causal sliding-window attention: 4*D per (query,
-    key) pair inside the window (QK^T and PV), pairs = sum_i min(i+1, W)."""
-    pairs = sum(min(i + 1, W) for i in range(T)) if W > 0 else T * (T + 1) // 2
-    return 4 * D * pairs * B * H
 
 
 def setup_cfg3(torch, be, dev):
@@ -352,10 +439,7 @@ def setup_cfg3(torch, be, dev):
         be.swa_prefill(qd, kd, vd, out, w["window"])
         out_h.copy_(out.view(torch.int16), non_blocking=True)
 
-    info = dict(workload="cfg3 PLaMo-3 sliding-window causal attention prefill", sequences=8, tokens=4096,
-                q_heads=16, kv_heads=4, head_dim=128, window=1024, io_dtype="bf16 in, bf16 out",
-                l2="inputs 201 MB > L2")
-    return dict(step=step, e2e_step=e2e_step, flops=swa_flops(), tokens=8 * 4096, info=info,
+    return dict(step=step, e2e_step=e2e_step, flops=workloads.swa_flops(), tokens=8 * 4096, info=config_info("3"),
                 h2d=(qh.numel() + kh.numel() + vh.numel()) * 2, d2h=out_h.numel() * 2, kernels_per_step=1,
                 e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg3"), out=out, traffic_key="cfg3")
 
@@ -394,16 +478,9 @@ def setup_cfg5(torch, be, dev):
 
     h2d = sum(x.numel() * 2 for x in hosts) + 2 * gh.numel() * 4
     d2h = core_h.numel() * 4 + st_h.numel() * 4
-    info = dict(workload="cfg5 Qwen3.5 Gated DeltaNet chunked prefill", sequences=8, tokens=8192, qk_heads=16,
-                v_heads=32, d=128, chunk=64, io_dtype="bf16 q/k/v, f32 g/beta, f32 out and final state",
-                l2="inputs 0.56 GB > L2")
-    # Algorithmic work: canonical chunked-WY FLOPs and the bytes that must cross HBM.
-    flops = 65536 * 32 * (10 * 64 * 128 + 6 * 128 * 128)
-    nbytes = 2 * (8 * 8192 * 16 * 128 * 2) + 8 * 8192 * 32 * 128 * 2 + 2 * 8 * 8192 * 32 * 4 \
-        + 8 * 8192 * 32 * 128 * 4 + 8 * 32 * 128 * 128 * 4
-    return dict(step=step, e2e_step=e2e_step, flops=flops, hbm_bytes=nbytes, tokens=8 * 8192, info=info, h2d=h2d,
-                d2h=d2h, kernels_per_step=2, e2e_kernels_per_step=2, cpu=dict(w=w, kind="cfg5"), out=core,
-                traffic_key="cfg5")
+    return dict(step=step, e2e_step=e2e_step, flops=workloads.cfg5_flops(), hbm_bytes=workloads.cfg5_bytes(),
+                tokens=8 * 8192, info=config_info("5"), h2d=h2d, d2h=d2h, kernels_per_step=2, e2e_kernels_per_step=2,
+                cpu=dict(w=w, kind="cfg5"), out=core, traffic_key="cfg5")
 
 
 def setup_cfg6(torch, be, dev):
@@ -448,10 +525,7 @@ def setup_cfg6(torch, be, dev):
                           gamma, st, st, out, NK, NV, w["eps"])
         out_h.copy_(out, non_blocking=True)
 
-    info = dict(workload="cfg6 = cfg4 as a whole Qwen3.5 GDN layer step (conv1d K=4 + g/beta + recurrence + "
-                         "gated RMSNorm, fused)", sequences=B, qk_heads=NK, v_heads=NV, d=D,
-                state="f32 [64,32,128,128] in place, conv state f32 [64,3,8192] ping-pong",
-                l2="rotates 2 state copies (> L2)")
+    info = config_info("6")
     return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg6_bytes(), tokens=B, info=info,
                 h2d=sum(v.numel() * 4 for v in hs.values()), d2h=out_h.numel() * 4, kernels_per_step=1,
                 e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg6"), out=out, traffic_key="cfg6",
@@ -509,11 +583,7 @@ def setup_cfg7(torch, be, dev):
         be.attention(q_out, cache, out, pos)
         out_h.copy_(out, non_blocking=True)
 
-    info = dict(workload="cfg7 = cfg1 as a whole qwen3 attention layer step (q/k RMSNorm + RoPE + Q8_0 K/V "
-                         "append + attention, fused prologue)", q_heads=H, kv_heads=KV, head_dim=Dh,
-                context=pos + 1, kv_dtype="Q8_0 (the reference's cache format)", l2=f"rotates {copies} cache copies (> L2)",
-                launch="device-resident warm-up and timed steps (and the comparison arm's) each run as one CUDA "
-                       "graph of the op calls; e2e calls the API directly")
+    info = config_info("7")
     return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg7_bytes(), tokens=1, info=info,
                 h2d=sum(t.numel() * 4 for t in hs.values()), d2h=out_h.numel() * 4, kernels_per_step=2,
                 e2e_kernels_per_step=2, cpu=dict(w=w, kind="cfg7"), out=out, traffic_key="cfg7",
@@ -521,7 +591,10 @@ def setup_cfg7(torch, be, dev):
                               "attention_q8)", step=unfused, kernels_per_step=7), graph_period=copies)
 
 
-SETUPS = {1: setup_cfg1, 2: setup_cfg2, 3: setup_cfg3, 4: setup_cfg4, 5: setup_cfg5, 6: setup_cfg6, 7: setup_cfg7}
+
+
+SETUPS = {"1": setup_cfg1, "2": setup_cfg2, "2q8": setup_cfg2q8, "3": setup_cfg3, "4": setup_cfg4,
+          "5": setup_cfg5, "6": setup_cfg6, "7": setup_cfg7}
 
 
 # ---------------------------------------------------------------------------
@@ -545,6 +618,31 @@ def cpu_sample(kind: str, w: dict, threads: int, budget_s: float = 12.0):
             reps += 1
         dt = time.perf_counter() - t0
         return done_bytes / dt / 1e9, done_b / dt, f"{reps} full passes of cfg2 (64 sequences, f16 KV) on {threads} threads", threads
+    if kind == "cfg2q8":
+        # The reference's own setting: runAttentionQ8 over a Q8_0 cache.  The
+        # first sequences of cfg2 are quantised (appendKvQ8) and timed.
+        nseq = w.get("_q8_nseq", 4)
+        if "_q8" not in w:
+            rows = int(w["lens"][:nseq].sum())
+            kq, vq = np.zeros((rows, 8, 128), np.int8), np.zeros((rows, 8, 128), np.int8)
+            ks, vs = np.zeros((rows, 8, 4), np.float32), np.zeros((rows, 8, 4), np.float32)
+            oracle.append_kv_q8(w["k"][:rows].astype(np.float32), kq, ks, 0)
+            oracle.append_kv_q8(w["v"][:rows].astype(np.float32), vq, vs, 0)
+            w["_q8"] = (kq, ks, vq, vs)
+        kq, ks, vq, vs = w["_q8"]
+        lens = w["lens"][:nseq]
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            oracle.attention_batch(np.ascontiguousarray(w["q"][:nseq]), kq, vq, w["pos_base"][:nseq],
+                                   w["row_offset"][:nseq], 0, oracle.KV_Q8_0, ks, vs, threads=threads)
+            reps += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+        dt = time.perf_counter() - t0
+        return (reps * workloads.cfg2_q8_bytes(lens) / dt / 1e9, reps * nseq / dt,
+                f"{reps} passes over the first {nseq} sequences of cfg2 on a Q8_0 cache (appendKvQ8 of the same "
+                f"values), {threads} thread(s)", threads)
     if kind == "cfg1":
         t0 = time.perf_counter()
         n = 0
@@ -613,27 +711,19 @@ def cpu_sample(kind: str, w: dict, threads: int, budget_s: float = 12.0):
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the reference's algorithm (oracle port) on the host."""
+    """--impl reference: the reference's algorithm (its JS-semantics C
+    restatement, oracle/) on the host cores, on the same workload and config
+    as the GPU arm, plus the reference's own setting (one thread over a Q8_0
+    cache) for the decode configurations."""
     if rank != 0:
         return 0
-    import oracle
     from hachiue_b200 import workloads
     threads = os.cpu_count() or 1
-    if args.config == 2:
-        w = workloads.decode_cfg2()
-    elif args.config == 1:
-        w = workloads.decode_cfg1()
-    elif args.config == 3:
-        w = workloads.swa_cfg3()
-    elif args.config == 5:
-        w = workloads.gdn_prefill_cfg5()
-    elif args.config == 6:
-        w = workloads.gdn_layer_cfg6()
-    elif args.config == 7:
-        w = workloads.attn_layer_cfg7()
-    else:
-        w = workloads.gdn_decode_cfg4()
-    kind = f"cfg{args.config}"
+    loaders = {"1": workloads.decode_cfg1, "2": workloads.decode_cfg2, "2q8": workloads.decode_cfg2,
+               "3": workloads.swa_cfg3, "4": workloads.gdn_decode_cfg4, "5": workloads.gdn_prefill_cfg5,
+               "6": workloads.gdn_layer_cfg6, "7": workloads.attn_layer_cfg7}
+    w = loaders[args.config]()
+    kind = "cfg" + args.config
     for _ in range(args.warmup):
         cpu_sample(kind, w, threads, budget_s=0.5)
     vals = []
@@ -641,104 +731,54 @@ def run_reference(args, world, rank):
     desc = ""
     cores = threads
     for _ in range(args.steps):
-        gbs, tps, desc, cores = cpu_sample(kind, w, threads, budget_s=2.0)
-        vals.append(gbs)
+        v, _, desc, cores = cpu_sample(kind, w, threads, budget_s=2.0)
+        vals.append(v)
     elapsed = time.perf_counter() - t_all
     value = statistics.median(vals)
+    unit = metric_unit(args.config)
     line = {
-        "impl": "reference", "metric": metric_name(args.config), "value": round(value, 4),
-        "unit": metric_unit(args.config),
+        "impl": "reference", "metric": metric_name(args.config), "value": round(value, 4), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1000 * elapsed / max(args.steps, 1), 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(args.config), "data": "synthetic",
-        "config": {"workload": f"cfg{args.config} (see --impl ours)", "parallelism": "host threads"},
-        "cpu_baseline": {"value": round(value, 4), "unit": metric_unit(args.config), "cores": cores, "kind": "port",
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(args.config), "data": DATA,
+        "config": config_info(args.config), "parallelism": f"{cores} host threads",
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": cores, "kind": "port",
                          "sample": desc + "; the reference is TypeScript with no runtime on this box, so its "
                                           "JS-semantics C restatement (oracle/) is timed"},
-        "e2e": {"value": round(value, 4), "unit": metric_unit(args.config), "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if args.config in ("1", "2"):
+        # the reference's own setting: runAttentionQ8 is single-threaded JS over
+        # the engine's Q8_0 cache (src/wasm-backend.ts:826-895)
+        if args.config == "2":
+            v1, _, d1, c1 = cpu_sample("cfg2q8", w, 1, budget_s=4.0)
+            unit1 = "GB/s (Q8_0 algorithmic bytes)"
+        else:
+            v1, _, d1, c1 = cpu_sample("cfg1", w, 1, budget_s=3.0)
+            unit1 = unit
+        line["reference_setting"] = {"value": round(v1, 4), "unit": unit1, "cores": c1, "kind": "port",
+                                     "sample": d1 + " (the reference's own setting: one JS thread"
+                                     + (", Q8_0 KV cache)" if args.config == "2" else ")")}
     print(json.dumps(line), flush=True)
     return 0
 
 
-def metric_name(cfg: int) -> str:
-    return {1: "decode attn HBM GB/s", 2: "decode attn HBM GB/s", 3: "SWA prefill TFLOP/s",
-            4: "GDN decode HBM GB/s", 5: "GDN chunked prefill TFLOP/s", 6: "GDN layer step HBM GB/s",
-            7: "attention layer step HBM GB/s"}[cfg]
-
-
-def metric_unit(cfg: int) -> str:
-    return "TFLOP/s" if cfg in (3, 5) else "GB/s"
-
-
-def dtype_name(cfg: int) -> str:
-    return {1: "f32", 2: "f16", 3: "bf16", 4: "f32", 5: "bf16", 6: "f32", 7: "q8_0 cache, f32 math"}[cfg]
+DATA = "synthetic (seeded numpy PCG64, benchmark-config shapes)"
 
 
 # ---------------------------------------------------------------------------
-def main(argv=None):
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=2, choices=sorted(SETUPS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    args = ap.parse_args(argv)
-    args.warmup = max(args.warmup, 3)
-    world, rank, local = dist_setup(args)
-    if args.impl == "reference":
-        return run_reference(args, world, rank)
-
-    import torch
-    import torch.distributed as dist
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-
-    from hachiue_b200 import CudaBackend
-    be = CudaBackend(local)
-    W = SETUPS[args.config](torch, be, dev)
+# measurement
+# ---------------------------------------------------------------------------
+def measure(torch, dist, W, args, world, dev, clocks, gather=None):
+    """Times W's device-resident step (``value``: CUDA events around the
+    whole timed region, and around each step's kernels for the roofline),
+    then its end-to-end step, then its comparison arm.  Returns the times."""
     stream = torch.cuda.current_stream(dev)
-
-    # The per-step NCCL all-gather of the outputs runs on NCCL's stream while the
-    # next step computes: each step's output is staged into one of two buffers
-    # and gathered asynchronously; a buffer is reused only after the stream has
-    # waited for its previous gather, and every gather completes before the
-    # timed region closes.
-    gather_out, stage, pending = [], [], [None, None]
-    if world > 1:
-        gather_out = [torch.empty((world,) + tuple(W["out"].shape), device=dev, dtype=W["out"].dtype)
-                      for _ in range(2)]
-        stage = [torch.empty_like(W["out"]) for _ in range(2)]
-
-    def gather(i):
-        if world == 1:
-            return
-        j = i & 1
-        if pending[j] is not None:
-            pending[j].wait()
-        stage[j].copy_(W["out"])
-        pending[j] = dist.all_gather_into_tensor(gather_out[j], stage[j], async_op=True)
-
-    def drain():
-        for j in range(2):
-            if pending[j] is not None:
-                pending[j].wait()
-                pending[j] = None
-
-    def full_step(i):
-        W["step"](i)
-        gather(i)
-
-    # Latency-bound configurations (one sequence, a few launches of ~10 us) run
-    # their device-resident steps as CUDA graphs, as a serving loop would: the
-    # timed graph holds exactly the K timed steps (the warm-up graph the W
-    # warm-up steps), so the launches are not paced by Python.  Single GPU only.
     graph_mode = bool(W.get("graph_period")) and world == 1
+    gather = gather or (lambda i, out: None)
+
+    def out_of(i):
+        return W["outs"][i & 1] if "outs" in W else W["out"]
 
     def capture(fn, n):
         for i in range(min(n, W["graph_period"])):  # every input variant once, outside capture
@@ -755,25 +795,28 @@ def main(argv=None):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    # ---- device-resident timing ----
+    def max_over_ranks(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident ----
     if graph_mode:
         g_warm, g_timed = capture(W["step"], args.warmup), capture(W["step"], args.steps)
         g_warm.replay()
     else:
         for i in range(args.warmup):
-            full_step(i)
-    drain()
+            W["step"](i)
+            gather(i, out_of(i))
+    gather(None, None)  # drain
     barrier()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    clocks = ClockSampler(local)
-    clocks.start()
-    clocks.wait_ready()
+    t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    clocks.mark_start()
-    t_start.record(stream)
+    c0 = time.perf_counter()
+    t0e.record(stream)
     if graph_mode:
         g_timed.replay()
     else:
@@ -781,53 +824,35 @@ def main(argv=None):
             kev[i][0].record(stream)
             W["step"](i)
             kev[i][1].record(stream)
-            gather(i)
-    drain()
-    t_end.record(stream)
+            gather(i, out_of(i))
+    gather(None, None)
+    t1e.record(stream)
     barrier()
-    clocks.mark_end()
-    clk = clocks.stop()
-    total_ms = t_start.elapsed_time(t_end)
-    # in a graph the steps run back to back: a step's average duration is the
-    # whole replay's over K (gaps between launches included)
-    kernel_ms = [total_ms / args.steps] * args.steps if graph_mode else [a.elapsed_time(b) for a, b in kev]
-    if world > 1:
-        t = torch.tensor([total_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    status = be.device_status()
-    if status:
-        raise RuntimeError(f"device status {status} after the timed region")
-
-    ms_per_step = total_ms / args.steps
-    tensor = "flops" in W
-    work = W["flops"] if tensor else W["bytes"]
-    scale = 1e12 if tensor else 1e9  # TFLOP/s or GB/s
-    value = world * work / (ms_per_step / 1e3) / scale
-    kavg = statistics.mean(kernel_ms)
-    achieved = work / (kavg / 1e3) / scale
+    c1 = time.perf_counter()
+    total_ms = max_over_ranks(t0e.elapsed_time(t1e))
+    kernel_ms = (t0e.elapsed_time(t1e) / args.steps if graph_mode
+                 else statistics.mean(a.elapsed_time(b) for a, b in kev))
+    clk = clocks.summary(c0, c1) if clocks else None
 
     # ---- end to end through the public API (host buffers) ----
+    begin, end = W.get("e2e_begin", lambda: None), W.get("e2e_end", lambda: None)
+    begin()
     for i in range(args.warmup):
         W["e2e_step"](i)
-        gather(i)
-    drain()
+    end()
     barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c2 = time.perf_counter()
     e0.record(stream)
+    begin()
     for i in range(args.steps):
         W["e2e_step"](i)
-        gather(i)
-    drain()
+    end()
     e1.record(stream)
     barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = world * work / (e2e_ms / args.steps / 1e3) / scale
+    c3 = time.perf_counter()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    clk_e2e = clocks.summary(c2, c3) if clocks else None
 
     # ---- comparison arm of the same workload (device-resident, as `value`) ----
     alt = None
@@ -839,8 +864,7 @@ def main(argv=None):
             for i in range(args.warmup):
                 W["alt"]["step"](i)
         barrier()
-        a0 = torch.cuda.Event(enable_timing=True)
-        a1 = torch.cuda.Event(enable_timing=True)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record(stream)
         if graph_mode:
             ga_timed.replay()
@@ -849,58 +873,262 @@ def main(argv=None):
                 W["alt"]["step"](i)
         a1.record(stream)
         barrier()
-        alt_ms = a0.elapsed_time(a1) / args.steps
-        alt = {"name": W["alt"]["name"], "ms_per_step": round(alt_ms, 5),
-               "value": round(world * work / (alt_ms / 1e3) / scale, 2), "unit": metric_unit(args.config),
+        alt = {"name": W["alt"]["name"], "ms_per_step": round(a0.elapsed_time(a1) / args.steps, 5),
                "gpu_launches_per_step": W["alt"]["kernels_per_step"]}
+    return dict(total_ms=total_ms, kernel_ms=kernel_ms, e2e_ms=e2e_ms, alt=alt, clocks=clk, clocks_e2e=clk_e2e)
 
+
+def entry(cfg, W, res, peaks, peak_src, world, steps, cpu):
+    """One configuration's measurement as a JSON object (the headline line's
+    fields, or a ``secondary`` entry)."""
+    tensor = "flops" in W
+    work = W["flops"] if tensor else W["bytes"]
+    scale = 1e12 if tensor else 1e9  # TFLOP/s or GB/s
+    unit = metric_unit(cfg)
+    ms = res["total_ms"] / steps
+    value = world * work / (ms / 1e3) / scale
+    kms = res["kernel_ms"]
+    achieved = work / (kms / 1e3) / scale
+    peak = peaks["bf16_tflops"] if tensor else peaks["hbm_gbs"]
+    roof = {"bound": "tensor" if tensor else "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 4), "peak_source": peak_src + (" bf16 burst" if tensor else " copy"),
+            ("algorithmic_flops_per_launch" if tensor else "algorithmic_bytes_per_launch"): work,
+            "kernel_ms": round(kms, 5), "traffic": load_traffic(W["traffic_key"])}
+    if "hbm_bytes" in W:  # tensor work at I/O dtypes whose bytes take longer than its flops: the HBM roof binds
+        gbs = W["hbm_bytes"] / (kms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(gbs, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peak_src + " copy",
+                "algorithmic_bytes_per_launch": W["hbm_bytes"], "kernel_ms": round(kms, 5),
+                "traffic": load_traffic(W["traffic_key"]), "tensor_achieved_tflops": round(achieved, 2),
+                "tensor_frac": round(achieved / peaks["bf16_tflops"], 4)}
+    e2e_ms = res["e2e_ms"] / steps
+    d = {"metric": metric_name(cfg), "value": round(value, 2), "unit": unit, "ms_per_step": round(ms, 5),
+         "dtype": dtype_name(cfg), "config": W["info"],
+         "tokens_per_s": round(world * W["tokens"] / (ms / 1e3), 1), "roofline": roof,
+         "e2e": {"value": round(world * work / (e2e_ms / 1e3) / scale, 2), "unit": unit,
+                 "h2d_bytes_per_step": W["h2d"], "d2h_bytes_per_step": W["d2h"], "ms_per_step": round(e2e_ms, 5),
+                 "clocks": res["clocks_e2e"]},
+         "gpu_launches": steps * W["kernels_per_step"], "e2e_gpu_launches": steps * W["e2e_kernels_per_step"],
+         "clocks": res["clocks"], "cpu_baseline": cpu}
+    if "e2e_note" in W:
+        d["e2e"]["pipelining"] = W["e2e_note"]
+    if res["alt"] is not None:
+        alt = dict(res["alt"])
+        alt["value"] = round(world * work / (alt["ms_per_step"] / 1e3) / scale, 2)
+        alt["unit"] = unit
+        d["comparison"] = alt
+    return d
+
+
+def cpu_entry(cfg, W, budget_s):
+    threads = os.cpu_count() or 1
+    v, _, desc, cores = cpu_sample(W["cpu"]["kind"], W["cpu"]["w"], threads, budget_s=budget_s)
+    return {"value": round(v, 4), "unit": metric_unit(cfg), "cores": cores, "kind": "port",
+            "sample": desc + " (the reference is TypeScript with no runtime here; its JS-semantics C restatement in "
+                             "oracle/ is timed)"}
+
+
+def strong_scaling(torch, dist, be, comm, args, world, rank, dev, W2):
+    """One configuration's fixed work split over the job's GPUs: cfg2 by KV
+    head (reusing the headline's device inputs) and cfg5 by QK head.  Each
+    step is the local kernels plus the all-gather of the per-head outputs
+    (hcu_allgather); both are timed with CUDA events, max over ranks."""
+    from hachiue_b200 import KV_F16, workloads
+    from hachiue_b200 import dist as hdist
+    from hachiue_b200.backend import KVCache
+    stream = torch.cuda.current_stream(dev)
+
+    def run(step, n_warm, n_steps):
+        for _ in range(n_warm):
+            step()
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for e in ev:
+            step(e)
+        t1.record(stream)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([t0.elapsed_time(t1) / n_steps, statistics.mean(a.elapsed_time(b) for a, b, _ in ev),
+                          statistics.mean(b.elapsed_time(c) for _, b, c in ev)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(x) for x in t.tolist()]
+
+    out = {}
+    # cfg2 by KV head: KV heads [lo, hi) of all 64 sequences and their G query heads
+    d = W2["dev_inputs"]
+    lo, hi = hdist.kv_head_range(8, world, rank)
+    G = 32 // 8
+    cache = KVCache(KV_F16, d["k"][:, lo:hi].contiguous(), d["v"][:, lo:hi].contiguous())
+    q_l = d["q"][:, :, lo * G:hi * G].contiguous()
+    out_l = torch.empty_like(q_l)
+    recv = torch.empty((world,) + tuple(out_l.shape), device=dev)
+
+    def step2(ev=None):
+        if ev:
+            ev[0].record(stream)
+        be.attention(q_l, cache, out_l, d["pos"], 0, kv_row_offset=d["off"], max_context=d["maxc"])
+        if ev:
+            ev[1].record(stream)
+        comm.all_gather(out_l, recv)
+        if ev:
+            ev[2].record(stream)
+
+    ms, attn_ms, gather_ms = run(step2, args.warmup, args.steps)
+    nbytes = workloads.cfg2_bytes(d["w"]["lens"])
+    out["cfg2_by_kv_head"] = {
+        "ms_per_step": round(ms, 5), "value": round(nbytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+        "work": "one cfg2 step (64 sequences) in total, split over the ranks", "kv_heads_per_rank": hi - lo,
+        "attention_ms": round(attn_ms, 5), "gather_ms": round(gather_ms, 5),
+        "gather_share": round(gather_ms / ms, 4), "gather_bytes_per_rank": out_l.numel() * 4,
+        "limiter": "all-gather latency" if gather_ms > attn_ms else "attention (HBM)"}
+    del cache, q_l, out_l, recv
+
+    # cfg5 by QK head: QK heads [lo, hi) and V heads {h : h % 16 in [lo, hi)}
+    w = workloads.gdn_prefill_cfg5()
+    ex = hdist.QKHeadShardedGDN(be, 16, 32)
+    cpu = [torch.from_numpy(np.ascontiguousarray(w[n]).view(np.int16)).view(torch.bfloat16) for n in ("q", "k", "v")]
+    cpu += [torch.from_numpy(w["g"]), torch.from_numpy(w["beta"])]
+    ql, kl, vl, gl, bl = (x.to(dev) for x in ex.shard_prefill(*cpu))
+    del cpu, w
+    core_l = torch.empty((8, 8192, ex.nvl, 128), device=dev)
+    st_l = torch.empty((8, ex.nvl, 128, 128), device=dev)
+    recv5 = torch.empty((world,) + tuple(core_l.shape), device=dev)
+
+    def step5(ev=None):
+        if ev:
+            ev[0].record(stream)
+        be.deltanet_chunked_prefill(ql, kl, vl, gl, bl, core_l, st_l)
+        if ev:
+            ev[1].record(stream)
+        comm.all_gather(core_l, recv5)
+        if ev:
+            ev[2].record(stream)
+
+    ms, pre_ms, gather_ms = run(step5, 3, min(args.steps, 10))
+    out["cfg5_by_qk_head"] = {
+        "ms_per_step": round(ms, 5), "value": round(workloads.cfg5_flops() / (ms / 1e3) / 1e12, 2),
+        "unit": "TFLOP/s", "work": "one cfg5 prefill (8 x 8192 tokens) in total, split over the ranks",
+        "qk_heads_per_rank": ex.nkl, "v_heads_per_rank": ex.nvl, "prefill_ms": round(pre_ms, 5),
+        "gather_ms": round(gather_ms, 5), "gather_share": round(gather_ms / ms, 4),
+        "gather_bytes_per_rank": core_l.numel() * 4,
+        "limiter": "all-gather of the f32 outputs over NVLink" if gather_ms > pre_ms else "prefill kernels"}
+    return out
+
+
+# ---------------------------------------------------------------------------
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="2", choices=sorted(SETUPS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
+    args = ap.parse_args(argv)
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    comm = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        from hachiue_b200.dist import RankComm
+        comm = RankComm(local)
+
+    from hachiue_b200 import CudaBackend
+    be = CudaBackend(local)
     peaks, peak_src = load_peaks()
+    clocks = ClockSampler(local)
+    clocks.start()
+    clocks.wait_ready()
+
+    W = SETUPS[args.config](torch, be, dev)
+
+    # Multi-GPU: each step's output is all-gathered (hcu_allgather) on a side
+    # stream while the next step computes; a step's output buffer is reused
+    # two steps later, after its gather.
+    gather = None
+    if world > 1:
+        gstream = torch.cuda.Stream(dev)
+        recv = [torch.empty((world,) + tuple((W["outs"][0] if "outs" in W else W["out"]).shape), device=dev,
+                            dtype=(W["outs"][0] if "outs" in W else W["out"]).dtype) for _ in range(2)]
+        stage = None if "outs" in W else [torch.empty_like(W["out"]) for _ in range(2)]
+        done = [None, None]
+
+        def gather(i, out):
+            cur = torch.cuda.current_stream(dev)
+            if i is None:  # drain
+                for j in range(2):
+                    if done[j] is not None:
+                        cur.wait_event(done[j])
+                        done[j] = None
+                return
+            j = i & 1
+            if done[j] is not None:
+                cur.wait_event(done[j])
+            src = out
+            if stage is not None:
+                stage[j].copy_(out)
+                src = stage[j]
+            ready = torch.cuda.Event()
+            ready.record(cur)
+            gstream.wait_event(ready)
+            with torch.cuda.stream(gstream):
+                comm.all_gather(src, recv[j])
+                done[j] = torch.cuda.Event()
+                done[j].record(gstream)
+
+    res = measure(torch, dist, W, args, world, dev, clocks, gather)
+    status = be.device_status()
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        gbs, _, desc, cores = cpu_sample(W["cpu"]["kind"], W["cpu"]["w"], threads)
-        cpu = {"value": round(gbs, 4), "unit": metric_unit(args.config), "cores": cores, "kind": "port",
-               "sample": desc + " (the reference is TypeScript with no runtime here; its JS-semantics C "
-                                "restatement in oracle/ is timed)"}
+        cpu = cpu_entry(args.config, W, 12.0)
+    head = entry(args.config, W, res, peaks, peak_src, world, args.steps, cpu)
 
+    line = {"metric": head.pop("metric"), "value": head.pop("value"), "unit": head.pop("unit"), "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head.pop("ms_per_step"),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": head.pop("dtype"),
+            "data": DATA, "config": head.pop("config"),
+            "parallelism": (f"dp{world}: each rank its own batch; per-head outputs all-gathered over NCCL "
+                            "(hcu_allgather) overlapped with the next step" if world > 1 else "single GPU")}
+    line.update(head)
+
+    if world > 1:
+        line["strong"] = strong_scaling(torch, dist, be, comm, args, world, rank, dev, W) if args.config == "2" else None
+    del W
+    torch.cuda.empty_cache()
+
+    if world == 1 and args.config == "2" and not args.no_secondary:
+        sec = {}
+        for cfg in ("2q8", "1", "3", "4", "5"):
+            Ws = SETUPS[cfg](torch, be, dev)
+            r = measure(torch, dist, Ws, args, 1, dev, clocks)
+            st = be.device_status()
+            if st:
+                raise RuntimeError(f"device status {st} after cfg{cfg}")
+            c = None if args.no_cpu_baseline else cpu_entry(cfg, Ws, 3.0)
+            sec["cfg" + cfg.replace("2q8", "2_q8")] = entry(cfg, Ws, r, peaks, peak_src, 1, args.steps, c)
+            del Ws
+            torch.cuda.empty_cache()
+        line["secondary"] = sec
+    clocks.stop()
     if rank == 0:
-        traffic = load_traffic(W["traffic_key"])
-        peak = peaks["bf16_tflops"] if tensor else peaks["hbm_gbs"]
-        hbm_roof = None
-        if "hbm_bytes" in W:  # tensor work at I/O dtypes whose bytes take longer than its FLOPs
-            gbs = W["hbm_bytes"] / (kavg / 1e3) / 1e9
-            hbm_roof = {"bound": "hbm", "achieved": round(gbs, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                        "frac": round(gbs / peaks["hbm_gbs"], 4), "algorithmic_bytes_per_launch": W["hbm_bytes"],
-                        "kernel_ms": round(kavg, 5), "traffic": load_traffic(W["traffic_key"]),
-                        "tensor_frac": round(achieved / peaks["bf16_tflops"], 4)}
-        line = {
-            "metric": metric_name(args.config), "value": round(value, 2), "unit": metric_unit(args.config),
-            "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(args.config),
-            "data": "synthetic (seeded numpy PCG64, benchmark-config shapes)",
-            "config": dict(W["info"], parallelism=f"dp{world} (sequences per rank) + NCCL all-gather of outputs, overlapped with the next step"
-                           if world > 1 else "single GPU"),
-            "tokens_per_s": round(world * W["tokens"] / (ms_per_step / 1e3), 1),
-            "roofline": {"bound": "tensor" if tensor else "hbm", "achieved": round(achieved, 2), "peak": peak,
-                         "unit": metric_unit(args.config), "frac": round(achieved / peak, 4),
-                         "peak_source": peak_src + (" bf16 burst" if tensor else " copy"),
-                         ("algorithmic_flops_per_launch" if tensor else "algorithmic_bytes_per_launch"): work,
-                         "kernel_ms": round(kavg, 5), "traffic": traffic},
-            "e2e": {"value": round(e2e_value, 2), "unit": metric_unit(args.config), "h2d_bytes_per_step": W["h2d"],
-                    "d2h_bytes_per_step": W["d2h"], "ms_per_step": round(e2e_ms / args.steps, 5)},
-            "gpu_launches": args.steps * W["kernels_per_step"],
-            "e2e_gpu_launches": args.steps * W["e2e_kernels_per_step"],
-            "clocks": clk,
-            "cpu_baseline": cpu,
-        }
-        if alt is not None:
-            line["comparison"] = alt
-        if hbm_roof is not None:
-            line["roofline"] = hbm_roof
         print(json.dumps(line), flush=True)
     be.close()
     if world > 1:
+        comm.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

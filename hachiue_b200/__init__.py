@@ -6,9 +6,9 @@ delta-rule recurrence (qwen35), as hand-written CUDA kernels behind the C ABI
 in include/hachiue_cuda.h.  ``CudaBackend`` is the Python host of that ABI and
 mirrors the reference's attention-dispatch seam (src/engine.ts:1056-1075).
 """
-from ._lib import (KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueError, LIB_PATH, load)  # noqa: F401
+from ._lib import (KV_BF16, KV_F16, KV_F32, KV_Q8_0, KV_Q8_0_WGSL, HachiueError, LIB_PATH, load)  # noqa: F401
 
-__all__ = ["CudaBackend", "KVCache", "SHADERS", "HachiueError", "KV_F32", "KV_F16", "KV_BF16", "KV_Q8_0",
+__all__ = ["CudaBackend", "KVCache", "SHADERS", "HachiueError", "KV_F32", "KV_F16", "KV_BF16", "KV_Q8_0", "KV_Q8_0_WGSL",
            "LIB_PATH", "load"]
 
 

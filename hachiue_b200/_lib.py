@@ -12,7 +12,9 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libhachiue_cuda.so")
 
 HCU_OK, HCU_EINVAL, HCU_ECUDA, HCU_ENCCL, HCU_ETIMEDOUT, HCU_ENOMEM, HCU_EUNSUPPORTED = range(7)
-KV_F32, KV_F16, KV_BF16, KV_Q8_0 = 0, 1, 2, 3
+KV_F32, KV_F16, KV_BF16, KV_Q8_0, KV_Q8_0_WGSL = 0, 1, 2, 3, 4
+OPT_ATTN_CUDA_CORES, OPT_ATTN_CHUNK, OPT_GDN_SCRATCH_MB, OPT_SWA_CTAS = 1, 2, 3, 4
+COMM_ID_BYTES = 128
 DT_F32, DT_BF16 = 0, 2
 
 STATUS_NAMES = {
@@ -29,6 +31,8 @@ EXPORTS = (
     "hcu_deltanet_gbeta", "hcu_deltanet_recur", "hcu_deltanet_decode", "hcu_swa_prefill",
     "hcu_deltanet_chunked_prefill", "hcu_deltanet_chunked_prefill_snap", "hcu_conv1d_causal", "hcu_deltanet_norm_gate", "hcu_gdn_layer_step",
     "hcu_rmsnorm", "hcu_rope", "hcu_split_q_gate", "hcu_sigmoid_gate", "hcu_attn_prologue",
+    "hcu_selftest_dirty_tickets", "hcu_attention_noalloc_status", "hcu_set_q8_convention", "hcu_set_option",
+    "hcu_comm_unique_id", "hcu_comm_init_rank", "hcu_kv_append_rows_kv",
 )
 
 
@@ -153,6 +157,13 @@ def load(path: str | None = None):
             "hcu_sigmoid_gate": ([vp, ctypes.c_uint64, vp, vp], i32),
             "hcu_attn_prologue": ([vp, ctypes.POINTER(hcu_attn_prologue_params)] + [vp] * 9
                                   + [ctypes.POINTER(hcu_kv_cache)], i32),
+            "hcu_selftest_dirty_tickets": ([vp], i32),
+            "hcu_attention_noalloc_status": ([ctypes.POINTER(u32), i32, vp], i32),
+            "hcu_set_q8_convention": ([vp, u32], i32),
+            "hcu_set_option": ([vp, i32, ctypes.c_int64], i32),
+            "hcu_comm_unique_id": ([ctypes.POINTER(ctypes.c_uint8)], i32),
+            "hcu_comm_init_rank": ([i32, i32, ctypes.POINTER(ctypes.c_uint8), i32, ctypes.POINTER(vp)], i32),
+            "hcu_kv_append_rows_kv": ([vp, u32, u32, u32, vp, vp, vp, ctypes.POINTER(hcu_kv_cache)], i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -21,7 +21,8 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from ._lib import (DT_BF16, DT_F32, KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueError, check, hcu_attention_params,
+from ._lib import (DT_BF16, DT_F32, KV_BF16, KV_F16, KV_F32, KV_Q8_0, KV_Q8_0_WGSL, HachiueError, check,
+                   hcu_attention_params,
                    hcu_attn_prologue_params, hcu_conv1d_params, hcu_deltanet_params, hcu_gdn_prefill_params, hcu_gdn_step_params, hcu_kv_cache,
                    hcu_swa_params)
 
@@ -29,7 +30,10 @@ from ._lib import (DT_BF16, DT_F32, KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueErr
 SHADERS = ("kv_append_q8", "attention_q8", "deltanet_gbeta", "deltanet_recur", "conv1d_causal", "deltanet_norm_gate",
            "rmsnorm", "rope", "split_q_gate", "sigmoid_gate")
 
-_DTYPE_OF_FORMAT = {KV_F32: torch.float32, KV_F16: torch.float16, KV_BF16: torch.bfloat16, KV_Q8_0: torch.int8}
+_DTYPE_OF_FORMAT = {KV_F32: torch.float32, KV_F16: torch.float16, KV_BF16: torch.bfloat16, KV_Q8_0: torch.int8,
+                    KV_Q8_0_WGSL: torch.int8}
+_OPTIONS = {"attn_cuda_cores": _lib.OPT_ATTN_CUDA_CORES, "attn_chunk": _lib.OPT_ATTN_CHUNK,
+            "gdn_scratch_mb": _lib.OPT_GDN_SCRATCH_MB, "swa_ctas": _lib.OPT_SWA_CTAS}
 
 
 def _current_raw_stream(index: int) -> int:
@@ -67,7 +71,7 @@ class KVCache:
         k = torch.zeros((rows, kv_heads, head_dim), dtype=dt, device=device)
         v = torch.zeros_like(k)
         ks = vs = None
-        if fmt == KV_Q8_0:
+        if fmt in (KV_Q8_0, KV_Q8_0_WGSL):
             ks = torch.zeros((rows, kv_heads, head_dim // 32), dtype=torch.float32, device=device)
             vs = torch.zeros_like(ks)
         return KVCache(fmt, k, v, ks, vs)
@@ -134,6 +138,22 @@ class CudaBackend:
         check(self.lib.hcu_device_status(self._h, ctypes.byref(st), int(clear)))
         return st.value
 
+    def set_option(self, name: str, value: int) -> None:
+        """hcu_set_option: ``attn_cuda_cores``, ``attn_chunk``,
+        ``gdn_scratch_mb`` or ``swa_ctas`` (0 restores the tuned default)."""
+        check(self.lib.hcu_set_option(self._h, _OPTIONS[name], int(value)))
+
+    def set_q8_convention(self, fmt: int) -> None:
+        """Q8_0 scale convention of :meth:`dispatch`: ``KV_Q8_0`` (the JS
+        backend's amax/127, default) or ``KV_Q8_0_WGSL`` (the WGSL ops' amax)."""
+        check(self.lib.hcu_set_q8_convention(self._h, fmt))
+
+    def selftest_dirty_tickets(self) -> None:
+        """Leave every split ticket partly counted, as a decode call whose
+        bounded wait gave up could; ``device_status(clear=True)`` re-arms them."""
+        self._bind_stream()
+        check(self.lib.hcu_selftest_dirty_tickets(self._h))
+
     def inject_failure(self, status: int, n: int = 1) -> None:
         """Make the next ``n`` op calls fail on the host with ``status``."""
         check(self.lib.hcu_inject_failure(self._h, status, n))
@@ -173,6 +193,16 @@ class CudaBackend:
         data, scale = (cache.k, cache.k_scale) if which == "k" else (cache.v, cache.v_scale)
         check(self.lib.hcu_kv_append_rows(self._h, n, KV, Dh, cache.fmt, _ptr(src.contiguous()), _ptr(dst_rows),
                                           _ptr(data), _ptr(scale)))
+
+    def kv_append_rows_kv(self, k_src: torch.Tensor, v_src: torch.Tensor, cache: KVCache,
+                          dst_rows: torch.Tensor) -> None:
+        """K and V rows of a decode step in one launch: row i of k_src / v_src
+        (f32 [n, KV, Dh], contiguous) goes to cache row dst_rows[i]."""
+        self._bind_stream()
+        n, KV, Dh = k_src.shape
+        kv = cache.c_struct()
+        check(self.lib.hcu_kv_append_rows_kv(self._h, n, KV, Dh, _ptr(k_src), _ptr(v_src), _ptr(dst_rows),
+                                             ctypes.byref(kv)))
 
     def attention(self, q: torch.Tensor, cache: KVCache, out: torch.Tensor, pos_base, window_size: int = 0,
                   kv_heads: int | None = None, kv_row_offset: torch.Tensor | None = None,

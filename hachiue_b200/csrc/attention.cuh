@@ -9,7 +9,6 @@
 namespace hcu {
 
 constexpr int kMaxSplits = 64;      // key splits per (sequence, KV head, query block)
-constexpr int kMaxUnits = 1 << 16;  // ticket slots at the head of the workspace
 
 struct AttnArgs {
   const float* q;
@@ -25,6 +24,7 @@ struct AttnArgs {
   int* counters;   // [kMaxUnits] split-merge tickets, 0 between calls
   uint32_t* status;
   const float* gate;  // null, or [B, S, H, Dh]: out *= sigmoid(gate) (qwen35 sigmoid_gate)
+  float q8_smul;      // Q8_0: element = q * scale * q8_smul (1, or 1/127 for the WGSL convention)
 };
 
 // Per-CTA geometry shared by both kernels.

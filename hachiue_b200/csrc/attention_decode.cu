@@ -20,9 +20,6 @@
 //  * Online softmax per row in the log2 domain (q pre-scaled by log2(e)/sqrt(Dh)).
 //  * Splits write (m, l, acc) partials to the handle's workspace; the last CTA
 //    of a unit (atomic ticket, no spinning) merges them and writes out.
-#include <stdlib.h>
-#include <string.h>
-
 #include "attention.cuh"
 
 namespace {
@@ -66,7 +63,7 @@ __device__ __forceinline__ void s8x4_to_f32(uint32_t w, float* f) {
 // Loads the lane's DPL elements of tile row `row` as f32 (Q8_0: times the
 // block scale, like `kQ * kS` in wasm-backend.ts:861-866).
 template <int FMT, int DH>
-__device__ __forceinline__ void load_row(const uint8_t* tile, const float* scales, int row, int lane,
+__device__ __forceinline__ void load_row(const uint8_t* tile, const float* scales, float smul, int row, int lane,
                                          float (&v)[DH / 32]) {
   constexpr int DPL = DH / 32;
   if constexpr (FMT == HCU_KV_F32) {
@@ -106,7 +103,7 @@ __device__ __forceinline__ void load_row(const uint8_t* tile, const float* scale
     }
   } else {  // Q8_0
     const int8_t* p = reinterpret_cast<const int8_t*>(tile + (size_t)row * DH) + lane * DPL;
-    const float s = scales[row * (DH / 32) + (lane * DPL) / 32];
+    const float s = scales[row * (DH / 32) + (lane * DPL) / 32] * smul;
     if constexpr (DPL == 4) {
       s8x4_to_f32(*reinterpret_cast<const uint32_t*>(p), v);
     } else {
@@ -268,7 +265,7 @@ __global__ void __launch_bounds__(NTHREADS, ctas_per_sm(R, DH))
 #pragma unroll
       for (int tt = 0; tt < TG; tt++) {
         float kvec[DPL];
-        load_row<FMT, DH>(ktile, kscale, wrow0 + t0 + tt, lane, kvec);
+        load_row<FMT, DH>(ktile, kscale, a.q8_smul, wrow0 + t0 + tt, lane, kvec);
 #pragma unroll
         for (int r = 0; r < R; r++) {
           float d = 0.f;
@@ -331,7 +328,7 @@ __global__ void __launch_bounds__(NTHREADS, ctas_per_sm(R, DH))
 #pragma unroll PV_UNROLL
     for (int t = 0; t < tcount; t++) {
       float vvec[DPL];
-      load_row<FMT, DH>(vtile, vscale, wrow0 + t, lane, vvec);
+      load_row<FMT, DH>(vtile, vscale, a.q8_smul, wrow0 + t, lane, vvec);
       float p[R];
       if constexpr (R % 4 == 0) {
 #pragma unroll
@@ -369,8 +366,16 @@ __global__ void __launch_bounds__(NTHREADS, ctas_per_sm(R, DH))
       cl[warp * R + r] = l[r];
     }
   }
-  named_bar(1, NW * 32);
-  if (aborted) return;
+  // One decision for all consumer warps (a bounded wait may give up in some
+  // warps only): the merge below synchronises them on named barriers.
+  aborted = !named_bar_and(1, NW * 32, !aborted);
+  if (aborted) {
+    // The status word holds the timeout.  A multi-split unit still takes its
+    // ticket so that the unit's last CTA re-arms it (its output is garbage,
+    // which the status reports); tickets stay consistent for the next call.
+    if (u.nsplit > 1) ticket_merge<R, DH, NW * 32>(a, u, tid, 1, reinterpret_cast<float*>(stages), s_last);
+    return;
+  }
 
   const int rows_valid = u.rows_valid;
   float* part = a.part + ((size_t)u.unit * a.max_splits + split) * R * (DH + 2);
@@ -461,11 +466,15 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   if (!p || !q || !kv || !out || !kv->k || !kv->v) return fail(HCU_EINVAL, "hcu_attention: null argument");
   const int S = (int)p->S, H = (int)p->H, KV = (int)p->KV, Dh = (int)p->Dh;
   const int batch = p->batch ? (int)p->batch : 1;
-  const int fmt = (int)kv->format;
+  // The WGSL Q8_0 convention differs only in its scale (amax instead of
+  // amax / 127): same kernels, with the scale multiplied by 1/127.
+  const bool q8_wgsl = kv->format == HCU_KV_Q8_0_WGSL;
+  const int fmt = q8_wgsl ? HCU_KV_Q8_0 : (int)kv->format;
   if (S < 1 || H < 1 || KV < 1) return fail(HCU_EINVAL, "hcu_attention: S, H and KV must be positive");
   if (H % KV) return fail(HCU_EINVAL, "hcu_attention: H (%d) is not a multiple of KV (%d)", H, KV);
   if (Dh != 128 && Dh != 256) return fail(HCU_EUNSUPPORTED, "hcu_attention: Dh=%d (built: 128, 256)", Dh);
-  if (fmt < HCU_KV_F32 || fmt > HCU_KV_Q8_0) return fail(HCU_EINVAL, "hcu_attention: unknown KV format %d", fmt);
+  if (fmt < HCU_KV_F32 || fmt > HCU_KV_Q8_0)
+    return fail(HCU_EINVAL, "hcu_attention: unknown KV format %u", kv->format);
   if (fmt == HCU_KV_Q8_0 && (!kv->k_scale || !kv->v_scale))
     return fail(HCU_EINVAL, "hcu_attention: Q8_0 cache needs k_scale and v_scale");
   if (batch > 1 && !p->pos_base && p->max_context == 0)
@@ -474,9 +483,8 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
     return fail(HCU_EINVAL, "hcu_attention: q and out must be 16-byte aligned");
   const int G = H / KV;
   // The tcgen05 kernel serves f16 / bf16 caches with Dh = 128; every other
-  // combination (and HCU_ATTN_IMPL=cuda) uses the CUDA-core kernel.
-  const char* impl = getenv("HCU_ATTN_IMPL");
-  const bool force_cuda = impl && !strcmp(impl, "cuda");
+  // combination (and HCU_OPT_ATTN_CUDA_CORES) uses the CUDA-core kernel.
+  const bool force_cuda = h->opt_attn_cuda_cores != 0;
   const int rmax_cuda = Dh == 128 ? 16 : 8;
   const int rmax_tc = fmt == HCU_KV_F16 ? 16 : 8;
   bool use_tc = !force_cuda && hcu::attn_tc_supported(fmt, Dh, G);
@@ -511,10 +519,7 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   long long want_splits = (target + units - 1) / units;
   if (want_splits < 1) want_splits = 1;
   long long chunk = (max_range + want_splits - 1) / want_splits;
-  if (const char* env = getenv("HCU_ATTN_CHUNK")) {
-    long long c = atoll(env);
-    if (c > 0) chunk = c;
-  }
+  if (h->opt_attn_chunk > 0) chunk = h->opt_attn_chunk;
   const long long min_chunk = (max_range + kMaxSplits - 1) / kMaxSplits;
   if (chunk < min_chunk) chunk = min_chunk;
   chunk = ((chunk + TT - 1) / TT) * TT;
@@ -522,7 +527,7 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   // Split-merge tickets live in a fixed region at the start of the workspace so
   // that no call's partials ever overlap another call's tickets (each ticket is
   // re-armed to 0 by the CTA that consumes it).
-  const size_t cnt_bytes = (size_t)kMaxUnits * sizeof(int);
+  const size_t cnt_bytes = kTicketBytes;
   auto need = [&](long long c) {
     long long ms = (max_range + c - 1) / c;
     return cnt_bytes + (size_t)units * ms * R * (Dh + 2) * sizeof(float);
@@ -585,6 +590,7 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   args.part = reinterpret_cast<float*>(static_cast<char*>(h->workspace) + cnt_bytes);
   args.status = h->dev_status;
   args.gate = p->gate;
+  args.q8_smul = q8_wgsl ? 1.f / 127.f : 1.f;
   dim3 grid((unsigned)max_splits, (unsigned)KV, (unsigned)(batch * nqb));
   if (use_tc) return hcu::launch_attn_tc(h, fmt, R, args, grid, tk, tv);
   switch (fmt) {

@@ -350,7 +350,9 @@ __global__ void __launch_bounds__(TC_THREADS, NC == 16 ? 2 : 1)
       const float v = warp_sum(lsum[r]);
       if (lane == 0) lred[sw * R + r] = v;
     }
-    named_bar(1, 128);
+    // One decision for the four softmax warps (a bounded wait may give up in
+    // some of them only): the merge below synchronises them on named barriers.
+    aborted = !named_bar_and(1, 128, !aborted);
 #pragma unroll
     for (int r = 0; r < R; r++) {
       lsum[r] = lred[r] + lred[R + r] + lred[2 * R + r] + lred[3 * R + r];
@@ -359,7 +361,13 @@ __global__ void __launch_bounds__(TC_THREADS, NC == 16 ? 2 : 1)
     // Hold the results until TMEM is released below.
     tc_fence_before();
     __syncthreads();
-    if (aborted) return;
+    if (aborted) {
+      // The status word holds the timeout.  A multi-split unit still takes its
+      // ticket so that the unit's last CTA re-arms it (its output is garbage,
+      // which the status reports); tickets stay consistent for the next call.
+      if (u.nsplit > 1) ticket_merge<R, TC_DH, 128>(a, u, t, 1, reinterpret_cast<float*>(stages), s_last);
+      return;
+    }
     if (u.nsplit == 1) {
 #pragma unroll
       for (int r = 0; r < R; r++)

@@ -21,7 +21,6 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[HCU_NOALLOC_SCR
 
 namespace {
 
-constexpr size_t kTicketBytes = (size_t)(1 << 16) * sizeof(int);  // the ticket region hcu_attention expects
 constexpr size_t kStatusBytes = 256;
 constexpr int kMaxDevices = 64;
 
@@ -29,6 +28,7 @@ struct NoallocDevice {
   bool ready = false;
   void* scratch = nullptr;  // device address of g_noalloc_scratch on this device
   int sm_count = 0;
+  int device = -1;
 };
 
 std::mutex g_mu;
@@ -53,22 +53,52 @@ int setup_device(int dev, NoallocDevice* out) {
       return hcu::fail(HCU_EUNSUPPORTED, "hcu_attention_noalloc: device %d is not sm_100a", dev);
     d.scratch = ptr;
     d.sm_count = sms;
+    d.device = dev;
     d.ready = true;
   }
   *out = d;
   return HCU_OK;
 }
 
+uint32_t* status_word(void* scratch) {
+  return reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(scratch) + HCU_NOALLOC_SCRATCH_BYTES - kStatusBytes);
+}
+
+int current_device(const char* op, NoallocDevice* d) {
+  int dev = -1;
+  HCU_TRY(hcu::check_cuda(cudaGetDevice(&dev), op));
+  if (dev < 0 || dev >= kMaxDevices) return hcu::fail(HCU_EINVAL, "%s: device %d", op, dev);
+  return setup_device(dev, d);
+}
+
 }  // namespace
+
+// For callers without a handle, the failure report of hcu_attention_noalloc:
+// a kernel whose bounded wait gave up records it in the status word at the end
+// of the static scratch (the only device memory these callers have), and this
+// copies it out (into the caller's host word; no allocation) and optionally
+// clears it.
+extern "C" int hcu_attention_noalloc_status(uint32_t* status, int clear, void* cuda_stream) {
+  if (!status) return hcu::fail(HCU_EINVAL, "hcu_attention_noalloc_status: null argument");
+  NoallocDevice d;
+  HCU_TRY(current_device("hcu_attention_noalloc_status", &d));
+  const cudaStream_t stream = reinterpret_cast<cudaStream_t>(cuda_stream);
+  HCU_TRY(hcu::check_cuda(cudaMemcpyAsync(status, status_word(d.scratch), sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                          stream),
+                          "hcu_attention_noalloc_status: read"));
+  HCU_TRY(hcu::check_cuda(cudaStreamSynchronize(stream), "hcu_attention_noalloc_status: sync"));
+  if (clear)
+    HCU_TRY(hcu::check_cuda(cudaMemsetAsync(status_word(d.scratch), 0, sizeof(uint32_t), stream),
+                            "hcu_attention_noalloc_status: clear"));
+  return HCU_OK;
+}
 
 extern "C" int hcu_attention_noalloc(const hcu_attention_params* p, const float* q, const hcu_kv_cache* kv,
                                      float* out, void* cuda_stream) {
   if (!p || !q || !kv || !out) return hcu::fail(HCU_EINVAL, "hcu_attention_noalloc: null argument");
-  int dev = -1;
-  HCU_TRY(hcu::check_cuda(cudaGetDevice(&dev), "hcu_attention_noalloc: cudaGetDevice"));
-  if (dev < 0 || dev >= kMaxDevices) return hcu::fail(HCU_EINVAL, "hcu_attention_noalloc: device %d", dev);
   NoallocDevice d;
-  HCU_TRY(setup_device(dev, &d));
+  HCU_TRY(current_device("hcu_attention_noalloc", &d));
+  const int dev = d.device;
 
   const cudaStream_t stream = reinterpret_cast<cudaStream_t>(cuda_stream);
   // Tickets must read 0 when a call starts.  A completed call leaves them at 0,
@@ -89,9 +119,8 @@ extern "C" int hcu_attention_noalloc(const hcu_attention_params* p, const float*
   view.stream = stream;
   view.workspace = d.scratch;
   view.workspace_bytes = HCU_NOALLOC_SCRATCH_BYTES - kStatusBytes;
-  view.dev_status =
-      reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(d.scratch) + HCU_NOALLOC_SCRATCH_BYTES - kStatusBytes);
-  static_assert(HCU_NOALLOC_SCRATCH_BYTES > kTicketBytes + kStatusBytes, "scratch smaller than the ticket region");
+  view.dev_status = status_word(d.scratch);
+  static_assert(HCU_NOALLOC_SCRATCH_BYTES > hcu::kTicketBytes + kStatusBytes, "scratch smaller than the ticket region");
 
   const int st = hcu_attention(&view, p, q, kv, out);
   if (st == HCU_ENOMEM)

@@ -177,7 +177,17 @@ __global__ void __launch_bounds__(128) attn_prologue_kernel(const ProArgs a) {
     // append the row to the cache at (row, head)
     const long long elem0 = (row * a.KV + head) * Dh;
     void* cache = kind == 1 ? a.kc : a.vc;
-    if (a.fmt == HCU_KV_Q8_0) {
+    if (a.fmt == HCU_KV_Q8_0_WGSL) {
+      float* scl = kind == 1 ? a.ks : a.vs;
+#pragma unroll
+      for (int j = 0; j < NJ; j++) {
+        float amax = fabsf(x[j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        static_cast<int8_t*>(cache)[elem0 + lane + 32 * j] = (int8_t)q8_quant_wgsl(x[j], amax);
+        if (lane == 0) scl[elem0 / 32 + j] = q8_scale_wgsl(amax);
+      }
+    } else if (a.fmt == HCU_KV_Q8_0) {
       float* scl = kind == 1 ? a.ks : a.vs;
 #pragma unroll
       for (int j = 0; j < NJ; j++) {  // block j = elements 32j .. 32j + 31, element lane
@@ -263,8 +273,9 @@ extern "C" int hcu_attn_prologue(hcu_handle h, const hcu_attn_prologue_params* p
   if (p->rotaryDim < 64 || p->rotaryDim % 64 || (int)p->rotaryDim > Dh)
     return fail(HCU_EUNSUPPORTED, "hcu_attn_prologue: rotaryDim %u (built: multiples of 64 up to Dh)", p->rotaryDim);
   const int fmt = (int)kv->format;
-  if (fmt < HCU_KV_F32 || fmt > HCU_KV_Q8_0) return fail(HCU_EINVAL, "hcu_attn_prologue: unknown KV format %d", fmt);
-  if (fmt == HCU_KV_Q8_0 && (!kv->k_scale || !kv->v_scale))
+  if (fmt < HCU_KV_F32 || fmt > HCU_KV_Q8_0_WGSL)
+    return fail(HCU_EINVAL, "hcu_attn_prologue: unknown KV format %d", fmt);
+  if ((fmt == HCU_KV_Q8_0 || fmt == HCU_KV_Q8_0_WGSL) && (!kv->k_scale || !kv->v_scale))
     return fail(HCU_EINVAL, "hcu_attn_prologue: Q8_0 cache needs k_scale and v_scale");
   const int batch = p->batch ? (int)p->batch : 1;
   if (p->S < 1 || p->H < 1 || p->KV < 1 || p->S > 65535 || batch > 65535)

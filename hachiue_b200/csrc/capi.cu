@@ -212,7 +212,38 @@ int hcu_device_status(hcu_handle h, uint32_t* status, int clear) {
   HCU_TRY(check_cuda(cudaMemcpyAsync(status, h->dev_status, sizeof(uint32_t), cudaMemcpyDeviceToHost, h->stream),
                      "hcu_device_status"));
   HCU_TRY(check_cuda(cudaStreamSynchronize(h->stream), "hcu_device_status"));
-  if (clear) HCU_TRY(check_cuda(cudaMemsetAsync(h->dev_status, 0, sizeof(uint32_t), h->stream), "hcu_device_status"));
+  if (clear) {
+    HCU_TRY(check_cuda(cudaMemsetAsync(h->dev_status, 0, sizeof(uint32_t), h->stream), "hcu_device_status"));
+    // A decode-attention call whose bounded wait gave up may have left split
+    // tickets partly counted; re-arm them all so the next call merges correctly.
+    HCU_TRY(check_cuda(cudaMemsetAsync(h->workspace, 0, hcu::kTicketBytes, h->stream), "hcu_device_status"));
+  }
+  return HCU_OK;
+}
+
+int hcu_selftest_dirty_tickets(hcu_handle h) {
+  if (!h) return fail(HCU_EINVAL, "hcu_selftest_dirty_tickets: null handle");
+  HCU_TRY(check_cuda(cudaSetDevice(h->device), "hcu_selftest_dirty_tickets"));
+  return check_cuda(cudaMemsetAsync(h->workspace, 0x01, hcu::kTicketBytes, h->stream), "hcu_selftest_dirty_tickets");
+}
+
+int hcu_set_option(hcu_handle h, int option, int64_t value) {
+  if (!h) return fail(HCU_EINVAL, "hcu_set_option: null handle");
+  if (value < 0) return fail(HCU_EINVAL, "hcu_set_option: negative value %lld", (long long)value);
+  switch (option) {
+    case HCU_OPT_ATTN_CUDA_CORES: h->opt_attn_cuda_cores = value; return HCU_OK;
+    case HCU_OPT_ATTN_CHUNK: h->opt_attn_chunk = value; return HCU_OK;
+    case HCU_OPT_GDN_SCRATCH_MB: h->opt_gdn_scratch_mb = value; return HCU_OK;
+    case HCU_OPT_SWA_CTAS: h->opt_swa_ctas = value; return HCU_OK;
+  }
+  return fail(HCU_EINVAL, "hcu_set_option: unknown option %d", option);
+}
+
+int hcu_set_q8_convention(hcu_handle h, uint32_t format) {
+  if (!h) return fail(HCU_EINVAL, "hcu_set_q8_convention: null handle");
+  if (format != HCU_KV_Q8_0 && format != HCU_KV_Q8_0_WGSL)
+    return fail(HCU_EINVAL, "hcu_set_q8_convention: format %u is not a Q8_0 convention", format);
+  h->q8_format = format;
   return HCU_OK;
 }
 
@@ -234,7 +265,8 @@ int hcu_dispatch(hcu_handle h, const char* shader, const uint32_t words[8], void
   };
   if (!strcmp(shader, "kv_append_q8")) {
     HCU_TRY(need(3));
-    return hcu_kv_append(h, words[0], words[1], words[2], words[3], HCU_KV_Q8_0,
+    if (!h) return fail(HCU_EINVAL, "kv_append_q8: null handle");
+    return hcu_kv_append(h, words[0], words[1], words[2], words[3], h->q8_format,
                          static_cast<const float*>(buffers[0]), buffers[1], static_cast<float*>(buffers[2]));
   }
   if (!strcmp(shader, "attention_q8")) {
@@ -247,8 +279,9 @@ int hcu_dispatch(hcu_handle h, const char* shader, const uint32_t words[8], void
     p.posBase = words[4];
     p.windowSize = words[5];
     p.batch = 1;
+    if (!h) return fail(HCU_EINVAL, "attention_q8: null handle");
     hcu_kv_cache kv{};
-    kv.format = HCU_KV_Q8_0;
+    kv.format = h->q8_format;
     kv.rows = p.posBase + p.S;
     kv.k = buffers[1];
     kv.k_scale = static_cast<float*>(buffers[2]);

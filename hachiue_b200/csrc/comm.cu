@@ -12,12 +12,15 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <string.h>
+
 #include <mutex>
 
 #include "context.h"
 
 struct hcu_comm_s {
-  int n = 0;
+  int n = 0;       // ranks driven by this process (devices[0..n), comms[0..n))
+  int nranks = 0;  // ranks of the whole communicator (n, or the job's size for hcu_comm_init_rank)
   int devices[HCU_COMM_MAX_DEVICES] = {};
   ncclComm_t comms[HCU_COMM_MAX_DEVICES] = {};
 };
@@ -28,6 +31,8 @@ using hcu::fail;
 
 struct NcclApi {
   decltype(&ncclCommInitAll) init_all = nullptr;
+  decltype(&ncclCommInitRank) init_rank = nullptr;
+  decltype(&ncclGetUniqueId) unique_id = nullptr;
   decltype(&ncclCommDestroy) destroy = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
   decltype(&ncclGroupStart) group_start = nullptr;
@@ -43,12 +48,15 @@ const NcclApi& nccl() {
     void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
     if (!lib) return;
     api.init_all = reinterpret_cast<decltype(api.init_all)>(dlsym(lib, "ncclCommInitAll"));
+    api.init_rank = reinterpret_cast<decltype(api.init_rank)>(dlsym(lib, "ncclCommInitRank"));
+    api.unique_id = reinterpret_cast<decltype(api.unique_id)>(dlsym(lib, "ncclGetUniqueId"));
     api.destroy = reinterpret_cast<decltype(api.destroy)>(dlsym(lib, "ncclCommDestroy"));
     api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(lib, "ncclAllGather"));
     api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(lib, "ncclGroupStart"));
     api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(lib, "ncclGroupEnd"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(lib, "ncclGetErrorString"));
-    api.ok = api.init_all && api.destroy && api.all_gather && api.group_start && api.group_end && api.error_string;
+    api.ok = api.init_all && api.init_rank && api.unique_id && api.destroy && api.all_gather && api.group_start &&
+             api.group_end && api.error_string;
   });
   return api;
 }
@@ -78,8 +86,47 @@ extern "C" int hcu_comm_create(int n, const int* devices, hcu_comm* comm) {
   hcu_comm c = new (std::nothrow) hcu_comm_s;
   if (!c) return fail(HCU_ENOMEM, "hcu_comm_create: out of host memory");
   c->n = n;
+  c->nranks = n;
   for (int i = 0; i < n; i++) c->devices[i] = devices[i];
   const int st = check_nccl(api.init_all(c->comms, n, c->devices), "hcu_comm_create: ncclCommInitAll");
+  if (st != HCU_OK) {
+    delete c;
+    return st;
+  }
+  *comm = c;
+  return HCU_OK;
+}
+
+extern "C" int hcu_comm_unique_id(uint8_t* id) {
+  if (!id) return fail(HCU_EINVAL, "hcu_comm_unique_id: null argument");
+  static_assert(sizeof(ncclUniqueId) == HCU_COMM_ID_BYTES, "NCCL unique id size");
+  const NcclApi& api = nccl();
+  if (!api.ok) return fail(HCU_ENCCL, "hcu_comm_unique_id: libnccl.so.2 could not be opened");
+  ncclUniqueId uid;
+  HCU_TRY(check_nccl(api.unique_id(&uid), "hcu_comm_unique_id: ncclGetUniqueId"));
+  memcpy(id, &uid, sizeof(uid));
+  return HCU_OK;
+}
+
+extern "C" int hcu_comm_init_rank(int nranks, int rank, const uint8_t* id, int device, hcu_comm* comm) {
+  if (!comm || !id) return fail(HCU_EINVAL, "hcu_comm_init_rank: null argument");
+  *comm = nullptr;
+  if (nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(HCU_EINVAL, "hcu_comm_init_rank: rank %d of %d", rank, nranks);
+  int count = 0;
+  HCU_TRY(hcu::check_cuda(cudaGetDeviceCount(&count), "hcu_comm_init_rank: cudaGetDeviceCount"));
+  if (device < 0 || device >= count) return fail(HCU_EINVAL, "hcu_comm_init_rank: device %d of %d", device, count);
+  const NcclApi& api = nccl();
+  if (!api.ok) return fail(HCU_ENCCL, "hcu_comm_init_rank: libnccl.so.2 could not be opened");
+  HCU_TRY(hcu::check_cuda(cudaSetDevice(device), "hcu_comm_init_rank: cudaSetDevice"));
+  hcu_comm c = new (std::nothrow) hcu_comm_s;
+  if (!c) return fail(HCU_ENOMEM, "hcu_comm_init_rank: out of host memory");
+  c->n = 1;
+  c->nranks = nranks;
+  c->devices[0] = device;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  const int st = check_nccl(api.init_rank(&c->comms[0], nranks, uid, rank), "hcu_comm_init_rank: ncclCommInitRank");
   if (st != HCU_OK) {
     delete c;
     return st;
@@ -108,16 +155,34 @@ extern "C" int hcu_allgather(hcu_comm comm, void* const* send, void* const* recv
   const NcclApi& api = nccl();
   int prev = 0;
   HCU_TRY(hcu::check_cuda(cudaGetDevice(&prev), "hcu_allgather: cudaGetDevice"));
+  // Every check that can fail runs before ncclGroupStart: once the group is
+  // open, a rank left out would make the others' all-gathers wait for it.
+  for (int i = 0; i < comm->n; i++) {
+    HCU_TRY(hcu::check_cuda(cudaSetDevice(comm->devices[i]), "hcu_allgather: cudaSetDevice"));
+    if (streams[i]) {
+      int sdev = -1;
+      cudaStream_t s = static_cast<cudaStream_t>(streams[i]);
+      int st = hcu::check_cuda(cudaStreamGetDevice(s, &sdev), "hcu_allgather: stream device");
+      if (st == HCU_OK && sdev != comm->devices[i])
+        st = fail(HCU_EINVAL, "hcu_allgather: stream of rank %d is on device %d, not %d", i, sdev, comm->devices[i]);
+      if (st != HCU_OK) {
+        cudaSetDevice(prev);
+        return st;
+      }
+    }
+  }
   HCU_TRY(check_nccl(api.group_start(), "hcu_allgather: ncclGroupStart"));
-  int st = HCU_OK;
-  for (int i = 0; i < comm->n && st == HCU_OK; i++) {
-    st = hcu::check_cuda(cudaSetDevice(comm->devices[i]), "hcu_allgather: cudaSetDevice");
-    if (st == HCU_OK)
-      st = check_nccl(api.all_gather(send[i], recv[i], bytes, ncclInt8, comm->comms[i],
-                                     static_cast<cudaStream_t>(streams[i])),
-                      "hcu_allgather: ncclAllGather");
+  // Inside the group only NCCL calls (whose errors NCCL itself knows about
+  // and reports at ncclGroupEnd) and cudaSetDevice on devices checked above.
+  ncclResult_t first = ncclSuccess;
+  for (int i = 0; i < comm->n; i++) {
+    cudaSetDevice(comm->devices[i]);
+    const ncclResult_t r = api.all_gather(send[i], recv[i], bytes, ncclInt8, comm->comms[i],
+                                          static_cast<cudaStream_t>(streams[i]));
+    if (r != ncclSuccess && first == ncclSuccess) first = r;
   }
   const int end = check_nccl(api.group_end(), "hcu_allgather: ncclGroupEnd");
   cudaSetDevice(prev);
-  return st != HCU_OK ? st : end;
+  if (first != ncclSuccess) return check_nccl(first, "hcu_allgather: ncclAllGather");
+  return end;
 }

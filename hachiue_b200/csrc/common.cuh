@@ -208,6 +208,18 @@ __device__ __forceinline__ float2 f16x2_to_f2(uint32_t w) {
   return __half22float2(h);
 }
 
+// Q8_0 quantisation of one element as the reference's WGSL kv_append_q8 does
+// it (src/kernels.ts:1318-1333), in f32: inv = 127 / amax (0 when amax is 0),
+// q = clamp(round(x * inv), -127, 127) with WGSL round()'s ties-to-even, and
+// the stored scale (amax / 127) * 127.  The JS twin (f64, Math.round) is in
+// kv_append.cu and attn_layer.cu.
+__device__ __forceinline__ int q8_quant_wgsl(float x, float amax) {
+  const float inv = amax > 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+  const float q = rintf(__fmul_rn(x, inv));
+  return (int)fminf(fmaxf(q, -127.f), 127.f);
+}
+__device__ __forceinline__ float q8_scale_wgsl(float amax) { return __fmul_rn(__fdiv_rn(amax, 127.f), 127.f); }
+
 // Warp all-reduce helpers.
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

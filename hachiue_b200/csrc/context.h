@@ -23,9 +23,22 @@ struct hcu_context {
   size_t scratch_bytes = 0;
   int inject_status = 0;
   int inject_count = 0;
+  uint32_t q8_format = HCU_KV_Q8_0;  // Q8_0 convention of hcu_dispatch (hcu_set_q8_convention)
+  // hcu_set_option values (0 = the tuned default)
+  int64_t opt_attn_cuda_cores = 0;
+  int64_t opt_attn_chunk = 0;
+  int64_t opt_gdn_scratch_mb = 0;
+  int64_t opt_swa_ctas = 0;
 };
 
 namespace hcu {
+
+// Split-merge tickets of the decode-attention kernels: one int per (sequence,
+// KV head, query block) unit at the head of the handle's workspace.  Every
+// ticket reads 0 between calls (the CTA that draws a unit's last ticket re-arms
+// it); hcu_device_status(clear) also zeroes them.
+constexpr int kMaxUnits = 1 << 16;
+constexpr size_t kTicketBytes = (size_t)kMaxUnits * sizeof(int);
 
 // Records `msg` as this thread's last error and returns `code`.
 int fail(int code, const char* fmt, ...);

@@ -971,14 +971,10 @@ int chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q
   }
   // Scratch: the prep outputs of one slab of chunks (17 KB per sequence, V head
   // and chunk).  The slab is as long as the scratch budget allows
-  // (HCU_GDN_SCRATCH_MB, default 1 GiB: one slab for 8 x 8192 tokens x 32 heads).
+  // (HCU_OPT_GDN_SCRATCH_MB, default 1 GiB: one slab for 8 x 8192 tokens x 32 heads).
   const long long nchunks = (T + hcu::GC - 1) / hcu::GC;
   const long long per_chunk = B * NV * (long long)hcu::UNIT_BYTES;
-  long long budget = 1024ll << 20;
-  if (const char* env = getenv("HCU_GDN_SCRATCH_MB")) {
-    const long long mb = atoll(env);
-    if (mb > 0) budget = mb << 20;
-  }
+  const long long budget = (h->opt_gdn_scratch_mb > 0 ? (long long)h->opt_gdn_scratch_mb : 1024ll) << 20;
   long long ns = budget / per_chunk;
   if (ns < 1) ns = 1;
   if (ns > nchunks) ns = nchunks;

@@ -554,13 +554,10 @@ int launch_swa(hcu_context* h, const SwaArgs& args, const CUtensorMap& tq, const
     return HCU_OK;
   }));
   // One CTA per SM (the shared memory admits no second), never more CTAs than
-  // items.  HCU_SWA_CTAS caps the grid (tests use it to give every CTA a long
+  // items.  HCU_OPT_SWA_CTAS caps the grid (tests use it to give every CTA a long
   // chain of items on small shapes).
   int grid = args.n_items < h->sm_count ? args.n_items : h->sm_count;
-  if (const char* env = getenv("HCU_SWA_CTAS")) {
-    const int c = atoi(env);
-    if (c > 0 && c < grid) grid = c;
-  }
+  if (h->opt_swa_ctas > 0 && h->opt_swa_ctas < grid) grid = (int)h->opt_swa_ctas;
   kern<<<grid, sw_threads(NHD), smem, h->stream>>>(tq, tk, tv, args);
   return after_launch("hcu_swa_prefill: launch");
 }

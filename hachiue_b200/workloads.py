@@ -121,6 +121,37 @@ def cfg2_bytes(lens: np.ndarray, H=32, KV=8, Dh=128) -> int:
     return int(lens.sum()) * KV * Dh * 2 * 2 + 2 * len(lens) * H * Dh * 4
 
 
+def cfg2_q8_bytes(lens: np.ndarray, H=32, KV=8, Dh=128) -> int:
+    """cfg2's shapes on the reference's Q8_0 cache: K and V int8 plus one f32
+    scale per 32 elements, read once; q read and out written (f32)."""
+    return int(lens.sum()) * KV * (Dh + Dh // 32 * 4) * 2 + 2 * len(lens) * H * Dh * 4
+
+
+def cfg2_lens(seed: int = 1, batch: int = 64, lo: int = 512, hi: int = 8193) -> np.ndarray:
+    """The per-sequence context lengths of :func:`decode_cfg2` (its first draw)."""
+    return np.random.default_rng(seed).integers(lo, hi, batch).astype(np.int64)
+
+
+def swa_flops(T=4096, W=1024, B=8, H=16, D=128) -> int:
+    """Algorithmic FLOPs of causal sliding-window attention: 4*D per (query,
+    key) pair inside the window (QK^T and PV), pairs = sum_i min(i+1, W)."""
+    pairs = sum(min(i + 1, W) for i in range(T)) if W > 0 else T * (T + 1) // 2
+    return 4 * D * pairs * B * H
+
+
+def cfg5_flops(B=8, T=8192, NV=32, C=64, D=128) -> int:
+    """Canonical chunked (WY) FLOPs of the GDN prefill: per token and V head
+    10*C*D + 6*D^2 (full C x C blocks, the C^3 triangular solve excluded)."""
+    return B * T * NV * (10 * C * D + 6 * D * D)
+
+
+def cfg5_bytes(B=8, T=8192, NK=16, NV=32, D=128) -> int:
+    """HBM bytes that must move: q, k, v bf16 in, g, beta f32 in, core f32 out,
+    final state f32 out."""
+    return (2 * B * T * NK * D * 2 + B * T * NV * D * 2 + 2 * B * T * NV * 4 + B * T * NV * D * 4
+            + B * NV * D * D * 4)
+
+
 def cfg1_bytes(T=1024, H=16, KV=8, Dh=128) -> int:
     return 2 * KV * T * Dh * 4 + 2 * H * Dh * 4
 
@@ -142,7 +173,7 @@ def gdn_layer_cfg6(seed: int = 6, batch: int = 64, NK: int = 16, NV: int = 32, D
                 conv_state=_normal(rng, (batch, K - 1, C)), a=_normal(rng, (batch, NV)), b=_normal(rng, (batch, NV)),
                 z=_normal(rng, (batch, NV * D)), gamma=(1 + _normal(rng, (D,), std=0.1)).astype(np.float32),
                 state=_normal(rng, (batch, NV, D, D), std=0.02), a_neg=-np.ones(NV, np.float32),
-                dt_bias=np.zeros(NV, np.float32), eps=1e-6, NK=NK, NV=NV, D=D, K=K)
+                dt_bias=np.zeros(NV, np.float32), eps=float(np.float32(1e-6)), NK=NK, NV=NV, D=D, K=K)
 
 
 def cfg6_bytes(B=64, NK=16, NV=32, D=128, K=4) -> int:
@@ -167,7 +198,7 @@ def attn_layer_cfg7(seed: int = 7, H: int = 16, KV: int = 8, Dh: int = 128, cont
     return dict(q=_normal(rng, (1, H, Dh)), k=_normal(rng, (1, KV, Dh)), v=_normal(rng, (1, KV, Dh)),
                 q_norm=(1 + _normal(rng, (Dh,), std=0.1)).astype(np.float32),
                 k_norm=(1 + _normal(rng, (Dh,), std=0.1)).astype(np.float32),
-                kq=kq, ks=ks, vq=vq, vs=vs, pos=context - 1, rot=Dh, theta=theta, eps=1e-6, H=H, KV=KV, Dh=Dh)
+                kq=kq, ks=ks, vq=vq, vs=vs, pos=context - 1, rot=Dh, theta=theta, eps=float(np.float32(1e-6)), H=H, KV=KV, Dh=Dh)
 
 
 def cfg7_bytes(H=16, KV=8, Dh=128, context=1024) -> int:

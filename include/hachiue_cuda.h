@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define HCU_ABI_VERSION 2  /* 2: hcu_attention_params.gate */
+#define HCU_ABI_VERSION 3  /* 2: hcu_attention_params.gate; 3: HCU_KV_Q8_0_WGSL */
 
 /* Status codes. */
 #define HCU_OK 0
@@ -55,6 +55,14 @@ extern "C" {
 #define HCU_KV_F16 1
 #define HCU_KV_BF16 2
 #define HCU_KV_Q8_0 3
+/* Q8_0 as the reference's WGSL ops store it: the scale array holds amax
+ * (kv_append_q8 writes (amax/127)*127 in f32, src/kernels.ts:1333) and an
+ * element dequantises as max(q/127, -1) * amax (unpack4x8snorm,
+ * src/kernels.ts:1386-1411).  HCU_KV_Q8_0 is the JS backend's convention
+ * (scale = amax/127, element = q * scale, src/wasm-backend.ts:815,861).  Both
+ * hold the same int8 values up to the rounding rule (WGSL round() is
+ * half-to-even in f32, the JS Math.round half-up in f64). */
+#define HCU_KV_Q8_0_WGSL 4
 
 /* Element types of the tensor-core prefill inputs and outputs. */
 #define HCU_DT_F32 0
@@ -87,6 +95,23 @@ int hcu_set_stream(hcu_handle h, void *cuda_stream);
 void *hcu_get_stream(hcu_handle h);
 int hcu_stream_sync(hcu_handle h);
 
+/* Tuning options of one handle, for tests and profiling; every default is the
+ * tuned choice, and 0 restores it.  Options are read when an op is called
+ * (never from the environment).
+ *   HCU_OPT_ATTN_CUDA_CORES  1: decode attention always on the CUDA-core
+ *                            kernel (otherwise f16 / bf16 / Q8_0 caches with
+ *                            Dh 128 use the tcgen05 kernels)
+ *   HCU_OPT_ATTN_CHUNK       keys per split-K split (rounded up to a tile)
+ *   HCU_OPT_GDN_SCRATCH_MB   scratch budget of the chunked GDN prefill, in MiB
+ *                            (default 1024); smaller budgets process the
+ *                            prompt in slabs of chunks
+ *   HCU_OPT_SWA_CTAS         cap on the SWA prefill's persistent grid */
+#define HCU_OPT_ATTN_CUDA_CORES 1
+#define HCU_OPT_ATTN_CHUNK 2
+#define HCU_OPT_GDN_SCRATCH_MB 3
+#define HCU_OPT_SWA_CTAS 4
+int hcu_set_option(hcu_handle h, int option, int64_t value);
+
 int hcu_alloc(hcu_handle h, size_t bytes, void **device_ptr);
 int hcu_free(hcu_handle h, void *device_ptr);
 int hcu_memset(hcu_handle h, void *device_ptr, int value, size_t bytes);
@@ -96,9 +121,17 @@ int hcu_copy_to_host(hcu_handle h, void *host_dst, const void *device_src, size_
 /* Device-side status word of the handle: 0, or a bit set by a kernel whose
  * bounded wait gave up (1 = pipeline barrier timeout) or that found its
  * arguments inconsistent and skipped its work (2, e.g. a sequence longer than
- * hcu_attention_params.max_context).  Reading it
- * synchronises the stream.  `clear` resets it. */
+ * hcu_attention_params.max_context).  Reading it synchronises the stream.
+ * `clear` resets it and re-arms the decode-attention split tickets that a
+ * call which gave up may have left partly counted. */
 int hcu_device_status(hcu_handle h, uint32_t *status, int clear);
+
+/* Test hook for failure detection: marks every split-merge ticket of the
+ * handle's workspace as partly counted, the state a decode-attention call whose
+ * bounded wait gave up can leave behind.  hcu_device_status(h, .., clear = 1)
+ * re-arms them; until then decode attention on this handle may not merge its
+ * splits (outputs unwritten).  No kernel runs and nothing can hang. */
+int hcu_selftest_dirty_tickets(hcu_handle h);
 
 /* Single-process multi-GPU: the reference drives one GPUDevice from one Node
  * process (src/engine.ts:320), so a multi-GPU host of this library drives
@@ -112,11 +145,22 @@ int hcu_comm_create(int n, const int *devices, hcu_comm *comm);
  * (synchronise its streams first). */
 int hcu_comm_destroy(hcu_comm comm);
 
+/* Multi-process form (one process per GPU, as under torchrun): rank 0 makes
+ * an id with hcu_comm_unique_id and passes its HCU_COMM_ID_BYTES bytes to
+ * every rank over any host channel; each rank then joins with its own device
+ * (ncclCommInitRank, which returns once all `nranks` ranks have joined).  The
+ * communicator drives one local rank: hcu_allgather takes one send, receive
+ * and stream entry. */
+#define HCU_COMM_ID_BYTES 128
+int hcu_comm_unique_id(uint8_t *id);
+int hcu_comm_init_rank(int nranks, int rank, const uint8_t *id, int device, hcu_comm *comm);
+
 /* All-gather of the sharded path's per-rank outputs, the one collective of
- * the multi-GPU layout: rank i sends `bytes` from send[i] (device memory of
- * devices[i]) and receives every rank's block, rank-major, into recv[i]
- * (n * bytes).  streams[i] is a CUDA stream of devices[i] (NULL: its default
- * stream); the call enqueues and returns. */
+ * the multi-GPU layout: each rank this process drives (entry i: devices[i])
+ * sends `bytes` from send[i] and receives every rank's block, rank-major,
+ * into recv[i] (nranks * bytes).  streams[i] is a CUDA stream of that
+ * device (NULL: its default stream); the call enqueues and returns.  Every
+ * argument is checked before any rank's collective is enqueued. */
 int hcu_allgather(hcu_comm comm, void *const *send, void *const *recv, size_t bytes, void *const *streams);
 
 /* Test hook for failure detection: the next `n` op calls on this handle fail
@@ -134,6 +178,13 @@ int hcu_selftest_wait_timeout(hcu_handle h);
 /* ------------------------------------------------------------------------ */
 /* The reference's dispatch seam                                              */
 /* ------------------------------------------------------------------------ */
+
+/* Q8_0 convention of the dispatch seam's "kv_append_q8" / "attention_q8":
+ * HCU_KV_Q8_0 (the default: the JS backend's scales, amax/127) or
+ * HCU_KV_Q8_0_WGSL (the WGSL ops' scales, amax), so that a cache written by
+ * the reference's own WebGPU kv_append_q8 reads correctly here and the
+ * reverse.  Per handle. */
+int hcu_set_q8_convention(hcu_handle h, uint32_t format);
 
 /* Run the op the reference names `shader` with its uniform words and storage
  * buffers in binding order (src/engine.ts:1056-1075).  Supported names and the
@@ -163,9 +214,9 @@ int hcu_selftest_wait_timeout(hcu_handle h);
  *   "sigmoid_gate"   words [N]                                  (kernels.ts:1249)
  *                    buffers [gate f32, att f32 (gated in place)]
  *
- * Q8 scales are stored as in the JS backend (amax/127, wasm-backend.ts:815),
- * not the WGSL's amax (kernels.ts:1333); a cache written by this library is
- * read consistently by it.  Unknown names fail with
+ * Q8 scales follow the handle's convention (hcu_set_q8_convention): by
+ * default the JS backend's amax/127 (wasm-backend.ts:815), or the WGSL ops'
+ * amax (kernels.ts:1333).  Unknown names fail with
  * "hachiue: missing pipeline <name>" (src/engine.ts:1066). */
 int hcu_dispatch(hcu_handle h, const char *shader, const uint32_t words[8],
                  void *const *buffers, int n_buffers);
@@ -237,10 +288,18 @@ int hcu_attention(hcu_handle h, const hcu_attention_params *p, const float *q,
  *  - All calls share the one array (its tickets are cleared at the start of
  *    each call), so calls that overlap on the GPU race: issue them on one
  *    stream or otherwise serialise them.
- *  - Device-side wait timeouts are recorded in the array, not reported. */
+ *  - A device-side wait that gives up (the output is then invalid) sets a
+ *    status word inside the array; read it with hcu_attention_noalloc_status. */
 #define HCU_NOALLOC_SCRATCH_BYTES (8u << 20)
 int hcu_attention_noalloc(const hcu_attention_params *p, const float *q, const hcu_kv_cache *kv,
                           float *out, void *cuda_stream);
+
+/* The device status word of hcu_attention_noalloc on the current device (the
+ * bits of hcu_device_status), for callers without a handle: copies it to
+ * *status after the work queued on `cuda_stream` (NULL = default stream)
+ * completes, and with `clear` resets it.  Allocates nothing; like the entry
+ * point, it has no counterpart in the reference. */
+int hcu_attention_noalloc_status(uint32_t *status, int clear, void *cuda_stream);
 
 /* Append S rows of K or V (f32 [S, KV, Dh]) at cache row posBase in `format`.
  * For Q8_0 this is appendKvQ8 (src/wasm-backend.ts:793-824) bit for bit:
@@ -258,6 +317,13 @@ int hcu_kv_append(hcu_handle h, uint32_t S, uint32_t KV, uint32_t Dh, uint32_t p
  * dst_rows[i] must be a row of the cache. */
 int hcu_kv_append_rows(hcu_handle h, uint32_t n, uint32_t KV, uint32_t Dh, uint32_t format,
                        const float *src, const int64_t *dst_rows, void *data, float *scale);
+
+/* The K and V rows of a decode step in one launch: row i of k_src and of
+ * v_src (f32 [n, KV, Dh]) goes to cache row dst_rows[i] of kv->k and kv->v,
+ * in kv->format, with hcu_kv_append's per-row arithmetic.  The engine issues
+ * the two appends as two kv_append_q8 dispatches (src/engine.ts:1448-1449). */
+int hcu_kv_append_rows_kv(hcu_handle h, uint32_t n, uint32_t KV, uint32_t Dh, const float *k_src,
+                          const float *v_src, const int64_t *dst_rows, const hcu_kv_cache *kv);
 
 /* g = aNeg[h]*softplus(a + dtBias[h]), beta = sigmoid(b); a, b f32 [S, H];
  * out f32 [2, S, H] (g block, then beta block).  deltanet_gbeta

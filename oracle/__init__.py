@@ -57,8 +57,9 @@ def lib():
                                                       i64, i64, i32]
             L.oracle_f16_to_f64.argtypes = [ctypes.c_uint16]
             L.oracle_conv1d_causal.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32]
-            L.oracle_deltanet_norm_gate.argtypes = [vp, vp, vp, vp, i32, i32, ctypes.c_float]
-            L.oracle_rmsnorm.argtypes = [vp, vp, vp, i32, i32, ctypes.c_float, i32]
+            L.oracle_deltanet_norm_gate.argtypes = [vp, vp, vp, vp, i32, i32, ctypes.c_double]
+            L.oracle_rmsnorm.argtypes = [vp, vp, vp, i32, i32, ctypes.c_double, i32]
+            L.oracle_append_kv_q8_wgsl.argtypes = [vp, vp, vp, i32, i32, i32, i32]
             L.oracle_rope.argtypes = [vp, i32, i32, i32, i32, i32, vp, vp]
             L.oracle_sigmoid_gate.argtypes = [vp, vp, i64]
             L.oracle_f16_to_f64.restype = ctypes.c_double
@@ -72,7 +73,7 @@ def _p(a: np.ndarray):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
-KV_F32, KV_F16, KV_BF16, KV_Q8_0 = 0, 1, 2, 3
+KV_F32, KV_F16, KV_BF16, KV_Q8_0, KV_Q8_0_WGSL = 0, 1, 2, 3, 4
 
 
 def append_kv_q8(src: np.ndarray, cache_q: np.ndarray, cache_s: np.ndarray, pos_base: int) -> None:
@@ -82,6 +83,16 @@ def append_kv_q8(src: np.ndarray, cache_q: np.ndarray, cache_s: np.ndarray, pos_
     assert src.dtype == np.float32 and cache_q.dtype == np.int8 and cache_s.dtype == np.float32
     assert cache_q.shape[0] >= pos_base + S
     lib().oracle_append_kv_q8(_p(src), _p(cache_q), _p(cache_s), S, KV, Dh, pos_base)
+
+
+def append_kv_q8_wgsl(src: np.ndarray, cache_q: np.ndarray, cache_amax: np.ndarray, pos_base: int) -> None:
+    """kv_append_q8 WGSL semantics (src/kernels.ts:1287-1335): like
+    :func:`append_kv_q8` in f32 with round() ties-to-even, and the scale array
+    receives amax ((amax / 127) * 127 in f32)."""
+    S, KV, Dh = src.shape
+    assert src.dtype == np.float32 and cache_q.dtype == np.int8 and cache_amax.dtype == np.float32
+    assert cache_q.shape[0] >= pos_base + S
+    lib().oracle_append_kv_q8_wgsl(_p(src), _p(cache_q), _p(cache_amax), S, KV, Dh, pos_base)
 
 
 def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, pos_base: int, window: int = 0,
@@ -161,7 +172,9 @@ def conv1d_causal(qkv_mixed: np.ndarray, conv_w: np.ndarray, conv_state: np.ndar
 
 def deltanet_norm_gate(core: np.ndarray, z: np.ndarray, gamma: np.ndarray, eps: float) -> np.ndarray:
     """Gated RMSNorm (src/wasm-backend.ts:1104-1117): core, z f32 [rows, DV],
-    gamma f32 [DV] -> y f32 [rows, DV]."""
+    gamma f32 [DV] -> y f32 [rows, DV].  ``eps`` is added as an f64 number, as
+    the JS adds arch.rmsEps (which the GGUF loader reads with getFloat32,
+    src/gguf.ts:312,464, so it holds an f32 value)."""
     DV = gamma.shape[0]
     c = np.ascontiguousarray(core, np.float32).reshape(-1, DV)
     zz = np.ascontiguousarray(z, np.float32).reshape(-1, DV)
@@ -172,7 +185,8 @@ def deltanet_norm_gate(core: np.ndarray, z: np.ndarray, gamma: np.ndarray, eps: 
 
 
 def rmsnorm(x: np.ndarray, gamma: np.ndarray, eps: float, add_unit_offset: bool = False) -> np.ndarray:
-    """runRmsNorm (src/wasm-backend.ts:427-444) over rows of gamma's length."""
+    """runRmsNorm (src/wasm-backend.ts:427-444) over rows of gamma's length;
+    ``eps`` is added as an f64 number, like arch.rmsEps."""
     dim = gamma.shape[0]
     xx = np.ascontiguousarray(x, np.float32).reshape(-1, dim)
     y = np.zeros_like(xx)

@@ -123,6 +123,33 @@ void oracle_append_kv_q8(const float *src, int8_t *cacheQ, float *cacheS, int S,
   }
 }
 
+/* kv_append_q8 WGSL semantics (src/kernels.ts:1287-1335): f32 arithmetic,
+ * amax over the 32-element block, inv = 127/amax (0 when amax is 0), q =
+ * clamp(i32(round(v * inv)), -127, 127) with WGSL round()'s ties-to-even
+ * (rintf in the default rounding mode), and the stored scale (amax/127)*127. */
+void oracle_append_kv_q8_wgsl(const float *src, int8_t *cacheQ, float *cacheAmax, int S, int kvHeads,
+                              int headDim, int posBase) {
+  const int blocksPerToken = kvHeads * (headDim >> 5);
+  const int totalBlocks = S * blocksPerToken;
+  for (int blk = 0; blk < totalBlocks; blk++) {
+    const int s = blk / blocksPerToken;
+    const int rem = blk % blocksPerToken;
+    const long srcBase = ((long)s * blocksPerToken + rem) * 32;
+    const long dstBlk = ((long)(posBase + s)) * blocksPerToken + rem;
+    float amax = 0.0f;
+    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(src[srcBase + i]));
+    const volatile float scale = amax / 127.0f;
+    const volatile float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+    for (int i = 0; i < 32; i++) {
+      const volatile float prod = src[srcBase + i] * inv;
+      float q = rintf(prod);
+      q = q < -127.0f ? -127.0f : (q > 127.0f ? 127.0f : q);
+      cacheQ[dstBlk * 32 + i] = (int8_t)q;
+    }
+    cacheAmax[dstBlk] = scale * 127.0f;
+  }
+}
+
 /* ------------------------------------------------------------------------ */
 /* runAttentionQ8 (src/wasm-backend.ts:826-895)                               */
 /*                                                                          */
@@ -469,7 +496,7 @@ void oracle_conv1d_causal(const float *qkvMixed, const float *convW, float *conv
 /* src/kernels.ts:1578-1611).  core, z, y f32 [rows, DV]; gamma f32 [DV].    */
 /* ------------------------------------------------------------------------ */
 void oracle_deltanet_norm_gate(const float *core, const float *z, const float *gamma, float *y, int rows, int DV,
-                               float eps) {
+                               double eps) {
   for (int r = 0; r < rows; r++) {
     const long base = (long)r * DV;
     double sumSq = 0.0;
@@ -477,7 +504,7 @@ void oracle_deltanet_norm_gate(const float *core, const float *z, const float *g
       const double c = core[base + i];
       sumSq += c * c;
     }
-    const double inv = 1.0 / sqrt(sumSq / DV + (double)eps);
+    const double inv = 1.0 / sqrt(sumSq / DV + eps);
     for (int i = 0; i < DV; i++) {
       const double zz = z[base + i];
       y[base + i] = fround((double)gamma[i] * ((double)core[base + i] * inv) * (zz / (1.0 + exp(-zz))));
@@ -490,7 +517,7 @@ void oracle_deltanet_norm_gate(const float *core, const float *z, const float *g
 /* (runRmsNorm, src/wasm-backend.ts:427-444; WGSL twin rmsnorm,              */
 /* src/kernels.ts:324-355, whose addUnitOffset adds 1 to gamma).             */
 /* ------------------------------------------------------------------------ */
-void oracle_rmsnorm(const float *x, const float *gamma, float *y, int rows, int dim, float eps, int addUnitOffset) {
+void oracle_rmsnorm(const float *x, const float *gamma, float *y, int rows, int dim, double eps, int addUnitOffset) {
   for (int r = 0; r < rows; r++) {
     const long base = (long)r * dim;
     double sumSq = 0.0;
@@ -498,7 +525,7 @@ void oracle_rmsnorm(const float *x, const float *gamma, float *y, int rows, int 
       const double v = x[base + i];
       sumSq += v * v;
     }
-    const double inv = 1.0 / sqrt(sumSq / dim + (double)eps);
+    const double inv = 1.0 / sqrt(sumSq / dim + eps);
     for (int i = 0; i < dim; i++) {
       const double g = addUnitOffset ? 1.0 + (double)gamma[i] : (double)gamma[i];
       y[base + i] = fround((double)x[base + i] * inv * g);

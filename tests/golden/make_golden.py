@@ -20,6 +20,9 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 import oracle  # noqa: E402
 
+# rmsEps as the GGUF loader holds it: an f32 value (src/gguf.ts:312,464)
+EPS = float(np.float32(1e-6))
+
 
 def attention_q8_case(rng, S, H, KV, Dh, pos_base, window):
     """The engine's exact sequence for one layer and segment (src/engine.ts
@@ -152,12 +155,12 @@ def main():
         # the layer's neighbours of the recurrence (conv1d_causal, deltanet_norm_gate, and the fused step)
         "conv1d_segment": conv1d_case(rng, 5, 96, 4, True),
         "conv1d_fresh": conv1d_case(rng, 2, 64, 4, False),
-        "norm_gate": norm_gate_case(rng, 6, 128, 1e-6),
-        "gdn_layer_step": gdn_layer_case(rng, 2, 1, 2, 128, 4, True, 1e-6),
-        "gdn_layer_fresh": gdn_layer_case(rng, 1, 1, 3, 128, 4, False, 1e-6),
+        "norm_gate": norm_gate_case(rng, 6, 128, EPS),
+        "gdn_layer_step": gdn_layer_case(rng, 2, 1, 2, 128, 4, True, EPS),
+        "gdn_layer_fresh": gdn_layer_case(rng, 1, 1, 3, 128, 4, False, EPS),
         # the full-attention layer's neighbours (q/k RMSNorm, RoPE, Q8_0 append, sigmoid gate)
-        "attn_layer_qwen3": attn_layer_case(rng, 2, 8, 4, 128, 128, 40, False, 1e-6),
-        "attn_layer_qwen35": attn_layer_case(rng, 1, 4, 2, 256, 64, 30, True, 1e-6),
+        "attn_layer_qwen3": attn_layer_case(rng, 2, 8, 4, 128, 128, 40, False, EPS),
+        "attn_layer_qwen35": attn_layer_case(rng, 1, 4, 2, 256, 64, 30, True, EPS),
     }
     for name, arrays in cases.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)

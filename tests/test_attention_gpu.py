@@ -9,7 +9,7 @@ import pytest
 import torch
 
 import oracle
-from hachiue_b200 import KV_BF16, KV_F16, KV_F32, KV_Q8_0, HachiueError, workloads
+from hachiue_b200 import KV_BF16, KV_F16, KV_F32, KV_Q8_0, KV_Q8_0_WGSL, HachiueError, workloads
 from hachiue_b200.backend import KVCache
 from tests.conftest import rel_l2
 
@@ -186,14 +186,12 @@ def test_errors_are_reported(backend):
 @pytest.mark.parametrize("fmt", [KV_F16, KV_BF16])
 @pytest.mark.parametrize("H,KV,S,pos,W", [(32, 8, 1, 4000, 0), (16, 4, 3, 700, 0), (8, 2, 5, 1000, 300),
                                           (4, 4, 1, 129, 0), (16, 2, 1, 2049, 0), (12, 3, 2, 63, 17)])
-def test_tensor_core_and_cuda_core_paths(backend, monkeypatch, impl, fmt, H, KV, S, pos, W):
+def test_tensor_core_and_cuda_core_paths(backend, request, impl, fmt, H, KV, S, pos, W):
     """The tcgen05 kernel (default for f16 / bf16, Dh=128) and the CUDA-core
-    kernel (HCU_ATTN_IMPL=cuda) against the oracle: GQA groups 1-8, S > 1,
+    kernel (option attn_cuda_cores) against the oracle: GQA groups 1-8, S > 1,
     windows, tile-edge context lengths."""
-    if impl == "cuda":
-        monkeypatch.setenv("HCU_ATTN_IMPL", "cuda")
-    else:
-        monkeypatch.delenv("HCU_ATTN_IMPL", raising=False)
+    backend.set_option("attn_cuda_cores", int(impl == "cuda"))
+    request.addfinalizer(lambda: backend.set_option("attn_cuda_cores", 0))
     rng = np.random.default_rng(H + KV + S + pos + W + fmt)
     rows = pos + S
     q = rng.standard_normal((S, H, 128), dtype=np.float32)
@@ -263,4 +261,77 @@ def test_bounded_wait_reports_a_timeout(backend):
     backend.attention(T(q), cache, out, 39)
     torch.cuda.synchronize()
     assert rel_l2(out.cpu().numpy(), oracle.attention(q, k, v, 39)) < TOL
+    assert backend.device_status() == 0
+
+
+@pytest.mark.parametrize("name", ["attn_q8_decode", "attn_q8_segment", "attn_q8_swa", "attn_q8_dh256"])
+def test_q8_wgsl_convention_via_dispatch(backend, request, name):
+    """The dispatch seam in the WGSL ops' Q8_0 convention (scale array = amax,
+    src/kernels.ts:1287-1335 and :1386-1411): kv_append_q8 writes exactly what
+    the WGSL append writes (f32, round() ties-to-even), attention_q8 over that
+    cache matches both the WGSL-semantics oracle and runAttentionQ8 on the
+    same int8 values, and a cache the reference's WGSL append wrote (here its
+    restatement, on the CPU) reads correctly."""
+    backend.set_q8_convention(KV_Q8_0_WGSL)
+    request.addfinalizer(lambda: backend.set_q8_convention(KV_Q8_0))
+    d = g(name)
+    S, H, KV, Dh, pos, W = (int(x) for x in d["meta"])
+    rows = pos + S
+    nb = Dh // 32
+    kq_ref, vq_ref = np.zeros((rows, KV, Dh), np.int8), np.zeros((rows, KV, Dh), np.int8)
+    ka_ref, va_ref = np.zeros((rows, KV, nb), np.float32), np.zeros((rows, KV, nb), np.float32)
+    cache = KVCache.allocate(rows, KV, Dh, KV_Q8_0_WGSL)
+    kf, vf = T(d["k"]), T(d["v"])
+    for lo, hi in ((0, pos), (pos, rows)):
+        if hi > lo:
+            for src, q8, sc in ((kf, cache.k, cache.k_scale), (vf, cache.v, cache.v_scale)):
+                backend.dispatch("kv_append_q8", [hi - lo, KV, Dh, lo], [src[lo:hi].contiguous(), q8, sc])
+            oracle.append_kv_q8_wgsl(np.ascontiguousarray(d["k"][lo:hi]), kq_ref, ka_ref, lo)
+            oracle.append_kv_q8_wgsl(np.ascontiguousarray(d["v"][lo:hi]), vq_ref, va_ref, lo)
+    out = torch.zeros((S, H, Dh), device=dev)
+    q = d["q"]
+    backend.dispatch("attention_q8", [S, H, KV, Dh, pos, W, 0, 0],
+                     [T(q), cache.k, cache.k_scale, cache.v, cache.v_scale, out])
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(cache.k.cpu().numpy(), kq_ref)
+    np.testing.assert_array_equal(cache.k_scale.cpu().numpy(), ka_ref)
+    np.testing.assert_array_equal(cache.v.cpu().numpy(), vq_ref)
+    np.testing.assert_array_equal(cache.v_scale.cpu().numpy(), va_ref)
+    ref_wgsl = oracle.attention_q8_wgsl(q, kq_ref, ka_ref, vq_ref, va_ref, pos, W)
+    ref_js = oracle.attention(q, kq_ref, vq_ref, pos, W, KV_Q8_0, ka_ref / np.float32(127), va_ref / np.float32(127))
+    got = out.cpu().numpy()
+    assert rel_l2(got, ref_wgsl) < TOL
+    assert rel_l2(got, ref_js) < TOL
+    # a cache written by the reference's WGSL append, read through the seam
+    oc = KVCache(KV_Q8_0_WGSL, T(kq_ref), T(vq_ref), T(ka_ref), T(va_ref))
+    out2 = torch.zeros_like(out)
+    backend.dispatch("attention_q8", [S, H, KV, Dh, pos, W, 0, 0], [T(q), oc.k, oc.k_scale, oc.v, oc.v_scale, out2])
+    torch.cuda.synchronize()
+    assert rel_l2(out2.cpu().numpy(), ref_wgsl) < TOL
+    assert backend.device_status() == 0
+
+
+def test_dirty_tickets_are_rearmed_by_a_status_clear(backend):
+    """Split tickets left partly counted, as by a call whose bounded wait gave
+    up, keep every split of a unit from merging (its output stays unwritten);
+    hcu_device_status(clear) re-arms them and the next call matches the
+    oracle."""
+    rng = np.random.default_rng(41)
+    pos, H, KV = 6000, 8, 2  # one sequence, 2 units of many splits
+    q = rng.standard_normal((1, H, 128), dtype=np.float32)
+    k = rng.standard_normal((pos + 1, KV, 128), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((pos + 1, KV, 128), dtype=np.float32).astype(np.float16)
+    cache = KVCache(KV_F16, T(k.view(np.int16), torch.float16), T(v.view(np.int16), torch.float16))
+    assert backend.device_status() == 0
+    backend.selftest_dirty_tickets()
+    out = torch.full((1, H, 128), float("nan"), device=dev)
+    backend.attention(T(q), cache, out, pos)
+    torch.cuda.synchronize()
+    assert np.isnan(out.cpu().numpy()).all()  # no unit drew its last ticket
+    assert backend.device_status(clear=True) == 0  # no timeout was recorded; the clear re-arms the tickets
+    out.fill_(float("nan"))
+    backend.attention(T(q), cache, out, pos)
+    torch.cuda.synchronize()
+    ref = oracle.attention(q, k.view(np.uint16), v.view(np.uint16), pos, 0, KV_F16)
+    assert rel_l2(out.cpu().numpy(), ref) < TOL
     assert backend.device_status() == 0

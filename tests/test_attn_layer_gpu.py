@@ -93,7 +93,7 @@ def test_layer_step_q8_against_the_oracle(backend, S, H, KV, Dh, rot, pos, split
         oracle.append_kv_q8(hist_k, kq, ks, 0)
         oracle.append_kv_q8(hist_v, vq, vs, 0)
     cos, sin = oracle.rope_tables(rot, rows, 1e6)
-    eps = 1e-6
+    eps = float(np.float32(1e-6))  # GGUF stores rmsEps as f32 (src/gguf.ts:312,464)
     qd = d["q"][..., :Dh] if split else d["q"]
     gate = d["q"][..., Dh:] if split else None
     cache = KVCache(KV_Q8_0, T(kq), T(vq), T(ks), T(vs))

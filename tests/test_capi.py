@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_version_and_no_error(lib):
-    assert lib.hcu_version() == 2
+    assert lib.hcu_version() == 3
     assert lib.hcu_last_error() == b""
 
 

@@ -26,7 +26,7 @@ def T(x):
 def test_hybrid_decode_loop(backend):
     rng = np.random.default_rng(31)
     NK, NV, D, K = 2, 4, 128, 4
-    H, KVH, Dh, rot, eps = 4, 2, 128, 64, 1e-6
+    H, KVH, Dh, rot, eps = 4, 2, 128, 64, float(np.float32(1e-6))  # an f32 value, as GGUF stores it
     arch = ModelArch("qwen35", 4, H, KVH, Dh, eps, rot, 64,
                      hybrid=HybridLayerConfig(hybrid_layer_types(4, 4), NK, NV, D, K))
     st = LayerStates(arch, max_seq_len=16, kv_format=KV_Q8_0)

@@ -119,10 +119,11 @@ def test_cfg5_qwen35_chunked_prefill(backend, cfg5):
         assert rel_l2(st[b, h], rs) < REL
 
 
-def test_slabs_carry_the_state(backend, monkeypatch):
+def test_slabs_carry_the_state(backend, request):
     """A scratch budget of 1 MiB splits 64 chunks into slabs (one prep + chain
     launch pair each); the state crosses slab boundaries through state_out."""
-    monkeypatch.setenv("HCU_GDN_SCRATCH_MB", "1")
+    backend.set_option("gdn_scratch_mb", 1)
+    request.addfinalizer(lambda: backend.set_option("gdn_scratch_mb", 0))
     rng = np.random.default_rng(7)
     B, T, NK, NV = 1, 4096, 1, 2
     qb, kb, vb, g, beta = make_inputs(rng, B, T, NK, NV, 0.05)

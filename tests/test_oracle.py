@@ -279,3 +279,39 @@ def test_rmsnorm_rope_gate_match_closed_forms():
     gate = rng.standard_normal(x.shape, dtype=np.float32)
     np.testing.assert_allclose(oracle.sigmoid_gate(gate, x), x64 / (1 + np.exp(-gate.astype(np.float64))),
                                rtol=1e-6, atol=1e-6)
+
+
+def test_wgsl_q8_append_known_answers():
+    """kv_append_q8's WGSL semantics (src/kernels.ts:1318-1333): round() ties
+    to even where the JS Math.round goes up; the scale array holds
+    (amax/127)*127 in f32; an all-zero block stores scale 0 and zeros."""
+    src = np.zeros((1, 2, 32), np.float32)
+    src[0, 0, :4] = [2.5, -2.5, 3.5, 127.0]  # amax 127 -> inv 1: the products are the values themselves
+    qw, aw = np.zeros((1, 2, 32), np.int8), np.zeros((1, 2, 1), np.float32)
+    qj, sj = np.zeros((1, 2, 32), np.int8), np.zeros((1, 2, 1), np.float32)
+    oracle.append_kv_q8_wgsl(src, qw, aw, 0)
+    oracle.append_kv_q8(src, qj, sj, 0)
+    assert list(qw[0, 0, :4]) == [2, -2, 4, 127]
+    assert list(qj[0, 0, :4]) == [3, -2, 4, 127]
+    assert aw[0, 0, 0] == np.float32(np.float32(127.0) / np.float32(127.0)) * np.float32(127.0)
+    assert sj[0, 0, 0] == np.float32(1.0)
+    assert (qw[0, 1] == 0).all() and aw[0, 1, 0] == 0
+
+
+def test_wgsl_and_js_q8_conventions_agree():
+    """On random rows both conventions store the same int8 values up to a
+    rare tie or last-bit difference, and their attention outputs agree."""
+    rng = np.random.default_rng(5)
+    rows, KV, Dh, H = 300, 2, 128, 4
+    x = rng.standard_normal((rows, KV, Dh), dtype=np.float32)
+    qw, aw = np.zeros((rows, KV, Dh), np.int8), np.zeros((rows, KV, Dh // 32), np.float32)
+    qj, sj = np.zeros_like(qw), np.zeros_like(aw)
+    oracle.append_kv_q8_wgsl(x, qw, aw, 0)
+    oracle.append_kv_q8(x, qj, sj, 0)
+    diff = np.abs(qw.astype(np.int32) - qj.astype(np.int32))
+    assert diff.max() <= 1 and (diff > 0).mean() < 1e-3
+    np.testing.assert_allclose(aw / 127.0, sj, rtol=1e-6)
+    q = rng.standard_normal((1, H, Dh), dtype=np.float32)
+    a = oracle.attention_q8_wgsl(q, qw, aw, qw, aw, rows - 1)
+    b = oracle.attention(q, qw, qw, rows - 1, 0, oracle.KV_Q8_0, aw / np.float32(127), aw / np.float32(127))
+    assert np.linalg.norm(a - b) / np.linalg.norm(b) < 1e-5

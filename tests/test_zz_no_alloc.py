@@ -5,8 +5,10 @@ reserves its whole HBM budget in its own pool, or a plugin behind a stateless
 FFI call that cannot keep a handle (creating one allocates a workspace).  The
 entry point takes no handle and uses a fixed-size static device array as its
 split-K scratch.  This test calls it through the C ABI and checks it against
-the allocating entry point (hcu_attention) on two calls in a row, for the
-tensor-core path (f16 cache) and the CUDA-core path (f32 cache), then checks
+the allocating entry point (hcu_attention) and against the oracle
+(runAttentionQ8's restatement) on two calls in a row, for the tensor-core path
+(f16 cache) and the CUDA-core path (f32 cache); checks that its status word,
+the only failure report such a caller has, reads 0 and clears; then checks
 that an oversized call is refused with a clear error.  It is collected last so
 a failure here never hides the other tests' results.
 """
@@ -16,6 +18,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle
 from hachiue_b200 import KV_F16, KV_F32, CudaBackend, HachiueError, _lib
 from hachiue_b200.backend import KVCache
 from tests.conftest import rel_l2
@@ -66,6 +69,13 @@ def test_noalloc_matches_hcu_attention_twice(fmt):
     ref_np = ref.cpu().numpy()
     be.close()
 
+    if fmt == KV_F16:
+        kc, vc, ofmt = kf.astype(np.float16).view(np.uint16), vf.astype(np.float16).view(np.uint16), oracle.KV_F16
+    else:
+        kc, vc, ofmt = kf, vf, oracle.KV_F32
+    want = oracle.attention_batch(q.cpu().numpy(), kc, vc, lens - 1, off, 0, ofmt)
+    assert rel_l2(ref_np, want) < TOL
+
     p = _params(q, pos, roff, maxc, KV)
     for _ in range(2):
         out = torch.full_like(q, float("nan"))
@@ -74,6 +84,23 @@ def test_noalloc_matches_hcu_attention_twice(fmt):
         got = out.cpu().numpy()
         assert np.isfinite(got).all()
         assert rel_l2(got, ref_np) < TOL
+        assert rel_l2(got, want) < TOL
+        assert _status(clear=False) == 0
+
+
+def _status(clear: bool) -> int:
+    lib = _lib.load()
+    st = ctypes.c_uint32(0xFFFFFFFF)
+    _lib.check(lib.hcu_attention_noalloc_status(ctypes.byref(st), int(clear),
+                                                ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    return st.value
+
+
+def test_noalloc_status_word_reads_and_clears():
+    """The handle-free status word: 0 after good calls, and a clear leaves it 0."""
+    torch.zeros(1, device="cuda")  # a context on the current device
+    assert _status(clear=True) == 0
+    assert _status(clear=False) == 0
 
 
 def test_noalloc_refuses_oversized_calls():
