@@ -928,7 +928,7 @@ def cpu_entry(cfg, W, budget_s):
                              "oracle/ is timed)"}
 
 
-def strong_scaling(torch, dist, be, comm, args, world, rank, dev, W2):
+def strong_scaling(torch, dist, be, comm, comm_bulk, args, world, rank, dev, W2):
     """One configuration's fixed work split over the job's GPUs: cfg2 by KV
     head (reusing the headline's device inputs) and cfg5 by QK head.  Each
     step is the local kernels plus the all-gather of the per-head outputs
@@ -1003,7 +1003,7 @@ def strong_scaling(torch, dist, be, comm, args, world, rank, dev, W2):
         be.deltanet_chunked_prefill(ql, kl, vl, gl, bl, core_l, st_l)
         if ev:
             ev[1].record(stream)
-        comm.all_gather(core_l, recv5)
+        comm_bulk.all_gather(core_l, recv5)
         if ev:
             ev[2].record(stream)
 
@@ -1043,7 +1043,8 @@ def main(argv=None):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
         from hachiue_b200.dist import RankComm
-        comm = RankComm(local)
+        comm = RankComm(local, max_ctas=4)  # per-step gathers of about 1 MB that overlap the next step
+        comm_bulk = RankComm(local)  # the strong-scaling gathers of whole outputs
 
     from hachiue_b200 import CudaBackend
     be = CudaBackend(local)
@@ -1106,7 +1107,8 @@ def main(argv=None):
     line.update(head)
 
     if world > 1:
-        line["strong"] = strong_scaling(torch, dist, be, comm, args, world, rank, dev, W) if args.config == "2" else None
+        line["strong"] = (strong_scaling(torch, dist, be, comm, comm_bulk, args, world, rank, dev, W)
+                          if args.config == "2" else None)
     del W
     torch.cuda.empty_cache()
 
@@ -1129,6 +1131,7 @@ def main(argv=None):
     be.close()
     if world > 1:
         comm.close()
+        comm_bulk.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -162,7 +162,7 @@ def load(path: str | None = None):
             "hcu_set_q8_convention": ([vp, u32], i32),
             "hcu_set_option": ([vp, i32, ctypes.c_int64], i32),
             "hcu_comm_unique_id": ([ctypes.POINTER(ctypes.c_uint8)], i32),
-            "hcu_comm_init_rank": ([i32, i32, ctypes.POINTER(ctypes.c_uint8), i32, ctypes.POINTER(vp)], i32),
+            "hcu_comm_init_rank": ([i32, i32, ctypes.POINTER(ctypes.c_uint8), i32, i32, ctypes.POINTER(vp)], i32),
             "hcu_kv_append_rows_kv": ([vp, u32, u32, u32, vp, vp, vp, ctypes.POINTER(hcu_kv_cache)], i32),
         }
         for name, (args, res) in sig.items():

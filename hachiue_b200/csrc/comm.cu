@@ -32,6 +32,7 @@ using hcu::fail;
 struct NcclApi {
   decltype(&ncclCommInitAll) init_all = nullptr;
   decltype(&ncclCommInitRank) init_rank = nullptr;
+  decltype(&ncclCommInitRankConfig) init_rank_config = nullptr;
   decltype(&ncclGetUniqueId) unique_id = nullptr;
   decltype(&ncclCommDestroy) destroy = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
@@ -49,14 +50,15 @@ const NcclApi& nccl() {
     if (!lib) return;
     api.init_all = reinterpret_cast<decltype(api.init_all)>(dlsym(lib, "ncclCommInitAll"));
     api.init_rank = reinterpret_cast<decltype(api.init_rank)>(dlsym(lib, "ncclCommInitRank"));
+    api.init_rank_config = reinterpret_cast<decltype(api.init_rank_config)>(dlsym(lib, "ncclCommInitRankConfig"));
     api.unique_id = reinterpret_cast<decltype(api.unique_id)>(dlsym(lib, "ncclGetUniqueId"));
     api.destroy = reinterpret_cast<decltype(api.destroy)>(dlsym(lib, "ncclCommDestroy"));
     api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(lib, "ncclAllGather"));
     api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(lib, "ncclGroupStart"));
     api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(lib, "ncclGroupEnd"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(lib, "ncclGetErrorString"));
-    api.ok = api.init_all && api.init_rank && api.unique_id && api.destroy && api.all_gather && api.group_start &&
-             api.group_end && api.error_string;
+    api.ok = api.init_all && api.init_rank && api.init_rank_config && api.unique_id && api.destroy &&
+             api.all_gather && api.group_start && api.group_end && api.error_string;
   });
   return api;
 }
@@ -108,7 +110,8 @@ extern "C" int hcu_comm_unique_id(uint8_t* id) {
   return HCU_OK;
 }
 
-extern "C" int hcu_comm_init_rank(int nranks, int rank, const uint8_t* id, int device, hcu_comm* comm) {
+extern "C" int hcu_comm_init_rank(int nranks, int rank, const uint8_t* id, int device, int max_ctas,
+                                  hcu_comm* comm) {
   if (!comm || !id) return fail(HCU_EINVAL, "hcu_comm_init_rank: null argument");
   *comm = nullptr;
   if (nranks < 1 || rank < 0 || rank >= nranks)
@@ -116,6 +119,7 @@ extern "C" int hcu_comm_init_rank(int nranks, int rank, const uint8_t* id, int d
   int count = 0;
   HCU_TRY(hcu::check_cuda(cudaGetDeviceCount(&count), "hcu_comm_init_rank: cudaGetDeviceCount"));
   if (device < 0 || device >= count) return fail(HCU_EINVAL, "hcu_comm_init_rank: device %d of %d", device, count);
+  if (max_ctas < 0) return fail(HCU_EINVAL, "hcu_comm_init_rank: max_ctas %d", max_ctas);
   const NcclApi& api = nccl();
   if (!api.ok) return fail(HCU_ENCCL, "hcu_comm_init_rank: libnccl.so.2 could not be opened");
   HCU_TRY(hcu::check_cuda(cudaSetDevice(device), "hcu_comm_init_rank: cudaSetDevice"));
@@ -126,7 +130,19 @@ extern "C" int hcu_comm_init_rank(int nranks, int rank, const uint8_t* id, int d
   c->devices[0] = device;
   ncclUniqueId uid;
   memcpy(&uid, id, sizeof(uid));
-  const int st = check_nccl(api.init_rank(&c->comms[0], nranks, uid, rank), "hcu_comm_init_rank: ncclCommInitRank");
+  int st;
+  if (max_ctas > 0) {
+    // Collectives of this communicator occupy at most max_ctas SMs: the path's
+    // per-step all-gathers are small and overlap the next step's kernels,
+    // which need the SMs more than the gather needs channels.
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.minCTAs = 1;
+    cfg.maxCTAs = max_ctas;
+    st = check_nccl(api.init_rank_config(&c->comms[0], nranks, uid, rank, &cfg),
+                    "hcu_comm_init_rank: ncclCommInitRankConfig");
+  } else {
+    st = check_nccl(api.init_rank(&c->comms[0], nranks, uid, rank), "hcu_comm_init_rank: ncclCommInitRank");
+  }
   if (st != HCU_OK) {
     delete c;
     return st;

@@ -234,7 +234,9 @@ class RankComm:
     (hcu_comm_init_rank).  ``all_gather`` enqueues hcu_allgather on the
     device's current torch stream."""
 
-    def __init__(self, device: int, group=None):
+    def __init__(self, device: int, group=None, max_ctas: int = 0):
+        """``max_ctas`` > 0 caps the SMs the gathers occupy (small per-step
+        gathers overlapping the next step's kernels); 0 is NCCL's choice."""
         import ctypes
         from . import _lib
         self._ct, self._lib, self.lib = ctypes, _lib, _lib.load()
@@ -247,7 +249,8 @@ class RankComm:
         dist.broadcast(t, src=0, group=group)
         uid = (ctypes.c_uint8 * _lib.COMM_ID_BYTES)(*t.cpu().tolist())
         h = ctypes.c_void_p()
-        _lib.check(self.lib.hcu_comm_init_rank(self.world, self.rank, uid, self.device, ctypes.byref(h)))
+        _lib.check(self.lib.hcu_comm_init_rank(self.world, self.rank, uid, self.device, int(max_ctas),
+                                               ctypes.byref(h)))
         self._c = h
 
     def all_gather(self, send: torch.Tensor, recv: torch.Tensor) -> None:

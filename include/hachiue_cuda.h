@@ -148,12 +148,14 @@ int hcu_comm_destroy(hcu_comm comm);
 /* Multi-process form (one process per GPU, as under torchrun): rank 0 makes
  * an id with hcu_comm_unique_id and passes its HCU_COMM_ID_BYTES bytes to
  * every rank over any host channel; each rank then joins with its own device
- * (ncclCommInitRank, which returns once all `nranks` ranks have joined).  The
- * communicator drives one local rank: hcu_allgather takes one send, receive
- * and stream entry. */
+ * (ncclCommInitRank, which returns once all `nranks` ranks have joined).
+ * max_ctas > 0 caps the SMs its collectives occupy (ncclConfig_t.maxCTAs),
+ * for small gathers that overlap the next step's kernels; 0 leaves NCCL's
+ * choice.  The communicator drives one local rank: hcu_allgather takes one
+ * send, receive and stream entry. */
 #define HCU_COMM_ID_BYTES 128
 int hcu_comm_unique_id(uint8_t *id);
-int hcu_comm_init_rank(int nranks, int rank, const uint8_t *id, int device, hcu_comm *comm);
+int hcu_comm_init_rank(int nranks, int rank, const uint8_t *id, int device, int max_ctas, hcu_comm *comm);
 
 /* All-gather of the sharded path's per-rank outputs, the one collective of
  * the multi-GPU layout: each rank this process drives (entry i: devices[i])
