@@ -165,6 +165,9 @@ __device__ void ticket_merge(const AttnArgs& a, const AttnUnit& u, int tid, int 
 int launch_attn_tc(hcu_context* h, int fmt, int R, const AttnArgs& args, dim3 grid, const CUtensorMap& tk,
                    const CUtensorMap& tv);
 bool attn_tc_supported(int fmt, int Dh, int R);
+// Host launcher of the Q8_0 tcgen05 kernel (attention_decode_q8tc.cu): R <= 4.
+int launch_attn_q8tc(hcu_context* h, int R, const AttnArgs& args, dim3 grid, const CUtensorMap& tk,
+                     const CUtensorMap& tv, const CUtensorMap& tks, const CUtensorMap& tvs);
 constexpr int kTcTile = 128;  // tokens per tcgen05 tile
 
 }  // namespace hcu

@@ -482,11 +482,12 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   if (reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
     return fail(HCU_EINVAL, "hcu_attention: q and out must be 16-byte aligned");
   const int G = H / KV;
-  // The tcgen05 kernel serves f16 / bf16 caches with Dh = 128; every other
-  // combination (and HCU_OPT_ATTN_CUDA_CORES) uses the CUDA-core kernel.
+  // The tcgen05 kernels serve f16 / bf16 (attention_decode_tc.cu) and Q8_0
+  // (attention_decode_q8tc.cu) caches with Dh = 128; every other combination
+  // (and HCU_OPT_ATTN_CUDA_CORES) uses the CUDA-core kernel.
   const bool force_cuda = h->opt_attn_cuda_cores != 0;
   const int rmax_cuda = Dh == 128 ? 16 : 8;
-  const int rmax_tc = fmt == HCU_KV_F16 ? 16 : 8;
+  const int rmax_tc = fmt == HCU_KV_F16 ? 16 : (fmt == HCU_KV_Q8_0 ? 4 : 8);
   bool use_tc = !force_cuda && hcu::attn_tc_supported(fmt, Dh, G);
   const int rmax = use_tc ? rmax_tc : rmax_cuda;
   if (G > rmax) return fail(HCU_EUNSUPPORTED, "hcu_attention: group size %d > %d", G, rmax);
@@ -551,7 +552,8 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   {
     uint64_t dims[3] = {(uint64_t)Dh, (uint64_t)KV, (uint64_t)kv->rows};
     uint64_t strides[2] = {(uint64_t)Dh * es, (uint64_t)KV * Dh * es};
-    uint32_t box[3] = {use_tc ? 64u : (uint32_t)Dh, 1u, (uint32_t)TT};
+    // 128-byte boxes for the tensor cores: 64 16-bit or 128 8-bit elements
+    uint32_t box[3] = {use_tc ? (fmt == HCU_KV_Q8_0 ? 128u : 64u) : (uint32_t)Dh, 1u, (uint32_t)TT};
     const CUtensorMapSwizzle sw = use_tc ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
     HCU_TRY(hcu::make_tensor_map(&tk, dt, 3, kv->k, dims, strides, box, sw));
     HCU_TRY(hcu::make_tensor_map(&tv, dt, 3, kv->v, dims, strides, box, sw));
@@ -592,6 +594,7 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   args.gate = p->gate;
   args.q8_smul = q8_wgsl ? 1.f / 127.f : 1.f;
   dim3 grid((unsigned)max_splits, (unsigned)KV, (unsigned)(batch * nqb));
+  if (use_tc && fmt == HCU_KV_Q8_0) return hcu::launch_attn_q8tc(h, R, args, grid, tk, tv, tks, tvs);
   if (use_tc) return hcu::launch_attn_tc(h, fmt, R, args, grid, tk, tv);
   switch (fmt) {
     case HCU_KV_F32: return launch_d<HCU_KV_F32>(h, Dh, R, args, grid, tk, tv, tks, tvs);

@@ -417,6 +417,7 @@ bool attn_tc_supported(int fmt, int Dh, int R) {
   if (Dh != TC_DH) return false;
   if (fmt == HCU_KV_F16) return R <= 16;
   if (fmt == HCU_KV_BF16) return R <= 8;
+  if (fmt == HCU_KV_Q8_0) return R <= 4;  // attention_decode_q8tc.cu
   return false;
 }
 

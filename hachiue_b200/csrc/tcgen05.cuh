@@ -1,6 +1,6 @@
 // tcgen05.cuh - 5th-generation tensor core (tcgen05 / TMEM) helpers, sm_100a.
 //
-// Shared-memory matrix descriptors, the kind::f16 instruction descriptor, TMEM
+// Shared-memory matrix descriptors, the kind::f16 / tf32 / i8 instruction descriptors, TMEM
 // allocation, MMA issue / commit and TMEM loads, as inline PTX.  Field layouts
 // follow the PTX ISA's tcgen05 "matrix descriptor" and "instruction descriptor"
 // tables (the same layouts CUTLASS's cute/arch/mma_sm100_desc.hpp encodes).
@@ -46,6 +46,15 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn_major,
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// kind::i8 instruction descriptor: s32 accumulate, signed int8 A and B, M x N.
+// MN-major is valid for 8-bit operands (as for f16 / bf16 / tf32).
+__host__ __device__ constexpr uint32_t idesc_s8(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (2u << 4)                                   // D format: s32
+         | (1u << 7) | (1u << 10)                    // A, B: signed 8-bit
+         | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16)
+         | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 // Byte offset of (row, byte_in_row) inside a 128B-swizzled region whose rows
 // are 128 B and whose base is 1024-B aligned (16-byte chunk index XOR row % 8).
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t byte_in_row) {
@@ -80,6 +89,18 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem], kind::i8 (K = 32 per instruction, s32
+// accumulate, exact), issued by one thread.
+__device__ __forceinline__ void mma_s8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

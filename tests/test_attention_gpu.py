@@ -335,3 +335,66 @@ def test_dirty_tickets_are_rearmed_by_a_status_clear(backend):
     ref = oracle.attention(q, k.view(np.uint16), v.view(np.uint16), pos, 0, KV_F16)
     assert rel_l2(out.cpu().numpy(), ref) < TOL
     assert backend.device_status() == 0
+
+
+@pytest.mark.parametrize("impl", ["tc", "cuda"])
+@pytest.mark.parametrize("H,KV,S,pos,W,vscale", [(32, 8, 1, 4000, 0, 1.0), (16, 8, 1, 1023, 0, 1.0),
+                                                 (8, 8, 1, 128, 0, 1.0), (16, 4, 3, 700, 0, 1.0),
+                                                 (8, 2, 5, 1000, 300, 1.0), (4, 2, 8, 129, 0, 1.0),
+                                                 (12, 3, 2, 63, 17, 1.0), (16, 8, 1, 6000, 0, 1e-5),
+                                                 (16, 8, 1, 3000, 0, 3e4), (8, 4, 2, 255, 1, 1.0)])
+def test_q8_tensor_core_and_cuda_core_paths(backend, request, impl, H, KV, S, pos, W, vscale):
+    """Q8_0 caches on the int8 tensor-core kernel (default for GQA groups up to
+    4 with Dh 128) and on the CUDA-core kernel, against runAttentionQ8: groups
+    1-4, S > 1, windows (1 included), tile-edge and multi-split contexts, and
+    rows whose magnitudes (hence block scales) vary by 10^3 within a tile, for
+    V values of scale 1e-5 to 3e4."""
+    backend.set_option("attn_cuda_cores", int(impl == "cuda"))
+    request.addfinalizer(lambda: backend.set_option("attn_cuda_cores", 0))
+    rng = np.random.default_rng(H * 7 + KV + S + pos + W)
+    rows = pos + S
+    q = rng.standard_normal((S, H, 128), dtype=np.float32)
+    mag = np.exp(rng.uniform(-3.5, 3.5, (rows, KV, 4))).astype(np.float32).repeat(32, axis=2)
+    kf = rng.standard_normal((rows, KV, 128), dtype=np.float32) * mag
+    vf = (rng.standard_normal((rows, KV, 128), dtype=np.float32) * mag[:, ::-1] * np.float32(vscale)).astype(np.float32)
+    cache = KVCache.allocate(rows, KV, 128, KV_Q8_0)
+    backend.kv_append(T(kf), cache, "k", 0)
+    backend.kv_append(T(np.ascontiguousarray(vf)), cache, "v", 0)
+    out = torch.full((S, H, 128), float("nan"), device=dev)
+    backend.attention(T(q), cache, out, pos, W)
+    torch.cuda.synchronize()
+    kq, vq = cache.k.cpu().numpy(), cache.v.cpu().numpy()
+    ks, vs = cache.k_scale.cpu().numpy(), cache.v_scale.cpu().numpy()
+    ref = oracle.attention(q, kq, vq, pos, W, KV_Q8_0, ks, vs)
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_l2(got, ref) < TOL
+    assert backend.device_status() == 0
+
+
+@pytest.mark.parametrize("impl", ["tc", "cuda"])
+def test_q8_batched_ragged_sequences(backend, request, impl):
+    """cfg2's layout on a Q8_0 cache: a packed batch of ragged sequences with
+    per-sequence positions and row offsets, H = 32, KV = 8."""
+    backend.set_option("attn_cuda_cores", int(impl == "cuda"))
+    request.addfinalizer(lambda: backend.set_option("attn_cuda_cores", 0))
+    rng = np.random.default_rng(77)
+    lens = np.array([1, 127, 128, 129, 700, 4096, 8045, 2049])
+    off = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    B, H, KV = len(lens), 32, 8
+    kf = rng.standard_normal((lens.sum(), KV, 128), dtype=np.float32)
+    vf = rng.standard_normal((lens.sum(), KV, 128), dtype=np.float32)
+    cache = KVCache.allocate(int(lens.sum()), KV, 128, KV_Q8_0)
+    backend.kv_append(T(kf), cache, "k", 0)
+    backend.kv_append(T(vf), cache, "v", 0)
+    q = rng.standard_normal((B, 1, H, 128), dtype=np.float32)
+    out = torch.full((B, 1, H, 128), float("nan"), device=dev)
+    backend.attention(T(q), cache, out, T((lens - 1).astype(np.int32)), 0, kv_row_offset=T(off.astype(np.int64)),
+                      max_context=int(lens.max()))
+    torch.cuda.synchronize()
+    ref = oracle.attention_batch(q, cache.k.cpu().numpy(), cache.v.cpu().numpy(), lens - 1, off, 0, KV_Q8_0,
+                                 cache.k_scale.cpu().numpy(), cache.v_scale.cpu().numpy())
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_l2(got, ref) < TOL
+    assert backend.device_status() == 0
