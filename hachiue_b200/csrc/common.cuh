@@ -99,6 +99,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   }
 }
 
+// Bounded wait without the suspend hint, for a single issuing thread whose
+// latency from the phase completing to its next instruction matters (an MMA
+// issuer): the plain try_wait returns as soon as the phase completes.  The
+// clock is read every 64 polls.
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((n & 63) == 0 && globaltimer() - t0 > HCU_WAIT_NS) {
+      if (status) atomicOr(status, HCU_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // Untiled bulk copy of `bytes` (a multiple of 16, both addresses 16-byte
 // aligned) from global memory into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -225,6 +241,30 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+// 2^x and 1/x on the SFU (approximate: ~2 ulp; subnormal results flush to 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Warp maxima with one redux.sync instead of a shuffle tree: floats mapped to
+// integers of the same order (negative values with their magnitude bits
+// flipped), reduced as integers, mapped back.  Not for NaN inputs.
+__device__ __forceinline__ float warp_max_redux(float v) {
+  const int b = __float_as_int(v);
+  const int key = __reduce_max_sync(0xffffffffu, b >= 0 ? b : (b ^ 0x7fffffff));
+  return __int_as_float(key >= 0 ? key : (key ^ 0x7fffffff));
+}
+// The same for values known to be >= 0 (their bit patterns order as integers).
+__device__ __forceinline__ float warp_max_nonneg(float v) {
+  return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
 }
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -27,6 +27,19 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// The same for a 64-byte-swizzled operand (layout code 4).  MN-major with
+// 8-bit elements: rows of 64 B along M/N (one swizzle atom), rows along K;
+// sbo = byte distance between 8-row K groups (512 for dense 64-B rows).
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version (sm_100)
+  d |= (uint64_t)4u << 61;  // layout: SWIZZLE_64B
+  return d;
+}
+
 // kind::f16 instruction descriptor: f32 accumulate, f16 or bf16 A/B, M x N.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a_mn_major, bool b_mn_major) {
   return (1u << 4)                                   // D format: f32
@@ -46,11 +59,14 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn_major,
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-// kind::i8 instruction descriptor: s32 accumulate, signed int8 A and B, M x N.
+// kind::i8 instruction descriptor: s32 accumulate, signed int8 A, M x N.
 // MN-major is valid for 8-bit operands (as for f16 / bf16 / tf32).
-__host__ __device__ constexpr uint32_t idesc_s8(int M, int N, bool a_mn_major, bool b_mn_major) {
+// b_unsigned selects an unsigned 8-bit B operand (A stays signed).
+__host__ __device__ constexpr uint32_t idesc_s8(int M, int N, bool a_mn_major, bool b_mn_major,
+                                               bool b_unsigned = false) {
   return (2u << 4)                                   // D format: s32
-         | (1u << 7) | (1u << 10)                    // A, B: signed 8-bit
+         | (1u << 7)                                 // A: signed 8-bit
+         | ((b_unsigned ? 0u : 1u) << 10)            // B: signed or unsigned 8-bit
          | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16)
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
@@ -168,6 +184,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 8 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
 
 // 32 consecutive columns of this thread's lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
