@@ -45,7 +45,6 @@ constexpr int TILE = 2 * BOX;                 // [128 x 128] bf16 tile
 constexpr int KV_STAGES = 2;
 constexpr int KV_STAGE = 2 * TILE;            // K tile + V tile
 constexpr float RESCALE_LOG2 = 8.f;
-constexpr int kSwaPolyPairs = 0;  // of every 8 column pairs, exponentials on the FMA pipe
 
 struct SwaArgs {
   int B, T, H, KV, W, G, nqt;
@@ -126,34 +125,9 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   return d;
 }
 
-// 2^x for two values on the FMA pipe, so that part of the exponentials
-// bypasses the SFU (16 results per clock per SM, the softmax's bottleneck).
-// x = j + f with j = round(x) (adding 1.5 * 2^23 rounds to nearest and leaves
-// j in the low mantissa bits), 2^f from a cubic in f on [-0.5, 0.5] fitted
-// for least maximum relative error (7.5e-5, far below the 2^-9 of the bf16
-// that P is rounded to), and 2^j added into the exponent field.  x is first
-// clamped at -125 so the result stays a normal float (masked scores give
-// about 2^-125 instead of 0, which no f32 row sum or P.V product can see).
-__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& p0, float& p1) {
-  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
-  constexpr float C0 = 0.99992812f, C1 = 0.69326097f, C2 = 0.24261054f, C3 = 0.05517132f;
-  const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
-  const uint64_t t = add2(x, f2_pack(kRound, kRound));
-  const uint64_t f = fma2(add2(t, f2_pack(-kRound, -kRound)), f2_pack(-1.f, -1.f), x);
-  uint64_t q = fma2(f2_pack(C3, C3), f, f2_pack(C2, C2));
-  q = fma2(q, f, f2_pack(C1, C1));
-  q = fma2(q, f, f2_pack(C0, C0));
-  float q0, q1, t0, t1;
-  f2_unpack(q, q0, q1);
-  f2_unpack(t, t0, t1);
-  p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
-  p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
-}
-
 // P for 64 columns (two 32-column chunks) packed as 32 bf16x2 words; adds to
-// the row sum (two packed accumulators).  NPOLY of every 8 column pairs take
-// the FMA-pipe exponential, the rest the SFU.
-template <bool FULL, int NPOLY>
+// the row sum (two packed accumulators).
+template <bool FULL>
 __device__ __forceinline__ void chunk_p(const uint32_t (&r0)[32], const uint32_t (&r1)[32], int col0, int lo, int hi,
                                         uint64_t scale2, uint64_t negm2, uint64_t (&ls2)[2], uint32_t (&pk)[32]) {
 #pragma unroll
@@ -167,13 +141,7 @@ __device__ __forceinline__ void chunk_p(const uint32_t (&r0)[32], const uint32_t
       v0 = (c >= lo && c <= hi) ? v0 : -INFINITY;
       v1 = (c + 1 >= lo && c + 1 <= hi) ? v1 : -INFINITY;
     }
-    float p0, p1;
-    if ((i & 7) < NPOLY) {
-      exp2_poly2(v0, v1, p0, p1);
-    } else {
-      p0 = fast_exp2(v0);
-      p1 = fast_exp2(v1);
-    }
+    const float p0 = fast_exp2(v0), p1 = fast_exp2(v1);
     ls2[i & 1] = add2(ls2[i & 1], f2_pack(p0, p1));
     pk[i] = pack_bf16x2(p0, p1);
   }
@@ -224,7 +192,7 @@ __device__ __forceinline__ int swa_item_index(int k) {
 //   s_full / p_full / o_done once per key tile and head,
 //   o_free            once per item and head: the epilogue has moved O out of
 //                     TMEM, so the next item's first P.V may overwrite it.
-template <int NHD, int NPOLY>
+template <int NHD>
 __global__ void __launch_bounds__(sw_threads(NHD), 1)
     swa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const SwaArgs a) {
@@ -467,7 +435,7 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         uint64_t ls2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
         {
           uint32_t pk[32];
-          chunk_p<true, NPOLY>(s0, s1, 0, lo, hi, scale2, negm2, ls2, pk);
+          chunk_p<true>(s0, s1, 0, lo, hi, scale2, negm2, ls2, pk);
           tmem_st32(sc, pk);
         }
         // Keys 0..63 of P are in TMEM: the first half of P.V may start.
@@ -477,7 +445,7 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         if (lane == 0) mbar_arrive(&p_half[hd]);
         {
           uint32_t pk[32];
-          chunk_p<true, NPOLY>(s2, s3, 64, lo, hi, scale2, negm2, ls2, pk);
+          chunk_p<true>(s2, s3, 64, lo, hi, scale2, negm2, ls2, pk);
           tmem_st32(sc + 32, pk);
         }
         {
@@ -546,7 +514,7 @@ template <int NHD>
 int launch_swa(hcu_context* h, const SwaArgs& args, const CUtensorMap& tq, const CUtensorMap& tk,
                const CUtensorMap& tv) {
   constexpr size_t smem = 1024 + NHD * TILE + KV_STAGES * KV_STAGE + 16 * 8 + 16;
-  auto kern = swa_prefill_kernel<NHD, kSwaPolyPairs>;
+  auto kern = swa_prefill_kernel<NHD>;
   static std::atomic<uint64_t> attr_done{0};  // per device
   HCU_TRY(once_per_device(attr_done, h->device, [&]() -> int {
     HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
