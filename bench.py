@@ -972,7 +972,7 @@ def strong_scaling(torch, dist, be, comm, comm_bulk, args, world, rank, dev, W2)
         be.attention(q_l, cache, out_l, d["pos"], 0, kv_row_offset=d["off"], max_context=d["maxc"])
         if ev:
             ev[1].record(stream)
-        comm.all_gather(out_l, recv)
+        comm_bulk.all_gather(out_l, recv)  # in line with the step: NCCL's full channel count
         if ev:
             ev[2].record(stream)
 
