@@ -119,6 +119,32 @@ def test_cfg5_qwen35_chunked_prefill(backend, cfg5):
         assert rel_l2(st[b, h], rs) < REL
 
 
+def test_cfg5_whole_output_against_recurrent_kernel(backend, cfg5):
+    """Every output and final state of config 5 (8 sequences x 8192 tokens x
+    32 V heads) against the token-serial f32 CUDA kernel (hcu_deltanet_recur,
+    itself checked against the oracle at 1e-4) on the same bf16-rounded inputs."""
+    w = cfg5
+    B, T, NK, NV = 8, 8192, 16, 32
+    q, k, v = to_dev_bf16(w["q"]), to_dev_bf16(w["k"]), to_dev_bf16(w["v"])
+    g, beta = torch.from_numpy(w["g"]).to(dev), torch.from_numpy(w["beta"]).to(dev)
+    core = torch.full((B, T, NV, 128), float("nan"), device=dev)
+    st = torch.zeros((B, NV, 128, 128), device=dev)
+    backend.deltanet_chunked_prefill(q, k, v, g, beta, core, st)
+    qkv = torch.cat([q.float().flatten(2), k.float().flatten(2), v.float().flatten(2)], 2).contiguous()
+    gb = torch.stack([g, beta], 1).contiguous()  # [B, 2, T, NV]
+    core2 = torch.zeros((B, T, NV, 128), device=dev)
+    st2 = torch.zeros((B, NV, 128, 128), device=dev)
+    backend.deltanet_recur(qkv, gb, st2, core2, st2, NK, NV, False)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(core).all()) and bool(torch.isfinite(st).all())
+    for b in range(B):
+        d = core[b] - core2[b]
+        assert float(d.norm() / core2[b].norm()) < REL, b
+        assert float(d.abs().max()) < ABS, b
+        assert float((st[b] - st2[b]).norm() / st2[b].norm()) < REL, b
+    assert backend.device_status() == 0
+
+
 def test_slabs_carry_the_state(backend, request):
     """A scratch budget of 1 MiB splits 64 chunks into slabs (one prep + chain
     launch pair each); the state crosses slab boundaries through state_out."""

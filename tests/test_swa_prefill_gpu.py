@@ -97,6 +97,44 @@ def test_cfg3_plamo3_swa_prefill(backend, cfg3):
     assert torch.equal(out, out2)
 
 
+def test_cfg3_whole_output_against_f32_reference(backend, cfg3):
+    """Every output of config 3 (8 sequences x 4096 queries x 16 heads)
+    against softmax(Q K^T / sqrt(128)) V in f32 on the GPU with the window
+    band of attention_q8 (src/kernels.ts:1373-1377): keys max(0, i - 1023) .. i.
+    The oracle-checked slices above pin this closed form's semantics; this
+    covers the rest of the output."""
+    w = cfg3
+    q, k, v = bf16_dev(w["q"]), bf16_dev(w["k"]), bf16_dev(w["v"])
+    out = torch.empty((8, 4096, 16, 128), device=dev, dtype=torch.bfloat16)
+    backend.swa_prefill(q, k, v, out, w["window"])
+    torch.cuda.synchronize()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        T, W = 4096, w["window"]
+        i = torch.arange(T, device=dev)
+        band = (i[None, :] <= i[:, None]) & (i[None, :] > i[:, None] - W)  # [query, key]
+        err2 = ref2 = 0.0
+        worst = 0.0
+        for b in range(8):
+            for g in range(4):  # KV head g serves query heads 4g .. 4g + 3
+                qh = q[b, :, 4 * g:4 * g + 4].float().permute(1, 0, 2)  # [4, T, 128]
+                kh, vh = k[b, :, g].float(), v[b, :, g].float()
+                s = torch.matmul(qh, kh.t()) / np.sqrt(128.0)
+                s = s.masked_fill(~band, float("-inf"))
+                ref = torch.matmul(torch.softmax(s, dim=-1), vh)  # [4, T, 128]
+                got = out[b, :, 4 * g:4 * g + 4].float().permute(1, 0, 2)
+                d = got - ref
+                err2 += float((d.double() ** 2).sum())
+                ref2 += float((ref.double() ** 2).sum())
+                worst = max(worst, float(d.abs().max()))
+                assert float(d.norm() / ref.norm()) < REL, (b, g)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert (err2 / ref2) ** 0.5 < REL
+    assert worst < ABS
+
+
 def test_rejects_bad_arguments(backend):
     q = torch.zeros((1, 128, 2, 64), device=dev, dtype=torch.bfloat16)
     with pytest.raises(HachiueError, match="D=64"):
