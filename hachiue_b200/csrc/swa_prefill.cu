@@ -34,16 +34,18 @@ namespace {
 
 // Warpgroup 0: warp 0 TMA, warp 1 MMA + TMEM (warps 2, 3 idle); warpgroup 1 + hd:
 // softmax of head hd.  With two heads the 384 threads launch with 168
-// registers each (64,512); the control warpgroup drops to 72 and the softmax
-// warpgroups rise to 216: 128 * 72 + 256 * 216 = 64,512.
+// registers each (64,512); the control warpgroup drops to 56 and the softmax
+// warpgroups rise to 224: 128 * 56 + 256 * 224 = 64,512.
 __host__ __device__ constexpr int sw_threads(int nhd) { return 128 + 128 * nhd; }
-constexpr uint32_t REG_CTRL = 72, REG_SOFTMAX = 216;
+constexpr uint32_t REG_CTRL = 56, REG_SOFTMAX = 224;
 static_assert(128 * REG_CTRL + 256 * REG_SOFTMAX == 384 * 168, "register split of the two-head kernel");
 constexpr int BM = 128, BN = 128, HD = 128;
 constexpr int BOX = BM * 128;                 // [128 rows x 64 bf16] = 16 KB
 constexpr int TILE = 2 * BOX;                 // [128 x 128] bf16 tile
 constexpr int KV_STAGES = 2;
 constexpr int KV_STAGE = 2 * TILE;            // K tile + V tile
+constexpr int OSTAGE = BOX;                   // output staging per head: [128 rows x 64 bf16]
+constexpr int NBARS = 18;
 constexpr float RESCALE_LOG2 = 8.f;
 
 struct SwaArgs {
@@ -77,16 +79,20 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 }
 
 // Sets the scores of columns outside this row's valid range lo..hi (tile
-// column indices) to -inf, in one 32-column chunk starting at column C0.
-// Chunks that every row of the warp keeps whole are skipped (a warp vote), so
-// only the one or two chunks a causal diagonal or window edge cuts through
-// pay a compare and select per element.
+// column indices) to -inf, in one 32-column chunk starting at column C0, and
+// returns whether no row of the warp keeps any column of it (warp-uniform;
+// the chunk is then left as it is and skipped by the max and P).  Chunks
+// that every row of the warp keeps whole are left alone too, so only the one
+// or two chunks a causal diagonal or window edge cuts through pay a compare
+// and select per element.
 template <int C0>
-__device__ __forceinline__ void mask_chunk(uint32_t (&r)[32], int lo, int hi) {
-  if (__all_sync(0xffffffffu, lo <= C0 && hi >= C0 + 31)) return;
+__device__ __forceinline__ bool mask_chunk(uint32_t (&r)[32], int lo, int hi) {
+  if (__all_sync(0xffffffffu, lo <= C0 && hi >= C0 + 31)) return false;
+  if (__all_sync(0xffffffffu, hi < C0 || lo > C0 + 31)) return true;
   const int a = lo - C0, b = hi - C0;
 #pragma unroll
   for (int i = 0; i < 32; i++) r[i] = (i >= a && i <= b) ? r[i] : 0xff800000u;  // -inf
+  return false;
 }
 
 // Row max of one 32-column chunk; `lo`..`hi` is the valid column range (all
@@ -125,25 +131,24 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   return d;
 }
 
-// P for 64 columns (two 32-column chunks) packed as 32 bf16x2 words; adds to
-// the row sum (two packed accumulators).
-template <bool FULL>
-__device__ __forceinline__ void chunk_p(const uint32_t (&r0)[32], const uint32_t (&r1)[32], int col0, int lo, int hi,
-                                        uint64_t scale2, uint64_t negm2, uint64_t (&ls2)[2], uint32_t (&pk)[32]) {
+// P for one 32-column chunk packed as 16 bf16x2 words pk[OFF..OFF+15]; adds
+// to the row sum (two packed accumulators).  A chunk that no row of the warp
+// keeps (EMPTY, warp-uniform) is all zeros without an exponential.
+template <int OFF>
+__device__ __forceinline__ void chunk_p(const uint32_t (&r)[32], bool empty, uint64_t scale2, uint64_t negm2,
+                                        uint64_t (&ls2)[2], uint32_t (&pk)[32]) {
+  if (empty) {
 #pragma unroll
-  for (int i = 0; i < 32; i++) {
-    const uint32_t x0 = i < 16 ? r0[2 * i] : r1[2 * i - 32];
-    const uint32_t x1 = i < 16 ? r0[2 * i + 1] : r1[2 * i - 31];
+    for (int i = 0; i < 16; i++) pk[OFF + i] = 0u;
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 16; i++) {
     float v0, v1;
-    f2_unpack(fma2(f2_pack(__uint_as_float(x0), __uint_as_float(x1)), scale2, negm2), v0, v1);
-    if (!FULL) {
-      const int c = col0 + 2 * i;
-      v0 = (c >= lo && c <= hi) ? v0 : -INFINITY;
-      v1 = (c + 1 >= lo && c + 1 <= hi) ? v1 : -INFINITY;
-    }
+    f2_unpack(fma2(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), scale2, negm2), v0, v1);
     const float p0 = fast_exp2(v0), p1 = fast_exp2(v1);
     ls2[i & 1] = add2(ls2[i & 1], f2_pack(p0, p1));
-    pk[i] = pack_bf16x2(p0, p1);
+    pk[OFF + i] = pack_bf16x2(p0, p1);
   }
 }
 
@@ -201,28 +206,29 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* qsm = smem;                      // [NHD][TILE]
   uint8_t* kvsm = qsm + NHD * TILE;         // [KV_STAGES][K tile | V tile]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(kvsm + KV_STAGES * KV_STAGE);
-  uint64_t* q_full = bars;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* kv_full = bars + 2;   // [KV_STAGES]
-  uint64_t* kv_empty = bars + 4;  // [KV_STAGES]
-  uint64_t* s_full = bars + 6;    // [NHD]
-  uint64_t* p_full = bars + 8;    // [NHD]
-  uint64_t* o_done = bars + 10;   // [NHD]
-  uint64_t* o_free = bars + 12;   // [NHD]
-  uint64_t* p_half = bars + 14;   // [NHD]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint8_t* osm = kvsm + KV_STAGES * KV_STAGE;  // [NHD][OSTAGE]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(osm + NHD * OSTAGE);
+  uint64_t* q_full = bars;        // [NHD]
+  uint64_t* q_empty = bars + 2;   // [NHD]
+  uint64_t* kv_full = bars + 4;   // [KV_STAGES]
+  uint64_t* kv_empty = bars + 6;  // [KV_STAGES]
+  uint64_t* s_full = bars + 8;    // [NHD]
+  uint64_t* p_full = bars + 10;   // [NHD]
+  uint64_t* o_done = bars + 12;   // [NHD]
+  uint64_t* o_free = bars + 14;   // [NHD]
+  uint64_t* p_half = bars + 16;   // [NHD]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
     for (int i = 0; i < KV_STAGES; i++) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
     for (int i = 0; i < 2; i++) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
@@ -257,13 +263,22 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         const int idx = swa_item_index(k);
         if (idx >= a.n_items) break;
         const SwaItem it = swa_item<NHD>(a, idx);
-        if (k > 0 && !mbar_wait(q_empty, (k - 1) & 1, a.status)) break;
-        mbar_arrive_expect_tx(q_full, NHD * TILE);
-        for (int hd = 0; hd < NHD; hd++) {
-          tma_load_4d(qsm + hd * TILE, &tmQ, q_full, 0, it.h0 + hd, it.m0, it.b);
-          tma_load_4d(qsm + hd * TILE + BOX, &tmQ, q_full, 64, it.h0 + hd, it.m0, it.b);
-        }
-        for (int j = 0; j < it.ntiles; j++, kt++) {
+        // Q of head hd loads once the previous item's last Q.K^T of that head
+        // has read the buffer.
+        auto load_q = [&](int hd) {
+          if (k > 0 && !mbar_wait(&q_empty[hd], (k - 1) & 1, a.status)) return false;
+          mbar_arrive_expect_tx(&q_full[hd], TILE);
+          tma_load_4d(qsm + hd * TILE, &tmQ, &q_full[hd], 0, it.h0 + hd, it.m0, it.b);
+          tma_load_4d(qsm + hd * TILE + BOX, &tmQ, &q_full[hd], 64, it.h0 + hd, it.m0, it.b);
+          return true;
+        };
+        // Order of the buffers' release by the MMAs: head 0's Q, the stage of
+        // the item's first K / V tile, then head 1's Q.
+        if (!load_q(0)) break;
+        for (int j = 0; ok && j < it.ntiles; j++, kt++) {
+          if (j == 1)
+            for (int hd = 1; ok && hd < NHD; hd++) ok = load_q(hd);
+          if (!ok) break;
           const int s = kt % KV_STAGES;
           if (kt >= KV_STAGES && !mbar_wait(&kv_empty[s], ((kt - KV_STAGES) / KV_STAGES) & 1, a.status)) {
             ok = false;
@@ -277,6 +292,8 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
           tma_load_4d(st + TILE, &tmV, &kv_full[s], 0, it.g, n0, it.b);
           tma_load_4d(st + TILE + BOX, &tmV, &kv_full[s], 64, it.g, n0, it.b);
         }
+        if (ok && it.ntiles == 1)
+          for (int hd = 1; ok && hd < NHD; hd++) ok = load_q(hd);
       }
     }
   } else if (warp == 1) {
@@ -304,23 +321,31 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
           mma_f16_ts(tmem + o_col(hd), tmem + s_col(hd) + ks * 8, bd, idesc_pv, (acc || ks > 0) ? 1u : 0u);
         }
       };
+      // The tiles of consecutive items form one stream: a head's next Q.K^T
+      // (the item's next tile, or the next item's first) issues right behind
+      // its P.V of the current tile, which has consumed the P it overwrites.
       int kt = 0;  // key tiles consumed (ring position and per-head tile count)
       bool ok = true;
-      for (int k = 0; ok; k++) {
-        const int idx = swa_item_index(k);
-        if (idx >= a.n_items) break;
-        const int ntiles = swa_item<NHD>(a, idx).ntiles;
-        if (!mbar_wait(q_full, k & 1, a.status) ||
-            !mbar_wait(&kv_full[kt % KV_STAGES], (kt / KV_STAGES) & 1, a.status))
-          break;
-        tc_fence_after();
-        // Ordered after the previous item's last P.V of each head (same
-        // issuing thread), which has consumed that head's P.
-        for (int hd = 0; hd < NHD; hd++) qk(hd, kt % KV_STAGES);
-        if (ntiles == 1) mma_commit(q_empty);
+      int idx = swa_item_index(0);
+      int ntiles = idx < a.n_items ? swa_item<NHD>(a, idx).ntiles : 0;
+      if (ntiles > 0) {
+        for (int hd = 0; hd < NHD; hd++) {
+          if (!mbar_wait(&q_full[hd], 0, a.status) || (hd == 0 && !mbar_wait(&kv_full[0], 0, a.status))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          qk(hd, 0);
+          if (ntiles == 1) mma_commit(&q_empty[hd]);  // the item's last Q.K^T of this head
+        }
+      }
+      for (int k = 0; ok && ntiles > 0; k++) {
+        idx = swa_item_index(k + 1);
+        const int ntiles1 = idx < a.n_items ? swa_item<NHD>(a, idx).ntiles : 0;
         for (int j = 0; ok && j < ntiles; j++) {
           const int t = kt + j;
           const int s = t % KV_STAGES;
+          const bool last = j + 1 == ntiles;
           for (int hd = 0; hd < NHD; hd++) {
             if (!mbar_wait(&p_half[hd], t & 1, a.status) ||
                 (j == 0 && k > 0 && !mbar_wait(&o_free[hd], (k - 1) & 1, a.status))) {
@@ -337,19 +362,21 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
             pv_half(hd, s, 1, true);
             mma_commit(&o_done[hd]);
             if (hd == NHD - 1) mma_commit(&kv_empty[s]);
-            if (j + 1 < ntiles) {
+            if (!last || ntiles1 > 0) {
               const int s1 = (t + 1) % KV_STAGES;
-              if (hd == 0 && !mbar_wait(&kv_full[s1], ((t + 1) / KV_STAGES) & 1, a.status)) {
+              if ((hd == 0 && !mbar_wait(&kv_full[s1], ((t + 1) / KV_STAGES) & 1, a.status)) ||
+                  (last && !mbar_wait(&q_full[hd], (k + 1) & 1, a.status))) {
                 ok = false;
                 break;
               }
               tc_fence_after();
               qk(hd, s1);  // overwrites S / P of this head: ordered after the P.V above
-              if (hd == NHD - 1 && j + 2 == ntiles) mma_commit(q_empty);  // the item's last Q.K^T
+              if (last ? ntiles1 == 1 : j + 2 == ntiles) mma_commit(&q_empty[hd]);
             }
           }
         }
         kt += ntiles;
+        ntiles = ntiles1;
       }
     }
   }
@@ -361,6 +388,72 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t sc = tmem + lane_off + s_col(hd), oc = tmem + lane_off + o_col(hd);
+    // Epilogue of one item: O / l out of TMEM and into the output.  It runs
+    // after the NEXT item's first P is in TMEM (O of the finished item has
+    // long been complete by then), so the MMA round trip of that first tile
+    // covers it; o_free then lets the next item's first P.V overwrite O.
+    // bf16 output goes 64 columns at a time: each warp turns its 32 rows
+    // around in its own 4 KB of the head's staging buffer (thread = row on
+    // the way in, 8 threads per 128-byte row segment on the way out), so
+    // every global store instruction writes four whole 128-byte segments.
+    // fin_idx: the finished item (-1: none), fin_l: this row's sum of P, t_last:
+    // its last key tile.
+    auto epilogue = [&](int fin_idx, float fin_l, int t_last) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(&o_done[hd], t_last & 1, a.status))) return false;
+      const SwaItem f = swa_item<NHD>(a, fin_idx);
+      tc_fence_after();
+      uint32_t o[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; c++) tmem_ld32(oc + 32 * c, o[c]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[hd]);
+      const float inv = 1.f / fin_l;
+      if (a.out_bf16) {
+        uint8_t* wst = osm + hd * OSTAGE + quarter * 4096;  // this warp's rows
+        // Read-out: lane -> row 4i + (lane >> 3) of the warp, 16-byte piece lane & 7.
+        const int rr = lane >> 3, seg = lane & 7;
+        const size_t rstride = (size_t)a.H * HD;  // elements between consecutive tokens
+        __nv_bfloat16* gp = static_cast<__nv_bfloat16*>(a.out) +
+                            (((size_t)f.b * a.T + f.m0 + quarter * 32 + rr) * a.H + f.h0 + hd) * HD + 8 * seg;
+        const int rows_left = a.T - (f.m0 + quarter * 32 + rr);  // rows 4i with 4i < rows_left exist
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+#pragma unroll
+          for (int c = 0; c < 8; c++) {
+            const uint32_t* v = &o[2 * half + (c >> 2)][8 * (c & 3)];
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[0]) * inv, __uint_as_float(v[1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(v[2]) * inv, __uint_as_float(v[3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(v[4]) * inv, __uint_as_float(v[5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(v[6]) * inv, __uint_as_float(v[7]) * inv);
+            *reinterpret_cast<uint4*>(wst + lane * 128 + ((c ^ (lane & 7)) << 4)) = w;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const int r = 4 * i + rr;
+            const uint4 w = *reinterpret_cast<const uint4*>(wst + r * 128 + ((seg ^ (r & 7)) << 4));
+            if (4 * i < rows_left) *reinterpret_cast<uint4*>(gp + 4 * i * rstride + 64 * half) = w;
+          }
+          __syncwarp();
+        }
+      } else if (f.m0 + row < a.T) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) +
+                                                (((size_t)f.b * a.T + f.m0 + row) * a.H + f.h0 + hd) * HD);
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+            dst[8 * c + i] = make_float4(__uint_as_float(o[c][4 * i]) * inv, __uint_as_float(o[c][4 * i + 1]) * inv,
+                                         __uint_as_float(o[c][4 * i + 2]) * inv,
+                                         __uint_as_float(o[c][4 * i + 3]) * inv);
+      }
+      return true;
+    };
+    int fin_idx = -1;
+    float fin_l = 0.f;
     int kt = 0;  // key tiles processed, over all items
     bool ok = true;
     for (int k = 0; ok; k++) {
@@ -388,17 +481,18 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         tmem_ld32(sc + 64, s2);
         tmem_ld32(sc + 96, s3);
         tmem_ld_wait();
+        bool e0 = false, e1 = false, e2 = false, e3 = false;  // chunks no row of the warp keeps
         if (!full) {  // tile cut by the causal diagonal, the window edge or T
-          mask_chunk<0>(s0, lo, hi);
-          mask_chunk<32>(s1, lo, hi);
-          mask_chunk<64>(s2, lo, hi);
-          mask_chunk<96>(s3, lo, hi);
+          e0 = mask_chunk<0>(s0, lo, hi);
+          e1 = mask_chunk<32>(s1, lo, hi);
+          e2 = mask_chunk<64>(s2, lo, hi);
+          e3 = mask_chunk<96>(s3, lo, hi);
         }
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        chunk_max<true>(s0, 0, lo, hi, mx4);
-        chunk_max<true>(s1, 32, lo, hi, mx4);
-        chunk_max<true>(s2, 64, lo, hi, mx4);
-        chunk_max<true>(s3, 96, lo, hi, mx4);
+        if (!e0) chunk_max<true>(s0, 0, lo, hi, mx4);
+        if (!e1) chunk_max<true>(s1, 32, lo, hi, mx4);
+        if (!e2) chunk_max<true>(s2, 64, lo, hi, mx4);
+        if (!e3) chunk_max<true>(s3, 96, lo, hi, mx4);
         const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
         // The running max grew by more than 2^8 (or this is the first finite
         // max): move to the new max.  Rows that already accumulated O rescale
@@ -435,7 +529,8 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         uint64_t ls2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
         {
           uint32_t pk[32];
-          chunk_p<true>(s0, s1, 0, lo, hi, scale2, negm2, ls2, pk);
+          chunk_p<0>(s0, e0, scale2, negm2, ls2, pk);
+          chunk_p<16>(s1, e1, scale2, negm2, ls2, pk);
           tmem_st32(sc, pk);
         }
         // Keys 0..63 of P are in TMEM: the first half of P.V may start.
@@ -445,7 +540,8 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         if (lane == 0) mbar_arrive(&p_half[hd]);
         {
           uint32_t pk[32];
-          chunk_p<true>(s2, s3, 64, lo, hi, scale2, negm2, ls2, pk);
+          chunk_p<0>(s2, e2, scale2, negm2, ls2, pk);
+          chunk_p<16>(s3, e3, scale2, negm2, ls2, pk);
           tmem_st32(sc + 32, pk);
         }
         {
@@ -458,48 +554,20 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[hd]);
-      }
-      // ---------------- epilogue: O / l ----------------
-      // O comes out of TMEM in one go (128 registers; the S registers are
-      // dead here), then o_free lets the next item's first P.V overwrite it
-      // while this warp normalises and stores.
-      if (ok && !__all_sync(0xffffffffu, mbar_wait(&o_done[hd], (kt + it.ntiles - 1) & 1, a.status))) ok = false;
-      if (!ok) break;  // warp-uniform
-      tc_fence_after();
-      uint32_t o[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; c++) tmem_ld32(oc + 32 * c, o[c]);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[hd]);
-      if (query < a.T) {
-        const float inv = 1.f / l;
-        const size_t obase = (((size_t)it.b * a.T + query) * a.H + (it.h0 + hd)) * HD;
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-          if (a.out_bf16) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + obase + 32 * c);
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(o[c][8 * i + 0]) * inv, __uint_as_float(o[c][8 * i + 1]) * inv);
-              w.y = pack_bf16x2(__uint_as_float(o[c][8 * i + 2]) * inv, __uint_as_float(o[c][8 * i + 3]) * inv);
-              w.z = pack_bf16x2(__uint_as_float(o[c][8 * i + 4]) * inv, __uint_as_float(o[c][8 * i + 5]) * inv);
-              w.w = pack_bf16x2(__uint_as_float(o[c][8 * i + 6]) * inv, __uint_as_float(o[c][8 * i + 7]) * inv);
-              dst[i] = w;
-            }
-          } else {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + obase + 32 * c);
-#pragma unroll
-            for (int i = 0; i < 8; i++)
-              dst[i] = make_float4(__uint_as_float(o[c][4 * i]) * inv, __uint_as_float(o[c][4 * i + 1]) * inv,
-                                   __uint_as_float(o[c][4 * i + 2]) * inv, __uint_as_float(o[c][4 * i + 3]) * inv);
+        if (j == 0 && fin_idx >= 0) {
+          if (!epilogue(fin_idx, fin_l, kt - 1)) {
+            ok = false;
+            break;
           }
+          fin_idx = -1;
         }
       }
+      if (!ok) break;  // warp-uniform
+      fin_idx = idx;
+      fin_l = l;
       kt += it.ntiles;
     }
+    if (ok && fin_idx >= 0) epilogue(fin_idx, fin_l, kt - 1);
   }
   tc_fence_before();
   __syncthreads();
@@ -513,7 +581,8 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
 template <int NHD>
 int launch_swa(hcu_context* h, const SwaArgs& args, const CUtensorMap& tq, const CUtensorMap& tk,
                const CUtensorMap& tv) {
-  constexpr size_t smem = 1024 + NHD * TILE + KV_STAGES * KV_STAGE + 16 * 8 + 16;
+  constexpr size_t smem = 1024 + NHD * TILE + KV_STAGES * KV_STAGE + NHD * OSTAGE + NBARS * 8 + 16;
+  static_assert(smem <= 227 * 1024, "shared memory of the SWA kernel");
   auto kern = swa_prefill_kernel<NHD>;
   static std::atomic<uint64_t> attr_done{0};  // per device
   HCU_TRY(once_per_device(attr_done, h->device, [&]() -> int {
