@@ -298,7 +298,10 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // The whole warp walks the loop (every value in it is warp-uniform); one
+    // elected lane issues each tcgen05 instruction.
+    {
+      const bool leader = elect_one_sync();
       constexpr uint32_t idesc_qk = idesc_f16(BM, BN, true, false, false);
       constexpr uint32_t idesc_pv = idesc_f16(BM, HD, true, false, true);
       const uint32_t q0 = smem_u32(qsm), kv0 = smem_u32(kvsm);
@@ -307,9 +310,9 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         for (int ks = 0; ks < 8; ks++) {
           const uint64_t ad = smem_desc_sw128(q0 + hd * TILE + (ks >> 2) * BOX + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = smem_desc_sw128(kv0 + s * KV_STAGE + (ks >> 2) * BOX + (ks & 3) * 32, 16, 1024);
-          mma_f16_ss(tmem + s_col(hd), ad, bd, idesc_qk, ks > 0);
+          if (leader) mma_f16_ss(tmem + s_col(hd), ad, bd, idesc_qk, ks > 0);
         }
-        mma_commit(&s_full[hd]);
+        if (leader) mma_commit(&s_full[hd]);
       };
       // P.V in two halves of 64 keys (k-steps 0-3, 4-7): the first runs
       // while the softmax still computes the second half of P.
@@ -318,7 +321,7 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         for (int i = 0; i < 4; i++) {
           const int ks = 4 * half + i;
           const uint64_t bd = smem_desc_sw128(kv0 + s * KV_STAGE + TILE + ks * 2048, BOX, 1024);  // MN-major V
-          mma_f16_ts(tmem + o_col(hd), tmem + s_col(hd) + ks * 8, bd, idesc_pv, (acc || ks > 0) ? 1u : 0u);
+          if (leader) mma_f16_ts(tmem + o_col(hd), tmem + s_col(hd) + ks * 8, bd, idesc_pv, (acc || ks > 0) ? 1u : 0u);
         }
       };
       // The tiles of consecutive items form one stream: a head's next Q.K^T
@@ -330,13 +333,14 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
       int ntiles = idx < a.n_items ? swa_item<NHD>(a, idx).ntiles : 0;
       if (ntiles > 0) {
         for (int hd = 0; hd < NHD; hd++) {
-          if (!mbar_wait(&q_full[hd], 0, a.status) || (hd == 0 && !mbar_wait(&kv_full[0], 0, a.status))) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&q_full[hd], 0, a.status) &&
+                                           (hd > 0 || mbar_wait(&kv_full[0], 0, a.status)))) {
             ok = false;
             break;
           }
           tc_fence_after();
           qk(hd, 0);
-          if (ntiles == 1) mma_commit(&q_empty[hd]);  // the item's last Q.K^T of this head
+          if (ntiles == 1 && leader) mma_commit(&q_empty[hd]);  // the item's last Q.K^T of this head
         }
       }
       for (int k = 0; ok && ntiles > 0; k++) {
@@ -347,31 +351,33 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
           const int s = t % KV_STAGES;
           const bool last = j + 1 == ntiles;
           for (int hd = 0; hd < NHD; hd++) {
-            if (!mbar_wait(&p_half[hd], t & 1, a.status) ||
-                (j == 0 && k > 0 && !mbar_wait(&o_free[hd], (k - 1) & 1, a.status))) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&p_half[hd], t & 1, a.status) &&
+                                             (j > 0 || k == 0 || mbar_wait(&o_free[hd], (k - 1) & 1, a.status)))) {
               ok = false;
               break;
             }
             tc_fence_after();
             pv_half(hd, s, 0, j > 0);
-            if (!mbar_wait(&p_full[hd], t & 1, a.status)) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[hd], t & 1, a.status))) {
               ok = false;
               break;
             }
             tc_fence_after();
             pv_half(hd, s, 1, true);
-            mma_commit(&o_done[hd]);
-            if (hd == NHD - 1) mma_commit(&kv_empty[s]);
+            if (leader) {
+              mma_commit(&o_done[hd]);
+              if (hd == NHD - 1) mma_commit(&kv_empty[s]);
+            }
             if (!last || ntiles1 > 0) {
               const int s1 = (t + 1) % KV_STAGES;
-              if ((hd == 0 && !mbar_wait(&kv_full[s1], ((t + 1) / KV_STAGES) & 1, a.status)) ||
-                  (last && !mbar_wait(&q_full[hd], (k + 1) & 1, a.status))) {
+              if (!__all_sync(0xffffffffu, (hd > 0 || mbar_wait(&kv_full[s1], ((t + 1) / KV_STAGES) & 1, a.status)) &&
+                                               (!last || mbar_wait(&q_full[hd], (k + 1) & 1, a.status)))) {
                 ok = false;
                 break;
               }
               tc_fence_after();
               qk(hd, s1);  // overwrites S / P of this head: ordered after the P.V above
-              if (last ? ntiles1 == 1 : j + 2 == ntiles) mma_commit(&q_empty[hd]);
+              if ((last ? ntiles1 == 1 : j + 2 == ntiles) && leader) mma_commit(&q_empty[hd]);
             }
           }
         }

@@ -168,6 +168,19 @@ __device__ __forceinline__ void warpgroup_reg_alloc() {
 
 // Arrive on `bar` once every tcgen05 operation issued so far by this thread
 // has completed.
+// True in exactly one lane of the (converged) warp.  MMA and commit issue
+// loops run on the whole warp, so their descriptors and addresses are
+// warp-uniform values, and one elected lane issues each instruction.
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
