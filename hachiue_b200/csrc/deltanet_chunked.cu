@@ -201,11 +201,14 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (tid == 0) {
-    prefetch_tensormap(&tmW);
+  if (warp == 0) {
+    // One elected lane issues the loads and the MMAs; the whole warp waits
+    // and forms the (warp-uniform) descriptors.
+    const bool leader = elect_one_sync();
     // warm L2 with the K / Q chunk that the CTA one wave later (a.ahead
     // blocks further in launch order) will load
-    {
+    if (leader) {
+      prefetch_tensormap(&tmW);
       const long long lin = blockIdx.x + (long long)gridDim.x * (blockIdx.y + (long long)gridDim.y * blockIdx.z) +
                             a.ahead;
       const int cf = (int)(lin % gridDim.x), yf = (int)((lin / gridDim.x) % gridDim.y);
@@ -217,22 +220,22 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         tma_prefetch_l2_4d(&tmK, 64, hf, tf, (int)bf);
         tma_prefetch_l2_4d(&tmQ, 64, hf, tf, (int)bf);
       }
+      mbar_arrive_expect_tx(bar_kq, 32768);
+      tma_load_4d(sm + P_OFF_KQ, &tmK, bar_kq, 0, hk, t0, b);
+      tma_load_4d(sm + P_OFF_KQ + 8192, &tmQ, bar_kq, 0, hk, t0, b);
+      tma_load_4d(sm + P_OFF_KQ + 16384, &tmK, bar_kq, 64, hk, t0, b);
+      tma_load_4d(sm + P_OFF_KQ + 24576, &tmQ, bar_kq, 64, hk, t0, b);
     }
-    mbar_arrive_expect_tx(bar_kq, 32768);
-    tma_load_4d(sm + P_OFF_KQ, &tmK, bar_kq, 0, hk, t0, b);
-    tma_load_4d(sm + P_OFF_KQ + 8192, &tmQ, bar_kq, 0, hk, t0, b);
-    tma_load_4d(sm + P_OFF_KQ + 16384, &tmK, bar_kq, 64, hk, t0, b);
-    tma_load_4d(sm + P_OFF_KQ + 24576, &tmQ, bar_kq, 64, hk, t0, b);
-    if (mbar_wait(bar_kq, 0, a.status)) {
+    if (__all_sync(0xffffffffu, mbar_wait(bar_kq, 0, a.status))) {
       tc_fence_after();
       constexpr uint32_t id_f = idesc_f16(128, 128, true, false, false);
       const uint32_t kq = smem_u32(sm + P_OFF_KQ);
 #pragma unroll
       for (int ks = 0; ks < 8; ks++) {
         const uint64_t d = smem_desc_sw128(kq + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
-        mma_f16_ss(tmem, d, d, id_f, ks > 0);
+        if (leader) mma_f16_ss(tmem, d, d, id_f, ks > 0);
       }
-      mma_commit(bar_f);
+      if (leader) mma_commit(bar_f);
     }
   }
 
@@ -453,14 +456,16 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       fence_proxy_async();
       named_bar(bid, 128);
       constexpr uint32_t id_l3 = idesc_tf32(64, 32, false, false);
-      if (t == 0) {
+      if (quad == 0) {
+        const bool leader = elect_one_sync();
         tc_fence_after();
         const uint32_t ub = smem_u32(U11), ab = smem_u32(A21);
 #pragma unroll
-        for (int ks = 0; ks < 4; ks++)
-          mma_tf32_ss(tl3, smem_desc_sw128(ub + ks * 32, 16, 1024), smem_desc_sw128(ab + ks * 32, 16, 1024), id_l3,
-                      ks > 0);
-        mma_commit(&bar_l3a[wg]);
+        for (int ks = 0; ks < 4; ks++) {
+          const uint64_t ad = smem_desc_sw128(ub + ks * 32, 16, 1024), bd = smem_desc_sw128(ab + ks * 32, 16, 1024);
+          if (leader) mma_tf32_ss(tl3, ad, bd, id_l3, ks > 0);
+        }
+        if (leader) mma_commit(&bar_l3a[wg]);
       }
       ok = __all_sync(0xffffffffu, mbar_wait(&bar_l3a[wg], 0, a.status));
       if (ok && quad < 2) {
@@ -480,15 +485,17 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       fence_proxy_async();
       tc_fence_before();
       ok = named_bar_and(bid, 128, ok);
-      if (ok && t == 0) {
+      if (ok && quad == 0) {
+        const bool leader = elect_one_sync();
         tc_fence_after();
         // A operand rows 32-63 are T22's; rows 0-31 read A21 and are not used
         const uint32_t tb = smem_u32(A21), xb = smem_u32(X2T);
 #pragma unroll
-        for (int ks = 0; ks < 4; ks++)
-          mma_tf32_ss(tl3 + 32, smem_desc_sw128(tb + ks * 32, 16, 1024), smem_desc_sw128(xb + ks * 32, 16, 1024),
-                      id_l3, ks > 0);
-        mma_commit(&bar_l3b[wg]);
+        for (int ks = 0; ks < 4; ks++) {
+          const uint64_t ad = smem_desc_sw128(tb + ks * 32, 16, 1024), bd = smem_desc_sw128(xb + ks * 32, 16, 1024);
+          if (leader) mma_tf32_ss(tl3 + 32, ad, bd, id_l3, ks > 0);
+        }
+        if (leader) mma_commit(&bar_l3b[wg]);
       }
       if (ok && quad >= 2) {
         ok = __all_sync(0xffffffffu, mbar_wait(&bar_l3b[wg], 0, a.status));
@@ -547,17 +554,19 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       fence_proxy_async();
       tc_fence_before();
       ok = named_bar_and(bid, 128, ok);
-      if (ok && t == 0) {
+      if (ok && quad == 0) {
         // QKm Tb (M = 128: rows 64-127 are QKm's, from TMEM lanes 64-127; rows
         // 0-63 read lanes 0-63 of the same columns and are not used)
+        const bool leader = elect_one_sync();
         tc_fence_after();
         constexpr uint32_t id_g = idesc_tf32(128, 64, false, false);
         const uint32_t tb = smem_u32(TbT);
 #pragma unroll
-        for (int ks = 0; ks < 8; ks++)
-          mma_tf32_ts(tl3, tmem + 64 * wg + 8 * ks, smem_desc_sw128(tb + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024),
-                      id_g, ks > 0);
-        mma_commit(&bar_g[wg]);
+        for (int ks = 0; ks < 8; ks++) {
+          const uint64_t bd = smem_desc_sw128(tb + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024);
+          if (leader) mma_tf32_ts(tl3, tmem + 64 * wg + 8 * ks, bd, id_g, ks > 0);
+        }
+        if (leader) mma_commit(&bar_g[wg]);
       }
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_g[wg], 0, a.status));
       if (ok && quad >= 2) {
@@ -710,38 +719,51 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // The whole warp walks the loop (its values are warp-uniform); one
+    // elected lane issues each tcgen05 instruction.
+    {
+      const bool leader = elect_one_sync();
       constexpr uint32_t id_n64 = idesc_f16(128, 64, true, false, true);  // K-major A, MN-major B
       constexpr uint32_t id_e = idesc_f16(128, 64, true, true, true);     // MN-major A (K^T)
       const uint32_t s0 = smem_u32(sm);
       for (int c = 0; c < n; c++) {
         const uint32_t ph = c & 1;
         // (a) [X; QS] = [K; Q] S0   (M = 128, N = 64, K = 128)
-        if (!mbar_wait(kq_full, ph, a.status) || !mbar_wait(bar_s0, ph, a.status)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(kq_full, ph, a.status) && mbar_wait(bar_s0, ph, a.status))) break;
         tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 8; ks++)
-          mma_f16_ss(tmem + TC_P, smem_desc_sw128(s0 + C_OFF_KQ + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
-                     smem_desc_sw128(s0 + C_OFF_S0B + ks * 2048, 8192, 1024), id_n64, ks > 0);
-        mma_commit(bar_a);
-        mma_commit(kq_empty);
+        for (int ks = 0; ks < 8; ks++) {
+          const uint64_t ad = smem_desc_sw128(s0 + C_OFF_KQ + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(s0 + C_OFF_S0B + ks * 2048, 8192, 1024);
+          if (leader) mma_f16_ss(tmem + TC_P, ad, bd, id_n64, ks > 0);
+        }
+        if (leader) {
+          mma_commit(bar_a);
+          mma_commit(kq_empty);
+        }
         // (c) [Tb R'; O2] = W R'   (M = 128, N = 64, K = 64)
-        if (!mbar_wait(bar_R, ph, a.status) || !mbar_wait(w_full, ph, a.status)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_R, ph, a.status) && mbar_wait(w_full, ph, a.status))) break;
         tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 4; ks++)
-          mma_f16_ss(tmem + TC_Q, smem_desc_sw128(s0 + C_OFF_W + ks * 32, 16, 1024),
-                     smem_desc_sw128(s0 + C_OFF_RB + ks * 2048, 8192, 1024), id_n64, ks > 0);
-        mma_commit(bar_c);
+        for (int ks = 0; ks < 4; ks++) {
+          const uint64_t ad = smem_desc_sw128(s0 + C_OFF_W + ks * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(s0 + C_OFF_RB + ks * 2048, 8192, 1024);
+          if (leader) mma_f16_ss(tmem + TC_Q, ad, bd, id_n64, ks > 0);
+        }
+        if (leader) mma_commit(bar_c);
         // (e) U = K^T Dsb   (M = 128, N = 64, K = 64)
-        if (!mbar_wait(bar_D, ph, a.status) || !mbar_wait(ke_full, ph, a.status)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_D, ph, a.status) && mbar_wait(ke_full, ph, a.status))) break;
         tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 4; ks++)
-          mma_f16_ss(tmem + TC_P, smem_desc_sw128(s0 + C_OFF_KE + ks * 2048, 8192, 1024),
-                     smem_desc_sw128(s0 + C_OFF_DSB + ks * 2048, 8192, 1024), id_e, ks > 0);
-        mma_commit(bar_e);
-        mma_commit(ke_empty);
+        for (int ks = 0; ks < 4; ks++) {
+          const uint64_t ad = smem_desc_sw128(s0 + C_OFF_KE + ks * 2048, 8192, 1024);
+          const uint64_t bd = smem_desc_sw128(s0 + C_OFF_DSB + ks * 2048, 8192, 1024);
+          if (leader) mma_f16_ss(tmem + TC_P, ad, bd, id_e, ks > 0);
+        }
+        if (leader) {
+          mma_commit(bar_e);
+          mma_commit(ke_empty);
+        }
       }
     }
   } else {
