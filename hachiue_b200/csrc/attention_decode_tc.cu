@@ -201,32 +201,35 @@ __global__ void __launch_bounds__(TC_THREADS, NC == 16 ? 2 : 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // The whole warp walks the loop (its values are warp-uniform); one
+    // elected lane issues each tcgen05 instruction.
+    {
+      const bool leader = elect_one_sync();
       constexpr uint32_t idesc_qk = idesc_f16(128, NC, BF16, false, false);
       constexpr uint32_t idesc_pv = idesc_f16(128, NC, BF16, true, false);
       const uint32_t st0 = smem_u32(stages), qs0 = smem_u32(qs), ps0 = smem_u32(ps);
       for (int j = 0; j <= ntiles; ++j) {
         if (j < ntiles) {
           const int s = j % TC_KST, x = j & 1;
-          if (!mbar_wait(&k_full[s], (j / TC_KST) & 1, a.status)) break;
-          if (j >= 2 && !mbar_wait(&s_free[x], ((j - 2) >> 1) & 1, a.status)) break;
+          if (!__all_sync(0xffffffffu, mbar_wait(&k_full[s], (j / TC_KST) & 1, a.status))) break;
+          if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&s_free[x], ((j - 2) >> 1) & 1, a.status))) break;
           tc_fence_after();
           const uint32_t kb = st0 + s * HALF_BYTES;
 #pragma unroll
           for (int ks = 0; ks < 8; ks++) {
             const uint64_t ad = smem_desc_sw128(kb + (ks >> 2) * BOX_BYTES + (ks & 3) * 32, 16, 1024);
             const uint64_t bd = smem_desc_sw128(qs0 + (ks >> 2) * QS_BLK + (ks & 3) * 32, 16, 1024);
-            mma_f16_ss(tmem + S_COL + x * NC, ad, bd, idesc_qk, ks > 0);
+            if (leader) mma_f16_ss(tmem + S_COL + x * NC, ad, bd, idesc_qk, ks > 0);
           }
-          mma_commit(&s_full[x]);
-          mma_commit(&k_empty[s]);
+          if (leader) mma_commit(&s_full[x]);
+          if (leader) mma_commit(&k_empty[s]);
         }
         if (j >= 1) {
           const int jp = j - 1, xp = jp & 1;
           // V(jp) landed (the softmax also waits for it before zeroing rows of a partial tile)
-          if (!mbar_wait(v_full, jp & 1, a.status)) break;
-          if (!mbar_wait(&p_full[xp], (jp >> 1) & 1, a.status)) break;
-          if (jp >= 2 && !mbar_wait(&o_free[xp], ((jp - 2) >> 1) & 1, a.status)) break;
+          if (!__all_sync(0xffffffffu, mbar_wait(v_full, jp & 1, a.status))) break;
+          if (!__all_sync(0xffffffffu, mbar_wait(&p_full[xp], (jp >> 1) & 1, a.status))) break;
+          if (jp >= 2 && !__all_sync(0xffffffffu, mbar_wait(&o_free[xp], ((jp - 2) >> 1) & 1, a.status))) break;
           tc_fence_after();
           const uint32_t vb = st0 + TC_KST * HALF_BYTES;
           const uint32_t pb = ps0 + xp * 2 * QS_BLK;
@@ -234,10 +237,10 @@ __global__ void __launch_bounds__(TC_THREADS, NC == 16 ? 2 : 1)
           for (int ks = 0; ks < 8; ks++) {
             const uint64_t ad = smem_desc_sw128(vb + ks * 2048, BOX_BYTES, 1024);  // MN-major V^T
             const uint64_t bd = smem_desc_sw128(pb + (ks >> 2) * QS_BLK + (ks & 3) * 32, 16, 1024);
-            mma_f16_ss(tmem + O_COL + xp * NC, ad, bd, idesc_pv, ks > 0);
+            if (leader) mma_f16_ss(tmem + O_COL + xp * NC, ad, bd, idesc_pv, ks > 0);
           }
-          mma_commit(&o_full[xp]);
-          mma_commit(v_empty);
+          if (leader) mma_commit(&o_full[xp]);
+          if (leader) mma_commit(v_empty);
         }
       }
     }
