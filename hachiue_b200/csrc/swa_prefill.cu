@@ -191,12 +191,14 @@ __device__ __forceinline__ int swa_item_index(int k) {
 // Persistent kernel: one CTA per SM loops over its items.  All barriers run
 // continuously across items; their parities come from item and tile counters
 // that every role advances identically:
-//   q_full / q_empty  once per item (Q of the next item loads as soon as the
-//                     current item's last Q.K^T has read the Q tiles),
+//   q_full / q_empty  once per item and head (Q of the head's next item loads
+//                     as soon as its last Q.K^T of the current item has read
+//                     the Q tiles),
 //   kv_full / kv_empty once per key tile, ring index over all items,
-//   s_full / p_full / o_done once per key tile and head,
+//   s_full / p_half / p_full once per key tile and head,
 //   o_free            once per item and head: the epilogue has moved O out of
-//                     TMEM, so the next item's first P.V may overwrite it.
+//                     TMEM, so the next item's first P.V may overwrite it,
+//   o_done            once per head, after the CTA's last P.V.
 template <int NHD>
 __global__ void __launch_bounds__(sw_threads(NHD), 1)
     swa_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -365,7 +367,11 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
             tc_fence_after();
             pv_half(hd, s, 1, true);
             if (leader) {
-              mma_commit(&o_done[hd]);
+              // o_done only after the CTA's last P.V of the head: any other
+              // P.V is followed by a Q.K^T of the same head, whose s_full
+              // arrive (a commit tracks every earlier MMA of this thread)
+              // already tells the softmax that O is complete.
+              if (last && ntiles1 == 0) mma_commit(&o_done[hd]);
               if (hd == NHD - 1) mma_commit(&kv_empty[s]);
             }
             if (!last || ntiles1 > 0) {
@@ -402,10 +408,11 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
     // around in its own 4 KB of the head's staging buffer (thread = row on
     // the way in, 8 threads per 128-byte row segment on the way out), so
     // every global store instruction writes four whole 128-byte segments.
-    // fin_idx: the finished item (-1: none), fin_l: this row's sum of P, t_last:
-    // its last key tile.
-    auto epilogue = [&](int fin_idx, float fin_l, int t_last) -> bool {
-      if (!__all_sync(0xffffffffu, mbar_wait(&o_done[hd], t_last & 1, a.status))) return false;
+    // fin_idx: the finished item, fin_l: this row's sum of P.  O is complete
+    // once the next item's first S is in (its Q.K^T follows the last P.V);
+    // after the CTA's last item, o_done says so.
+    auto epilogue = [&](int fin_idx, float fin_l, bool last_item) -> bool {
+      if (last_item && !__all_sync(0xffffffffu, mbar_wait(&o_done[hd], 0, a.status))) return false;
       const SwaItem f = swa_item<NHD>(a, fin_idx);
       tc_fence_after();
       uint32_t o[4][32];
@@ -507,12 +514,7 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         const bool move = mx > m_use + RESCALE_LOG2 || (j == 0 && mx > m_use);
         const bool rescale_o = move && j > 0 && m_use != -INFINITY;
         const float f = rescale_o ? exp2f(m_use - mx) : 1.f;
-        if (__any_sync(0xffffffffu, rescale_o)) {
-          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[hd], (t - 1) & 1, a.status))) {  // P.V of tile j-1 landed
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale_o)) {  // P.V of tile j-1 has landed (s_full of tile j)
 #pragma unroll
           for (int c = 0; c < 4; c++) {
             uint32_t r[32];
@@ -561,7 +563,7 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[hd]);
         if (j == 0 && fin_idx >= 0) {
-          if (!epilogue(fin_idx, fin_l, kt - 1)) {
+          if (!epilogue(fin_idx, fin_l, false)) {
             ok = false;
             break;
           }
@@ -573,7 +575,7 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
       fin_l = l;
       kt += it.ntiles;
     }
-    if (ok && fin_idx >= 0) epilogue(fin_idx, fin_l, kt - 1);
+    if (ok && fin_idx >= 0) epilogue(fin_idx, fin_l, true);
   }
   tc_fence_before();
   __syncthreads();

@@ -54,19 +54,21 @@ def test_small_shapes(backend, B, T, H, KV, W, out_dtype):
 
 @pytest.mark.parametrize("ctas", [1, 3])
 @pytest.mark.parametrize("B,T,H,KV,W", [(2, 700, 8, 2, 1024), (1, 515, 6, 3, 0), (3, 257, 2, 1, 129)])
-def test_persistent_item_chains(backend, request, ctas, B, T, H, KV, W):
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_persistent_item_chains(backend, request, ctas, B, T, H, KV, W, out_dtype):
     """The kernel is persistent (one CTA per SM walks a list of work items);
     capping the grid at 1 or 3 CTAs makes every CTA run a long chain of
     items with different key ranges and head groups, and odd rounds of the
-    snake order, on shapes the oracle checks whole."""
+    snake order, on shapes the oracle checks whole.  Each item's output is
+    written while the next item runs (bf16 through the staging buffer)."""
     backend.set_option("swa_ctas", ctas)
     request.addfinalizer(lambda: backend.set_option("swa_ctas", 0))
     rng = np.random.default_rng(B * 11 + T + H + W + ctas)
     qb, kb, vb = rand_bf16(rng, (B, T, H, 128)), rand_bf16(rng, (B, T, KV, 128)), rand_bf16(rng, (B, T, KV, 128))
-    out = torch.full((B, T, H, 128), float("nan"), device=dev, dtype=torch.float32)
+    out = torch.full((B, T, H, 128), float("nan"), device=dev, dtype=out_dtype)
     backend.swa_prefill(bf16_dev(qb), bf16_dev(kb), bf16_dev(vb), out, W)
     torch.cuda.synchronize()
-    o = out.cpu().numpy()
+    o = out.float().cpu().numpy()
     assert np.isfinite(o).all()
     for b in range(B):
         check_slice(o, qb, kb, vb, b, 0, T, W)
