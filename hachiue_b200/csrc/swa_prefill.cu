@@ -413,7 +413,6 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
     // after the CTA's last item, o_done says so.
     auto epilogue = [&](int fin_idx, float fin_l, bool last_item) -> bool {
       if (last_item && !__all_sync(0xffffffffu, mbar_wait(&o_done[hd], 0, a.status))) return false;
-      const SwaItem f = swa_item<NHD>(a, fin_idx);
       tc_fence_after();
       uint32_t o[4][32];
 #pragma unroll
@@ -422,6 +421,7 @@ __global__ void __launch_bounds__(sw_threads(NHD), 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_free[hd]);
+      const SwaItem f = swa_item<NHD>(a, fin_idx);  // after o_free: the next P.V waits for it
       const float inv = 1.f / fin_l;
       if (a.out_bf16) {
         uint8_t* wst = osm + hd * OSTAGE + quarter * 4096;  // this warp's rows
