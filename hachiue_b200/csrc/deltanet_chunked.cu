@@ -147,6 +147,22 @@ __device__ __forceinline__ void store_row64(uint8_t* region, int row, const floa
   for (int u = 0; u < 8; u++) *reinterpret_cast<uint4*>(region + sw128_offset(row, 16 * u)) = pack8(x + 8 * u);
 }
 
+// Writes 64 f32 values as two 128-byte bf16 rows of 128B-swizzled regions:
+// hi = bf16(x) and lo = bf16(x - hi).
+__device__ __forceinline__ void store_row64_hilo(uint8_t* hi, uint8_t* lo, int row, const float (&x)[64]) {
+#pragma unroll
+  for (int u = 0; u < 8; u++) {
+    const uint4 h = pack8(x + 8 * u);
+    uint4 l;
+    l.x = pack2(x[8 * u + 0] - bf16_lo(h.x), x[8 * u + 1] - bf16_hi(h.x));
+    l.y = pack2(x[8 * u + 2] - bf16_lo(h.y), x[8 * u + 3] - bf16_hi(h.y));
+    l.z = pack2(x[8 * u + 4] - bf16_lo(h.z), x[8 * u + 5] - bf16_hi(h.z));
+    l.w = pack2(x[8 * u + 6] - bf16_lo(h.w), x[8 * u + 7] - bf16_hi(h.w));
+    *reinterpret_cast<uint4*>(hi + sw128_offset(row, 16 * u)) = h;
+    *reinterpret_cast<uint4*>(lo + sw128_offset(row, 16 * u)) = l;
+  }
+}
+
 // 64 TMEM columns of this thread's lane as f32.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&x)[64]) {
   uint32_t r0[32], r1[32];
@@ -158,13 +174,6 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&x)[64]) {
     x[i] = __uint_as_float(r0[i]);
     x[32 + i] = __uint_as_float(r1[i]);
   }
-}
-
-// Float index of element (r, c) of a 64 x 64 f32 matrix held as two swizzled
-// 64 x 32 halves: half c / 32 (2048 floats), row r (32 floats), 16-byte chunk
-// (c % 32) / 4 XOR r % 8.
-__device__ __forceinline__ int swf(int r, int c) {
-  return ((c >> 5) << 11) + (r << 5) + ((((c >> 2) & 7) ^ (r & 7)) << 2) + (c & 3);
 }
 
 // =====================================================================
@@ -248,7 +257,6 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
     float* A21 = reinterpret_cast<float*>(wreg + P_WG_A21);
     float* T22 = reinterpret_cast<float*>(wreg + P_WG_T22);
     float* Tf = reinterpret_cast<float*>(wreg + P_WG_T);
-    float* TbT = Tf;  // swf layout, once T has been read
     float* Ad = reinterpret_cast<float*>(wreg + P_WG_A);
     float* gam2 = reinterpret_cast<float*>(wreg + P_WG_SC);  // gamma * log2(e)
     float* betv = gam2 + 64;
@@ -337,26 +345,30 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       } else {
         const int i = t - 64;
         const float z = gam2[i] + __log2f(iqv[i]);
-        float y[64];
+        // QKm row i, the A operand of QKm Tb from TMEM lane 64 + i, as two bf16
+        // terms: hi = bf16(x) in columns 64w..64w+31 and lo = bf16(x - hi) in the
+        // next 32 (two elements per column, the even one in the low half);
+        // 32 elements at a time
 #pragma unroll
-        for (int u = 0; u < 16; u++) {
-          const float4 w4 = reinterpret_cast<const float4*>(wv)[u];
-          const int j = 4 * u;
-          const bool live = u < 8 || quad == 3;
-          y[j + 0] = live && j + 0 <= i ? tf32_round(fast_ex2(z - w4.x) * f[j + 0]) : 0.f;
-          y[j + 1] = live && j + 1 <= i ? tf32_round(fast_ex2(z - w4.y) * f[j + 1]) : 0.f;
-          y[j + 2] = live && j + 2 <= i ? tf32_round(fast_ex2(z - w4.z) * f[j + 2]) : 0.f;
-          y[j + 3] = live && j + 3 <= i ? tf32_round(fast_ex2(z - w4.w) * f[j + 3]) : 0.f;
-        }
-        // QKm row i: A operand (tf32, from TMEM) of QKm Tb, lane 64 + i
-        uint32_t r0[32], r1[32];
+        for (int hh = 0; hh < 2; hh++) {
+          uint32_t rh[16], rl[16];
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-          r0[j] = __float_as_uint(y[j]);
-          r1[j] = __float_as_uint(y[32 + j]);
+          for (int u = 0; u < 8; u++) {
+            const float4 w4 = reinterpret_cast<const float4*>(wv)[8 * hh + u];
+            const int j = 32 * hh + 4 * u;
+            const bool live = hh == 0 || quad == 3;
+            const float y0 = live && j + 0 <= i ? fast_ex2(z - w4.x) * f[j + 0] : 0.f;
+            const float y1 = live && j + 1 <= i ? fast_ex2(z - w4.y) * f[j + 1] : 0.f;
+            const float y2 = live && j + 2 <= i ? fast_ex2(z - w4.z) * f[j + 2] : 0.f;
+            const float y3 = live && j + 3 <= i ? fast_ex2(z - w4.w) * f[j + 3] : 0.f;
+            rh[2 * u] = pack2(y0, y1);
+            rh[2 * u + 1] = pack2(y2, y3);
+            rl[2 * u] = pack2(y0 - bf16_lo(rh[2 * u]), y1 - bf16_hi(rh[2 * u]));
+            rl[2 * u + 1] = pack2(y2 - bf16_lo(rh[2 * u + 1]), y3 - bf16_hi(rh[2 * u + 1]));
+          }
+          tmem_st16(tmem + lo + 64 * wg + 16 * hh, rh);
+          tmem_st16(tmem + lo + 64 * wg + 32 + 16 * hh, rl);
         }
-        tmem_st32(tmem + lo + 64 * wg, r0);
-        tmem_st32(tmem + lo + 64 * wg + 32, r1);
         tmem_st_wait();
         tc_fence_before();
       }
@@ -516,8 +528,9 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       }
       tc_fence_before();
       ok = named_bar_and(bid, 128, ok);
-      // Tb = T diag(beta): row t is W row t; its transpose (rows of Tb^T, in
-      // T's place) is the K-major B operand of QKm Tb.
+      // Tb = T diag(beta): row t is W row t.  As two bf16 terms (hi = W row t,
+      // lo = the rounding residual in W's rows 64-127 until QKm Tb is done) it is
+      // the MN-major B operand of QKm Tb.
       float y[64];
       if (ok && t < 64) {
 #pragma unroll
@@ -533,7 +546,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
             y[j] = (j < t ? tv[e] : (j == t ? 1.f : 0.f)) * bb[e];
           }
         }
-        store_row64(wst, t, y);
+        store_row64_hilo(wst, wst + 8192, t, y);
         const float G = fast_ex2(gam2[t]), e63 = fast_ex2(gam2[63]);
         float* scu = a.sc + unit * SC_FLOATS;
         scu[t] = G * ikv[t];
@@ -541,30 +554,27 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         scu[128 + t] = ikv[t] * fast_ex2(gam2[63] - gam2[t]);
         scu[192 + t] = e63;
       }
-      named_bar(bid, 128);  // every row of T has been read
-      if (ok && t < 64) {
-        // Tb^T[n][t] = Tb[t][n] at swf(n, t): eight per-thread bases for n % 8
-        const int tb0 = ((t >> 5) << 11) + (t & 3), tcx = (t >> 2) & 7;
-        int offk[8];
-#pragma unroll
-        for (int k8 = 0; k8 < 8; k8++) offk[k8] = tb0 + ((tcx ^ k8) << 2);
-#pragma unroll
-        for (int n2 = 0; n2 < 64; n2++) TbT[offk[n2 & 7] + (n2 << 5)] = tf32_round(y[n2]);
-      }
       fence_proxy_async();
       tc_fence_before();
       ok = named_bar_and(bid, 128, ok);
       if (ok && quad == 0) {
-        // QKm Tb (M = 128: rows 64-127 are QKm's, from TMEM lanes 64-127; rows
-        // 0-63 read lanes 0-63 of the same columns and are not used)
+        // QKm Tb = QKm_hi Tb_hi + QKm_hi Tb_lo + QKm_lo Tb_hi (M = 128: rows 64-127
+        // are QKm's, from TMEM lanes 64-127; rows 0-63 read lanes 0-63 of the same
+        // columns and are not used)
         const bool leader = elect_one_sync();
         tc_fence_after();
-        constexpr uint32_t id_g = idesc_tf32(128, 64, false, false);
-        const uint32_t tb = smem_u32(TbT);
+        constexpr uint32_t id_g = idesc_f16(128, 64, true, false, true);  // bf16, A from TMEM, B MN-major
+        const uint32_t wb = smem_u32(wst);
+        const uint32_t qh = tmem + 64 * wg, ql = qh + 32;
 #pragma unroll
-        for (int ks = 0; ks < 8; ks++) {
-          const uint64_t bd = smem_desc_sw128(tb + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024);
-          if (leader) mma_tf32_ts(tl3, tmem + 64 * wg + 8 * ks, bd, id_g, ks > 0);
+        for (int ks = 0; ks < 4; ks++) {
+          const uint64_t bh = smem_desc_sw128(wb + ks * 2048, 8192, 1024);
+          const uint64_t bl = smem_desc_sw128(wb + 8192 + ks * 2048, 8192, 1024);
+          if (leader) {
+            mma_f16_ts(tl3, qh + 8 * ks, bh, id_g, ks > 0);
+            mma_f16_ts(tl3, qh + 8 * ks, bl, id_g, 1);
+            mma_f16_ts(tl3, ql + 8 * ks, bh, id_g, 1);
+          }
         }
         if (leader) mma_commit(&bar_g[wg]);
       }
