@@ -200,6 +200,13 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
   if (tid == 0) {
     for (int i = 0; i < P_NBAR; i++) mbar_init(&bars[i], 1);
     fence_barrier_init();
+    // The K / Q chunk is requested first of all, before the TMEM allocation
+    // and the block barrier (only this thread uses bar_kq before that barrier).
+    mbar_arrive_expect_tx(bar_kq, 32768);
+    tma_load_4d(sm + P_OFF_KQ, &tmK, bar_kq, 0, hk, t0, b);
+    tma_load_4d(sm + P_OFF_KQ + 8192, &tmQ, bar_kq, 0, hk, t0, b);
+    tma_load_4d(sm + P_OFF_KQ + 16384, &tmK, bar_kq, 64, hk, t0, b);
+    tma_load_4d(sm + P_OFF_KQ + 24576, &tmQ, bar_kq, 64, hk, t0, b);
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, 256);
@@ -211,8 +218,8 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // One elected lane issues the loads and the MMAs; the whole warp waits
-    // and forms the (warp-uniform) descriptors.
+    // One elected lane issues the MMAs; the whole warp waits and forms the
+    // (warp-uniform) descriptors.
     const bool leader = elect_one_sync();
     // warm L2 with the K / Q chunk that the CTA one wave later (a.ahead
     // blocks further in launch order) will load
@@ -229,11 +236,6 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         tma_prefetch_l2_4d(&tmK, 64, hf, tf, (int)bf);
         tma_prefetch_l2_4d(&tmQ, 64, hf, tf, (int)bf);
       }
-      mbar_arrive_expect_tx(bar_kq, 32768);
-      tma_load_4d(sm + P_OFF_KQ, &tmK, bar_kq, 0, hk, t0, b);
-      tma_load_4d(sm + P_OFF_KQ + 8192, &tmQ, bar_kq, 0, hk, t0, b);
-      tma_load_4d(sm + P_OFF_KQ + 16384, &tmK, bar_kq, 64, hk, t0, b);
-      tma_load_4d(sm + P_OFF_KQ + 24576, &tmQ, bar_kq, 64, hk, t0, b);
     }
     if (__all_sync(0xffffffffu, mbar_wait(bar_kq, 0, a.status))) {
       tc_fence_after();
@@ -406,7 +408,8 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         }
       } else {
         // zero the upper off-diagonal 16x16 blocks (0,1) and (2,3), in T and in
-        // the combine operands: the 32x32 diagonal blocks are read whole below
+        // the combine operands (the 32x32 diagonal blocks are read whole below),
+        // and T's upper 32x32 block, so that T's rows read whole
         for (int e = t - 64; e < 512; e += 64) {
           const int blk = e >> 8, r = (e >> 4) & 15, cc = e & 15;
           Tf[(blk * 32 + r) * AS + blk * 32 + 16 + cc] = 0.f;
@@ -418,6 +421,9 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
             T22[r * 32 + (((col >> 2) ^ (r & 7)) << 2) + (col & 3)] = 0.f;
           }
         }
+#pragma unroll
+        for (int e = t - 64; e < 256; e += 64)
+          *reinterpret_cast<float4*>(&Tf[(e >> 3) * AS + 32 + 4 * (e & 7)]) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
       named_bar(bid, 128);
       {
@@ -533,18 +539,15 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       // the MN-major B operand of QKm Tb.
       float y[64];
       if (ok && t < 64) {
+        // T's row t: unit diagonal, zeros (or -0) above it
 #pragma unroll
         for (int u = 0; u < 16; u++) {
-          const bool live = u < 8 || quad == 1;
-          float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (live) v4 = *reinterpret_cast<const float4*>(&Tf[t * AS + 4 * u]);
+          const float4 v4 = *reinterpret_cast<const float4*>(&Tf[t * AS + 4 * u]);
           const float4 b4 = reinterpret_cast<const float4*>(betv)[u];
-          const float tv[4] = {v4.x, v4.y, v4.z, v4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const int j = 4 * u + e;
-            y[j] = (j < t ? tv[e] : (j == t ? 1.f : 0.f)) * bb[e];
-          }
+          y[4 * u] = v4.x * b4.x;
+          y[4 * u + 1] = v4.y * b4.y;
+          y[4 * u + 2] = v4.z * b4.z;
+          y[4 * u + 3] = v4.w * b4.w;
         }
         store_row64_hilo(wst, wst + 8192, t, y);
         const float G = fast_ex2(gam2[t]), e63 = fast_ex2(gam2[63]);
