@@ -196,6 +196,16 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
   const int c = blockIdx.x, b = blockIdx.z;
   const int hk = blockIdx.y % a.NK, pair = blockIdx.y / a.NK;
   const int t0 = (a.c0 + c) * GC;
+  const int wg = warp >> 2, quad = warp & 3, t = quad * 32 + lane;
+  const int h = hk + (2 * pair + wg) * a.NK;
+  const bool active = h < a.NV;
+  // g and beta of this thread's row (t < 64), requested before the set-up
+  float gi = 0.f, bi = 0.f;
+  if (active && t < 64 && t0 + t < a.T) {
+    const size_t idx = (size_t)b * a.gb_seq + (size_t)(t0 + t) * a.gb_row + h;
+    gi = __ldg(a.g + idx);
+    bi = __ldg(a.beta + idx);
+  }
 
   if (tid == 0) {
     for (int i = 0; i < P_NBAR; i++) mbar_init(&bars[i], 1);
@@ -250,9 +260,6 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
     }
   }
 
-  const int wg = warp >> 2, quad = warp & 3, t = quad * 32 + lane;
-  const int h = hk + (2 * pair + wg) * a.NK;
-  const bool active = h < a.NV;
   {
     uint8_t* wreg = sm + P_OFF_WG + wg * P_WG_STRIDE;
     uint8_t* kqh = sm + P_OFF_KQ + wg * 16384;  // this warpgroup's half of the K/Q buffer, after (f)
@@ -275,12 +282,6 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
     const uint32_t bid = 1 + wg;
     const size_t unit = ((size_t)b * a.NV + h) * a.ns + c;
 
-    float gi = 0.f, bi = 0.f;
-    if (active && t < 64 && t0 + t < a.T) {
-      const size_t idx = (size_t)b * a.gb_seq + (size_t)(t0 + t) * a.gb_row + h;
-      gi = __ldg(a.g + idx);
-      bi = __ldg(a.beta + idx);
-    }
     bool ok = active && named_bar_and(bid, 128, mbar_wait(bar_f, 0, a.status));
     float nrm2 = 0.f, f[64];  // f: G row t (t < 64) or P row t - 64: k_t . k_j / q_i . k_j
     if (ok) {
