@@ -561,6 +561,11 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       fence_proxy_async();
       tc_fence_before();
       ok = named_bar_and(bid, 128, ok);
+      // W's rows 0-63 (Tb) are final: they go out now, read alongside QKm Tb
+      if (ok && t == 0) {
+        tma_store_2d(&tmW, wst, 0, (int)(unit * 128));
+        tma_store_commit();
+      }
       if (ok && quad == 0) {
         // QKm Tb = QKm_hi Tb_hi + QKm_hi Tb_lo + QKm_lo Tb_hi (M = 128: rows 64-127
         // are QKm's, from TMEM lanes 64-127; rows 0-63 read lanes 0-63 of the same
@@ -591,7 +596,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       }
       ok = named_bar_and(bid, 128, ok);
       if (ok && t == 0) {
-        tma_store_2d(&tmW, wst, 0, (int)(unit * 128));
+        tma_store_2d(&tmW, wst + 8192, 0, (int)(unit * 128 + 64));
         tma_store_commit_and_wait_read();
       }
     }
@@ -982,7 +987,7 @@ int chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q
       reinterpret_cast<uintptr_t>(snapshots) % 16)
     return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: core / state buffers must be 16-byte aligned");
   const long long snap_count = snap_every ? T / (hcu::GC * (long long)snap_every) : 0;
-  CUtensorMap tq, tk, tv, tw, ts, to;
+  CUtensorMap tq, tk, tv, tw, twh, ts, to;
   {
     uint64_t dims[4] = {128, (uint64_t)NK, (uint64_t)T, (uint64_t)B};
     uint64_t st[3] = {256, (uint64_t)qrow * 2, (uint64_t)qseq * 2};
@@ -1028,6 +1033,9 @@ int chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q
     uint32_t box[2] = {64, 128};
     HCU_TRY(hcu::make_tensor_map(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wbuf, dims, st, box,
                                  CU_TENSOR_MAP_SWIZZLE_128B));
+    uint32_t hbox[2] = {64, 64};  // the prep stores W as two 64-row halves
+    HCU_TRY(hcu::make_tensor_map(&twh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wbuf, dims, st, hbox,
+                                 CU_TENSOR_MAP_SWIZZLE_128B));
     uint64_t sdims[2] = {64, (uint64_t)units * 4};
     uint64_t sst[1] = {256};
     uint32_t sbox[2] = {64, 4};
@@ -1065,7 +1073,7 @@ int chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q
     pa.sc = sbuf;
     pa.status = h->dev_status;
     hcu::gdn_prep_kernel<<<dim3((unsigned)cnt, (unsigned)(NK * npair), (unsigned)B), hcu::PREP_THREADS,
-                           hcu::P_SMEM + 1024, h->stream>>>(tq, tk, tw, pa);
+                           hcu::P_SMEM + 1024, h->stream>>>(tq, tk, twh, pa);
     HCU_TRY(hcu::after_launch("hcu_deltanet_chunked_prefill: prep launch"));
     hcu::ChainArgs ca{};
     ca.T = (int)T;
