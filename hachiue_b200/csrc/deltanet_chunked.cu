@@ -147,19 +147,19 @@ __device__ __forceinline__ void store_row64(uint8_t* region, int row, const floa
   for (int u = 0; u < 8; u++) *reinterpret_cast<uint4*>(region + sw128_offset(row, 16 * u)) = pack8(x + 8 * u);
 }
 
-// Writes 64 f32 values as two 128-byte bf16 rows of 128B-swizzled regions:
-// hi = bf16(x) and lo = bf16(x - hi).
-__device__ __forceinline__ void store_row64_hilo(uint8_t* hi, uint8_t* lo, int row, const float (&x)[64]) {
+// Writes 32 f32 values as half hc (bytes 64 hc .. 64 hc + 63) of two 128-byte
+// bf16 rows of 128B-swizzled regions: hi = bf16(x) and lo = bf16(x - hi).
+__device__ __forceinline__ void store_row32_hilo(uint8_t* hi, uint8_t* lo, int row, int hc, const float (&x)[32]) {
 #pragma unroll
-  for (int u = 0; u < 8; u++) {
+  for (int u = 0; u < 4; u++) {
     const uint4 h = pack8(x + 8 * u);
     uint4 l;
     l.x = pack2(x[8 * u + 0] - bf16_lo(h.x), x[8 * u + 1] - bf16_hi(h.x));
     l.y = pack2(x[8 * u + 2] - bf16_lo(h.y), x[8 * u + 3] - bf16_hi(h.y));
     l.z = pack2(x[8 * u + 4] - bf16_lo(h.z), x[8 * u + 5] - bf16_hi(h.z));
     l.w = pack2(x[8 * u + 6] - bf16_lo(h.w), x[8 * u + 7] - bf16_hi(h.w));
-    *reinterpret_cast<uint4*>(hi + sw128_offset(row, 16 * u)) = h;
-    *reinterpret_cast<uint4*>(lo + sw128_offset(row, 16 * u)) = l;
+    *reinterpret_cast<uint4*>(hi + sw128_offset(row, 64 * hc + 16 * u)) = h;
+    *reinterpret_cast<uint4*>(lo + sw128_offset(row, 64 * hc + 16 * u)) = l;
   }
 }
 
@@ -538,25 +538,30 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       // Tb = T diag(beta): row t is W row t.  As two bf16 terms (hi = W row t,
       // lo = the rounding residual in W's rows 64-127 until QKm Tb is done) it is
       // the MN-major B operand of QKm Tb.
-      float y[64];
-      if (ok && t < 64) {
-        // T's row t: unit diagonal, zeros (or -0) above it
+      // Threads t and t + 64 take the two 32-column halves of row t % 64 (T's row:
+      // unit diagonal, zeros or -0 above it) and two of its four scalars each.
+      if (ok) {
+        const int row = t & 63, hc = t >> 6;
+        float yh[32];
 #pragma unroll
-        for (int u = 0; u < 16; u++) {
-          const float4 v4 = *reinterpret_cast<const float4*>(&Tf[t * AS + 4 * u]);
-          const float4 b4 = reinterpret_cast<const float4*>(betv)[u];
-          y[4 * u] = v4.x * b4.x;
-          y[4 * u + 1] = v4.y * b4.y;
-          y[4 * u + 2] = v4.z * b4.z;
-          y[4 * u + 3] = v4.w * b4.w;
+        for (int u = 0; u < 8; u++) {
+          const float4 v4 = *reinterpret_cast<const float4*>(&Tf[row * AS + 32 * hc + 4 * u]);
+          const float4 b4 = reinterpret_cast<const float4*>(betv)[8 * hc + u];
+          yh[4 * u] = v4.x * b4.x;
+          yh[4 * u + 1] = v4.y * b4.y;
+          yh[4 * u + 2] = v4.z * b4.z;
+          yh[4 * u + 3] = v4.w * b4.w;
         }
-        store_row64_hilo(wst, wst + 8192, t, y);
-        const float G = fast_ex2(gam2[t]), e63 = fast_ex2(gam2[63]);
+        store_row32_hilo(wst, wst + 8192, row, hc, yh);
         float* scu = a.sc + unit * SC_FLOATS;
-        scu[t] = G * ikv[t];
-        scu[64 + t] = G * iqv[t];
-        scu[128 + t] = ikv[t] * fast_ex2(gam2[63] - gam2[t]);
-        scu[192 + t] = e63;
+        if (hc == 0) {
+          const float G = fast_ex2(gam2[row]);
+          scu[row] = G * ikv[row];
+          scu[64 + row] = G * iqv[row];
+        } else {
+          scu[128 + row] = ikv[row] * fast_ex2(gam2[63] - gam2[row]);
+          scu[192 + row] = fast_ex2(gam2[63]);
+        }
       }
       fence_proxy_async();
       tc_fence_before();
@@ -589,6 +594,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       }
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_g[wg], 0, a.status));
       if (ok && quad >= 2) {
+        float y[64];
         tc_fence_after();
         tmem_ld64(tl3 + lo, y);
         store_row64(wst, t, y);  // W row 64 + i = (QKm Tb) row i
