@@ -607,6 +607,9 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       }
     }
   }
+  // A timed-out wait can skip the final store: W's early store must still have
+  // read shared memory before the CTA exits.
+  if (t == 0) tma_store_wait_read();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -647,8 +650,12 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
   float* scal = reinterpret_cast<float*>(sm + C_OFF_SC);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int dvb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int hk = h % a.NK;
+  // Grid (2 x V heads per QK head, QK heads, sequences): the CTAs of one QK
+  // head's V heads h = hk, hk + NK, ... and both value-column halves are
+  // adjacent, so they run together and share each chunk's K / Q tiles in L2.
+  const int dvb = blockIdx.x & 1, hk = blockIdx.y, b = blockIdx.z;
+  const int h = hk + (int)(blockIdx.x >> 1) * a.NK;
+  if (h >= a.NV) return;  // the whole CTA, before any barrier or allocation
   const int n = a.cnt;
   const size_t unit0 = ((size_t)b * a.NV + h) * a.ns;
 
@@ -1096,8 +1103,9 @@ int chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q
     ca.snap = snap_count > 0 ? snapshots : nullptr;
     ca.snap_every = (int)snap_every;
     ca.snap_count = snap_count;
-    hcu::gdn_chain_kernel<<<dim3(hcu::GD / hcu::DVB, (unsigned)NV, (unsigned)B), hcu::CHAIN_THREADS,
-                            hcu::C_SMEM + 1024, h->stream>>>(tq, tk, tv, tw, ts, to, ca);
+    const long long nvper = (NV + NK - 1) / NK;  // V heads per QK head (the last QK heads may have fewer)
+    const dim3 cgrid((unsigned)(hcu::GD / hcu::DVB * nvper), (unsigned)NK, (unsigned)B);
+    hcu::gdn_chain_kernel<<<cgrid, hcu::CHAIN_THREADS, hcu::C_SMEM + 1024, h->stream>>>(tq, tk, tv, tw, ts, to, ca);
     HCU_TRY(hcu::after_launch("hcu_deltanet_chunked_prefill: chain launch"));
   }
   return HCU_OK;
