@@ -22,6 +22,7 @@ struct AttnArgs {
   float qscale;    // log2(e) / sqrt(Dh)
   float* part;     // [units, max_splits, R, DH + 2]: acc[DH], m (log2), l
   int* counters;   // [kMaxUnits] split-merge tickets, 0 between calls
+  int cluster;     // 1: the split CTAs of a unit are one thread-block cluster and merge through DSMEM
   uint32_t* status;
   const float* gate;  // null, or [B, S, H, Dh]: out *= sigmoid(gate) (qwen35 sigmoid_gate)
   float q8_smul;      // Q8_0: element = q * scale * q8_smul (1, or 1/127 for the WGSL convention)
@@ -158,6 +159,66 @@ __device__ void ticket_merge(const AttnArgs& a, const AttnUnit& u, int tid, int 
     if (e < E && r < u.rows_valid) store_out(a, out_index(a, u, r, d, DH), acc[k]);
   }
   if (tid == 0) a.counters[u.unit] = 0;  // re-arm for the next call
+}
+
+// Thread-block cluster barrier over every thread of every CTA in the cluster
+// (release / acquire: shared-memory writes before it are visible to the
+// cluster's reads after it).  All threads of each warp execute it together.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The float at `local` (this CTA's shared memory) in the shared memory of
+// cluster CTA `rank`.
+__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+constexpr int kMaxClusterSplits = 16;  // the largest (non-portable) cluster the split CTAs of a unit may form
+
+// The cluster form of the split merge: CTA `split` of a unit's cluster left its
+// partial (acc[R][DH], m, l per row, layout [R][DH + 2]) at `cp` in its own
+// shared memory, and every CTA of the cluster has passed a cluster barrier.
+// Each CTA merges its slice of the unit's R * DH outputs, reading the partials
+// of all n splits through distributed shared memory.  Every thread of the CTA
+// (NT) takes part; the caller ends with a second cluster barrier, so no CTA
+// leaves while another still reads its partial.
+template <int R, int DH, int NT>
+__device__ __forceinline__ void cluster_merge(const AttnArgs& a, const AttnUnit& u, int n, const float* cp, int tid,
+                                              bool write) {
+  constexpr int E = R * DH;
+  constexpr size_t RS = DH + 2;
+  const int ncta = (int)gridDim.x, per = (E + ncta - 1) / ncta, e0 = (int)blockIdx.x * per;
+  for (int e = e0 + tid; e < min(E, e0 + per); e += NT) {
+    const int r = e / DH, d = e % DH;
+    float mv[kMaxClusterSplits], lv[kMaxClusterSplits], av[kMaxClusterSplits];
+#pragma unroll
+    for (int sp = 0; sp < kMaxClusterSplits; sp++) {
+      if (sp < n) {
+        mv[sp] = ld_cluster_f32(cp + r * RS + DH, sp);
+        lv[sp] = ld_cluster_f32(cp + r * RS + DH + 1, sp);
+        av[sp] = ld_cluster_f32(cp + r * RS + d, sp);
+      }
+    }
+    float M = -1e30f;
+#pragma unroll
+    for (int sp = 0; sp < kMaxClusterSplits; sp++)
+      if (sp < n) M = fmaxf(M, mv[sp]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < kMaxClusterSplits; sp++) {
+      if (sp < n) {
+        const float w = exp2f(mv[sp] - M);
+        L = fmaf(lv[sp], w, L);
+        A = fmaf(av[sp], w, A);
+      }
+    }
+    if (write && r < u.rows_valid) store_out(a, out_index(a, u, r, d, DH), A / L);
+  }
 }
 
 // Host launcher of the tcgen05 kernel (attention_decode_tc.cu).  Returns

@@ -164,15 +164,21 @@ __global__ void __launch_bounds__(NTHREADS, ctas_per_sm(R, DH))
   const int warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x;
   const AttnUnit u = attn_unit(a, split);
-  if (u.nsplit > (int)gridDim.x) {  // max_context under-stated by the caller: refuse, never half-merge
+  // In the cluster form every CTA of the unit's cluster reaches the cluster
+  // barriers, with or without work; otherwise a CTA without work leaves here,
+  // uniformly and before any barrier.
+  const bool clus = a.cluster != 0;
+  const bool badarg = u.nsplit > (int)gridDim.x;
+  if (badarg) {  // max_context under-stated by the caller: refuse, never half-merge
     if (split == 0 && threadIdx.x == 0) atomicOr(a.status, HCU_DEVERR_BADARG);
-    return;
+    if (!clus) return;
   }
-  if (split >= u.nsplit) return;  // uniform for the CTA, before any barrier
+  const bool has_work = !badarg && split < u.nsplit;
+  if (!clus && !has_work) return;
   const int g = u.g, b = u.b, pb = u.pb, q0 = u.q0, qn = u.qn;
   const int k_lo = u.k_lo, k_hi = u.k_hi;
   const long long roff = u.roff;
-  const int ntiles = (k_hi - k_lo + TT - 1) / TT;
+  const int ntiles = has_work ? (k_hi - k_lo + TT - 1) / TT : 0;
 
   if (tid == 0) {
     for (int s = 0; s < NST; s++) {
@@ -202,7 +208,12 @@ __global__ void __launch_bounds__(NTHREADS, ctas_per_sm(R, DH))
         }
       }
     }
-    return;  // the producer takes no part in the epilogue (named barriers below)
+    // the producer takes no part in the epilogue (named barriers below); in the
+    // cluster form it still joins the cluster barriers
+    if (!clus) return;
+    cluster_sync_all();
+    cluster_sync_all();
+    return;
   }
 
   // ---------------- consumers ----------------
@@ -369,6 +380,34 @@ __global__ void __launch_bounds__(NTHREADS, ctas_per_sm(R, DH))
   // One decision for all consumer warps (a bounded wait may give up in some
   // warps only): the merge below synchronises them on named barriers.
   aborted = !named_bar_and(1, NW * 32, !aborted);
+  if (clus) {
+    // This CTA's partial into its own shared memory (an empty one without
+    // work or after a timed-out wait), then the merge across the cluster.
+    float* cp = cl + NW * R;  // [R][DH + 2], after the per-warp partials read below
+    for (int e = tid; e < R * DH; e += NW * 32) {
+      const int r = e / DH, d = e % DH;
+      float M = -1e30f;
+#pragma unroll
+      for (int w = 0; w < NW; w++) M = fmaxf(M, cm[w * R + r]);
+      float L = 0.f, A = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; w++) {
+        const float f = exp2f(cm[w * R + r] - M);
+        L += cl[w * R + r] * f;
+        A += cb[(w * R + r) * DH + d] * f;
+      }
+      const bool keep = has_work && !aborted;
+      cp[r * (DH + 2) + d] = keep ? A : 0.f;
+      if (d == 0) {
+        cp[r * (DH + 2) + DH] = keep ? M : -1e30f;
+        cp[r * (DH + 2) + DH + 1] = keep ? L : 0.f;
+      }
+    }
+    cluster_sync_all();
+    cluster_merge<R, DH, NW * 32>(a, u, badarg ? 0 : min(u.nsplit, (int)gridDim.x), cp, tid, !badarg);
+    cluster_sync_all();
+    return;
+  }
   if (aborted) {
     // The status word holds the timeout.  A multi-split unit still takes its
     // ticket so that the unit's last CTA re-arms it (its output is garbage,
@@ -419,15 +458,36 @@ int launch_t(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap&
   constexpr int NST = stages_for(R, DH);
   const size_t smem = NST * C::STAGE_BYTES + 2 * NST * sizeof(uint64_t) + NW * C::TPW * R * sizeof(float) + 16;
   // the per-warp partials and the split merge reuse the stage buffers
-  static_assert((NW * R * DH + 2 * NW * R) * 4 <= NST * C::STAGE_BYTES && kMaxSplits * R * 4 <= NST * C::STAGE_BYTES,
+  static_assert((NW * R * DH + 2 * NW * R + R * (DH + 2)) * 4 <= NST * C::STAGE_BYTES &&
+                    kMaxSplits * R * 4 <= NST * C::STAGE_BYTES,
                 "merge buffers exceed the stage memory");
   static std::atomic<uint64_t> attr_done{0};  // per device
   HCU_TRY(once_per_device(attr_done, h->device, [&]() -> int {
     HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "hcu_attention: smem attribute"));
+    // clusters of up to kMaxClusterSplits (16) CTAs: above the portable 8
+    HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                       "hcu_attention: cluster attribute"));
     return HCU_OK;
   }));
-  kern<<<grid, NTHREADS, smem, h->stream>>>(tk, tv, tks, tvs, args);
+  if (!args.cluster) {
+    kern<<<grid, NTHREADS, smem, h->stream>>>(tk, tv, tks, tvs, args);
+    return after_launch("hcu_attention: launch");
+  }
+  // The split CTAs of a unit (gridDim.x of them) form one cluster.
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(NTHREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = h->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = grid.x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  HCU_TRY(check_cuda(cudaLaunchKernelEx(&cfg, kern, tk, tv, tks, tvs, args), "hcu_attention: cluster launch"));
   return after_launch("hcu_attention: launch");
 }
 
@@ -543,6 +603,12 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
                 need(chunk));
   const long long max_splits = (max_range + chunk - 1) / chunk;
   if (max_splits > kMaxSplits || chunk > 0x7fffffff) return fail(HCU_EINVAL, "hcu_attention: too many splits");
+  // A small CUDA-core launch merges its splits inside thread-block clusters
+  // (one per unit, through distributed shared memory) instead of through
+  // tickets and partials in L2: its merge is then a few hundred cycles rather
+  // than a few microseconds of dependent L2 round trips.
+  const bool cluster = !use_tc && max_splits >= 2 && max_splits <= hcu::kMaxClusterSplits &&
+                       units * max_splits <= 2LL * h->sm_count;
 
   // TMA descriptors over the whole cache: dims (Dh, KV, rows).  The tensor-core
   // kernel loads 64-element (128-byte) boxes with the 128-byte swizzle its
@@ -593,6 +659,7 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   args.max_splits = (int)max_splits;
   args.qscale = kLog2e / sqrtf((float)Dh);
   args.counters = static_cast<int*>(h->workspace);
+  args.cluster = cluster ? 1 : 0;
   args.part = reinterpret_cast<float*>(static_cast<char*>(h->workspace) + cnt_bytes);
   args.status = h->dev_status;
   args.gate = p->gate;

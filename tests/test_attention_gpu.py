@@ -398,3 +398,47 @@ def test_q8_batched_ragged_sequences(backend, request, impl):
     assert np.isfinite(got).all()
     assert rel_l2(got, ref) < TOL
     assert backend.device_status() == 0
+
+
+@pytest.mark.parametrize("fmt,H,KV,lens,W,cuda_cores", [
+    (KV_F32, 8, 2, [1, 50, 300, 1000], 0, 0),   # 16 splits of 64 keys; units with 1, 1, 5 and 16 splits
+    (KV_F32, 16, 8, [1000, 640], 300, 0),       # a window: 5 splits per unit
+    (KV_Q8_0, 32, 4, [900, 1024], 0, 0),        # GQA group 8 on Q8_0: the CUDA-core kernel, 4 splits of 256 keys
+    (KV_F16, 16, 8, [1024], 0, 1),              # f16 forced onto the CUDA-core kernel: 8 splits of 128 keys
+])
+def test_cluster_merge_of_small_launches(backend, request, fmt, H, KV, lens, W, cuda_cores):
+    """Small CUDA-core launches (a few sequences, at most 16 key splits per
+    unit) merge their splits inside thread-block clusters through distributed
+    shared memory; units whose sequence needs fewer splits than the cluster
+    holds leave empty partials in the other CTAs."""
+    backend.set_option("attn_cuda_cores", cuda_cores)
+    request.addfinalizer(lambda: backend.set_option("attn_cuda_cores", 0))
+    rng = np.random.default_rng(sum(lens) + H + KV + W)
+    lens = np.array(lens)
+    off = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    B = len(lens)
+    kf = rng.standard_normal((lens.sum(), KV, 128), dtype=np.float32)
+    vf = rng.standard_normal((lens.sum(), KV, 128), dtype=np.float32)
+    q = rng.standard_normal((B, 1, H, 128), dtype=np.float32)
+    if fmt == KV_Q8_0:
+        cache = KVCache.allocate(int(lens.sum()), KV, 128, KV_Q8_0)
+        backend.kv_append(T(kf), cache, "k", 0)
+        backend.kv_append(T(vf), cache, "v", 0)
+        kref, vref = cache.k.cpu().numpy(), cache.v.cpu().numpy()
+        scales = (cache.k_scale.cpu().numpy(), cache.v_scale.cpu().numpy())
+    elif fmt == KV_F16:
+        kh, vh = kf.astype(np.float16), vf.astype(np.float16)
+        cache = KVCache(KV_F16, T(kh.view(np.int16), torch.float16), T(vh.view(np.int16), torch.float16))
+        kref, vref, scales = kh.view(np.uint16), vh.view(np.uint16), ()
+    else:
+        cache = KVCache(KV_F32, T(kf), T(vf))
+        kref, vref, scales = kf, vf, ()
+    out = torch.full((B, 1, H, 128), float("nan"), device=dev)
+    backend.attention(T(q), cache, out, T((lens - 1).astype(np.int32)), W, kv_row_offset=T(off.astype(np.int64)),
+                      max_context=int(lens.max()))
+    torch.cuda.synchronize()
+    ref = oracle.attention_batch(q, kref, vref, lens - 1, off, W, fmt, *scales)
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_l2(got, ref) < TOL
+    assert backend.device_status() == 0
