@@ -3,6 +3,8 @@
 // attention_decode_tc.cu): launch arguments and the split-K epilogue.
 #pragma once
 
+#include <utility>
+
 #include "common.cuh"
 #include "context.h"
 
@@ -219,6 +221,26 @@ __device__ __forceinline__ void cluster_merge(const AttnArgs& a, const AttnUnit&
     }
     if (write && r < u.rows_valid) store_out(a, out_index(a, u, r, d, DH), A / L);
   }
+}
+
+// Launches `kern` with the split CTAs of each unit (gridDim.x of them, at most
+// kMaxClusterSplits) as one thread-block cluster.
+template <typename... KArgs, typename... Args>
+int launch_cluster_x(void (*kern)(KArgs...), dim3 grid, int threads, size_t smem, cudaStream_t stream,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3((unsigned)threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = grid.x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), "hcu_attention: cluster launch");
 }
 
 // Host launcher of the tcgen05 kernel (attention_decode_tc.cu).  Returns

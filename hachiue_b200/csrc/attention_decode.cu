@@ -474,20 +474,7 @@ int launch_t(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap&
     kern<<<grid, NTHREADS, smem, h->stream>>>(tk, tv, tks, tvs, args);
     return after_launch("hcu_attention: launch");
   }
-  // The split CTAs of a unit (gridDim.x of them) form one cluster.
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(NTHREADS, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = h->stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = grid.x;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  HCU_TRY(check_cuda(cudaLaunchKernelEx(&cfg, kern, tk, tv, tks, tvs, args), "hcu_attention: cluster launch"));
+  HCU_TRY(launch_cluster_x(kern, grid, NTHREADS, smem, h->stream, tk, tv, tks, tvs, args));
   return after_launch("hcu_attention: launch");
 }
 
@@ -603,11 +590,11 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
                 need(chunk));
   const long long max_splits = (max_range + chunk - 1) / chunk;
   if (max_splits > kMaxSplits || chunk > 0x7fffffff) return fail(HCU_EINVAL, "hcu_attention: too many splits");
-  // A small CUDA-core launch merges its splits inside thread-block clusters
+  // A small launch merges its splits inside thread-block clusters
   // (one per unit, through distributed shared memory) instead of through
   // tickets and partials in L2: its merge is then a few hundred cycles rather
   // than a few microseconds of dependent L2 round trips.
-  const bool cluster = !use_tc && max_splits >= 2 && max_splits <= hcu::kMaxClusterSplits &&
+  const bool cluster = (!use_tc || fmt != HCU_KV_Q8_0) && max_splits >= 2 && max_splits <= hcu::kMaxClusterSplits &&
                        units * max_splits <= 2LL * h->sm_count;
 
   // TMA descriptors over the whole cache: dims (Dh, KV, rows).  The tensor-core

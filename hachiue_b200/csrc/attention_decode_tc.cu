@@ -115,11 +115,22 @@ __global__ void __launch_bounds__(TC_THREADS, NC == 16 ? 2 : 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x;
   const AttnUnit u = attn_unit(a, split);
-  if (u.nsplit > (int)gridDim.x) {
-    if (split == 0 && tid == 0) atomicOr(a.status, HCU_DEVERR_BADARG);
+  // In the cluster form every CTA of the unit's cluster reaches the two
+  // cluster barriers; a CTA without work only contributes an empty partial.
+  const bool clus = a.cluster != 0;
+  const bool badarg = u.nsplit > (int)gridDim.x;
+  if (badarg && split == 0 && tid == 0) atomicOr(a.status, HCU_DEVERR_BADARG);
+  if (badarg || split >= u.nsplit) {
+    if (!clus) return;
+    float* cp = reinterpret_cast<float*>(stages);  // [R][Dh + 2]: acc, m, l
+    for (int e = tid; e < R * (TC_DH + 2); e += TC_THREADS) cp[e] = e % (TC_DH + 2) == TC_DH ? -1e30f : 0.f;
+    cluster_sync_all();
+    if (warp >= 2)
+      cluster_merge<R, TC_DH, 128>(a, u, badarg ? 0 : min(u.nsplit, (int)gridDim.x), cp, (warp & 3) * 32 + lane,
+                                   !badarg);
+    cluster_sync_all();
     return;
   }
-  if (split >= u.nsplit) return;
   const int ntiles = (u.k_hi - u.k_lo + TC_TT - 1) / TC_TT;
 
   if (tid == 0) {
@@ -364,6 +375,23 @@ __global__ void __launch_bounds__(TC_THREADS, NC == 16 ? 2 : 1)
     // Hold the results until TMEM is released below.
     tc_fence_before();
     __syncthreads();
+    if (clus) {
+      // This CTA's partial into its own shared memory (the stages are free),
+      // then the merge across the cluster.
+      float* cp = reinterpret_cast<float*>(stages);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        cp[r * (TC_DH + 2) + t] = aborted ? 0.f : acc[r];
+        if (t == 0) {
+          cp[r * (TC_DH + 2) + TC_DH] = aborted ? -1e30f : m[r];
+          cp[r * (TC_DH + 2) + TC_DH + 1] = aborted ? 0.f : lsum[r];
+        }
+      }
+      cluster_sync_all();
+      cluster_merge<R, TC_DH, 128>(a, u, u.nsplit, cp, t, true);
+      cluster_sync_all();
+      return;
+    }
     if (aborted) {
       // The status word holds the timeout.  A multi-split unit still takes its
       // ticket so that the unit's last CTA re-arms it (its output is garbage,
@@ -393,6 +421,10 @@ __global__ void __launch_bounds__(TC_THREADS, NC == 16 ? 2 : 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (clus) {
+    cluster_sync_all();
+    cluster_sync_all();
+  }
   if (warp == 1) {
     __syncwarp();
     tmem_dealloc(tmem, TMEM_COLS);
@@ -408,9 +440,15 @@ int launch(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap& t
   HCU_TRY(once_per_device(attr_done, h->device, [&]() -> int {
     HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "hcu_attention: tc smem attribute"));
+    HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                       "hcu_attention: tc cluster attribute"));
     return HCU_OK;
   }));
-  kern<<<grid, TC_THREADS, smem, h->stream>>>(tk, tv, args);
+  if (!args.cluster) {
+    kern<<<grid, TC_THREADS, smem, h->stream>>>(tk, tv, args);
+    return after_launch("hcu_attention: tc launch");
+  }
+  HCU_TRY(launch_cluster_x(kern, grid, TC_THREADS, smem, h->stream, tk, tv, args));
   return after_launch("hcu_attention: tc launch");
 }
 
