@@ -594,8 +594,8 @@ extern "C" int hcu_attention(hcu_handle h, const hcu_attention_params* p, const 
   // (one per unit, through distributed shared memory) instead of through
   // tickets and partials in L2: its merge is then a few hundred cycles rather
   // than a few microseconds of dependent L2 round trips.
-  const bool cluster = (!use_tc || fmt != HCU_KV_Q8_0) && max_splits >= 2 && max_splits <= hcu::kMaxClusterSplits &&
-                       units * max_splits <= 2LL * h->sm_count;
+  const bool cluster =
+      max_splits >= 2 && max_splits <= hcu::kMaxClusterSplits && units * max_splits <= 2LL * h->sm_count;
 
   // TMA descriptors over the whole cache: dims (Dh, KV, rows).  The tensor-core
   // kernel loads 64-element (128-byte) boxes with the 128-byte swizzle its

@@ -122,13 +122,23 @@ __global__ void __launch_bounds__(threads_of(R), 2)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x;
   const AttnUnit u = attn_unit(a, split);
-  if (u.nsplit > (int)gridDim.x) {
-    if (split == 0 && tid == 0) atomicOr(a.status, HCU_DEVERR_BADARG);
+  const bool softmax_warp = warp >= 2 && warp < 2 + NSW;
+  // In the cluster form every CTA of the unit's cluster reaches the two
+  // cluster barriers; a CTA without work only contributes an empty partial.
+  const bool clus = a.cluster != 0;
+  const bool badarg = u.nsplit > (int)gridDim.x;
+  if (badarg && split == 0 && tid == 0) atomicOr(a.status, HCU_DEVERR_BADARG);
+  if (badarg || split >= u.nsplit) {
+    if (!clus) return;
+    float* cp = reinterpret_cast<float*>(kslots);  // [R][Dh + 2]: acc, m, l
+    for (int e = tid; e < R * (Q8_DH + 2); e += threads_of(R)) cp[e] = e % (Q8_DH + 2) == Q8_DH ? -1e30f : 0.f;
+    cluster_sync_all();
+    if (softmax_warp)
+      cluster_merge<R, Q8_DH, 32 * NSW>(a, u, badarg ? 0 : min(u.nsplit, (int)gridDim.x), cp, tid - 64, !badarg);
+    cluster_sync_all();
     return;
   }
-  if (split >= u.nsplit) return;
   const int ntiles = (u.k_hi - u.k_lo + Q8_TT - 1) / Q8_TT;
-  const bool softmax_warp = warp >= 2 && warp < 2 + NSW;
 
   if (tid == 0) {
     for (int i = 0; i < KST; i++) {
@@ -420,6 +430,24 @@ __global__ void __launch_bounds__(threads_of(R), 2)
     for (int i = 0; i < RL; i++) lsum[i] = lred[i] + lred[RL + i] + lred[2 * RL + i] + lred[3 * RL + i];
     tc_fence_before();
     __syncthreads();
+    if (clus) {
+      // This CTA's partial into its own shared memory (the K slots are free),
+      // then the merge across the cluster.
+      float* cp = reinterpret_cast<float*>(kslots);
+#pragma unroll
+      for (int i = 0; i < RL; i++) {
+        const int r = wg * RL + i;
+        cp[r * (Q8_DH + 2) + t] = aborted ? 0.f : acc[i];
+        if (t == 0) {
+          cp[r * (Q8_DH + 2) + Q8_DH] = aborted ? -1e30f : m[i];
+          cp[r * (Q8_DH + 2) + Q8_DH + 1] = aborted ? 0.f : lsum[i];
+        }
+      }
+      cluster_sync_all();
+      cluster_merge<R, Q8_DH, 32 * NSW>(a, u, u.nsplit, cp, stid, true);
+      cluster_sync_all();
+      return;
+    }
     if (aborted) {
       // The status word holds the timeout; the unit's tickets stay consistent.
       if (u.nsplit > 1) ticket_merge<R, Q8_DH, 32 * NSW>(a, u, stid, 3, reinterpret_cast<float*>(kslots), s_last);
@@ -450,6 +478,10 @@ __global__ void __launch_bounds__(threads_of(R), 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (clus) {
+    cluster_sync_all();
+    cluster_sync_all();
+  }
   if (warp == 1) {
     __syncwarp();
     tmem_dealloc(tmem, TMEM_COLS);
@@ -464,9 +496,15 @@ int launch(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap& t
   HCU_TRY(once_per_device(attr_done, h->device, [&]() -> int {
     HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES),
                        "hcu_attention: q8 tc smem attribute"));
+    HCU_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                       "hcu_attention: q8 tc cluster attribute"));
     return HCU_OK;
   }));
-  kern<<<grid, threads_of(R), SMEM_BYTES, h->stream>>>(tk, tv, tks, tvs, args);
+  if (!args.cluster) {
+    kern<<<grid, threads_of(R), SMEM_BYTES, h->stream>>>(tk, tv, tks, tvs, args);
+    return after_launch("hcu_attention: q8 tc launch");
+  }
+  HCU_TRY(launch_cluster_x(kern, grid, threads_of(R), SMEM_BYTES, h->stream, tk, tv, tks, tvs, args));
   return after_launch("hcu_attention: q8 tc launch");
 }
 
