@@ -3,8 +3,6 @@
 // attention_decode_tc.cu): launch arguments and the split-K epilogue.
 #pragma once
 
-#include <utility>
-
 #include "common.cuh"
 #include "context.h"
 
@@ -223,24 +221,32 @@ __device__ __forceinline__ void cluster_merge(const AttnArgs& a, const AttnUnit&
   }
 }
 
-// Launches `kern` with the split CTAs of each unit (gridDim.x of them, at most
-// kMaxClusterSplits) as one thread-block cluster.
-template <typename... KArgs, typename... Args>
-int launch_cluster_x(void (*kern)(KArgs...), dim3 grid, int threads, size_t smem, cudaStream_t stream,
-                     Args&&... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3((unsigned)threads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = grid.x;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), "hcu_attention: cluster launch");
+// Launches a decode kernel `kern(maps..., args)`.  With args.cluster set, the
+// split CTAs of each unit (gridDim.x of them, at most kMaxClusterSplits) form
+// one thread-block cluster; if the device cannot schedule such a cluster, the
+// launch-configuration error is cleared and the kernel runs in its ticket form
+// instead (the handle's workspace holds the partials either way).
+template <typename... KArgs, typename... Maps>
+void launch_decode(void (*kern)(KArgs...), dim3 grid, int threads, size_t smem, cudaStream_t stream, AttnArgs args,
+                   const Maps&... maps) {
+  if (args.cluster) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = grid.x;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, maps..., args) == cudaSuccess) return;
+    (void)cudaGetLastError();
+    args.cluster = 0;
+  }
+  kern<<<grid, threads, smem, stream>>>(maps..., args);
 }
 
 // Host launcher of the tcgen05 kernel (attention_decode_tc.cu).  Returns

@@ -470,11 +470,7 @@ int launch_t(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap&
                        "hcu_attention: cluster attribute"));
     return HCU_OK;
   }));
-  if (!args.cluster) {
-    kern<<<grid, NTHREADS, smem, h->stream>>>(tk, tv, tks, tvs, args);
-    return after_launch("hcu_attention: launch");
-  }
-  HCU_TRY(launch_cluster_x(kern, grid, NTHREADS, smem, h->stream, tk, tv, tks, tvs, args));
+  launch_decode(kern, grid, NTHREADS, smem, h->stream, args, tk, tv, tks, tvs);
   return after_launch("hcu_attention: launch");
 }
 

@@ -500,11 +500,7 @@ int launch(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap& t
                        "hcu_attention: q8 tc cluster attribute"));
     return HCU_OK;
   }));
-  if (!args.cluster) {
-    kern<<<grid, threads_of(R), SMEM_BYTES, h->stream>>>(tk, tv, tks, tvs, args);
-    return after_launch("hcu_attention: q8 tc launch");
-  }
-  HCU_TRY(launch_cluster_x(kern, grid, threads_of(R), SMEM_BYTES, h->stream, tk, tv, tks, tvs, args));
+  launch_decode(kern, grid, threads_of(R), SMEM_BYTES, h->stream, args, tk, tv, tks, tvs);
   return after_launch("hcu_attention: q8 tc launch");
 }
 

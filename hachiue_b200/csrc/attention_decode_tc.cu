@@ -444,11 +444,7 @@ int launch(hcu_context* h, const AttnArgs& args, dim3 grid, const CUtensorMap& t
                        "hcu_attention: tc cluster attribute"));
     return HCU_OK;
   }));
-  if (!args.cluster) {
-    kern<<<grid, TC_THREADS, smem, h->stream>>>(tk, tv, args);
-    return after_launch("hcu_attention: tc launch");
-  }
-  HCU_TRY(launch_cluster_x(kern, grid, TC_THREADS, smem, h->stream, tk, tv, args));
+  launch_decode(kern, grid, TC_THREADS, smem, h->stream, args, tk, tv);
   return after_launch("hcu_attention: tc launch");
 }
 
