@@ -25,12 +25,13 @@
 //     chunk's operand  W = [Tb ; QKm Tb]  (128 x 64 bf16, the second half a
 //     tf32 tensor-core product) and the scalars c2, c3, c4, e to a scratch
 //     buffer.
-//   gdn_chain_kernel - the state recurrence: one CTA per (sequence, V head,
-//     64 value columns) walks the chunks in order with three MMAs per chunk,
-//     [X; QS] = [K; Q] S0,  [Tb R'; O2] = W R',  U = K^T Dsb  (Dsb = c4 Tb R'),
-//     keeping the f32 state in registers (one state row per thread) and its
-//     bf16 copy in shared memory as the next chunk's MMA operand.  Two CTAs
-//     fit per SM.
+//   gdn_chain_kernel - the state recurrence: one CTA per (sequence, V head)
+//     walks the chunks in order with three MMAs per chunk,
+//     [X; QS] = [K; Q] S0,  [Tb R'; O] = [0; c3 QS] + W R',  S1 = e S0 + K^T Dsb
+//     (Dsb = c4 Tb R'), keeping the f32 state in TMEM (MMA (e) accumulates
+//     onto e S0) and its bf16 copy in shared memory as the next chunk's MMA
+//     operand.  Two CTAs fit per SM, so a batch of up to 296 (sequence, V
+//     head) pairs is one wave.
 #include <stdlib.h>
 
 #include "common.cuh"
@@ -42,7 +43,6 @@ namespace {
 
 constexpr int GC = 64;   // chunk length
 constexpr int GD = 128;  // DK = DV
-constexpr int DVB = 64;  // value columns per chain CTA
 // scratch per (sequence, V head, chunk) unit
 constexpr int W_ELEMS = 128 * 64;  // bf16 operand W = [Tb; QKm Tb]
 constexpr int SC_FLOATS = 4 * 64;  // c2, c3, c4, e (e repeated)
@@ -79,20 +79,20 @@ static_assert(P_KQ_X1 + 2 * 16 * 20 * 4 <= 16384, "prep K/Q reuse");
 
 // ---------------- chain kernel layout ----------------
 constexpr int CHAIN_THREADS = 192;
-constexpr int C_OFF_KQ = 0;         // [d0: K | Q][d1: K | Q] bf16, A operand of [K;Q] S0
-constexpr int C_OFF_KE = 32768;     // [d0: K][d1: K] bf16, A operand (MN-major) of K^T Dsb
-constexpr int C_OFF_W = 49152;      // W, 128 rows K-major; after MMA (c) the chunk's f32 outputs
-                                    // [64 tokens][2 x 32 values] (two 128B-swizzled halves) for a TMA store
-constexpr int C_OFF_S0B = 65536;    // [128 dk][64 dv] bf16 state, MN-major B operand
-constexpr int C_OFF_V = 81920;      // [64 tokens][64 values] bf16
-constexpr int C_OFF_RB = 90112;     // R', MN-major B operand
-constexpr int C_OFF_DSB = 98304;    // Dsb, MN-major B operand
-constexpr int C_OFF_SC = 106496;    // [2][4][64] f32
+constexpr int C_OFF_KQ = 0;         // [d0: K | Q][d1: K | Q] bf16: the A operand of [K;Q] S0; its K rows
+                                    // are the MN-major A operand of K^T Dsb
+constexpr int C_OFF_W = 32768;      // W, 128 rows K-major
+constexpr int C_OFF_V = 49152;      // V [2 x 64 values][64 tokens] bf16; then R' in place (MN-major B of
+                                    // W R'), then Dsb in place (MN-major B of K^T Dsb)
+constexpr int C_OFF_S0B = 65536;    // [2 x 64 dv][128 dk] bf16 state, MN-major B operand of [K;Q] S0;
+                                    // between MMA (c) and the state update, the chunk's f32 outputs
+                                    // [4 x 32 values][64 tokens] (128B-swizzled boxes) for a TMA store
+constexpr int C_OFF_SC = 98304;     // [2][4][64] f32
 constexpr int C_OFF_BAR = C_OFF_SC + 2 * SC_FLOATS * 4;
 constexpr int C_NBAR = 18;
 constexpr int C_SMEM = C_OFF_BAR + C_NBAR * 8 + 16;
-// TMEM columns of the chain kernel: P = [X; QS] and later U, Q = [Tb R'; O2]
-constexpr uint32_t TC_P = 0, TC_Q = 64, C_TMEM_COLS = 128;
+// TMEM columns of the chain kernel: P = [X; QS], then [Tb R'; O]; S = the f32 state
+constexpr uint32_t TC_P = 0, TC_S = 128, C_TMEM_COLS = 256;
 
 struct PrepArgs {
   int T, NK, NV, c0, ns, ahead;
@@ -631,49 +631,49 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
   uint8_t* sm = align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C_OFF_BAR);
   uint64_t* kq_full = bars + 0;
-  uint64_t* kq_empty = bars + 1;  // MMA a done
-  uint64_t* ke_full = bars + 2;
-  uint64_t* ke_empty = bars + 3;  // MMA e done
-  uint64_t* v_full = bars + 4;
-  uint64_t* v_empty = bars + 5;   // R' written
-  uint64_t* w_full = bars + 6;
-  uint64_t* o_ready = bars + 7;   // MMA c done and the chunk's outputs staged in W's place
+  uint64_t* q_free = bars + 1;    // MMA (a) done: the Q rows may be refilled
+  uint64_t* kv_free = bars + 2;   // MMA (e) done: the K rows and V's buffer may be refilled
+  uint64_t* v_full = bars + 3;
+  uint64_t* w_full = bars + 4;
+  uint64_t* w_free = bars + 5;    // MMA (c) done
+  uint64_t* o_ready = bars + 6;   // the chunk's outputs staged in the state buffer
+  uint64_t* s0_free = bars + 7;   // those outputs stored: the state buffer may be rewritten
   uint64_t* sc_full = bars + 8;   // [2]
-  uint64_t* sc_empty = bars + 10; // [2] chunk finished by the chain warps
+  uint64_t* sc_empty = bars + 10; // [2] the chunk's scalars no longer read
   uint64_t* bar_a = bars + 12;    // [X; QS] in TMEM
-  uint64_t* bar_R = bars + 13;    // R' in shared memory
-  uint64_t* bar_c = bars + 14;    // [Tb R'; O2] in TMEM
-  uint64_t* bar_D = bars + 15;    // Dsb in shared memory, [X; QS] and [Tb R'; O2] read
-  uint64_t* bar_e = bars + 16;    // U in TMEM
-  uint64_t* bar_s0 = bars + 17;   // bf16 state written
+  uint64_t* bar_R = bars + 13;    // R' in shared memory, X zeroed and QS scaled in TMEM
+  uint64_t* bar_c = bars + 14;    // [Tb R'; O] in TMEM
+  uint64_t* bar_D = bars + 15;    // Dsb in shared memory and [Tb R'; O] read
+  uint64_t* bar_e = bars + 16;    // the new state in TMEM
+  uint64_t* bar_s0 = bars + 17;   // bf16 state written, e S in TMEM
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C_NBAR);
   float* scal = reinterpret_cast<float*>(sm + C_OFF_SC);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // Grid (2 x V heads per QK head, QK heads, sequences): the CTAs of one QK
-  // head's V heads h = hk, hk + NK, ... and both value-column halves are
-  // adjacent, so they run together and share each chunk's K / Q tiles in L2.
-  const int dvb = blockIdx.x & 1, hk = blockIdx.y, b = blockIdx.z;
-  const int h = hk + (int)(blockIdx.x >> 1) * a.NK;
+  // Grid (V heads per QK head, QK heads, sequences): the CTAs of one QK head's
+  // V heads h = hk, hk + NK, ... are adjacent, so they run together and share
+  // each chunk's K / Q tiles in L2.
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int h = hk + (int)blockIdx.x * a.NK;
   if (h >= a.NV) return;  // the whole CTA, before any barrier or allocation
   const int n = a.cnt;
   const size_t unit0 = ((size_t)b * a.NV + h) * a.ns;
 
   if (tid == 0) {
     mbar_init(kq_full, 1);
-    mbar_init(kq_empty, 1);
-    mbar_init(ke_full, 1);
-    mbar_init(ke_empty, 1);
+    mbar_init(q_free, 1);
+    mbar_init(kv_free, 1);
     mbar_init(v_full, 1);
-    mbar_init(v_empty, 2);
     mbar_init(w_full, 1);
+    mbar_init(w_free, 1);
     mbar_init(o_ready, 2);
+    mbar_init(s0_free, 1);
     for (int i = 0; i < 2; i++) {
       mbar_init(&sc_full[i], 1);
       mbar_init(&sc_empty[i], 4);
     }
     mbar_init(bar_a, 1);
-    mbar_init(bar_R, 2);
+    mbar_init(bar_R, 4);
     mbar_init(bar_c, 1);
     mbar_init(bar_D, 4);
     mbar_init(bar_e, 1);
@@ -698,14 +698,9 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
       prefetch_tensormap(&tmW);
       prefetch_tensormap(&tmS);
       prefetch_tensormap(&tmO);
-      // outputs of chunk j: staged by the output warps in W's buffer, stored here
-      auto store_outputs = [&](int j) {
-        const int tj = (a.c0 + j) * GC;
-        tma_store_4d(&tmO, sm + C_OFF_W, dvb * DVB, h, tj, b);
-        tma_store_4d(&tmO, sm + C_OFF_W + 8192, dvb * DVB + 32, h, tj, b);
-        tma_store_commit();
-        tma_store_wait_read();
-      };
+      // chunk 0's scalars: the state set-up reads its e
+      mbar_arrive_expect_tx(&sc_full[0], SC_FLOATS * 4);
+      tma_load_2d(scal, &tmS, &sc_full[0], 0, (int)unit0 * 4);
       int c = 0;
       for (; c < n; c++) {
         const int t0 = (a.c0 + c) * GC;
@@ -719,34 +714,51 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
           tma_prefetch_l2_4d(&tmK, 64, hk, t1, b);
           tma_prefetch_l2_4d(&tmQ, 0, hk, t1, b);
           tma_prefetch_l2_4d(&tmQ, 64, hk, t1, b);
-          tma_prefetch_l2_4d(&tmV, dvb * DVB, h, t1, b);
+          tma_prefetch_l2_4d(&tmV, 0, h, t1, b);
+          tma_prefetch_l2_4d(&tmV, 64, h, t1, b);
           tma_prefetch_l2_2d(&tmW, 0, (u + 1) * 128);
-          tma_prefetch_l2_2d(&tmS, 0, (u + 1) * 4);
         }
-        if (c >= 1 && !mbar_wait(kq_empty, pe, a.status)) break;
+        // Q rows as soon as the previous chunk's MMA (a) is done
+        if (c >= 1 && !mbar_wait(q_free, pe, a.status)) break;
         mbar_arrive_expect_tx(kq_full, 32768);
-        tma_load_4d(sm + C_OFF_KQ, &tmK, kq_full, 0, hk, t0, b);
         tma_load_4d(sm + C_OFF_KQ + 8192, &tmQ, kq_full, 0, hk, t0, b);
-        tma_load_4d(sm + C_OFF_KQ + 16384, &tmK, kq_full, 64, hk, t0, b);
         tma_load_4d(sm + C_OFF_KQ + 24576, &tmQ, kq_full, 64, hk, t0, b);
-        if (c >= 1 && !mbar_wait(v_empty, pe, a.status)) break;
-        mbar_arrive_expect_tx(v_full, 8192);
-        tma_load_4d(sm + C_OFF_V, &tmV, v_full, dvb * DVB, h, t0, b);
-        if (c >= 2 && !mbar_wait(&sc_empty[c & 1], ((c - 2) >> 1) & 1, a.status)) break;
-        mbar_arrive_expect_tx(&sc_full[c & 1], SC_FLOATS * 4);
-        tma_load_2d(scal + (c & 1) * SC_FLOATS, &tmS, &sc_full[c & 1], 0, u * 4);
-        if (c >= 1) {
-          if (!mbar_wait(o_ready, pe, a.status)) break;
-          store_outputs(c - 1);
-        }
+        if (c >= 1 && !mbar_wait(w_free, pe, a.status)) break;
         mbar_arrive_expect_tx(w_full, W_ELEMS * 2);
         tma_load_2d(sm + C_OFF_W, &tmW, w_full, 0, u * 128);
-        if (c >= 1 && !mbar_wait(ke_empty, pe, a.status)) break;
-        mbar_arrive_expect_tx(ke_full, 16384);
-        tma_load_4d(sm + C_OFF_KE, &tmK, ke_full, 0, hk, t0, b);
-        tma_load_4d(sm + C_OFF_KE + 8192, &tmK, ke_full, 64, hk, t0, b);
+        // the previous chunk's outputs, staged in the state buffer
+        if (c >= 1) {
+          if (!mbar_wait(o_ready, pe, a.status)) break;
+          const int tj = t0 - GC;
+#pragma unroll
+          for (int q4 = 0; q4 < 4; q4++) tma_store_4d(&tmO, sm + C_OFF_S0B + q4 * 8192, 32 * q4, h, tj, b);
+          tma_store_commit();
+        }
+        // K rows and V once the previous chunk's MMA (e) is done
+        if (c >= 1 && !mbar_wait(kv_free, pe, a.status)) break;
+        tma_load_4d(sm + C_OFF_KQ, &tmK, kq_full, 0, hk, t0, b);
+        tma_load_4d(sm + C_OFF_KQ + 16384, &tmK, kq_full, 64, hk, t0, b);
+        mbar_arrive_expect_tx(v_full, 16384);
+        tma_load_4d(sm + C_OFF_V, &tmV, v_full, 0, h, t0, b);
+        tma_load_4d(sm + C_OFF_V + 8192, &tmV, v_full, 64, h, t0, b);
+        if (c >= 1) {
+          tma_store_wait_read();
+          mbar_arrive(s0_free);
+        }
+        // the next chunk's scalars, into the buffer chunk c - 1 used
+        if (c + 1 < n) {
+          const int nb = (c + 1) & 1;
+          if (c >= 1 && !mbar_wait(&sc_empty[nb], ((c - 1) >> 1) & 1, a.status)) break;
+          mbar_arrive_expect_tx(&sc_full[nb], SC_FLOATS * 4);
+          tma_load_2d(scal + nb * SC_FLOATS, &tmS, &sc_full[nb], 0, (u + 1) * 4);
+        }
       }
-      if (c == n && n > 0 && mbar_wait(o_ready, (n - 1) & 1, a.status)) store_outputs(n - 1);
+      if (c == n && n > 0 && mbar_wait(o_ready, (n - 1) & 1, a.status)) {
+        const int tj = (a.c0 + n - 1) * GC;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; q4++) tma_store_4d(&tmO, sm + C_OFF_S0B + q4 * 8192, 32 * q4, h, tj, b);
+        tma_store_commit();
+      }
       tma_store_wait_all();
     }
   } else if (warp == 1) {
@@ -755,46 +767,49 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
     // elected lane issues each tcgen05 instruction.
     {
       const bool leader = elect_one_sync();
-      constexpr uint32_t id_n64 = idesc_f16(128, 64, true, false, true);  // K-major A, MN-major B
-      constexpr uint32_t id_e = idesc_f16(128, 64, true, true, true);     // MN-major A (K^T)
+      constexpr uint32_t id_k = idesc_f16(128, 128, true, false, true);  // K-major A, MN-major B
+      constexpr uint32_t id_e = idesc_f16(128, 128, true, true, true);   // MN-major A (K^T)
       const uint32_t s0 = smem_u32(sm);
       for (int c = 0; c < n; c++) {
         const uint32_t ph = c & 1;
-        // (a) [X; QS] = [K; Q] S0   (M = 128, N = 64, K = 128)
+        // (a) [X; QS] = [K; Q] S0   (M = 128, N = 128, K = 128)
         if (!__all_sync(0xffffffffu, mbar_wait(kq_full, ph, a.status) && mbar_wait(bar_s0, ph, a.status))) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ks++) {
           const uint64_t ad = smem_desc_sw128(s0 + C_OFF_KQ + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(s0 + C_OFF_S0B + ks * 2048, 8192, 1024);
-          if (leader) mma_f16_ss(tmem + TC_P, ad, bd, id_n64, ks > 0);
+          const uint64_t bd = smem_desc_sw128(s0 + C_OFF_S0B + ks * 2048, 16384, 1024);
+          if (leader) mma_f16_ss(tmem + TC_P, ad, bd, id_k, ks > 0);
         }
         if (leader) {
           mma_commit(bar_a);
-          mma_commit(kq_empty);
+          mma_commit(q_free);
         }
-        // (c) [Tb R'; O2] = W R'   (M = 128, N = 64, K = 64)
+        // (c) [Tb R'; O] += W R'   (M = 128, N = 128, K = 64), onto [0; c3 QS]
         if (!__all_sync(0xffffffffu, mbar_wait(bar_R, ph, a.status) && mbar_wait(w_full, ph, a.status))) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 4; ks++) {
           const uint64_t ad = smem_desc_sw128(s0 + C_OFF_W + ks * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(s0 + C_OFF_RB + ks * 2048, 8192, 1024);
-          if (leader) mma_f16_ss(tmem + TC_Q, ad, bd, id_n64, ks > 0);
+          const uint64_t bd = smem_desc_sw128(s0 + C_OFF_V + ks * 2048, 8192, 1024);
+          if (leader) mma_f16_ss(tmem + TC_P, ad, bd, id_k, 1);
         }
-        if (leader) mma_commit(bar_c);
-        // (e) U = K^T Dsb   (M = 128, N = 64, K = 64)
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_D, ph, a.status) && mbar_wait(ke_full, ph, a.status))) break;
+        if (leader) {
+          mma_commit(bar_c);
+          mma_commit(w_free);
+        }
+        // (e) S += K^T Dsb   (M = 128, N = 128, K = 64), onto e S
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_D, ph, a.status))) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 4; ks++) {
-          const uint64_t ad = smem_desc_sw128(s0 + C_OFF_KE + ks * 2048, 8192, 1024);
-          const uint64_t bd = smem_desc_sw128(s0 + C_OFF_DSB + ks * 2048, 8192, 1024);
-          if (leader) mma_f16_ss(tmem + TC_P, ad, bd, id_e, ks > 0);
+          const uint64_t ad = smem_desc_sw128(s0 + C_OFF_KQ + ks * 2048, 16384, 1024);
+          const uint64_t bd = smem_desc_sw128(s0 + C_OFF_V + ks * 2048, 8192, 1024);
+          if (leader) mma_f16_ss(tmem + TC_S, ad, bd, id_e, 1);
         }
         if (leader) {
           mma_commit(bar_e);
-          mma_commit(ke_empty);
+          mma_commit(kv_free);
         }
       }
     }
@@ -803,53 +818,70 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
     const int quad = warp & 3;
     const int t = quad * 32 + lane;  // state row (dk); row of [K; Q] / W results
     const uint32_t lo = (uint32_t)(quad * 32) << 16;
+    const uint32_t tp = tmem + lo + TC_P, tsr = tmem + lo + TC_S;
     uint8_t* s0b = sm + C_OFF_S0B;
-    float st[64];
-    if (a.load_state) {
-      const float4* src =
-          reinterpret_cast<const float4*>(a.state_in + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * DVB);
+    uint8_t* vb = sm + C_OFF_V;
+    const size_t row = ((size_t)b * a.NV + h) * GD + t;  // this thread's state row in [B][NV][D][D]
+    // the state entering the slab: its bf16 copy for MMA (a), e_0 S for MMA (e)
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sc_full[0], 0, a.status));
+    if (ok) {
+      const float e0 = scal[192];
+      const float4* src = a.load_state ? reinterpret_cast<const float4*>(a.state_in + row * GD) : nullptr;
 #pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const float4 v = __ldg(src + i);
-        st[4 * i] = v.x;
-        st[4 * i + 1] = v.y;
-        st[4 * i + 2] = v.z;
-        st[4 * i + 3] = v.w;
+      for (int hf = 0; hf < 4; hf++) {
+        float x[32];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const float4 v = src ? __ldg(src + 8 * hf + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          x[4 * i] = v.x;
+          x[4 * i + 1] = v.y;
+          x[4 * i + 2] = v.z;
+          x[4 * i + 3] = v.w;
+        }
+        uint32_t r[32];
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+          *reinterpret_cast<uint4*>(s0b + (hf >> 1) * 16384 + sw128_offset(t, 64 * (hf & 1) + 16 * u)) =
+              pack8(x + 8 * u);
+#pragma unroll
+        for (int j = 0; j < 32; j++) r[j] = __float_as_uint(e0 * x[j]);
+        tmem_st32(tsr + 32 * hf, r);
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 64; i++) st[i] = 0.f;
+      tmem_st_wait();
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_s0);
     }
-    store_row64(s0b, t, st);
-    fence_proxy_async();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar_s0);
-    bool ok = true;
     for (int c = 0; c < n && ok; c++) {
       const uint32_t ph = c & 1;
       const float* sc = scal + (c & 1) * SC_FLOATS;
       if (quad < 2) {
-        // R'_t = V_t - c2_t X_t   (token t); V's row is read before X lands
+        // R'_t = V_t - c2_t X_t (token t), in place of V; X zeroed so that
+        // MMA (c) leaves Tb R' in its rows
         ok = __all_sync(0xffffffffu,
                         mbar_wait(v_full, ph, a.status) && mbar_wait(&sc_full[c & 1], (c >> 1) & 1, a.status));
         if (!ok) break;
         const float c2 = sc[t];
-        uint4 vrow[8];
+        uint4 vrow[16];
 #pragma unroll
-        for (int u = 0; u < 8; u++) vrow[u] = *reinterpret_cast<const uint4*>(sm + C_OFF_V + sw128_offset(t, 16 * u));
+        for (int u = 0; u < 16; u++)
+          vrow[u] = *reinterpret_cast<const uint4*>(vb + (u >> 3) * 8192 + sw128_offset(t, 16 * (u & 7)));
         ok = __all_sync(0xffffffffu, mbar_wait(bar_a, ph, a.status));
         if (!ok) break;
         tc_fence_after();
+        uint32_t zero[32];
 #pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
+        for (int j = 0; j < 32; j++) zero[j] = 0u;
+#pragma unroll
+        for (int hf = 0; hf < 4; hf++) {
           uint32_t xr[32];
-          tmem_ld32(tmem + lo + TC_P + 32 * hf, xr);
+          tmem_ld32(tp + 32 * hf, xr);
           tmem_ld_wait();
 #pragma unroll
           for (int u = 0; u < 4; u++) {
-            const uint32_t off = sw128_offset(t, 64 * hf + 16 * u);
-            const uint4 vw = vrow[4 * hf + u];
+            const int vu = 4 * hf + u;  // 16-byte chunk of the row: 64-value block vu / 8, chunk vu % 8
+            const uint4 vw = vrow[vu];
             const uint32_t vs[4] = {vw.x, vw.y, vw.z, vw.w};
             float r[8];
 #pragma unroll
@@ -857,34 +889,34 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
               r[2 * e] = fmaf(-c2, __uint_as_float(xr[8 * u + 2 * e]), bf16_lo(vs[e]));
               r[2 * e + 1] = fmaf(-c2, __uint_as_float(xr[8 * u + 2 * e + 1]), bf16_hi(vs[e]));
             }
-            *reinterpret_cast<uint4*>(sm + C_OFF_RB + off) = pack8(r);
+            *reinterpret_cast<uint4*>(vb + (vu >> 3) * 8192 + sw128_offset(t, 16 * (vu & 7))) = pack8(r);
           }
+          tmem_st32(tp + 32 * hf, zero);
         }
+        tmem_st_wait();
         fence_proxy_async();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(bar_R);
-          mbar_arrive(v_empty);
-        }
-        // Dsb_t = c4_t (row t of Tb R'), the bf16 operand of the state update
+        if (lane == 0) mbar_arrive(bar_R);
+        // Dsb_t = c4_t (row t of Tb R'), in place of R', the B operand of MMA (e)
         ok = __all_sync(0xffffffffu, mbar_wait(bar_c, ph, a.status));
         if (!ok) break;
         tc_fence_after();
         const float c4 = sc[128 + t];
 #pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
+        for (int hf = 0; hf < 4; hf++) {
           uint32_t dr[32];
-          tmem_ld32(tmem + lo + TC_Q + 32 * hf, dr);
+          tmem_ld32(tp + 32 * hf, dr);
           tmem_ld_wait();
 #pragma unroll
           for (int u = 0; u < 4; u++) {
+            const int vu = 4 * hf + u;
             uint4 w;
             w.x = pack2(c4 * __uint_as_float(dr[8 * u + 0]), c4 * __uint_as_float(dr[8 * u + 1]));
             w.y = pack2(c4 * __uint_as_float(dr[8 * u + 2]), c4 * __uint_as_float(dr[8 * u + 3]));
             w.z = pack2(c4 * __uint_as_float(dr[8 * u + 4]), c4 * __uint_as_float(dr[8 * u + 5]));
             w.w = pack2(c4 * __uint_as_float(dr[8 * u + 6]), c4 * __uint_as_float(dr[8 * u + 7]));
-            *reinterpret_cast<uint4*>(sm + C_OFF_DSB + sw128_offset(t, 64 * hf + 16 * u)) = w;
+            *reinterpret_cast<uint4*>(vb + (vu >> 3) * 8192 + sw128_offset(t, 16 * (vu & 7))) = w;
           }
         }
         fence_proxy_async();
@@ -892,75 +924,110 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_D);
       } else {
-        // O_i = c3_i QS_i + O2_i   (token i = t - 64)
+        // QS_i *= c3_i (token i = t - 64): MMA (c) then leaves O_i = c3_i QS_i + O2_i
         ok = __all_sync(0xffffffffu,
-                        mbar_wait(bar_c, ph, a.status) && mbar_wait(&sc_full[c & 1], (c >> 1) & 1, a.status));
+                        mbar_wait(bar_a, ph, a.status) && mbar_wait(&sc_full[c & 1], (c >> 1) & 1, a.status));
         if (!ok) break;
         tc_fence_after();
         const int i = t - 64;
         const float c3 = sc[64 + i];
 #pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
-          uint32_t qs[32], o2[32];
-          tmem_ld32(tmem + lo + TC_P + 32 * hf, qs);
-          tmem_ld32(tmem + lo + TC_Q + 32 * hf, o2);
+        for (int hf = 0; hf < 4; hf++) {
+          uint32_t qs[32];
+          tmem_ld32(tp + 32 * hf, qs);
           tmem_ld_wait();
-          if (hf == 1) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) qs[j] = __float_as_uint(c3 * __uint_as_float(qs[j]));
+          tmem_st32(tp + 32 * hf, qs);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_R);
+        // O_i staged as f32 in the state buffer (read by MMA (a) already):
+        // four 32-value boxes of 64 token rows for the TMA store
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_c, ph, a.status));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int hf = 0; hf < 4; hf++) {
+          uint32_t o[32];
+          tmem_ld32(tp + 32 * hf, o);
+          tmem_ld_wait();
+          if (hf == 3) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_D);
           }
-          // row i of the staged outputs: 32 f32 = one 128-byte swizzled row of half hf
-          uint8_t* orow = sm + C_OFF_W + hf * 8192;
+          uint8_t* orow = s0b + hf * 8192;
 #pragma unroll
           for (int u = 0; u < 8; u++)
             *reinterpret_cast<float4*>(orow + sw128_offset(i, 16 * u)) =
-                make_float4(fmaf(c3, __uint_as_float(qs[4 * u]), __uint_as_float(o2[4 * u])),
-                            fmaf(c3, __uint_as_float(qs[4 * u + 1]), __uint_as_float(o2[4 * u + 1])),
-                            fmaf(c3, __uint_as_float(qs[4 * u + 2]), __uint_as_float(o2[4 * u + 2])),
-                            fmaf(c3, __uint_as_float(qs[4 * u + 3]), __uint_as_float(o2[4 * u + 3])));
+                make_float4(__uint_as_float(o[4 * u]), __uint_as_float(o[4 * u + 1]), __uint_as_float(o[4 * u + 2]),
+                            __uint_as_float(o[4 * u + 3]));
         }
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(o_ready);
       }
-      // S1 = e S0 + U, and its bf16 copy for the next chunk
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_e, ph, a.status));
+      // S1 = e S0 + U is in TMEM: snapshots and the final state from it, its
+      // bf16 copy for the next chunk's MMA (a) and e' S1 for its MMA (e)
+      const bool more = c + 1 < n;
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_e, ph, a.status) &&
+                                       (!more || (mbar_wait(s0_free, ph, a.status) &&
+                                                  mbar_wait(&sc_full[(c + 1) & 1], ((c + 1) >> 1) & 1, a.status))));
       if (!ok) break;
       tc_fence_after();
-      const float e = sc[192];
-#pragma unroll
-      for (int hf = 0; hf < 2; hf++) {
-        uint32_t ur[32];
-        tmem_ld32(tmem + lo + TC_P + 32 * hf, ur);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; j++) st[32 * hf + j] = fmaf(e, st[32 * hf + j], __uint_as_float(ur[j]));
-#pragma unroll
-        for (int u = 0; u < 4; u++)
-          *reinterpret_cast<uint4*>(s0b + sw128_offset(t, 64 * hf + 16 * u)) = pack8(st + 32 * hf + 8 * u);
-      }
-      fence_proxy_async();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar_s0);
-        mbar_arrive(&sc_empty[c & 1]);
-      }
+      const float e1 = more ? scal[((c + 1) & 1) * SC_FLOATS + 192] : 0.f;
+      float4* dst = nullptr;
       if (a.snap && (a.c0 + c + 1) % a.snap_every == 0) {
         const long long j = (a.c0 + c + 1) / a.snap_every - 1;  // < snap_count: the chunk is full
-        if (j < a.snap_count) {
-          float4* dst = reinterpret_cast<float4*>(
-              a.snap + ((((size_t)b * a.snap_count + j) * a.NV + h) * GD + t) * GD + dvb * DVB);
+        if (j < a.snap_count)
+          dst = reinterpret_cast<float4*>(a.snap + (((size_t)b * a.snap_count + j) * a.NV + h) * GD * GD +
+                                          (size_t)t * GD);
+      }
+      float4* fin = more ? nullptr : reinterpret_cast<float4*>(a.state_out + row * GD);
 #pragma unroll
-          for (int i = 0; i < 16; i++) dst[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+      for (int hf = 0; hf < 4; hf++) {
+        uint32_t sr[32];
+        tmem_ld32(tsr + 32 * hf, sr);
+        tmem_ld_wait();
+        if (dst) {
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+            dst[8 * hf + i] = make_float4(__uint_as_float(sr[4 * i]), __uint_as_float(sr[4 * i + 1]),
+                                          __uint_as_float(sr[4 * i + 2]), __uint_as_float(sr[4 * i + 3]));
+        }
+        if (fin) {
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+            fin[8 * hf + i] = make_float4(__uint_as_float(sr[4 * i]), __uint_as_float(sr[4 * i + 1]),
+                                          __uint_as_float(sr[4 * i + 2]), __uint_as_float(sr[4 * i + 3]));
+        }
+        if (more) {
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            uint4 w;
+            w.x = pack2(__uint_as_float(sr[8 * u + 0]), __uint_as_float(sr[8 * u + 1]));
+            w.y = pack2(__uint_as_float(sr[8 * u + 2]), __uint_as_float(sr[8 * u + 3]));
+            w.z = pack2(__uint_as_float(sr[8 * u + 4]), __uint_as_float(sr[8 * u + 5]));
+            w.w = pack2(__uint_as_float(sr[8 * u + 6]), __uint_as_float(sr[8 * u + 7]));
+            *reinterpret_cast<uint4*>(s0b + (hf >> 1) * 16384 + sw128_offset(t, 64 * (hf & 1) + 16 * u)) = w;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j++) sr[j] = __float_as_uint(e1 * __uint_as_float(sr[j]));
+          tmem_st32(tsr + 32 * hf, sr);
         }
       }
-    }
-    if (ok) {
-      float4* dst = reinterpret_cast<float4*>(a.state_out + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * DVB);
-#pragma unroll
-      for (int i = 0; i < 16; i++) dst[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+      if (more) {
+        tmem_st_wait();
+        fence_proxy_async();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_s0);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sc_empty[c & 1]);
     }
   }
   tc_fence_before();
@@ -1104,7 +1171,7 @@ int chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q
     ca.snap_every = (int)snap_every;
     ca.snap_count = snap_count;
     const long long nvper = (NV + NK - 1) / NK;  // V heads per QK head (the last QK heads may have fewer)
-    const dim3 cgrid((unsigned)(hcu::GD / hcu::DVB * nvper), (unsigned)NK, (unsigned)B);
+    const dim3 cgrid((unsigned)nvper, (unsigned)NK, (unsigned)B);
     hcu::gdn_chain_kernel<<<cgrid, hcu::CHAIN_THREADS, hcu::C_SMEM + 1024, h->stream>>>(tq, tk, tv, tw, ts, to, ca);
     HCU_TRY(hcu::after_launch("hcu_deltanet_chunked_prefill: chain launch"));
   }
