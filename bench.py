@@ -352,6 +352,24 @@ def setup_cfg2q8(torch, be, dev, d=None):
     return W
 
 
+def _pipelined_e2e(dev, host_in, host_out, compute):
+    """End-to-end steps through the public API over HostPipeline: every step
+    copies ``host_in`` (pinned) to the device, runs ``compute(i, device_inputs,
+    device_outputs)`` and reads the outputs back into ``host_out`` (pinned),
+    with step i+1's host-to-device copy and step i-1's device-to-host copy (the
+    two PCIe directions) overlapping each other and step i's kernels."""
+    from hachiue_b200.pipeline import HostPipeline
+    pipe = HostPipeline(dev, [(tuple(x.shape), x.dtype) for x in host_in], [(tuple(x.shape), x.dtype) for x in host_out])
+
+    def e2e_step(i):
+        pipe.submit(host_in, host_out, lambda ins, outs: compute(i, ins, outs))
+
+    return dict(e2e_step=e2e_step, e2e_begin=pipe.begin, e2e_end=pipe.drain,
+                h2d=sum(x.numel() * x.element_size() for x in host_in),
+                d2h=sum(x.numel() * x.element_size() for x in host_out),
+                e2e_note="HostPipeline: two slots; step i+1's H2D and step i-1's D2H overlap step i's kernels")
+
+
 def setup_cfg1(torch, be, dev):
     from hachiue_b200 import KV_F32, workloads
     from hachiue_b200.backend import KVCache
@@ -396,23 +414,16 @@ def setup_cfg4(torch, be, dev):
         st = states[i % copies]
         be.deltanet_decode(qkv, a, b, an, dtb, st, core, st, NK, NV)
 
-    qkv_h = torch.from_numpy(w["qkv"]).pin_memory()
-    a_h = torch.from_numpy(w["a"]).pin_memory()
-    b_h = torch.from_numpy(w["b"]).pin_memory()
-    core_h = torch.empty(core.shape).pin_memory()
-    qkv_d, a_d, b_d = torch.empty_like(qkv), torch.empty_like(a), torch.empty_like(b)
+    hosts = [torch.from_numpy(w[k]).pin_memory() for k in ("qkv", "a", "b")]
 
-    def e2e_step(i):
-        qkv_d.copy_(qkv_h, non_blocking=True)
-        a_d.copy_(a_h, non_blocking=True)
-        b_d.copy_(b_h, non_blocking=True)
+    def compute(i, ins, outs):
         st = states[i % copies]
-        be.deltanet_decode(qkv_d, a_d, b_d, an, dtb, st, core, st, NK, NV)
-        core_h.copy_(core, non_blocking=True)
+        be.deltanet_decode(ins[0], ins[1], ins[2], an, dtb, st, outs[0], st, NK, NV)
 
-    return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg4_bytes(), tokens=64, info=config_info("4"),
-                h2d=(qkv_h.numel() + a_h.numel() + b_h.numel()) * 4, d2h=core_h.numel() * 4, kernels_per_step=1,
-                e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg4"), out=core, traffic_key="cfg4")
+    W = dict(step=step, bytes=workloads.cfg4_bytes(), tokens=64, info=config_info("4"), kernels_per_step=1,
+             e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg4"), out=core, traffic_key="cfg4")
+    W.update(_pipelined_e2e(dev, hosts, [torch.empty(core.shape).pin_memory()], compute))
+    return W
 
 
 def setup_cfg3(torch, be, dev):
@@ -428,20 +439,17 @@ def setup_cfg3(torch, be, dev):
     def step(i):
         be.swa_prefill(q, k, v, out, w["window"])
 
-    qh, kh, vh = (torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).pin_memory() for x in (w["q"], w["k"], w["v"]))
+    hosts = [torch.from_numpy(np.ascontiguousarray(w[x]).view(np.int16)).pin_memory() for x in ("q", "k", "v")]
     out_h = torch.empty((8, 4096, 16, 128), dtype=torch.int16).pin_memory()
-    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
-    def e2e_step(i):
-        qd.view(torch.int16).copy_(qh, non_blocking=True)
-        kd.view(torch.int16).copy_(kh, non_blocking=True)
-        vd.view(torch.int16).copy_(vh, non_blocking=True)
-        be.swa_prefill(qd, kd, vd, out, w["window"])
-        out_h.copy_(out.view(torch.int16), non_blocking=True)
+    def compute(i, ins, outs):
+        qd, kd, vd = (x.view(torch.bfloat16) for x in ins)
+        be.swa_prefill(qd, kd, vd, outs[0].view(torch.bfloat16), w["window"])
 
-    return dict(step=step, e2e_step=e2e_step, flops=workloads.swa_flops(), tokens=8 * 4096, info=config_info("3"),
-                h2d=(qh.numel() + kh.numel() + vh.numel()) * 2, d2h=out_h.numel() * 2, kernels_per_step=1,
-                e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg3"), out=out, traffic_key="cfg3")
+    W = dict(step=step, flops=workloads.swa_flops(), tokens=8 * 4096, info=config_info("3"), kernels_per_step=1,
+             e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg3"), out=out, traffic_key="cfg3")
+    W.update(_pipelined_e2e(dev, hosts, [out_h], compute))
+    return W
 
 
 def setup_cfg5(torch, be, dev):
@@ -460,32 +468,19 @@ def setup_cfg5(torch, be, dev):
     def step(i):
         be.deltanet_chunked_prefill(q, k, v, g, beta, core, st)
 
-    # End to end: q, k, v, g, beta from pinned host memory, the outputs and the
-    # final state read back, pipelined over two slots so that step i+1's
-    # host-to-device copy and step i-1's device-to-host copy (the two PCIe
-    # directions) overlap each other and step i's kernels.
-    from hachiue_b200.pipeline import HostPipeline
     hosts = [torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).pin_memory() for x in (w["q"], w["k"], w["v"])]
     hosts += [torch.from_numpy(w["g"]).pin_memory(), torch.from_numpy(w["beta"]).pin_memory()]
-    core_h = torch.empty(core.shape).pin_memory()
-    st_h = torch.empty(st.shape).pin_memory()
-    pipe = HostPipeline(dev, [(tuple(x.shape), x.dtype) for x in hosts],
-                        [(tuple(core.shape), torch.float32), (tuple(st.shape), torch.float32)])
 
-    def compute(ins, outs):
+    def compute(i, ins, outs):
         qd, kd, vd = (x.view(torch.bfloat16) for x in ins[:3])
         be.deltanet_chunked_prefill(qd, kd, vd, ins[3], ins[4], outs[0], outs[1])
 
-    def e2e_step(i):
-        pipe.submit(hosts, [core_h, st_h], compute)
-
-    h2d = sum(x.numel() * x.element_size() for x in hosts)
-    d2h = core_h.numel() * 4 + st_h.numel() * 4
-    return dict(step=step, e2e_step=e2e_step, e2e_begin=pipe.begin, e2e_end=pipe.drain,
-                flops=workloads.cfg5_flops(), hbm_bytes=workloads.cfg5_bytes(),
-                tokens=8 * 8192, info=config_info("5"), h2d=h2d, d2h=d2h, kernels_per_step=2, e2e_kernels_per_step=2,
-                cpu=dict(w=w, kind="cfg5"), out=core, traffic_key="cfg5",
-                e2e_note="HostPipeline: two slots; step i+1's H2D and step i-1's D2H overlap step i's kernels")
+    W = dict(step=step, flops=workloads.cfg5_flops(), hbm_bytes=workloads.cfg5_bytes(), tokens=8 * 8192,
+             info=config_info("5"), kernels_per_step=2, e2e_kernels_per_step=2, cpu=dict(w=w, kind="cfg5"), out=core,
+             traffic_key="cfg5")
+    W.update(_pipelined_e2e(dev, hosts, [torch.empty(core.shape).pin_memory(), torch.empty(st.shape).pin_memory()],
+                            compute))
+    return W
 
 
 def setup_cfg6(torch, be, dev):
@@ -518,24 +513,20 @@ def setup_cfg6(torch, be, dev):
         be.deltanet_decode(qkv_conv[:, None], a[:, None], b[:, None], an, dtb, st, core, st, NK, NV)
         be.deltanet_norm_gate(core, z, gamma, out, w["eps"])
 
-    hs = {k: torch.from_numpy(np.ascontiguousarray(w[k])).pin_memory() for k in ("qkv", "a", "b", "z")}
-    out_h = torch.empty(out.shape).pin_memory()
-    dd = {k: torch.empty_like(v, device=dev) for k, v in hs.items()}
+    hosts = [torch.from_numpy(np.ascontiguousarray(w[k])).pin_memory() for k in ("qkv", "a", "b", "z")]
 
-    def e2e_step(i):
-        for k in hs:
-            dd[k].copy_(hs[k], non_blocking=True)
+    def compute(i, ins, outs):
         st = states[i % copies]
-        be.gdn_layer_step(dd["qkv"], conv_w, conv[i & 1], conv[(i + 1) & 1], dd["a"], dd["b"], an, dtb, dd["z"],
-                          gamma, st, st, out, NK, NV, w["eps"])
-        out_h.copy_(out, non_blocking=True)
+        be.gdn_layer_step(ins[0], conv_w, conv[i & 1], conv[(i + 1) & 1], ins[1], ins[2], an, dtb, ins[3], gamma, st,
+                          st, outs[0], NK, NV, w["eps"])
 
     info = config_info("6")
-    return dict(step=step, e2e_step=e2e_step, bytes=workloads.cfg6_bytes(), tokens=B, info=info,
-                h2d=sum(v.numel() * 4 for v in hs.values()), d2h=out_h.numel() * 4, kernels_per_step=1,
-                e2e_kernels_per_step=1, cpu=dict(w=w, kind="cfg6"), out=out, traffic_key="cfg6",
-                alt=dict(name="unfused: conv1d_causal (2 kernels) + recurrence with g/beta + norm_gate",
-                         step=unfused, kernels_per_step=4))
+    W = dict(step=step, bytes=workloads.cfg6_bytes(), tokens=B, info=info, kernels_per_step=1, e2e_kernels_per_step=1,
+             cpu=dict(w=w, kind="cfg6"), out=out, traffic_key="cfg6",
+             alt=dict(name="unfused: conv1d_causal (2 kernels) + recurrence with g/beta + norm_gate",
+                      step=unfused, kernels_per_step=4))
+    W.update(_pipelined_e2e(dev, hosts, [torch.empty(out.shape).pin_memory()], compute))
+    return W
 
 
 def setup_cfg7(torch, be, dev):
