@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(_PKG, "libhachiue_cuda.so")
 
 HCU_OK, HCU_EINVAL, HCU_ECUDA, HCU_ENCCL, HCU_ETIMEDOUT, HCU_ENOMEM, HCU_EUNSUPPORTED = range(7)
 KV_F32, KV_F16, KV_BF16, KV_Q8_0, KV_Q8_0_WGSL = 0, 1, 2, 3, 4
-OPT_ATTN_CUDA_CORES, OPT_ATTN_CHUNK, OPT_GDN_SCRATCH_MB, OPT_SWA_CTAS = 1, 2, 3, 4
+OPT_ATTN_CUDA_CORES, OPT_ATTN_CHUNK, OPT_GDN_SCRATCH_MB, OPT_SWA_CTAS, OPT_GDN_CHAIN_COLS = 1, 2, 3, 4, 5
 COMM_ID_BYTES = 128
 DT_F32, DT_BF16 = 0, 2
 

@@ -33,7 +33,8 @@ SHADERS = ("kv_append_q8", "attention_q8", "deltanet_gbeta", "deltanet_recur", "
 _DTYPE_OF_FORMAT = {KV_F32: torch.float32, KV_F16: torch.float16, KV_BF16: torch.bfloat16, KV_Q8_0: torch.int8,
                     KV_Q8_0_WGSL: torch.int8}
 _OPTIONS = {"attn_cuda_cores": _lib.OPT_ATTN_CUDA_CORES, "attn_chunk": _lib.OPT_ATTN_CHUNK,
-            "gdn_scratch_mb": _lib.OPT_GDN_SCRATCH_MB, "swa_ctas": _lib.OPT_SWA_CTAS}
+            "gdn_scratch_mb": _lib.OPT_GDN_SCRATCH_MB, "swa_ctas": _lib.OPT_SWA_CTAS,
+            "gdn_chain_cols": _lib.OPT_GDN_CHAIN_COLS}
 
 
 def _current_raw_stream(index: int) -> int:
@@ -140,7 +141,8 @@ class CudaBackend:
 
     def set_option(self, name: str, value: int) -> None:
         """hcu_set_option: ``attn_cuda_cores``, ``attn_chunk``,
-        ``gdn_scratch_mb`` or ``swa_ctas`` (0 restores the tuned default)."""
+        ``gdn_scratch_mb``, ``swa_ctas`` or ``gdn_chain_cols`` (0 restores the
+        tuned default)."""
         check(self.lib.hcu_set_option(self._h, _OPTIONS[name], int(value)))
 
     def set_q8_convention(self, fmt: int) -> None:

@@ -235,6 +235,12 @@ int hcu_set_option(hcu_handle h, int option, int64_t value) {
     case HCU_OPT_ATTN_CHUNK: h->opt_attn_chunk = value; return HCU_OK;
     case HCU_OPT_GDN_SCRATCH_MB: h->opt_gdn_scratch_mb = value; return HCU_OK;
     case HCU_OPT_SWA_CTAS: h->opt_swa_ctas = value; return HCU_OK;
+    case HCU_OPT_GDN_CHAIN_COLS:
+      if (value != 0 && value != 64 && value != 128)
+        return fail(HCU_EINVAL, "hcu_set_option: HCU_OPT_GDN_CHAIN_COLS must be 0, 64 or 128 (got %lld)",
+                    (long long)value);
+      h->opt_gdn_chain_cols = value;
+      return HCU_OK;
   }
   return fail(HCU_EINVAL, "hcu_set_option: unknown option %d", option);
 }

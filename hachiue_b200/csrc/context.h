@@ -29,6 +29,7 @@ struct hcu_context {
   int64_t opt_attn_chunk = 0;
   int64_t opt_gdn_scratch_mb = 0;
   int64_t opt_swa_ctas = 0;
+  int64_t opt_gdn_chain_cols = 0;
 };
 
 namespace hcu {

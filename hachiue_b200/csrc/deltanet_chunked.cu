@@ -32,6 +32,11 @@
 //     onto e S0) and its bf16 copy in shared memory as the next chunk's MMA
 //     operand.  Two CTAs fit per SM, so a batch of up to 296 (sequence, V
 //     head) pairs is one wave.
+//   gdn_chain_split_kernel - the same recurrence with two CTAs per (sequence,
+//     V head), 64 value columns each, the f32 state in registers (one state
+//     row per thread).  Each CTA's chunk is shorter, so batches whose
+//     2 x (sequence, V head) CTAs still fit one wave (at most 148 pairs) take
+//     this kernel.
 #include <stdlib.h>
 
 #include "common.cuh"
@@ -93,6 +98,23 @@ constexpr int C_NBAR = 18;
 constexpr int C_SMEM = C_OFF_BAR + C_NBAR * 8 + 16;
 // TMEM columns of the chain kernel: P = [X; QS], then [Tb R'; O]; S = the f32 state
 constexpr uint32_t TC_P = 0, TC_S = 128, C_TMEM_COLS = 256;
+
+// ---------------- split chain kernel layout (64 value columns per CTA) ----------------
+constexpr int R_COLS = 64;
+constexpr int R_OFF_KQ = 0;         // [d0: K | Q][d1: K | Q] bf16, A operand of [K;Q] S0
+constexpr int R_OFF_KE = 32768;     // [d0: K][d1: K] bf16, A operand (MN-major) of K^T Dsb
+constexpr int R_OFF_W = 49152;      // W, 128 rows K-major; after MMA (c) the chunk's f32 outputs
+                                    // [64 tokens][2 x 32 values] (two 128B-swizzled halves) for a TMA store
+constexpr int R_OFF_S0B = 65536;    // [128 dk][64 dv] bf16 state, MN-major B operand
+constexpr int R_OFF_V = 81920;      // [64 tokens][64 values] bf16
+constexpr int R_OFF_RB = 90112;     // R', MN-major B operand
+constexpr int R_OFF_DSB = 98304;    // Dsb, MN-major B operand
+constexpr int R_OFF_SC = 106496;    // [2][4][64] f32
+constexpr int R_OFF_BAR = R_OFF_SC + 2 * SC_FLOATS * 4;
+constexpr int R_NBAR = 18;
+constexpr int R_SMEM = R_OFF_BAR + R_NBAR * 8 + 16;
+// TMEM columns of the split chain kernel: P = [X; QS] and later U, Q = [Tb R'; O2]
+constexpr uint32_t RT_P = 0, RT_Q = 64, R_TMEM_COLS = 128;
 
 struct PrepArgs {
   int T, NK, NV, c0, ns, ahead;
@@ -1039,6 +1061,359 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
   }
 }
 
+// =====================================================================
+// split chain: two CTAs per (sequence, V head), the state in registers
+// =====================================================================
+__global__ void __launch_bounds__(CHAIN_THREADS, 2)
+    gdn_chain_split_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmO,
+                     const ChainArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + R_OFF_BAR);
+  uint64_t* kq_full = bars + 0;
+  uint64_t* kq_empty = bars + 1;  // MMA a done
+  uint64_t* ke_full = bars + 2;
+  uint64_t* ke_empty = bars + 3;  // MMA e done
+  uint64_t* v_full = bars + 4;
+  uint64_t* v_empty = bars + 5;   // R' written
+  uint64_t* w_full = bars + 6;
+  uint64_t* o_ready = bars + 7;   // MMA c done and the chunk's outputs staged in W's place
+  uint64_t* sc_full = bars + 8;   // [2]
+  uint64_t* sc_empty = bars + 10; // [2] chunk finished by the chain warps
+  uint64_t* bar_a = bars + 12;    // [X; QS] in TMEM
+  uint64_t* bar_R = bars + 13;    // R' in shared memory
+  uint64_t* bar_c = bars + 14;    // [Tb R'; O2] in TMEM
+  uint64_t* bar_D = bars + 15;    // Dsb in shared memory, [X; QS] and [Tb R'; O2] read
+  uint64_t* bar_e = bars + 16;    // U in TMEM
+  uint64_t* bar_s0 = bars + 17;   // bf16 state written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + R_NBAR);
+  float* scal = reinterpret_cast<float*>(sm + R_OFF_SC);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Grid (2 x V heads per QK head, QK heads, sequences): the CTAs of one QK
+  // head's V heads h = hk, hk + NK, ... and both value-column halves are
+  // adjacent, so they run together and share each chunk's K / Q tiles in L2.
+  const int dvb = blockIdx.x & 1, hk = blockIdx.y, b = blockIdx.z;
+  const int h = hk + (int)(blockIdx.x >> 1) * a.NK;
+  if (h >= a.NV) return;  // the whole CTA, before any barrier or allocation
+  const int n = a.cnt;
+  const size_t unit0 = ((size_t)b * a.NV + h) * a.ns;
+
+  if (tid == 0) {
+    mbar_init(kq_full, 1);
+    mbar_init(kq_empty, 1);
+    mbar_init(ke_full, 1);
+    mbar_init(ke_empty, 1);
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 2);
+    mbar_init(w_full, 1);
+    mbar_init(o_ready, 2);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&sc_full[i], 1);
+      mbar_init(&sc_empty[i], 4);
+    }
+    mbar_init(bar_a, 1);
+    mbar_init(bar_R, 2);
+    mbar_init(bar_c, 1);
+    mbar_init(bar_D, 4);
+    mbar_init(bar_e, 1);
+    mbar_init(bar_s0, 4);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, R_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&tmK);
+      prefetch_tensormap(&tmQ);
+      prefetch_tensormap(&tmV);
+      prefetch_tensormap(&tmW);
+      prefetch_tensormap(&tmS);
+      prefetch_tensormap(&tmO);
+      // outputs of chunk j: staged by the output warps in W's buffer, stored here
+      auto store_outputs = [&](int j) {
+        const int tj = (a.c0 + j) * GC;
+        tma_store_4d(&tmO, sm + R_OFF_W, dvb * R_COLS, h, tj, b);
+        tma_store_4d(&tmO, sm + R_OFF_W + 8192, dvb * R_COLS + 32, h, tj, b);
+        tma_store_commit();
+        tma_store_wait_read();
+      };
+      int c = 0;
+      for (; c < n; c++) {
+        const int t0 = (a.c0 + c) * GC;
+        const int u = (int)(unit0 + c);
+        const uint32_t pe = (c - 1) & 1;
+        if (c + 1 < n) {
+          // warm L2 with the next chunk's tiles: its loads below are issued only
+          // when this chunk frees the buffers, a chunk's time before they are needed
+          const int t1 = t0 + GC;
+          tma_prefetch_l2_4d(&tmK, 0, hk, t1, b);
+          tma_prefetch_l2_4d(&tmK, 64, hk, t1, b);
+          tma_prefetch_l2_4d(&tmQ, 0, hk, t1, b);
+          tma_prefetch_l2_4d(&tmQ, 64, hk, t1, b);
+          tma_prefetch_l2_4d(&tmV, dvb * R_COLS, h, t1, b);
+          tma_prefetch_l2_2d(&tmW, 0, (u + 1) * 128);
+          tma_prefetch_l2_2d(&tmS, 0, (u + 1) * 4);
+        }
+        if (c >= 1 && !mbar_wait(kq_empty, pe, a.status)) break;
+        mbar_arrive_expect_tx(kq_full, 32768);
+        tma_load_4d(sm + R_OFF_KQ, &tmK, kq_full, 0, hk, t0, b);
+        tma_load_4d(sm + R_OFF_KQ + 8192, &tmQ, kq_full, 0, hk, t0, b);
+        tma_load_4d(sm + R_OFF_KQ + 16384, &tmK, kq_full, 64, hk, t0, b);
+        tma_load_4d(sm + R_OFF_KQ + 24576, &tmQ, kq_full, 64, hk, t0, b);
+        if (c >= 1 && !mbar_wait(v_empty, pe, a.status)) break;
+        mbar_arrive_expect_tx(v_full, 8192);
+        tma_load_4d(sm + R_OFF_V, &tmV, v_full, dvb * R_COLS, h, t0, b);
+        if (c >= 2 && !mbar_wait(&sc_empty[c & 1], ((c - 2) >> 1) & 1, a.status)) break;
+        mbar_arrive_expect_tx(&sc_full[c & 1], SC_FLOATS * 4);
+        tma_load_2d(scal + (c & 1) * SC_FLOATS, &tmS, &sc_full[c & 1], 0, u * 4);
+        if (c >= 1) {
+          if (!mbar_wait(o_ready, pe, a.status)) break;
+          store_outputs(c - 1);
+        }
+        mbar_arrive_expect_tx(w_full, W_ELEMS * 2);
+        tma_load_2d(sm + R_OFF_W, &tmW, w_full, 0, u * 128);
+        if (c >= 1 && !mbar_wait(ke_empty, pe, a.status)) break;
+        mbar_arrive_expect_tx(ke_full, 16384);
+        tma_load_4d(sm + R_OFF_KE, &tmK, ke_full, 0, hk, t0, b);
+        tma_load_4d(sm + R_OFF_KE + 8192, &tmK, ke_full, 64, hk, t0, b);
+      }
+      if (c == n && n > 0 && mbar_wait(o_ready, (n - 1) & 1, a.status)) store_outputs(n - 1);
+      tma_store_wait_all();
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    // The whole warp walks the loop (its values are warp-uniform); one
+    // elected lane issues each tcgen05 instruction.
+    {
+      const bool leader = elect_one_sync();
+      constexpr uint32_t id_n64 = idesc_f16(128, 64, true, false, true);  // K-major A, MN-major B
+      constexpr uint32_t id_e = idesc_f16(128, 64, true, true, true);     // MN-major A (K^T)
+      const uint32_t s0 = smem_u32(sm);
+      for (int c = 0; c < n; c++) {
+        const uint32_t ph = c & 1;
+        // (a) [X; QS] = [K; Q] S0   (M = 128, N = 64, K = 128)
+        if (!__all_sync(0xffffffffu, mbar_wait(kq_full, ph, a.status) && mbar_wait(bar_s0, ph, a.status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+          const uint64_t ad = smem_desc_sw128(s0 + R_OFF_KQ + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(s0 + R_OFF_S0B + ks * 2048, 8192, 1024);
+          if (leader) mma_f16_ss(tmem + RT_P, ad, bd, id_n64, ks > 0);
+        }
+        if (leader) {
+          mma_commit(bar_a);
+          mma_commit(kq_empty);
+        }
+        // (c) [Tb R'; O2] = W R'   (M = 128, N = 64, K = 64)
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_R, ph, a.status) && mbar_wait(w_full, ph, a.status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+          const uint64_t ad = smem_desc_sw128(s0 + R_OFF_W + ks * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(s0 + R_OFF_RB + ks * 2048, 8192, 1024);
+          if (leader) mma_f16_ss(tmem + RT_Q, ad, bd, id_n64, ks > 0);
+        }
+        if (leader) mma_commit(bar_c);
+        // (e) U = K^T Dsb   (M = 128, N = 64, K = 64)
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_D, ph, a.status) && mbar_wait(ke_full, ph, a.status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+          const uint64_t ad = smem_desc_sw128(s0 + R_OFF_KE + ks * 2048, 8192, 1024);
+          const uint64_t bd = smem_desc_sw128(s0 + R_OFF_DSB + ks * 2048, 8192, 1024);
+          if (leader) mma_f16_ss(tmem + RT_P, ad, bd, id_e, ks > 0);
+        }
+        if (leader) {
+          mma_commit(bar_e);
+          mma_commit(ke_empty);
+        }
+      }
+    }
+  } else {
+    // ---------------- chain warps 2-5: TMEM lane quadrant = warp % 4 ----------------
+    const int quad = warp & 3;
+    const int t = quad * 32 + lane;  // state row (dk); row of [K; Q] / W results
+    const uint32_t lo = (uint32_t)(quad * 32) << 16;
+    uint8_t* s0b = sm + R_OFF_S0B;
+    float st[64];
+    if (a.load_state) {
+      const float4* src =
+          reinterpret_cast<const float4*>(a.state_in + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * R_COLS);
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const float4 v = __ldg(src + i);
+        st[4 * i] = v.x;
+        st[4 * i + 1] = v.y;
+        st[4 * i + 2] = v.z;
+        st[4 * i + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; i++) st[i] = 0.f;
+    }
+    store_row64(s0b, t, st);
+    fence_proxy_async();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_s0);
+    bool ok = true;
+    for (int c = 0; c < n && ok; c++) {
+      const uint32_t ph = c & 1;
+      const float* sc = scal + (c & 1) * SC_FLOATS;
+      if (quad < 2) {
+        // R'_t = V_t - c2_t X_t   (token t); V's row is read before X lands
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(v_full, ph, a.status) && mbar_wait(&sc_full[c & 1], (c >> 1) & 1, a.status));
+        if (!ok) break;
+        const float c2 = sc[t];
+        uint4 vrow[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) vrow[u] = *reinterpret_cast<const uint4*>(sm + R_OFF_V + sw128_offset(t, 16 * u));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_a, ph, a.status));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+          uint32_t xr[32];
+          tmem_ld32(tmem + lo + RT_P + 32 * hf, xr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const uint32_t off = sw128_offset(t, 64 * hf + 16 * u);
+            const uint4 vw = vrow[4 * hf + u];
+            const uint32_t vs[4] = {vw.x, vw.y, vw.z, vw.w};
+            float r[8];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              r[2 * e] = fmaf(-c2, __uint_as_float(xr[8 * u + 2 * e]), bf16_lo(vs[e]));
+              r[2 * e + 1] = fmaf(-c2, __uint_as_float(xr[8 * u + 2 * e + 1]), bf16_hi(vs[e]));
+            }
+            *reinterpret_cast<uint4*>(sm + R_OFF_RB + off) = pack8(r);
+          }
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar_R);
+          mbar_arrive(v_empty);
+        }
+        // Dsb_t = c4_t (row t of Tb R'), the bf16 operand of the state update
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_c, ph, a.status));
+        if (!ok) break;
+        tc_fence_after();
+        const float c4 = sc[128 + t];
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+          uint32_t dr[32];
+          tmem_ld32(tmem + lo + RT_Q + 32 * hf, dr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            uint4 w;
+            w.x = pack2(c4 * __uint_as_float(dr[8 * u + 0]), c4 * __uint_as_float(dr[8 * u + 1]));
+            w.y = pack2(c4 * __uint_as_float(dr[8 * u + 2]), c4 * __uint_as_float(dr[8 * u + 3]));
+            w.z = pack2(c4 * __uint_as_float(dr[8 * u + 4]), c4 * __uint_as_float(dr[8 * u + 5]));
+            w.w = pack2(c4 * __uint_as_float(dr[8 * u + 6]), c4 * __uint_as_float(dr[8 * u + 7]));
+            *reinterpret_cast<uint4*>(sm + R_OFF_DSB + sw128_offset(t, 64 * hf + 16 * u)) = w;
+          }
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_D);
+      } else {
+        // O_i = c3_i QS_i + O2_i   (token i = t - 64)
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(bar_c, ph, a.status) && mbar_wait(&sc_full[c & 1], (c >> 1) & 1, a.status));
+        if (!ok) break;
+        tc_fence_after();
+        const int i = t - 64;
+        const float c3 = sc[64 + i];
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+          uint32_t qs[32], o2[32];
+          tmem_ld32(tmem + lo + RT_P + 32 * hf, qs);
+          tmem_ld32(tmem + lo + RT_Q + 32 * hf, o2);
+          tmem_ld_wait();
+          if (hf == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_D);
+          }
+          // row i of the staged outputs: 32 f32 = one 128-byte swizzled row of half hf
+          uint8_t* orow = sm + R_OFF_W + hf * 8192;
+#pragma unroll
+          for (int u = 0; u < 8; u++)
+            *reinterpret_cast<float4*>(orow + sw128_offset(i, 16 * u)) =
+                make_float4(fmaf(c3, __uint_as_float(qs[4 * u]), __uint_as_float(o2[4 * u])),
+                            fmaf(c3, __uint_as_float(qs[4 * u + 1]), __uint_as_float(o2[4 * u + 1])),
+                            fmaf(c3, __uint_as_float(qs[4 * u + 2]), __uint_as_float(o2[4 * u + 2])),
+                            fmaf(c3, __uint_as_float(qs[4 * u + 3]), __uint_as_float(o2[4 * u + 3])));
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_ready);
+      }
+      // S1 = e S0 + U, and its bf16 copy for the next chunk
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_e, ph, a.status));
+      if (!ok) break;
+      tc_fence_after();
+      const float e = sc[192];
+#pragma unroll
+      for (int hf = 0; hf < 2; hf++) {
+        uint32_t ur[32];
+        tmem_ld32(tmem + lo + RT_P + 32 * hf, ur);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j++) st[32 * hf + j] = fmaf(e, st[32 * hf + j], __uint_as_float(ur[j]));
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+          *reinterpret_cast<uint4*>(s0b + sw128_offset(t, 64 * hf + 16 * u)) = pack8(st + 32 * hf + 8 * u);
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(bar_s0);
+        mbar_arrive(&sc_empty[c & 1]);
+      }
+      if (a.snap && (a.c0 + c + 1) % a.snap_every == 0) {
+        const long long j = (a.c0 + c + 1) / a.snap_every - 1;  // < snap_count: the chunk is full
+        if (j < a.snap_count) {
+          float4* dst = reinterpret_cast<float4*>(
+              a.snap + ((((size_t)b * a.snap_count + j) * a.NV + h) * GD + t) * GD + dvb * R_COLS);
+#pragma unroll
+          for (int i = 0; i < 16; i++) dst[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+        }
+      }
+    }
+    if (ok) {
+      float4* dst = reinterpret_cast<float4*>(a.state_out + (((size_t)b * a.NV + h) * GD + t) * GD + dvb * R_COLS);
+#pragma unroll
+      for (int i = 0; i < 16; i++) dst[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, R_TMEM_COLS);
+  }
+}
+
 }  // namespace
 }  // namespace hcu
 
@@ -1130,10 +1505,18 @@ int chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q
     HCU_TRY(hcu::check_cuda(cudaFuncSetAttribute(hcu::gdn_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  hcu::C_SMEM + 1024),
                             "hcu_deltanet_chunked_prefill: smem attribute"));
+    HCU_TRY(hcu::check_cuda(cudaFuncSetAttribute(hcu::gdn_chain_split_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, hcu::R_SMEM + 1024),
+                            "hcu_deltanet_chunked_prefill: smem attribute"));
     return HCU_OK;
   }));
   const long long gb_row = p->gb_row_stride ? (long long)p->gb_row_stride : NV;
   const long long gb_seq = p->gb_seq_stride ? (long long)p->gb_seq_stride : T * gb_row;
+  // The recurrence kernel: two 64-column CTAs per (sequence, V head) walk the
+  // chunks faster than one 128-column CTA, so they are used while the batch
+  // still fits one wave of two CTAs per SM; larger batches take one CTA per head.
+  const long long ncol = h->opt_gdn_chain_cols ? h->opt_gdn_chain_cols
+                         : (2 * B * NV <= 2LL * h->sm_count ? 64 : 128);
   const long long npair = ((NV + NK - 1) / NK + 1) / 2;  // V heads per QK head, two per prep CTA
   if (NK * npair > 65535) return fail(HCU_EINVAL, "hcu_deltanet_chunked_prefill: too many heads");
   for (long long s = 0; s < nslab; s++) {
@@ -1171,8 +1554,14 @@ int chunked_prefill(hcu_handle h, const hcu_gdn_prefill_params* p, const void* q
     ca.snap_every = (int)snap_every;
     ca.snap_count = snap_count;
     const long long nvper = (NV + NK - 1) / NK;  // V heads per QK head (the last QK heads may have fewer)
-    const dim3 cgrid((unsigned)nvper, (unsigned)NK, (unsigned)B);
-    hcu::gdn_chain_kernel<<<cgrid, hcu::CHAIN_THREADS, hcu::C_SMEM + 1024, h->stream>>>(tq, tk, tv, tw, ts, to, ca);
+    if (ncol == 128) {
+      const dim3 cgrid((unsigned)nvper, (unsigned)NK, (unsigned)B);
+      hcu::gdn_chain_kernel<<<cgrid, hcu::CHAIN_THREADS, hcu::C_SMEM + 1024, h->stream>>>(tq, tk, tv, tw, ts, to, ca);
+    } else {
+      const dim3 cgrid((unsigned)(hcu::GD / hcu::R_COLS * nvper), (unsigned)NK, (unsigned)B);
+      hcu::gdn_chain_split_kernel<<<cgrid, hcu::CHAIN_THREADS, hcu::R_SMEM + 1024, h->stream>>>(tq, tk, tv, tw, ts,
+                                                                                                 to, ca);
+    }
     HCU_TRY(hcu::after_launch("hcu_deltanet_chunked_prefill: chain launch"));
   }
   return HCU_OK;

@@ -105,11 +105,16 @@ int hcu_stream_sync(hcu_handle h);
  *   HCU_OPT_GDN_SCRATCH_MB   scratch budget of the chunked GDN prefill, in MiB
  *                            (default 1024); smaller budgets process the
  *                            prompt in slabs of chunks
- *   HCU_OPT_SWA_CTAS         cap on the SWA prefill's persistent grid */
+ *   HCU_OPT_SWA_CTAS         cap on the SWA prefill's persistent grid
+ *   HCU_OPT_GDN_CHAIN_COLS   value columns per CTA of the chunked GDN
+ *                            prefill's state recurrence: 128 (one CTA per
+ *                            sequence and V head) or 64 (two); by default
+ *                            64 when that still fits one wave, else 128 */
 #define HCU_OPT_ATTN_CUDA_CORES 1
 #define HCU_OPT_ATTN_CHUNK 2
 #define HCU_OPT_GDN_SCRATCH_MB 3
 #define HCU_OPT_SWA_CTAS 4
+#define HCU_OPT_GDN_CHAIN_COLS 5
 int hcu_set_option(hcu_handle h, int option, int64_t value);
 
 int hcu_alloc(hcu_handle h, size_t bytes, void **device_ptr);

@@ -48,6 +48,15 @@ def make_inputs(rng, B, T, NK, NV, decay=1.0):
     return bf16_bits(q), bf16_bits(k), bf16_bits(v), g, beta
 
 
+@pytest.fixture(params=[64, 128])
+def chain_cols(backend, request):
+    """Both widths of the recurrence kernel's CTAs (64 or 128 value columns;
+    the library picks one by occupancy), forced through HCU_OPT_GDN_CHAIN_COLS."""
+    backend.set_option("gdn_chain_cols", request.param)
+    yield request.param
+    backend.set_option("gdn_chain_cols", 0)
+
+
 def run(backend, qb, kb, vb, g, beta, state0=None):
     B, T, NK, _ = qb.shape
     NV = vb.shape[2]
@@ -64,7 +73,7 @@ def run(backend, qb, kb, vb, g, beta, state0=None):
                                                   (1, 1000, 1, 2, 1.0, False), (1, 640, 2, 2, 0.02, True),
                                                   (1, 129, 1, 1, 0.0, False), (1, 256, 1, 2, 4.0, True),
                                                   (1, 130, 2, 3, 1.0, False)])
-def test_small_shapes(backend, B, T, NK, NV, decay, load):
+def test_small_shapes(backend, chain_cols, B, T, NK, NV, decay, load):
     """One chunk, a partial last chunk, many chunks, weak decay (the state
     carries across chunks), no decay at all and strong decay (in-chunk decay
     factors far below f32 range); zero or loaded initial state; V heads not a
@@ -83,7 +92,7 @@ def test_small_shapes(backend, B, T, NK, NV, decay, load):
     assert backend.device_status() == 0
 
 
-def test_agrees_with_recurrent_kernel(backend):
+def test_agrees_with_recurrent_kernel(backend, chain_cols):
     """Same inputs through the token-serial CUDA kernel (hcu_deltanet_recur)."""
     rng = np.random.default_rng(42)
     B, T, NK, NV = 1, 300, 2, 4
@@ -145,7 +154,7 @@ def test_cfg5_whole_output_against_recurrent_kernel(backend, cfg5):
     assert backend.device_status() == 0
 
 
-def test_slabs_carry_the_state(backend, request):
+def test_slabs_carry_the_state(backend, chain_cols, request):
     """A scratch budget of 1 MiB splits 64 chunks into slabs (one prep + chain
     launch pair each); the state crosses slab boundaries through state_out."""
     backend.set_option("gdn_scratch_mb", 1)
@@ -162,7 +171,7 @@ def test_slabs_carry_the_state(backend, request):
     assert backend.device_status() == 0
 
 
-def test_state_snapshots_for_prefix_reuse(backend):
+def test_state_snapshots_for_prefix_reuse(backend, chain_cols):
     """Snapshots every 4 chunks: each equals, bit for bit, the final state of a
     prefill over that prefix; resuming from a snapshot reproduces the rest of
     the full prefill's outputs and its final state bit for bit (the restore
@@ -224,3 +233,9 @@ def test_snapshot_arguments_are_checked(backend):
         backend.deltanet_chunked_prefill(to_dev_bf16(qb), to_dev_bf16(kb), to_dev_bf16(vb),
                                          torch.from_numpy(g).to(dev), torch.from_numpy(beta).to(dev), core, st,
                                          snapshots=torch.empty((1, 0, 2, 128, 128), device=dev), snap_every=0)
+
+
+def test_chain_width_option_is_checked(backend):
+    from hachiue_b200 import HachiueError
+    with pytest.raises(HachiueError, match="HCU_OPT_GDN_CHAIN_COLS"):
+        backend.set_option("gdn_chain_cols", 96)
