@@ -452,9 +452,15 @@ def setup_cfg3(torch, be, dev):
     return W
 
 
+# Prompt length of configuration 5 (8192 in the benchmark set; --cfg5-tokens
+# shortens it for ncu captures of the same kernels on a smaller case).
+CFG5_TOKENS = 8192
+
+
 def setup_cfg5(torch, be, dev):
     from hachiue_b200 import workloads
-    w = workloads.gdn_prefill_cfg5()
+    T = CFG5_TOKENS
+    w = workloads.gdn_prefill_cfg5(T=T)
 
     def bf(x):
         return torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).to(dev).view(torch.bfloat16)
@@ -462,7 +468,7 @@ def setup_cfg5(torch, be, dev):
     q, k, v = bf(w["q"]), bf(w["k"]), bf(w["v"])
     g = torch.from_numpy(w["g"]).to(dev)
     beta = torch.from_numpy(w["beta"]).to(dev)
-    core = torch.empty((8, 8192, 32, 128), device=dev)
+    core = torch.empty((8, T, 32, 128), device=dev)
     st = torch.empty((8, 32, 128, 128), device=dev)
 
     def step(i):
@@ -475,9 +481,13 @@ def setup_cfg5(torch, be, dev):
         qd, kd, vd = (x.view(torch.bfloat16) for x in ins[:3])
         be.deltanet_chunked_prefill(qd, kd, vd, ins[3], ins[4], outs[0], outs[1])
 
-    W = dict(step=step, flops=workloads.cfg5_flops(), hbm_bytes=workloads.cfg5_bytes(), tokens=8 * 8192,
-             info=config_info("5"), kernels_per_step=2, e2e_kernels_per_step=2, cpu=dict(w=w, kind="cfg5"), out=core,
-             traffic_key="cfg5")
+    info = config_info("5")
+    if T != 8192:
+        in_bytes = workloads.cfg5_bytes(T=T) - 8 * T * 32 * 128 * 4 - 8 * 32 * 128 * 128 * 4
+        info.update(tokens=T, l2=f"inputs {in_bytes / 1e9:.2f} GB" + (" > L2" if in_bytes > 126e6 else ", within L2"))
+    W = dict(step=step, flops=workloads.cfg5_flops(T=T), hbm_bytes=workloads.cfg5_bytes(T=T), tokens=8 * T,
+             info=info, kernels_per_step=2, e2e_kernels_per_step=2, cpu=dict(w=w, kind="cfg5"), out=core,
+             traffic_key="cfg5" if T == 8192 else None)
     W.update(_pipelined_e2e(dev, hosts, [torch.empty(core.shape).pin_memory(), torch.empty(st.shape).pin_memory()],
                             compute))
     return W
@@ -889,13 +899,14 @@ def entry(cfg, W, res, peaks, peak_src, world, steps, cpu):
     roof = {"bound": "tensor" if tensor else "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 4), "peak_source": peak_src + (" bf16 burst" if tensor else " copy"),
             ("algorithmic_flops_per_launch" if tensor else "algorithmic_bytes_per_launch"): work,
-            "kernel_ms": round(kms, 5), "traffic": load_traffic(W["traffic_key"])}
+            "kernel_ms": round(kms, 5), "traffic": load_traffic(W["traffic_key"]) if W["traffic_key"] else None}
     if "hbm_bytes" in W:  # tensor work at I/O dtypes whose bytes take longer than its flops: the HBM roof binds
         gbs = W["hbm_bytes"] / (kms / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": round(gbs, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peak_src + " copy",
                 "algorithmic_bytes_per_launch": W["hbm_bytes"], "kernel_ms": round(kms, 5),
-                "traffic": load_traffic(W["traffic_key"]), "tensor_achieved_tflops": round(achieved, 2),
+                "traffic": load_traffic(W["traffic_key"]) if W["traffic_key"] else None,
+                "tensor_achieved_tflops": round(achieved, 2),
                 "tensor_frac": round(achieved / peaks["bf16_tflops"], 4)}
     e2e_ms = res["e2e_ms"] / steps
     d = {"metric": metric_name(cfg), "value": round(value, 2), "unit": unit, "ms_per_step": round(ms, 5),
@@ -1024,7 +1035,13 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--cfg5-tokens", type=int, default=8192,
+                    help="prompt length of configuration 5 (a multiple of 64; shorter only for profiling captures)")
     args = ap.parse_args(argv)
+    global CFG5_TOKENS
+    if args.cfg5_tokens != 8192 and (args.cfg5_tokens < 64 or args.cfg5_tokens % 64):
+        ap.error("--cfg5-tokens must be a positive multiple of 64")
+    CFG5_TOKENS = args.cfg5_tokens
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
