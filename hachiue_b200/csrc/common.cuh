@@ -166,6 +166,10 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
 __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until the shared memory of every committed bulk store has been read.
 __device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Every committed store group but the most recent one has read its source.
+__device__ __forceinline__ void tma_store_wait_read_all_but_last() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // Waits until every committed bulk store has completed.
 __device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void tma_store_commit_and_wait_read() {

@@ -86,12 +86,14 @@ static_assert(P_KQ_X1 + 2 * 16 * 20 * 4 <= 16384, "prep K/Q reuse");
 constexpr int CHAIN_THREADS = 192;
 constexpr int C_OFF_KQ = 0;         // [d0: K | Q][d1: K | Q] bf16: the A operand of [K;Q] S0; its K rows
                                     // are the MN-major A operand of K^T Dsb
-constexpr int C_OFF_W = 32768;      // W, 128 rows K-major
+constexpr int C_OFF_W = 32768;      // W, 128 rows K-major; after MMA (c), output boxes 0-1 (below)
 constexpr int C_OFF_V = 49152;      // V [2 x 64 values][64 tokens] bf16; then R' in place (MN-major B of
                                     // W R'), then Dsb in place (MN-major B of K^T Dsb)
 constexpr int C_OFF_S0B = 65536;    // [2 x 64 dv][128 dk] bf16 state, MN-major B operand of [K;Q] S0;
-                                    // between MMA (c) and the state update, the chunk's f32 outputs
-                                    // [4 x 32 values][64 tokens] (128B-swizzled boxes) for a TMA store
+                                    // between MMA (c) and the state update, its second half holds output
+                                    // boxes 2-3.  The chunk's f32 outputs are four boxes of [64 tokens][32
+                                    // values] (128B-swizzled) for TMA stores: boxes 0-1 in W's buffer, 2-3
+                                    // here, so the state update writes its first half without waiting
 constexpr int C_OFF_SC = 98304;     // [2][4][64] f32
 constexpr int C_OFF_BAR = C_OFF_SC + 2 * SC_FLOATS * 4;
 constexpr int C_NBAR = 18;
@@ -720,6 +722,16 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
       prefetch_tensormap(&tmW);
       prefetch_tensormap(&tmS);
       prefetch_tensormap(&tmO);
+      // a chunk's outputs: boxes 2-3 (state buffer) as one store group, then
+      // boxes 0-1 (W's buffer) as another
+      auto store_outputs = [&](int tj) {
+        tma_store_4d(&tmO, sm + C_OFF_S0B + 16384, 64, h, tj, b);
+        tma_store_4d(&tmO, sm + C_OFF_S0B + 24576, 96, h, tj, b);
+        tma_store_commit();
+        tma_store_4d(&tmO, sm + C_OFF_W, 0, h, tj, b);
+        tma_store_4d(&tmO, sm + C_OFF_W + 8192, 32, h, tj, b);
+        tma_store_commit();
+      };
       // chunk 0's scalars: the state set-up reads its e
       mbar_arrive_expect_tx(&sc_full[0], SC_FLOATS * 4);
       tma_load_2d(scal, &tmS, &sc_full[0], 0, (int)unit0 * 4);
@@ -745,16 +757,10 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
         mbar_arrive_expect_tx(kq_full, 32768);
         tma_load_4d(sm + C_OFF_KQ + 8192, &tmQ, kq_full, 0, hk, t0, b);
         tma_load_4d(sm + C_OFF_KQ + 24576, &tmQ, kq_full, 64, hk, t0, b);
-        if (c >= 1 && !mbar_wait(w_free, pe, a.status)) break;
-        mbar_arrive_expect_tx(w_full, W_ELEMS * 2);
-        tma_load_2d(sm + C_OFF_W, &tmW, w_full, 0, u * 128);
-        // the previous chunk's outputs, staged in the state buffer
+        // the previous chunk's outputs, staged in W's buffer and the state buffer
         if (c >= 1) {
           if (!mbar_wait(o_ready, pe, a.status)) break;
-          const int tj = t0 - GC;
-#pragma unroll
-          for (int q4 = 0; q4 < 4; q4++) tma_store_4d(&tmO, sm + C_OFF_S0B + q4 * 8192, 32 * q4, h, tj, b);
-          tma_store_commit();
+          store_outputs(t0 - GC);
         }
         // K rows and V once the previous chunk's MMA (e) is done
         if (c >= 1 && !mbar_wait(kv_free, pe, a.status)) break;
@@ -764,9 +770,14 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
         tma_load_4d(sm + C_OFF_V, &tmV, v_full, 0, h, t0, b);
         tma_load_4d(sm + C_OFF_V + 8192, &tmV, v_full, 64, h, t0, b);
         if (c >= 1) {
-          tma_store_wait_read();
+          tma_store_wait_read_all_but_last();  // the state buffer's half is read
           mbar_arrive(s0_free);
+          tma_store_wait_read();  // and W's buffer
         }
+        // W once the previous chunk's MMA (c) is done and its outputs left W's buffer
+        if (c >= 1 && !mbar_wait(w_free, pe, a.status)) break;
+        mbar_arrive_expect_tx(w_full, W_ELEMS * 2);
+        tma_load_2d(sm + C_OFF_W, &tmW, w_full, 0, u * 128);
         // the next chunk's scalars, into the buffer chunk c - 1 used
         if (c + 1 < n) {
           const int nb = (c + 1) & 1;
@@ -775,12 +786,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
           tma_load_2d(scal + nb * SC_FLOATS, &tmS, &sc_full[nb], 0, (u + 1) * 4);
         }
       }
-      if (c == n && n > 0 && mbar_wait(o_ready, (n - 1) & 1, a.status)) {
-        const int tj = (a.c0 + n - 1) * GC;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; q4++) tma_store_4d(&tmO, sm + C_OFF_S0B + q4 * 8192, 32 * q4, h, tj, b);
-        tma_store_commit();
-      }
+      if (c == n && n > 0 && mbar_wait(o_ready, (n - 1) & 1, a.status)) store_outputs((a.c0 + n - 1) * GC);
       tma_store_wait_all();
     }
   } else if (warp == 1) {
@@ -966,8 +972,9 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_R);
-        // O_i staged as f32 in the state buffer (read by MMA (a) already):
-        // four 32-value boxes of 64 token rows for the TMA store
+        // O_i staged as f32 for the TMA stores, four 32-value boxes of 64 token
+        // rows: boxes 0-1 in W's buffer (read by MMA (c) already), 2-3 in the
+        // state buffer's second half (read by MMA (a))
         ok = __all_sync(0xffffffffu, mbar_wait(bar_c, ph, a.status));
         if (!ok) break;
         tc_fence_after();
@@ -981,7 +988,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_D);
           }
-          uint8_t* orow = s0b + hf * 8192;
+          uint8_t* orow = hf < 2 ? sm + C_OFF_W + hf * 8192 : s0b + 16384 + (hf - 2) * 8192;
 #pragma unroll
           for (int u = 0; u < 8; u++)
             *reinterpret_cast<float4*>(orow + sw128_offset(i, 16 * u)) =
@@ -996,8 +1003,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
       // bf16 copy for the next chunk's MMA (a) and e' S1 for its MMA (e)
       const bool more = c + 1 < n;
       ok = __all_sync(0xffffffffu, mbar_wait(bar_e, ph, a.status) &&
-                                       (!more || (mbar_wait(s0_free, ph, a.status) &&
-                                                  mbar_wait(&sc_full[(c + 1) & 1], ((c + 1) >> 1) & 1, a.status))));
+                                       (!more || mbar_wait(&sc_full[(c + 1) & 1], ((c + 1) >> 1) & 1, a.status)));
       if (!ok) break;
       tc_fence_after();
       const float e1 = more ? scal[((c + 1) & 1) * SC_FLOATS + 192] : 0.f;
@@ -1011,6 +1017,11 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
       float4* fin = more ? nullptr : reinterpret_cast<float4*>(a.state_out + row * GD);
 #pragma unroll
       for (int hf = 0; hf < 4; hf++) {
+        if (hf == 2 && more) {
+          // the state buffer's second half: once this chunk's output boxes 2-3 left it
+          ok = __all_sync(0xffffffffu, mbar_wait(s0_free, ph, a.status));
+          if (!ok) break;
+        }
         uint32_t sr[32];
         tmem_ld32(tsr + 32 * hf, sr);
         tmem_ld_wait();
@@ -1041,6 +1052,7 @@ __global__ void __launch_bounds__(CHAIN_THREADS, 2)
           tmem_st32(tsr + 32 * hf, sr);
         }
       }
+      if (!ok) break;
       if (more) {
         tmem_st_wait();
         fence_proxy_async();
