@@ -23,3 +23,9 @@ def test_reference_arm_line():
     assert d["value"] > 0 and d["unit"] == "GB/s" and d["metric"] == "decode attn HBM GB/s"
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_cfg5_tokens_must_be_a_positive_multiple_of_64():
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--config", "5", "--cfg5-tokens", "100"],
+                       capture_output=True, text=True, timeout=300, cwd=ROOT)
+    assert r.returncode == 2 and "--cfg5-tokens must be a positive multiple of 64" in r.stderr
