@@ -1,0 +1,77 @@
+"""The chunked (WY) form of the gated delta rule that the prefill kernels
+compute, restated in float64 numpy in the order the kernels use it, against
+the oracle's token-serial recurrence (src/wasm-backend.ts:1047-1102).  CPU only.
+
+Per V head and 64-token chunk, with S0 the entering state ([dk][dv]), gamma
+the in-chunk cumulative sum of g, ik / iq the key / query norm factors and
+K, Q, V the raw chunk rows:
+
+  prep (gdn_prep_kernel):
+    A_ij   = beta_i ik_i ik_j exp(gamma_i - gamma_j) k_i.k_j   (j < i)
+    T      = (I + A)^-1,  Tb = T diag(beta)
+    QKm_ij = iq_i ik_j exp(gamma_i - gamma_j) q_i.k_j          (j <= i)
+    W      = [Tb; QKm Tb],  c2 = exp(gamma) ik,  c3 = exp(gamma) iq,
+    c4     = ik exp(gamma_last - gamma),  e = exp(gamma_last)
+  recurrence (gdn_chain_kernel, state in TMEM):
+    [X; QS]     = [K; Q] S0
+    R'          = V - diag(c2) X
+    [Tb R'; O]  = [0; diag(c3) QS] + W R'     (X zeroed, QS scaled in place)
+    S1          = e S0 + K^T diag(c4) (Tb R')   (accumulated onto e S0)
+"""
+import numpy as np
+import pytest
+
+import oracle
+
+C = 64
+
+
+def chunked(q, k, v, g, beta, S0):
+    """q, k, v [T, D]; g, beta [T]; S0 [D, D].  Returns (out [T, D], S_T)."""
+    T, D = q.shape
+    ik = 1 / np.sqrt((k * k).sum(1) + 1e-6)
+    iq = 1 / np.sqrt((q * q).sum(1) + 1e-6) / np.sqrt(D)
+    S = S0.copy()
+    out = np.zeros((T, D))
+    for c0 in range(0, T, C):
+        sl = slice(c0, min(c0 + C, T))
+        n = sl.stop - sl.start
+        K, Q, V, b, ikc, iqc = k[sl], q[sl], v[sl], beta[sl], ik[sl], iq[sl]
+        gam = np.cumsum(g[sl])
+        i, j = np.indices((n, n))
+        dec = np.where(j <= i, np.exp(np.where(j <= i, gam[:, None] - gam[None, :], 0.0)), 0.0)
+        A = np.where(j < i, b[:, None] * ikc[:, None] * ikc[None, :] * dec * (K @ K.T), 0.0)
+        Tb = np.linalg.inv(np.eye(n) + A) * b[None, :]
+        QKm = iqc[:, None] * ikc[None, :] * dec * (Q @ K.T)
+        W = np.vstack([Tb, QKm @ Tb])
+        c2, c3 = np.exp(gam) * ikc, np.exp(gam) * iqc
+        c4, e = ikc * np.exp(gam[-1] - gam), np.exp(gam[-1])
+        P = np.vstack([K @ S, Q @ S])
+        Rp = V - c2[:, None] * P[:n]
+        P = np.vstack([np.zeros((n, D)), c3[:, None] * P[n:]]) + W @ Rp
+        out[sl] = P[n:]
+        S = e * S + K.T @ (c4[:, None] * P[:n])
+    return out, S
+
+
+@pytest.mark.parametrize("T,decay,load", [(64, 1.0, False), (150, 1.0, True), (256, 0.05, True), (200, 4.0, False),
+                                          (129, 0.0, True)])
+def test_chunked_form_matches_token_serial_oracle(T, decay, load):
+    rng = np.random.default_rng(T + int(10 * decay))
+    D = 128
+    q, k, v = (rng.standard_normal((T, D)) for _ in range(3))
+    a = rng.standard_normal(T)
+    g = -decay * (np.maximum(a, 0) + np.log1p(np.exp(-np.abs(a))))
+    beta = 1 / (1 + np.exp(-rng.standard_normal(T)))
+    S0 = 0.05 * rng.standard_normal((D, D)) if load else np.zeros((D, D))
+    f32 = lambda x: np.ascontiguousarray(x, dtype=np.float32)  # noqa: E731
+    qkv = f32(np.concatenate([q, k, v], 1))
+    gb = f32(np.stack([g, beta])[:, :, None])
+    ref_out, ref_S = oracle.deltanet_recur(qkv, gb, f32(S0)[None], 1, 1, load)
+    # the same f32 inputs in float64
+    q, k, v = (qkv[:, i * D:(i + 1) * D].astype(np.float64) for i in range(3))
+    out, S = chunked(q, k, v, gb[0, :, 0].astype(np.float64), gb[1, :, 0].astype(np.float64),
+                     f32(S0).astype(np.float64))
+    rel = lambda a, b: np.linalg.norm(a - b) / np.linalg.norm(b)  # noqa: E731
+    assert rel(out, ref_out[:, 0]) < 1e-4
+    assert rel(S, ref_S[0]) < 1e-4
