@@ -37,7 +37,52 @@ def bf16(x):
     return u.astype(np.uint32).view(np.float32).astype(np.float64)
 
 
-def chunked(q, k, v, g, beta, S0, operand=lambda x: x):
+def tf32(x):
+    """Round f32 to tf32 as the prep does: add half an ulp of the 10-bit mantissa, truncate."""
+    u = np.asarray(x, dtype=np.float32).view(np.uint32)
+    return ((u.astype(np.uint64) + 0x1000) & 0xFFFFE000).astype(np.uint32).view(np.float32)
+
+
+def blocked_inverse(A):
+    """(I + A)^-1 of a strictly lower-triangular 64 x 64 f32 A (tf32 values) the
+    way gdn_prep_kernel builds it: 16 x 16 diagonal blocks by forward
+    substitution in f32 (every element rounded to tf32), the 32 x 32 blocks
+    T[2p+1][2p] = -T[2p+1][2p+1] A[2p+1][2p] T[2p][2p] in f32, and the 64 x 64
+    block T[1][0] = -T22 (A21 T11) on the tf32 tensor cores (A21 T11 rounded to
+    tf32 in between)."""
+    f32 = np.float32
+    T = np.zeros((64, 64), f32)
+    for base in range(0, 64, 16):
+        Ab = A[base:base + 16, base:base + 16]
+        blk = np.zeros((16, 16), f32)
+        for r in range(16):
+            acc = np.zeros(16, f32)
+            for j in range(r):
+                acc = (Ab[r, j].astype(np.float64) * blk[j] + acc).astype(f32)  # fmaf
+            blk[r] = tf32(np.where(np.arange(16) == r, f32(1), -acc))
+        T[base:base + 16, base:base + 16] = blk
+    for p in (0, 1):
+        rb, cb = 16 * (2 * p + 1), 32 * p
+        X1 = (A[rb:rb + 16, cb:cb + 16].astype(np.float64) @ T[cb:cb + 16, cb:cb + 16]).astype(f32)
+        T[rb:rb + 16, cb:cb + 16] = tf32(-(T[rb:rb + 16, rb:rb + 16].astype(np.float64) @ X1).astype(f32))
+    X2 = tf32((A[32:64, 0:32].astype(np.float64) @ T[0:32, 0:32]).astype(f32))
+    T[32:64, 0:32] = (-(T[32:64, 32:64].astype(np.float64) @ X2)).astype(f32)
+    return T.astype(np.float64)
+
+
+def exact_inverse(A):
+    return np.linalg.inv(np.eye(A.shape[0]) + A)
+
+
+def kernel_inverse(A):
+    """The prep's T for a chunk of n <= 64 tokens: A rounded to tf32, padded."""
+    n = A.shape[0]
+    Ap = np.zeros((64, 64), np.float32)
+    Ap[:n, :n] = tf32(A.astype(np.float32))
+    return blocked_inverse(Ap)[:n, :n]
+
+
+def chunked(q, k, v, g, beta, S0, operand=lambda x: x, inverse=exact_inverse):
     """q, k, v [T, D]; g, beta [T]; S0 [D, D].  Returns (out [T, D], S_T).
     ``operand`` rounds what the kernels hold as bf16 MMA operands: the state
     copy, R', W and Dsb (identity: the exact chunked form)."""
@@ -54,7 +99,7 @@ def chunked(q, k, v, g, beta, S0, operand=lambda x: x):
         i, j = np.indices((n, n))
         dec = np.where(j <= i, np.exp(np.where(j <= i, gam[:, None] - gam[None, :], 0.0)), 0.0)
         A = np.where(j < i, b[:, None] * ikc[:, None] * ikc[None, :] * dec * (K @ K.T), 0.0)
-        Tb = np.linalg.inv(np.eye(n) + A) * b[None, :]
+        Tb = inverse(A) * b[None, :]
         QKm = iqc[:, None] * ikc[None, :] * dec * (Q @ K.T)
         W = operand(np.vstack([Tb, QKm @ Tb]))
         c2, c3 = np.exp(gam) * ikc, np.exp(gam) * iqc
@@ -108,6 +153,35 @@ def test_bf16_operands_stay_inside_the_gpu_tolerance(T, decay, load):
     ref_out, ref_S = oracle.deltanet_recur(f32(np.concatenate([q, k, v], 1)), f32(np.stack([g, beta])[:, :, None]),
                                            f32(S0)[None], 1, 1, load)
     out, S = chunked(q, k, v, g.astype(np.float64), beta.astype(np.float64), S0.astype(np.float64), operand=bf16)
+    rel = lambda a, b: np.linalg.norm(a - b) / np.linalg.norm(b)  # noqa: E731
+    assert rel(out, ref_out[:, 0]) < 1e-2
+    assert rel(S, ref_S[0]) < 1e-2
+
+
+def test_blocked_tf32_inverse():
+    """The prep's blocked tf32 inverse against the exact one, alone and inside
+    the chunked form with bf16 operands (still inside the GPU bound)."""
+    rng = np.random.default_rng(11)
+    D, T = 128, 256
+    k = rng.standard_normal((64, D))
+    ik = 1 / np.sqrt((k * k).sum(1) + 1e-6)
+    b = 1 / (1 + np.exp(-rng.standard_normal(64)))
+    gam = np.cumsum(-np.log1p(np.exp(rng.standard_normal(64))))
+    i, j = np.indices((64, 64))
+    A = np.where(j < i, b[:, None] * ik[:, None] * ik[None, :] * np.exp(np.where(j < i, gam[:, None] - gam[None, :], 0))
+                 * (k @ k.T), 0.0)
+    Te, Tk = exact_inverse(A), kernel_inverse(A)
+    assert np.linalg.norm(Tk - Te) / np.linalg.norm(Te) < 1e-4  # measured 7.5e-6
+    q, kk, v = (bf16(rng.standard_normal((T, D))) for _ in range(3))
+    a = rng.standard_normal(T)
+    g = (-(np.maximum(a, 0) + np.log1p(np.exp(-np.abs(a))))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal(T)))).astype(np.float32)
+    S0 = (0.02 * rng.standard_normal((D, D))).astype(np.float32)
+    f32 = lambda x: np.ascontiguousarray(x, dtype=np.float32)  # noqa: E731
+    ref_out, ref_S = oracle.deltanet_recur(f32(np.concatenate([q, kk, v], 1)), f32(np.stack([g, beta])[:, :, None]),
+                                           f32(S0)[None], 1, 1, True)
+    out, S = chunked(q, kk, v, g.astype(np.float64), beta.astype(np.float64), S0.astype(np.float64), operand=bf16,
+                     inverse=kernel_inverse)
     rel = lambda a, b: np.linalg.norm(a - b) / np.linalg.norm(b)  # noqa: E731
     assert rel(out, ref_out[:, 0]) < 1e-2
     assert rel(S, ref_S[0]) < 1e-2
