@@ -41,3 +41,18 @@ def test_sizes_and_offsets_match_the_header(tmp_path):
         assert int(c_layout[name]) == ctypes.sizeof(cls), name
         for field, _ in cls._fields_:
             assert int(c_layout[f"{name}.{field}"]) == getattr(cls, field).offset, (name, field)
+
+
+def test_constants_match_the_header():
+    """Every HCU_* integer constant the Python binding also defines (as X or
+    HCU_X) has the header's value: formats, dtypes, options, status codes."""
+    from hachiue_b200 import _lib
+    text = open(os.path.join(ROOT, "include", "hachiue_cuda.h")).read()
+    defines = {name: int(value) for name, value in re.findall(r"#define HCU_([A-Z0-9_]+)\s+(\d+)\b", text)}
+    mirrored = 0
+    for name, value in defines.items():
+        for attr in (name, "HCU_" + name):
+            if hasattr(_lib, attr):
+                assert getattr(_lib, attr) == value, (attr, getattr(_lib, attr), value)
+                mirrored += 1
+    assert mirrored >= 20
